@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""Key-switching throughput of the B200-native CKKS hybrid key switch.
+
+Workload: N = 2^16, L = 35 ciphertext primes (one 58-bit
++ 34 x 42-bit), P = 5 x 60-bit special primes (alpha = 5, dnum = 7),
+ternary secret of Hamming weight 192, Gaussian error sigma 3.2; a batch of 64
+ciphertexts, ciphertext i rotated by step i+1 with its own Galois key (64 keys,
+18.8 GB resident in HBM).  One step = the 64 rotations.  Inputs (2.3 GB of
+ciphertexts + the keys) are far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  With N > 1 (torchrun), the ciphertext limbs
+are sharded cyclically over the ranks (limb j on rank j % N) and the 64 key
+switches are computed jointly: strong scaling, value = total key switches /
+the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LOG_N = 16
+QBITS = [58] + [42] * 34
+PBITS = [60] * 5
+BATCH = 64
+SCALE = 2.0 ** 40
+METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if r[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.rows)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port running the identical rotation key switch
+# ---------------------------------------------------------------------------
+def cpu_rotation_rate(n_rot: int):
+    from oracle.oracle import Oracle, gen_primes, set_threads
+    threads = os.cpu_count() or 1
+    set_threads(threads)
+    pr = gen_primes(LOG_N, QBITS + PBITS)
+    o = Oracle(LOG_N, pr[:len(QBITS)], pr[len(QBITS):])
+    s = o.secret(0, 192)
+    elt = o.galois_elt(1)
+    key = o.keygen_galois(s, elt, 1001)
+    rng = np.random.default_rng(5)
+    z = rng.uniform(-1, 1, o.N // 2)
+    ct = o.encrypt(s, o.encode(z, SCALE, len(QBITS)), len(QBITS), 7)
+    t0 = time.perf_counter()
+    for _ in range(n_rot):
+        ct = o.apply_galois(ct, len(QBITS), elt, key)
+    dt = time.perf_counter() - t0
+    return n_rot / dt, threads, dt
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the oracle port of the reference path on the host cores."""
+    if rank != 0:
+        return
+    from oracle.oracle import Oracle, gen_primes, set_threads
+    threads = os.cpu_count() or 1
+    set_threads(threads)
+    pr = gen_primes(LOG_N, QBITS + PBITS)
+    o = Oracle(LOG_N, pr[:len(QBITS)], pr[len(QBITS):])
+    s = o.secret(0, 192)
+    rng = np.random.default_rng(5)
+    z = rng.uniform(-1, 1, o.N // 2)
+    ct = o.encrypt(s, o.encode(z, SCALE, len(QBITS)), len(QBITS), 7)
+    keys = {}
+    times = []
+    for it in range(args.warmup + args.steps):
+        step = (it % BATCH) + 1
+        elt = o.galois_elt(step)
+        if elt not in keys:
+            keys = {elt: o.keygen_galois(s, elt, 1000 + step)}
+        t0 = time.perf_counter()
+        ct = o.apply_galois(ct, len(QBITS), elt, keys[elt])
+        dt = time.perf_counter() - t0
+        if it >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    value = len(times) / total
+    line = {
+        "metric": METRIC, "value": value, "unit": "key-switches/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u64",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config3-rotation", "N": 1 << LOG_N, "L": len(QBITS),
+                   "alpha": len(PBITS), "dnum": 7, "sample": "one rotation key switch per step"},
+        "cpu_baseline": {"value": value, "unit": "key-switches/s", "cores": threads,
+                         "kind": "port",
+                         "sample": "%d rotation key switches at config 3 (oracle/ C++ port, "
+                                   "OpenMP over limbs)" % len(times)},
+        "e2e": {"value": value, "unit": "key-switches/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world):
+    import torch
+    import torch.distributed as dist
+    from comp390project_b200 import KS_KEY_GALOIS, KsContext, gen_primes, secret_generate
+
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(dev)
+    pr = gen_primes(LOG_N, QBITS + PBITS)
+    q, p = pr[:len(QBITS)], pr[len(QBITS):]
+    L = len(q)
+    if world > 1:
+        ctx = KsContext.from_process_group(LOG_N, q, p, device=dev)
+    else:
+        ctx = KsContext(LOG_N, q, p, device=dev)
+    N = 1 << LOG_N
+    nloc = ctx.n_local_limbs(L)
+    B = args.batch
+    steps_of = [i + 1 for i in range(B)]
+    # keys: one Galois key per rotation step, generated on the device
+    s = secret_generate(LOG_N, 0, 192)
+    for st in steps_of:
+        ctx.key_generate(KS_KEY_GALOIS, ctx.galois_elt(st), s, 1000 + st)
+    torch.cuda.synchronize()
+    # ciphertexts: uniform residues per owned limb (a fresh encryption is
+    # uniform in this distribution); [B][2][nloc][N]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+    cts = torch.empty((B, 2, nloc, N), dtype=torch.int64, device="cuda")
+    for sl in range(nloc):
+        j = rank + sl * world
+        cts[:, :, sl, :] = torch.randint(0, int(q[j]), (B, 2, N), generator=g, device="cuda",
+                                         dtype=torch.int64)
+    views = [cts[i] for i in range(B)]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ctx.rotate_batch(views, steps_of, L, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    time.sleep(0.3)
+    ctx.profile_enable(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    launches = 0
+    for _ in range(args.steps):
+        step()
+        launches += ctx.last_launch_count()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ctx.profile_enable(False)
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    prof = ctx.profile_read()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    total_ks = B * args.steps
+    value = total_ks / (ms / 1000.0)
+
+    # dominant stage and its roofline (two-pass NTT counted as one transform)
+    stages = {k: v for k, v in prof.items() if v[1] > 0}
+    dom = max(stages, key=lambda k: stages[k][0])
+    per_launch_ms = stages[dom][0] / stages[dom][1]
+    QlP = L + len(p)
+    beta = 7
+    U = 8 * N
+    n_out = len(range(rank, L, world)) + sum(1 for i in range(len(p)) if (L + i) % world == rank)
+    n_q = nloc
+    alg = {
+        "modup_ntt": (beta * n_out - sum(1 for j in range(rank, L, world))) * 2 * U,
+        "inner_product": (beta * n_out * 3 + 2 * n_out) * U,
+        "modup_bconv": (beta * 0 + L) * U + (beta * n_out - n_q) * U,
+        "moddown_ntt": 2 * n_q * 2 * U,
+        "intt_input": n_q * 2 * U,
+        "galois": 4 * n_q * U,
+        "moddown_finish": (2 * n_out + 2 * n_q + 3 * n_q) * U,
+        "moddown_bconv": (2 * len(p) + 2 * n_q) * U,
+        "intt_p": 2 * len(p) * 2 * U,
+    }
+    peak, peak_kind = measured_peaks()
+    achieved = alg.get(dom, 0) / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
+
+    # end to end through the C ABI with host buffers (pinned), copies timed
+    e2e = None
+    if args.e2e_steps > 0:
+        host_in = torch.empty_like(cts, device="cpu").pin_memory()
+        host_in.copy_(cts)
+        host_out = torch.empty_like(host_in).pin_memory()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            cts.copy_(host_in, non_blocking=True)
+            step()
+            host_out.copy_(cts, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ems], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        nbytes = host_in.numel() * 8
+        e2e = {"value": B * args.e2e_steps / (ems / 1000.0), "unit": "key-switches/s",
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, dt = cpu_rotation_rate(2)
+        cpu = {"value": rate, "unit": "key-switches/s", "cores": cores, "kind": "port",
+               "sample": "2 rotation key switches at config 3 on the host (%.1f s), oracle/ "
+                         "C++ port with OpenMP over limbs" % dt}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "key-switches/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic",
+            "config": {"workload": "config3-rotation: 64 ciphertexts, steps 1..64, 64 Galois keys",
+                       "N": N, "L": L, "alpha": len(p), "dnum": beta, "batch": B,
+                       "parallelism": "limb-sharded x%d (input broadcast)" % world,
+                       "l2": "inputs (2.3 GB cts + 18.8 GB keys) exceed L2; no flush"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "launch_ms": per_launch_ms},
+            "stages_ms_per_ks": {k: v[0] / total_ks for k, v in stages.items()},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    run_ours(args, rank, world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,257 @@
+"""Python host side over the C ABI: one ``KsContext`` per GPU / rank.
+
+Device buffers are torch tensors (dtype int64 holding uint64 words, the
+PhantomCiphertext layout [poly][limb][N]); torch supplies memory and streams
+only, every computation runs in libks_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _capi
+from ._capi import (KS_KEY_GALOIS, KS_KEY_RELIN, KS_MODE_INPUT_BROADCAST, KS_NCCL_ID_BYTES,
+                    check, ks_params)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _stream_ptr(stream, device) -> Optional[int]:
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def gen_primes(log_n: int, bit_sizes: Sequence[int]) -> np.ndarray:
+    """Phantom/SEAL CoeffModulus::Create rule (through the C ABI, host only)."""
+    bits = (C.c_int * len(bit_sizes))(*[int(b) for b in bit_sizes])
+    out = np.zeros(len(bit_sizes), dtype=np.uint64)
+    check(_capi.load().ks_gen_primes(int(log_n), bits, len(bit_sizes),
+                                     out.ctypes.data_as(C.POINTER(C.c_uint64))))
+    return out
+
+
+def secret_generate(log_n: int, seed: int, hamming_weight: int = 0) -> np.ndarray:
+    out = np.zeros(1 << log_n, dtype=np.int8)
+    check(_capi.load().ks_secret_generate(int(log_n), int(seed), int(hamming_weight),
+                                          out.ctypes.data_as(C.POINTER(C.c_int8))))
+    return out
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(KS_NCCL_ID_BYTES)
+    check(_capi.load().ks_nccl_unique_id(buf, KS_NCCL_ID_BYTES))
+    return buf.raw
+
+
+class KsContext:
+    """Key-switching context of one device (rank ``rank`` of ``world``)."""
+
+    def __init__(self, log_n: int, q: Sequence[int], p: Sequence[int], device: int = 0,
+                 rank: int = 0, world: int = 1, nccl_id: Optional[bytes] = None,
+                 mode: int = KS_MODE_INPUT_BROADCAST, max_batch: int = 1, _handle=None):
+        self.lib = _capi.load()
+        self.log_n = int(log_n)
+        self.N = 1 << self.log_n
+        self.q = np.ascontiguousarray(q, dtype=np.uint64)
+        self.p = np.ascontiguousarray(p, dtype=np.uint64)
+        self.L, self.alpha = len(self.q), len(self.p)
+        self.device, self.rank, self.world, self.mode = int(device), int(rank), int(world), mode
+        self.h = None
+        if _handle is not None:
+            self.h = _handle
+            return
+        prm = self._params(max_batch)
+        h = C.c_void_p()
+        idb = None
+        if world > 1:
+            if nccl_id is None or len(nccl_id) < KS_NCCL_ID_BYTES:
+                raise ValueError("world > 1 needs the NCCL unique id bytes")
+            idb = C.create_string_buffer(bytes(nccl_id), KS_NCCL_ID_BYTES)
+        check(self.lib.ks_ctx_create(C.byref(prm), self.device, self.rank, self.world, idb,
+                                     C.byref(h)))
+        self.h = h
+
+    def _params(self, max_batch=1):
+        self._qbuf = (C.c_uint64 * self.L)(*[int(x) for x in self.q])
+        self._pbuf = (C.c_uint64 * max(1, self.alpha))(*[int(x) for x in self.p] or [0])
+        return ks_params(self.log_n, self.L, self._qbuf, self.alpha, self._pbuf, int(self.mode),
+                         int(max_batch))
+
+    @classmethod
+    def create_all(cls, log_n, q, p, devices: Sequence[int], mode=KS_MODE_INPUT_BROADCAST):
+        """Single-process multi-GPU (ncclCommInitAll), one context per device."""
+        lib = _capi.load()
+        proto = cls.__new__(cls)
+        proto.q = np.ascontiguousarray(q, dtype=np.uint64)
+        proto.p = np.ascontiguousarray(p, dtype=np.uint64)
+        proto.L, proto.alpha, proto.log_n, proto.mode = len(proto.q), len(proto.p), int(log_n), mode
+        prm = proto._params()
+        n = len(devices)
+        devs = (C.c_int * n)(*devices)
+        hs = (C.c_void_p * n)()
+        check(lib.ks_ctx_create_all(C.byref(prm), devs, n, hs))
+        return [cls(log_n, q, p, device=devices[i], rank=i, world=n, mode=mode,
+                    _handle=C.c_void_p(hs[i])) for i in range(n)]
+
+    @classmethod
+    def from_process_group(cls, log_n, q, p, device: Optional[int] = None, group=None,
+                           mode=KS_MODE_INPUT_BROADCAST, max_batch=1):
+        """One context per torch.distributed rank; rank 0's NCCL id is broadcast."""
+        import torch.distributed as dist
+        torch = _torch()
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        if device is None:
+            device = torch.cuda.current_device()
+        obj = [nccl_unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(log_n, q, p, device=device, rank=rank, world=world,
+                   nccl_id=obj[0] if world > 1 else None, mode=mode, max_batch=max_batch)
+
+    # -- lifecycle -----------------------------------------------------------
+    def close(self):
+        if self.h is not None:
+            self.lib.ks_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        return check(rc, self.h)
+
+    # -- queries -------------------------------------------------------------
+    def n_local_limbs(self, total: int) -> int:
+        return self._check(self.lib.ks_n_local_limbs(self.h, int(total)))
+
+    def num_digits(self, level_limbs: int) -> int:
+        return self._check(self.lib.ks_num_digits(self.h, int(level_limbs)))
+
+    def galois_elt(self, step: int) -> int:
+        e = C.c_uint32()
+        self._check(self.lib.ks_galois_elt(self.h, int(step), C.byref(e)))
+        return int(e.value)
+
+    def key_words(self) -> int:
+        return int(self.lib.ks_key_words(self.h))
+
+    def last_launch_count(self) -> int:
+        return int(self.lib.ks_last_launch_count(self.h))
+
+    def profile_enable(self, on: bool = True):
+        self._check(self.lib.ks_profile_enable(self.h, 1 if on else 0))
+
+    def profile_read(self) -> dict:
+        n = int(self.lib.ks_profile_stage_count())
+        ms = (C.c_double * n)()
+        calls = (C.c_int * n)()
+        self._check(self.lib.ks_profile_read(self.h, ms, calls, n))
+        return {self.lib.ks_profile_stage_name(i).decode(): (float(ms[i]), int(calls[i]))
+                for i in range(n)}
+
+    def set_timeout_ms(self, ms: int):
+        self._check(self.lib.ks_set_timeout_ms(self.h, int(ms)))
+
+    # -- keys ----------------------------------------------------------------
+    def key_upload(self, kind: int, elt: int, key: np.ndarray):
+        key = np.ascontiguousarray(key, dtype=np.uint64)
+        self._check(self.lib.ks_key_upload(self.h, kind, int(elt), key.ctypes.data, key.size))
+
+    def key_upload_device(self, kind: int, elt: int, key, stream=None):
+        self._check(self.lib.ks_key_upload_device(self.h, kind, int(elt), self._ptr(key),
+                                                  key.numel(), _stream_ptr(stream, self.device)))
+
+    def key_generate(self, kind: int, elt: int, secret: np.ndarray, seed: int, stream=None):
+        s = np.ascontiguousarray(secret, dtype=np.int8)
+        self._check(self.lib.ks_key_generate(self.h, kind, int(elt), s.ctypes.data, int(seed),
+                                             _stream_ptr(stream, self.device)))
+
+    def key_download(self, kind: int, elt: int) -> np.ndarray:
+        beta = (self.L + self.alpha - 1) // self.alpha
+        limbs = len(range(self.rank, self.L + self.alpha, self.world))
+        out = np.zeros((beta, 2, limbs, self.N), dtype=np.uint64)
+        self._check(self.lib.ks_key_download(self.h, kind, int(elt), out.ctypes.data, out.size))
+        return out
+
+    def key_drop(self, kind: int, elt: int):
+        self._check(self.lib.ks_key_drop(self.h, kind, int(elt)))
+
+    # -- hot path ------------------------------------------------------------
+    def _ptr(self, t) -> int:
+        torch = _torch()
+        if not isinstance(t, torch.Tensor):
+            raise TypeError("expected a torch tensor")
+        if t.dtype not in (torch.int64, torch.uint64):
+            raise TypeError("expected int64/uint64 words")
+        if not t.is_cuda or t.device.index != self.device:
+            raise ValueError("tensor must live on cuda:%d" % self.device)
+        if not t.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return t.data_ptr()
+
+    def relinearize(self, ct, level_limbs: int, stream=None):
+        self._check(self.lib.ks_relinearize(self.h, self._ptr(ct), int(level_limbs),
+                                            _stream_ptr(stream, self.device)))
+
+    def apply_galois(self, ct, level_limbs: int, elt: int, stream=None):
+        self._check(self.lib.ks_apply_galois(self.h, self._ptr(ct), int(level_limbs), int(elt),
+                                             _stream_ptr(stream, self.device)))
+
+    def rotate(self, ct, level_limbs: int, step: int, stream=None):
+        self._check(self.lib.ks_rotate(self.h, self._ptr(ct), int(level_limbs), int(step),
+                                       _stream_ptr(stream, self.device)))
+
+    def rotate_batch(self, cts, steps: Sequence[int], level_limbs: int, stream=None):
+        n = len(cts)
+        ptrs = (C.c_void_p * n)(*[self._ptr(t) for t in cts])
+        st = (C.c_int * n)(*[int(s) for s in steps])
+        self._check(self.lib.ks_rotate_batch(self.h, ptrs, st, n, int(level_limbs),
+                                             _stream_ptr(stream, self.device)))
+
+    def rotate_hoisted(self, ct, level_limbs: int, steps: Sequence[int], outs, stream=None):
+        n = len(steps)
+        ptrs = (C.c_void_p * n)(*[self._ptr(t) for t in outs])
+        st = (C.c_int * n)(*[int(s) for s in steps])
+        self._check(self.lib.ks_rotate_hoisted(self.h, self._ptr(ct), int(level_limbs), st, n,
+                                               ptrs, _stream_ptr(stream, self.device)))
+
+    def ntt_forward(self, data, n_limbs: int, first_prime: int = 0, batch: int = 1, stream=None):
+        self._check(self.lib.ks_ntt_forward(self.h, self._ptr(data), int(n_limbs),
+                                            int(first_prime), int(batch),
+                                            _stream_ptr(stream, self.device)))
+
+    def ntt_inverse(self, data, n_limbs: int, first_prime: int = 0, batch: int = 1, stream=None):
+        self._check(self.lib.ks_ntt_inverse(self.h, self._ptr(data), int(n_limbs),
+                                            int(first_prime), int(batch),
+                                            _stream_ptr(stream, self.device)))
+
+    def scatter_limbs(self, global_buf, local_buf, n_polys: int, total_limbs: int, stream=None):
+        self._check(self.lib.ks_scatter_limbs(self.h, self._ptr(global_buf), self._ptr(local_buf),
+                                              int(n_polys), int(total_limbs),
+                                              _stream_ptr(stream, self.device)))
+
+    def gather_limbs(self, local_buf, global_buf, n_polys: int, total_limbs: int, stream=None):
+        self._check(self.lib.ks_gather_limbs(self.h, self._ptr(local_buf), self._ptr(global_buf),
+                                             int(n_polys), int(total_limbs),
+                                             _stream_ptr(stream, self.device)))
+
+    def allgather_limbs(self, local_buf, full_buf, total_limbs: int, stream=None):
+        self._check(self.lib.ks_allgather_limbs(self.h, self._ptr(local_buf), self._ptr(full_buf),
+                                                int(total_limbs),
+                                                _stream_ptr(stream, self.device)))
+
+
+__all__ = ["KsContext", "gen_primes", "secret_generate", "nccl_unique_id", "KS_KEY_RELIN",
+           "KS_KEY_GALOIS"]

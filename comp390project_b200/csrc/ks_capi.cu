@@ -1,0 +1,1074 @@
+// ks_capi.cu -- context set-up, key management, the hybrid key-switch
+// pipeline and the extern "C" entry points declared in include/ks_capi.h.
+//
+// Pipeline of one key switch on rank g of G (input-broadcast mode; G = 1 is
+// the single-GPU path), following the stage order of the reference's
+// keyswitching_output_aggregation (output_aggregation.cu:197-294) and
+// Phantom's keyswitch_inplace (input_broadcast.cu:172):
+//   1. automorphism of c0, c1 (rotation only)            -> g0, g1
+//   2. INTT of the input limbs, all-gather over ranks     -> coefficient form
+//   3. ModUp base extension of every digit to the owned QlP limbs, NTT
+//   4. inner product with the evaluation-key shard        -> cx (owned limbs)
+//   5. INTT of the owned P limbs of cx, all-gather        -> P part, coefficient form
+//   6. conversion P -> owned Q limbs, NTT
+//   7. (cx - conv) * P^-1, add to the ciphertext          -> ct (in place)
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/ks_capi.h"
+#include "ks_context.hpp"
+#include "ks_hostmath.hpp"
+
+using namespace ksb;
+
+struct ks_ctx {
+  Ctx c;
+};
+
+namespace {
+
+std::mutex g_err_mu;
+std::string g_err;
+
+void set_global_err(const std::string &s) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  g_err = s;
+}
+
+struct KsError {
+  int code;
+  std::string msg;
+};
+
+#define KS_CUDA(expr)                                                                     \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    if (_e != cudaSuccess)                                                                \
+      throw KsError{KS_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)};     \
+  } while (0)
+#define KS_NCCL(expr)                                                                     \
+  do {                                                                                    \
+    ncclResult_t _r = (expr);                                                             \
+    if (_r != ncclSuccess)                                                                \
+      throw KsError{KS_ERR_NCCL, std::string(#expr) + ": " + ncclGetErrorString(_r)};     \
+  } while (0)
+#define KS_REQUIRE(cond, msg)                                                             \
+  do {                                                                                    \
+    if (!(cond)) throw KsError{KS_ERR_INVALID, msg};                                      \
+  } while (0)
+
+template <class F>
+int guarded(ks_ctx *ctx, F &&f) {
+  try {
+    f();
+    return KS_OK;
+  } catch (const KsError &e) {
+    if (ctx) ctx->c.err = e.msg;
+    set_global_err(e.msg);
+    return e.code;
+  } catch (const std::exception &e) {
+    if (ctx) ctx->c.err = e.what();
+    set_global_err(e.what());
+    return KS_ERR_INVALID;
+  }
+}
+
+template <class T>
+T *dev_alloc(size_t n) {
+  void *p = nullptr;
+  if (n == 0) n = 1;
+  cudaError_t e = cudaMalloc(&p, n * sizeof(T));
+  if (e != cudaSuccess)
+    throw KsError{KS_ERR_ALLOC, std::string("cudaMalloc ") + std::to_string(n * sizeof(T)) +
+                                    " bytes: " + cudaGetErrorString(e)};
+  return static_cast<T *>(p);
+}
+
+template <class T>
+T *upload(const std::vector<T> &v) {
+  T *d = dev_alloc<T>(v.size());
+  if (!v.empty()) KS_CUDA(cudaMemcpy(d, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return d;
+}
+
+void up_ints(DevInts &t) { t.d = upload(t.h); }
+void up_i64(DevI64 &t) { t.d = upload(t.h); }
+
+inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+int n_local(int g, int G, int total) { return g < total ? (total - g - 1) / G + 1 : 0; }
+
+u64 mix64h(u64 z) {
+  z ^= z >> 30;
+  z *= 0xBF58476D1CE4E5B9ull;
+  z ^= z >> 27;
+  z *= 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return z;
+}
+// Per-(seed, domain) key of the counter hash prng(seed, dom, idx) =
+// mix64(key + (idx + 1) * golden); the CPU oracle uses the same definition.
+u64 prng_stream(u64 seed, u64 dom) { return mix64h(seed ^ mix64h(dom + 0x9E3779B97F4A7C15ull)); }
+u64 prng_at(u64 seed, u64 dom, u64 idx) {
+  return mix64h(prng_stream(seed, dom) + (idx + 1) * 0x9E3779B97F4A7C15ull);
+}
+enum : u64 { DOM_SECRET = 1, DOM_SECRET_SIGN = 2, DOM_KEY_A = 3, DOM_KEY_E = 4 };
+
+// ---------------------------------------------------------------------------
+// Context construction
+// ---------------------------------------------------------------------------
+void build_tables(Ctx &c) {
+  const int N = c.N, K = c.K;
+  std::vector<PrimeDev> pd(K);
+  std::vector<ulonglong2> fwd((size_t)K * N), inv((size_t)K * N);
+  std::vector<std::thread> th;
+  auto work = [&](int k) {
+    const u64 q = c.primes[k];
+    const u64 psi = h_min_psi(q, (u64)N), psii = h_invmod(psi, q);
+    std::vector<u64> pw(N), pwi(N);
+    pw[0] = pwi[0] = 1;
+    for (int i = 1; i < N; ++i) {
+      pw[i] = h_mulmod(pw[i - 1], psi, q);
+      pwi[i] = h_mulmod(pwi[i - 1], psii, q);
+    }
+    for (int i = 0; i < N; ++i) {
+      const uint32_t r = h_brev((uint32_t)i, c.log_n);
+      fwd[(size_t)k * N + i] = make_ulonglong2(pw[r], h_shoup(pw[r], q));
+      inv[(size_t)k * N + i] = make_ulonglong2(pwi[r], h_shoup(pwi[r], q));
+    }
+    PrimeDev &P = pd[k];
+    P.q = q;
+    P.two_q = 2 * q;
+    h_barrett_ratio(q, P.br_hi, P.br_lo);
+    P.ninv = h_invmod((u64)N % q, q);
+    P.ninv_sh = h_shoup(P.ninv, q);
+    P.w1ninv = h_mulmod(pwi[N / 2], P.ninv, q);
+    P.w1ninv_sh = h_shoup(P.w1ninv, q);
+  };
+  const int nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  for (int t0 = 0; t0 < nth; ++t0)
+    th.emplace_back([&, t0] {
+      for (int k = t0; k < K; k += nth) work(k);
+    });
+  for (auto &t : th) t.join();
+  c.d_primes = upload(pd);
+  c.d_tw_fwd = upload(fwd);
+  c.d_tw_inv = upload(inv);
+
+  // Discrete Gaussian CDT (sigma 3.2, |e| <= 19) for the synthetic keys.
+  std::vector<u64> T(20);
+  {
+    const double sigma = 3.2;
+    double rho[20], Z = 0, cum = 0;
+    for (int x = 0; x < 20; ++x) {
+      rho[x] = std::exp(-(double)x * x / (2 * sigma * sigma));
+      Z += (x == 0 ? 1.0 : 2.0) * rho[x];
+    }
+    for (int x = 0; x < 20; ++x) {
+      cum += (x == 0 ? 1.0 : 2.0) * rho[x];
+      T[x] = (x == 19) ? (1ull << 63) : (u64)(cum / Z * 9223372036854775808.0);
+    }
+  }
+  c.d_gauss = upload(T);
+}
+
+void build_moddown(Ctx &c) {
+  const int a = c.alpha, L = c.L;
+  if (a == 0) return;
+  std::vector<ulonglong2> phatinv(a), pinv(L);
+  std::vector<u64> w((size_t)L * a);
+  for (int i = 0; i < a; ++i) {
+    const u64 pi = c.primes[L + i];
+    u64 prod = 1;
+    for (int t = 0; t < a; ++t)
+      if (t != i) prod = h_mulmod(prod, c.primes[L + t] % pi, pi);
+    const u64 v = h_invmod(prod, pi);
+    phatinv[i] = make_ulonglong2(v, h_shoup(v, pi));
+  }
+  for (int j = 0; j < L; ++j) {
+    const u64 q = c.primes[j];
+    u64 P = 1;
+    for (int t = 0; t < a; ++t) P = h_mulmod(P, c.primes[L + t] % q, q);
+    const u64 v = h_invmod(P, q);
+    pinv[j] = make_ulonglong2(v, h_shoup(v, q));
+    for (int i = 0; i < a; ++i) {
+      u64 r = 1;
+      for (int t = 0; t < a; ++t)
+        if (t != i) r = h_mulmod(r, c.primes[L + t] % q, q);
+      w[(size_t)j * a + i] = r;
+    }
+  }
+  c.d_phatinv = upload(phatinv);
+  c.d_pinv = upload(pinv);
+  c.d_mdw = upload(w);
+  c.md = ModDownDev{a, L, c.d_phatinv, c.d_mdw, c.d_pinv};
+}
+
+void build_level(Ctx &c, Level &lv, int Ql) {
+  const int a = c.alpha, L = c.L, G = c.world, g = c.rank;
+  lv.Ql = Ql;
+  lv.QlP = Ql + a;
+  lv.beta = (Ql + a - 1) / a;
+  lv.prime_of.h.resize(lv.QlP);
+  for (int j = 0; j < lv.QlP; ++j) lv.prime_of.h[j] = j < Ql ? j : L + (j - Ql);
+  // owned output limbs: Q limbs j = g, g+G, ... then P limbs with key index (L+i) % G == g
+  for (int j = g; j < Ql; j += G) lv.out_j.h.push_back(j);
+  lv.n_q = (int)lv.out_j.h.size();
+  std::vector<int> own_p;
+  for (int i = 0; i < a; ++i)
+    if ((L + i) % G == g) own_p.push_back(i);
+  lv.n_p = (int)own_p.size();
+  for (int i : own_p) lv.out_j.h.push_back(Ql + i);
+  lv.n_out = (int)lv.out_j.h.size();
+  for (int s = 0; s < lv.n_out; ++s) {
+    const int j = lv.out_j.h[s];
+    lv.key_slot.h.push_back(lv.prime_of.h[j] / G);
+    lv.c_slot.h.push_back(j < Ql ? j / G : -1);
+  }
+  lv.coef_ml = (Ql + G - 1) / G;
+  for (int d = 0; d < lv.beta; ++d)
+    for (int s = 0; s < lv.n_out; ++s) {
+      const int j = lv.out_j.h[s];
+      const bool in_digit = j < Ql && j / a == d;
+      lv.t_jobs.h.push_back(in_digit ? -1 : lv.prime_of.h[j]);
+    }
+  for (int s = 0; s < lv.n_q; ++s) {
+    lv.q_index.h.push_back(lv.out_j.h[s]);
+    lv.cx_slot_q.h.push_back(s);
+  }
+  for (int p = 0; p < 2; ++p)
+    for (int s = 0; s < lv.n_q; ++s) lv.z_jobs.h.push_back(lv.out_j.h[s]);
+  // P part: offsets of the owned P slots that get inverse-transformed
+  const long long N = c.N;
+  for (int p = 0; p < 2; ++p)
+    for (int k = 0; k < lv.n_p; ++k) {
+      lv.p_jobs.h.push_back(L + own_p[k]);
+      if (G == 1) lv.p_offsets.h.push_back(((long long)p * lv.n_out + lv.n_q + k) * N);
+      else lv.p_offsets.h.push_back(((long long)k * 2 + p) * N);  // ysend [max_p][2][N]
+    }
+  // where P limb i of poly p lives after the (optional) all-gather
+  for (int p = 0; p < 2; ++p)
+    for (int i = 0; i < a; ++i) {
+      if (G == 1) {
+        lv.y_off.h.push_back(((long long)p * lv.n_out + lv.n_q + i) * N);
+      } else {
+        const int owner = (L + i) % G;
+        int pslot = 0;
+        for (int i2 = 0; i2 < i; ++i2)
+          if ((L + i2) % G == owner) ++pslot;
+        lv.y_off.h.push_back((((long long)owner * c.max_p_own + pslot) * 2 + p) * N);
+      }
+    }
+  // ModUp constants
+  std::vector<ulonglong2> qhi((size_t)lv.beta * a, make_ulonglong2(0, 0));
+  std::vector<u64> w((size_t)lv.beta * lv.QlP * a, 0);
+  for (int d = 0; d < lv.beta; ++d) {
+    const int lo = d * a, hi = std::min(Ql, lo + a);
+    for (int i = lo; i < hi; ++i) {
+      const u64 qi = c.primes[i];
+      u64 prod = 1;
+      for (int t = lo; t < hi; ++t)
+        if (t != i) prod = h_mulmod(prod, c.primes[t] % qi, qi);
+      const u64 v = h_invmod(prod, qi);
+      qhi[(size_t)d * a + (i - lo)] = make_ulonglong2(v, h_shoup(v, qi));
+    }
+    for (int j = 0; j < lv.QlP; ++j) {
+      const u64 m = c.primes[lv.prime_of.h[j]];
+      for (int i = lo; i < hi; ++i) {
+        u64 r = 1 % m;
+        for (int t = lo; t < hi; ++t)
+          if (t != i) r = h_mulmod(r, c.primes[t] % m, m);
+        w[((size_t)d * lv.QlP + j) * a + (i - lo)] = r;
+      }
+    }
+  }
+  up_ints(lv.prime_of);
+  up_ints(lv.out_j);
+  up_ints(lv.key_slot);
+  up_ints(lv.c_slot);
+  up_ints(lv.t_jobs);
+  up_ints(lv.q_index);
+  up_ints(lv.z_jobs);
+  up_ints(lv.cx_slot_q);
+  up_ints(lv.p_jobs);
+  up_i64(lv.p_offsets);
+  up_i64(lv.y_off);
+  lv.qhatinv = upload(qhi);
+  lv.w = upload(w);
+  lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w};
+  lv.lay = KsLayout{lv.n_out, lv.out_j.d, lv.key_slot.d, lv.c_slot.d, G, lv.coef_ml};
+}
+
+void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncclComm_t comm,
+              const void *nccl_id) {
+  KS_REQUIRE(prm != nullptr, "params is null");
+  KS_REQUIRE(ntt_supported_log_n((int)prm->log_n), "log_n must be in [12, 16]");
+  KS_REQUIRE(prm->n_q >= 1 && prm->q != nullptr, "need at least one Q prime");
+  KS_REQUIRE(prm->n_p >= 0 && prm->n_p <= KS_MAX_ALPHA, "alpha must be in [0, 8]");
+  KS_REQUIRE(prm->n_p == 0 || prm->p != nullptr, "P primes missing");
+  KS_REQUIRE(world >= 1 && rank >= 0 && rank < world, "bad rank/world");
+  KS_REQUIRE(prm->n_q + prm->n_p <= KS_MAX_PRIMES, "too many primes");
+  c.device = device;
+  c.rank = rank;
+  c.world = world;
+  c.mode = world > 1 ? prm->mode : KS_MODE_INPUT_BROADCAST;
+  KS_REQUIRE(c.mode == KS_MODE_INPUT_BROADCAST || c.mode == KS_MODE_OUTPUT_AGGREGATION,
+             "unknown mode");
+  if (c.mode == KS_MODE_OUTPUT_AGGREGATION)
+    throw KsError{KS_ERR_UNSUPPORTED, "output-aggregation mode is not built yet"};
+  c.max_batch = std::max(1, prm->max_batch);
+  c.log_n = (int)prm->log_n;
+  c.N = 1 << c.log_n;
+  c.L = prm->n_q;
+  c.alpha = prm->n_p;
+  c.K = c.L + c.alpha;
+  for (int i = 0; i < c.L; ++i) c.primes.push_back(prm->q[i]);
+  for (int i = 0; i < c.alpha; ++i) c.primes.push_back(prm->p[i]);
+  for (int k = 0; k < c.K; ++k) {
+    const u64 q = c.primes[k];
+    KS_REQUIRE(q > 2 && q < (1ull << 61), "primes must be below 2^61");
+    KS_REQUIRE(q % (2ull * c.N) == 1, "primes must be 1 mod 2N");
+    KS_REQUIRE(h_is_prime(q), "modulus is not prime");
+    for (int k2 = 0; k2 < k; ++k2) KS_REQUIRE(c.primes[k2] != q, "primes must be distinct");
+  }
+  KS_CUDA(cudaSetDevice(device));
+  build_tables(c);
+  for (int kj = rank; kj < c.K; kj += world) c.own_key.push_back(kj);
+  c.own_key_prime.h = c.own_key;
+  up_ints(c.own_key_prime);
+  if (c.alpha > 0) {
+    for (int g = 0; g < world; ++g) {
+      int cnt = 0;
+      for (int i = 0; i < c.alpha; ++i)
+        if ((c.L + i) % world == g) ++cnt;
+      c.max_p_own = std::max(c.max_p_own, cnt);
+    }
+    build_moddown(c);
+    c.levels.resize(c.L + 1);
+    for (int Ql = 1; Ql <= c.L; ++Ql) build_level(c, c.levels[Ql], Ql);
+    // scratch, sized for the top level
+    const Level &top = c.levels[c.L];
+    const size_t N = c.N;
+    const size_t nq = n_local(rank, world, c.L), ml = (c.L + world - 1) / world;
+    const size_t n_key_own = c.own_key.size();
+    size_t w_g = 2 * nq * N, w_coef = ml * N, w_coef_all = world > 1 ? world * ml * N : 0;
+    size_t w_t = std::max((size_t)top.beta * top.n_out * N, 3 * n_key_own * N);
+    size_t w_cx = 2 * (size_t)top.n_out * N;
+    size_t w_ys = world > 1 ? (size_t)c.max_p_own * 2 * N : 0;
+    size_t w_ya = world > 1 ? (size_t)world * c.max_p_own * 2 * N : 0;
+    size_t w_z = 2 * nq * N;
+    c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z;
+    c.arena = dev_alloc<u64>(c.arena_words);
+    u64 *p = c.arena;
+    c.s_g = p; p += w_g;
+    c.s_coef = p; p += w_coef;
+    c.s_coef_all = world > 1 ? p : c.s_coef; p += w_coef_all;
+    c.s_t = p; p += w_t;
+    c.s_cx = p; p += w_cx;
+    c.s_ysend = p; p += w_ys;
+    c.s_yall = p; p += w_ya;
+    c.s_z = p; p += w_z;
+  }
+  if (world > 1) {
+    if (comm) {
+      c.comm = comm;
+    } else {
+      KS_REQUIRE(nccl_id != nullptr, "world > 1 needs an NCCL unique id");
+      ncclUniqueId id;
+      std::memcpy(&id, nccl_id, sizeof(id));
+      KS_NCCL(ncclCommInitRank(&c.comm, world, id, rank));
+    }
+    c.own_comm = true;
+  }
+  KS_CUDA(cudaDeviceSynchronize());
+}
+
+void ctx_free(Ctx &c) {
+  cudaSetDevice(c.device);
+  cudaDeviceSynchronize();
+  auto f = [](void *p) {
+    if (p) cudaFree(p);
+  };
+  for (auto &kv : c.keys) f(kv.second.d);
+  c.keys.clear();
+  for (auto &lv : c.levels) {
+    for (DevInts *t : {&lv.prime_of, &lv.out_j, &lv.key_slot, &lv.c_slot, &lv.t_jobs,
+                       &lv.q_index, &lv.z_jobs, &lv.cx_slot_q, &lv.p_jobs})
+      f(t->d);
+    f(lv.p_offsets.d);
+    f(lv.y_off.d);
+    f(lv.qhatinv);
+    f(lv.w);
+  }
+  f(c.own_key_prime.d);
+  f(c.d_primes);
+  f(c.d_tw_fwd);
+  f(c.d_tw_inv);
+  f(c.d_gauss);
+  f(c.d_phatinv);
+  f(c.d_pinv);
+  f(c.d_mdw);
+  f(c.arena);
+  for (auto &pe : c.prof_events) {
+    cudaEventDestroy(pe.second.first);
+    cudaEventDestroy(pe.second.second);
+  }
+  for (auto e : c.event_pool) cudaEventDestroy(e);
+  if (c.comm && c.own_comm) ncclCommDestroy(c.comm);
+  c.comm = nullptr;
+}
+
+// ---------------------------------------------------------------------------
+// Keys
+// ---------------------------------------------------------------------------
+unsigned long long key_id(int kind, uint32_t elt) {
+  return ((unsigned long long)(kind == KS_KEY_RELIN ? 0 : 1) << 32) |
+         (kind == KS_KEY_RELIN ? 0u : elt);
+}
+
+void check_elt(const Ctx &c, uint32_t elt) {
+  KS_REQUIRE((elt & 1u) && elt < 2u * (uint32_t)c.N, "galois element must be odd and < 2N");
+}
+
+KeyShard &key_alloc(Ctx &c, int kind, uint32_t elt) {
+  KS_REQUIRE(c.alpha > 0, "context has no special primes (NTT-only context)");
+  KS_REQUIRE(kind == KS_KEY_RELIN || kind == KS_KEY_GALOIS, "unknown key kind");
+  if (kind == KS_KEY_GALOIS) check_elt(c, elt);
+  auto id = key_id(kind, elt);
+  auto it = c.keys.find(id);
+  if (it != c.keys.end()) return it->second;
+  KeyShard k;
+  k.limbs = (int)c.own_key.size();
+  k.beta = (c.L + c.alpha - 1) / c.alpha;
+  k.d = dev_alloc<u64>((size_t)k.beta * 2 * k.limbs * c.N);
+  return c.keys[id] = k;
+}
+
+const KeyShard &key_get(Ctx &c, int kind, uint32_t elt) {
+  auto it = c.keys.find(key_id(kind, elt));
+  if (it == c.keys.end())
+    throw KsError{KS_ERR_NO_KEY, kind == KS_KEY_RELIN
+                                     ? std::string("no relinearisation key uploaded")
+                                     : "no galois key for element " + std::to_string(elt)};
+  return it->second;
+}
+
+size_t full_key_words(const Ctx &c) {
+  return c.alpha ? (size_t)((c.L + c.alpha - 1) / c.alpha) * 2 * c.K * c.N : 0;
+}
+
+void key_upload(Ctx &c, int kind, uint32_t elt, const u64 *src, size_t n_words, bool from_dev,
+                cudaStream_t s) {
+  KS_REQUIRE(src != nullptr, "key pointer is null");
+  KS_REQUIRE(n_words == full_key_words(c), "key size mismatch: expected " +
+                                               std::to_string(full_key_words(c)) + " words");
+  KS_CUDA(cudaSetDevice(c.device));
+  KeyShard &k = key_alloc(c, kind, elt);
+  const size_t N = c.N;
+  const cudaMemcpyKind dir = from_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (c.world == 1) {
+    KS_CUDA(cudaMemcpyAsync(k.d, src, n_words * 8, dir, s));
+  } else {
+    // rows of the full layout [d][p][K] -> shard [d][p][own]
+    for (int d = 0; d < k.beta; ++d)
+      for (int p = 0; p < 2; ++p)
+        KS_CUDA(cudaMemcpy2DAsync(k.d + ((size_t)(2 * d + p) * k.limbs) * N, N * 8,
+                                  src + (((size_t)(2 * d + p) * c.K) + c.rank) * N,
+                                  (size_t)c.world * N * 8, N * 8, k.limbs, dir, s));
+  }
+  if (!from_dev) KS_CUDA(cudaStreamSynchronize(s));
+}
+
+void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 seed,
+                  cudaStream_t s) {
+  KS_REQUIRE(sk_host != nullptr, "secret is null");
+  KS_CUDA(cudaSetDevice(c.device));
+  KeyShard &k = key_alloc(c, kind, elt);
+  const int n = k.limbs, N = c.N;
+  const NttTables T = c.tables();
+  int8_t *d_sk = dev_alloc<int8_t>(N);
+  KS_CUDA(cudaMemcpyAsync(d_sk, sk_host, N, cudaMemcpyHostToDevice, s));
+  u64 *s_ntt = c.s_t, *snew = c.s_t + (size_t)n * N, *e = c.s_t + 2 * (size_t)n * N;
+  const int *prime = c.own_key_prime.d;
+  KS_CUDA(expand_ternary(d_sk, s_ntt, n, prime, c.d_primes, c.log_n, s));
+  LimbMap ms{s_ntt, N, nullptr, prime, 0, 1};
+  KS_CUDA(ntt_forward(ms, n, T, s));
+  if (kind == KS_KEY_GALOIS) KS_CUDA(galois_ntt(s_ntt, snew, n, c.log_n, elt, s));
+  else KS_CUDA(mul_pointwise(s_ntt, s_ntt, snew, n, prime, c.d_primes, c.log_n, s));
+  // per-slot constants
+  std::vector<int> in_digit(n);
+  std::vector<u64> pmodq(n);
+  u64 *d_pmq = dev_alloc<u64>(n);
+  int *d_in = dev_alloc<int>(n);
+  for (int sl = 0; sl < n; ++sl) {
+    const int kj = c.own_key[sl];
+    const u64 q = c.primes[kj];
+    u64 P = 1;
+    for (int i = 0; i < c.alpha; ++i) P = h_mulmod(P, c.primes[c.L + i] % q, q);
+    pmodq[sl] = P;
+  }
+  KS_CUDA(cudaMemcpyAsync(d_pmq, pmodq.data(), n * 8, cudaMemcpyHostToDevice, s));
+  const u64 sa = prng_stream(seed, DOM_KEY_A), se = prng_stream(seed, DOM_KEY_E);
+  std::vector<std::vector<int>> flags(k.beta, std::vector<int>(n));
+  for (int d = 0; d < k.beta; ++d) {
+    for (int sl = 0; sl < n; ++sl) {
+      const int kj = c.own_key[sl];
+      flags[d][sl] = (kj < c.L && kj / c.alpha == d) ? 1 : 0;
+    }
+    KS_CUDA(cudaMemcpyAsync(d_in, flags[d].data(), n * sizeof(int), cudaMemcpyHostToDevice, s));
+    KS_CUDA(sample_gauss(e, n, prime, c.d_primes, c.d_gauss, se, (u64)d * N, c.log_n, s));
+    LimbMap me{e, N, nullptr, prime, 0, 1};
+    KS_CUDA(ntt_forward(me, n, T, s));
+    u64 *kb = k.d + (size_t)(2 * d) * n * N, *ka = k.d + (size_t)(2 * d + 1) * n * N;
+    KS_CUDA(keygen_digit(kb, ka, s_ntt, snew, e, n, prime, prime, d_in, d_pmq, sa, d, c.K,
+                         c.d_primes, c.log_n, s));
+    KS_CUDA(cudaStreamSynchronize(s));  // flags buffer is reused per digit
+  }
+  cudaFree(d_sk);
+  cudaFree(d_pmq);
+  cudaFree(d_in);
+}
+
+// ---------------------------------------------------------------------------
+// Optional per-stage timing (bench accounting; off by default)
+// ---------------------------------------------------------------------------
+enum Stage {
+  ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_BCONV, ST_MODUP_NTT, ST_INNER_PROD, ST_INTT_P,
+  ST_MODDOWN_BCONV, ST_MODDOWN_NTT, ST_FINISH, ST_COMM, ST_COUNT
+};
+static const char *kStageNames[ST_COUNT] = {"galois",       "intt_input",      "modup_bconv",
+                                            "modup_ntt",    "inner_product",   "intt_p",
+                                            "moddown_bconv", "moddown_ntt",    "moddown_finish",
+                                            "collective"};
+
+cudaEvent_t pool_event(Ctx &c) {
+  if (!c.event_pool.empty()) {
+    cudaEvent_t e = c.event_pool.back();
+    c.event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e;
+  KS_CUDA(cudaEventCreate(&e));
+  return e;
+}
+
+struct StageTimer {
+  Ctx &c;
+  int st;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr;
+  StageTimer(Ctx &c_, int st_, cudaStream_t s_) : c(c_), st(st_), s(s_) {
+    if (c.profile) {
+      a = pool_event(c);
+      KS_CUDA(cudaEventRecord(a, s));
+    }
+  }
+  ~StageTimer() noexcept(false) {
+    if (c.profile && a) {
+      cudaEvent_t b = pool_event(c);
+      KS_CUDA(cudaEventRecord(b, s));
+      c.prof_events.push_back({st, {a, b}});
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Collectives
+// ---------------------------------------------------------------------------
+void allgather(Ctx &c, const u64 *send, u64 *recv, size_t words, cudaStream_t s) {
+  KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, c.comm, s));
+}
+
+// ---------------------------------------------------------------------------
+// The key switch
+// ---------------------------------------------------------------------------
+// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]).
+// rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
+void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_ntt, u64 *ct0,
+                    u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
+  const size_t N = c.N;
+  const NttTables T = c.tables();
+  // 2. coefficient form of the input, all-gathered
+  {
+    StageTimer tm(c, ST_INTT_IN, s);
+    KS_CUDA(cudaMemcpyAsync(c.s_coef, in_ntt, (size_t)lv.n_q * N * 8, cudaMemcpyDeviceToDevice,
+                            s));
+    LimbMap mc{c.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
+    KS_CUDA(ntt_inverse(mc, lv.n_q, T, s));
+    c.launches += 2;
+  }
+  if (c.world > 1) {
+    StageTimer tm(c, ST_COMM, s);
+    allgather(c, c.s_coef, c.s_coef_all, (size_t)lv.coef_ml * N, s);
+  }
+  // 3. ModUp: base extension + NTT
+  {
+    StageTimer tm(c, ST_MODUP_BCONV, s);
+    KS_CUDA(modup_bconv(c.s_coef_all, c.s_t, lv.mu, lv.lay, c.d_primes, c.log_n, s));
+    c.launches += 1;
+  }
+  {
+    StageTimer tm(c, ST_MODUP_NTT, s);
+    LimbMap mt{c.s_t, (long long)N, nullptr, lv.t_jobs.d, 0, 1};
+    KS_CUDA(ntt_forward(mt, lv.beta * lv.n_out, T, s));
+    c.launches += 2;
+  }
+  // 4. inner product
+  {
+    StageTimer tm(c, ST_INNER_PROD, s);
+    KS_CUDA(inner_product(c.s_t, in_ntt, key.d, key.limbs, c.s_cx, lv.mu, lv.lay, c.d_primes,
+                          c.log_n, s));
+    c.launches += 1;
+  }
+  // 5. P part to coefficient form
+  const u64 *y_base;
+  if (c.world == 1) {
+    StageTimer tm(c, ST_INTT_P, s);
+    LimbMap mp{c.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
+    KS_CUDA(ntt_inverse(mp, 2 * lv.n_p, T, s));
+    c.launches += 2;
+    y_base = c.s_cx;
+  } else {
+    {
+      StageTimer tm(c, ST_INTT_P, s);
+      for (int p = 0; p < 2; ++p)
+        for (int k = 0; k < lv.n_p; ++k)
+          KS_CUDA(cudaMemcpyAsync(c.s_ysend + ((size_t)k * 2 + p) * N,
+                                  c.s_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N, N * 8,
+                                  cudaMemcpyDeviceToDevice, s));
+      if (lv.n_p > 0) {
+        LimbMap mp{c.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
+        KS_CUDA(ntt_inverse(mp, 2 * lv.n_p, T, s));
+        c.launches += 2;
+      }
+    }
+    StageTimer tm(c, ST_COMM, s);
+    allgather(c, c.s_ysend, c.s_yall, (size_t)c.max_p_own * 2 * N, s);
+    y_base = c.s_yall;
+  }
+  // 6. P -> Q conversion and NTT
+  {
+    StageTimer tm(c, ST_MODDOWN_BCONV, s);
+    KS_CUDA(moddown_bconv(y_base, lv.y_off.d, c.s_z, lv.n_q, lv.q_index.d, c.md, c.d_primes,
+                          c.log_n, s));
+    c.launches += 1;
+  }
+  {
+    StageTimer tm(c, ST_MODDOWN_NTT, s);
+    LimbMap mz{c.s_z, (long long)N, nullptr, lv.z_jobs.d, 0, 1};
+    KS_CUDA(ntt_forward(mz, 2 * lv.n_q, T, s));
+    c.launches += 2;
+  }
+  // 7. finish
+  {
+    StageTimer tm(c, ST_FINISH, s);
+    KS_CUDA(moddown_finish(ct0, ct1, g0, c.s_cx, (int)(lv.n_out * N), lv.cx_slot_q.d, c.s_z,
+                           lv.n_q, lv.q_index.d, c.md, c.d_primes, c.log_n, rotate, s));
+    c.launches += 1;
+  }
+}
+
+const Level &level_of(Ctx &c, int Ql) {
+  KS_REQUIRE(c.alpha > 0, "context has no special primes (NTT-only context)");
+  KS_REQUIRE(Ql >= 1 && Ql <= c.L, "level_limbs out of range");
+  return c.levels[Ql];
+}
+
+void do_apply_galois(Ctx &c, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
+  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  check_elt(c, elt);
+  const Level &lv = level_of(c, Ql);
+  const KeyShard &key = key_get(c, KS_KEY_GALOIS, elt);
+  const size_t nq = lv.n_q, N = c.N;
+  KS_CUDA(cudaSetDevice(c.device));
+  // 1. automorphism of both polys -> g0, g1
+  {
+    StageTimer tm(c, ST_GALOIS, s);
+    KS_CUDA(galois_ntt(ct, c.s_g, 2 * (int)nq, c.log_n, elt, s));
+    c.launches += 1;
+  }
+  keyswitch_core(c, lv, key, c.s_g + nq * N, ct, ct + nq * N, c.s_g, true, s);
+}
+
+void do_relin(Ctx &c, u64 *ct, int Ql, cudaStream_t s) {
+  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  const Level &lv = level_of(c, Ql);
+  const KeyShard &key = key_get(c, KS_KEY_RELIN, 0);
+  const size_t nq = lv.n_q, N = c.N;
+  KS_CUDA(cudaSetDevice(c.device));
+  keyswitch_core(c, lv, key, ct + 2 * nq * N, ct, ct + nq * N, nullptr, false, s);
+}
+
+uint32_t elt_of_step(const Ctx &c, int step) {
+  const long long slots = c.N / 2;
+  long long st = ((step % slots) + slots) % slots;
+  return (uint32_t)h_powmod(3, (u64)st, 2ull * c.N);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int ks_gen_primes(uint32_t log_n, const int *bit_sizes, int n, uint64_t *out) {
+  return guarded(nullptr, [&] {
+    KS_REQUIRE(bit_sizes && out && n > 0, "bad arguments");
+    KS_REQUIRE(log_n >= 1 && log_n <= 20, "log_n out of range");
+    if (h_gen_primes((int)log_n, bit_sizes, n, out) != 0)
+      throw KsError{KS_ERR_INVALID, "not enough primes of the requested sizes"};
+  });
+}
+
+int ks_secret_generate(uint32_t log_n, uint64_t seed, int hamming_weight, int8_t *out) {
+  // Same specification as the CPU oracle's synthetic secret: uniform ternary
+  // (h <= 0) or exactly h nonzero +-1 entries chosen by a partial
+  // Fisher-Yates shuffle driven by the counter hash.
+  return guarded(nullptr, [&] {
+    KS_REQUIRE(out != nullptr && log_n >= 1 && log_n <= 20, "bad arguments");
+    const size_t N = (size_t)1 << log_n;
+    KS_REQUIRE(hamming_weight <= (int)N, "hamming weight larger than N");
+    if (hamming_weight <= 0) {
+      for (size_t k = 0; k < N; ++k)
+        out[k] = (int8_t)((int)(u64)(((unsigned __int128)prng_at(seed, DOM_SECRET, k) * 3) >> 64) - 1);
+      return;
+    }
+    std::vector<uint32_t> pos(N);
+    for (size_t k = 0; k < N; ++k) pos[k] = (uint32_t)k;
+    std::memset(out, 0, N);
+    for (int i = 0; i < hamming_weight; ++i) {
+      const size_t j =
+          i + (size_t)(u64)(((unsigned __int128)prng_at(seed, DOM_SECRET, (u64)i) * (N - i)) >> 64);
+      std::swap(pos[i], pos[j]);
+      out[pos[i]] = (prng_at(seed, DOM_SECRET_SIGN, (u64)i) & 1) ? -1 : 1;
+    }
+  });
+}
+
+int ks_nccl_unique_id(void *out, size_t n) {
+  return guarded(nullptr, [&] {
+    KS_REQUIRE(out != nullptr && n >= sizeof(ncclUniqueId), "buffer too small for an NCCL id");
+    ncclUniqueId id;
+    KS_NCCL(ncclGetUniqueId(&id));
+    std::memcpy(out, &id, sizeof(id));
+  });
+}
+
+int ks_ctx_create(const ks_params *prm, int device, int rank, int world, const void *nccl_id,
+                  ks_ctx **out) {
+  if (!out) {
+    set_global_err("out pointer is null");
+    return KS_ERR_INVALID;
+  }
+  *out = nullptr;
+  ks_ctx *ctx = new ks_ctx();
+  int rc = guarded(ctx, [&] { ctx_init(ctx->c, prm, device, rank, world, nullptr, nccl_id); });
+  if (rc != KS_OK) {
+    set_global_err(ctx->c.err);
+    ctx_free(ctx->c);
+    delete ctx;
+    return rc;
+  }
+  *out = ctx;
+  return KS_OK;
+}
+
+int ks_ctx_create_all(const ks_params *prm, const int *devices, int n, ks_ctx **outs) {
+  if (!outs || !devices || n < 1) {
+    set_global_err("bad arguments");
+    return KS_ERR_INVALID;
+  }
+  std::vector<ncclComm_t> comms(n, nullptr);
+  if (n > 1) {
+    ncclResult_t r = ncclCommInitAll(comms.data(), n, devices);
+    if (r != ncclSuccess) {
+      set_global_err(std::string("ncclCommInitAll: ") + ncclGetErrorString(r));
+      return KS_ERR_NCCL;
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    outs[i] = new ks_ctx();
+    int rc = guarded(outs[i], [&] { ctx_init(outs[i]->c, prm, devices[i], i, n, comms[i], nullptr); });
+    if (rc != KS_OK) {
+      set_global_err(outs[i]->c.err);
+      for (int k = 0; k <= i; ++k) {
+        ctx_free(outs[k]->c);
+        delete outs[k];
+        outs[k] = nullptr;
+      }
+      for (int k = i + 1; k < n; ++k)
+        if (comms[k]) ncclCommDestroy(comms[k]);
+      return rc;
+    }
+  }
+  return KS_OK;
+}
+
+int ks_ctx_destroy(ks_ctx *ctx) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx_free(ctx->c);
+  delete ctx;
+  return KS_OK;
+}
+
+int ks_last_error(const ks_ctx *ctx, char *buf, size_t n) {
+  if (!buf || n == 0) return KS_ERR_INVALID;
+  std::string s;
+  if (ctx) {
+    s = ctx->c.err;
+  } else {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    s = g_err;
+  }
+  std::snprintf(buf, n, "%s", s.c_str());
+  return KS_OK;
+}
+
+int ks_set_timeout_ms(ks_ctx *ctx, int ms) {
+  if (!ctx || ms < 0) return KS_ERR_INVALID;
+  ctx->c.timeout_ms = ms;
+  return KS_OK;
+}
+
+int ks_n_local_limbs(const ks_ctx *ctx, int total_limbs) {
+  if (!ctx || total_limbs < 0) return KS_ERR_INVALID;
+  return n_local(ctx->c.rank, ctx->c.world, total_limbs);
+}
+
+int ks_owner_of_limb(const ks_ctx *ctx, int limb) {
+  if (!ctx || limb < 0) return KS_ERR_INVALID;
+  return limb % ctx->c.world;
+}
+
+int ks_num_digits(const ks_ctx *ctx, int level_limbs) {
+  if (!ctx || ctx->c.alpha == 0 || level_limbs < 1) return KS_ERR_INVALID;
+  return (level_limbs + ctx->c.alpha - 1) / ctx->c.alpha;
+}
+
+int ks_galois_elt(const ks_ctx *ctx, int step, uint32_t *elt) {
+  if (!ctx || !elt) return KS_ERR_INVALID;
+  *elt = elt_of_step(ctx->c, step);
+  return KS_OK;
+}
+
+size_t ks_key_words(const ks_ctx *ctx) { return ctx ? full_key_words(ctx->c) : 0; }
+
+int ks_key_upload(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *host_key, size_t n) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] { key_upload(ctx->c, kind, elt, host_key, n, false, 0); });
+}
+
+int ks_key_upload_device(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *dev_key, size_t n,
+                         void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    key_upload(ctx->c, kind, elt, dev_key, n, true, (cudaStream_t)stream);
+  });
+}
+
+int ks_key_generate(ks_ctx *ctx, int kind, uint32_t elt, const int8_t *secret, uint64_t seed,
+                    void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] { key_generate(ctx->c, kind, elt, secret, seed, (cudaStream_t)stream); });
+}
+
+int ks_key_download(ks_ctx *ctx, int kind, uint32_t elt, uint64_t *host_key, size_t n) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    const KeyShard &k = key_get(c, kind, elt);
+    const size_t words = (size_t)k.beta * 2 * k.limbs * c.N;
+    KS_REQUIRE(host_key != nullptr && n >= words, "host buffer too small for the key shard");
+    KS_CUDA(cudaSetDevice(c.device));
+    KS_CUDA(cudaMemcpy(host_key, k.d, words * 8, cudaMemcpyDeviceToHost));
+  });
+}
+
+int ks_key_drop(ks_ctx *ctx, int kind, uint32_t elt) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    auto it = ctx->c.keys.find(key_id(kind, elt));
+    if (it == ctx->c.keys.end()) throw KsError{KS_ERR_NO_KEY, "no such key"};
+    KS_CUDA(cudaSetDevice(ctx->c.device));
+    KS_CUDA(cudaFree(it->second.d));
+    ctx->c.keys.erase(it);
+  });
+}
+
+int ks_relinearize(ks_ctx *ctx, uint64_t *ct, int level_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] { do_relin(ctx->c, ct, level_limbs, (cudaStream_t)stream); });
+}
+
+int ks_apply_galois(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t elt, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] { do_apply_galois(ctx->c, ct, level_limbs, elt, (cudaStream_t)stream); });
+}
+
+int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    do_apply_galois(ctx->c, ct, level_limbs, elt_of_step(ctx->c, step), (cudaStream_t)stream);
+  });
+}
+
+int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, int level_limbs,
+                    void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    KS_REQUIRE(cts != nullptr && steps != nullptr && n >= 0, "bad batch arguments");
+    for (int i = 0; i < n; ++i)
+      do_apply_galois(ctx->c, cts[i], level_limbs, elt_of_step(ctx->c, steps[i]),
+                      (cudaStream_t)stream);
+  });
+}
+
+int ks_rotate_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs, const int *steps, int n,
+                      uint64_t *const *outs, void *stream) {
+  (void)ct; (void)level_limbs; (void)steps; (void)n; (void)outs; (void)stream;
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.err = "hoisted rotations are not built yet";
+  return KS_ERR_UNSUPPORTED;
+}
+
+static int ntt_api(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,
+                   void *stream, bool fwd) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(data != nullptr && aligned16(data), "data pointer null or not 16-byte aligned");
+    KS_REQUIRE(n_limbs >= 1 && batch >= 1, "n_limbs and batch must be positive");
+    KS_REQUIRE(first_prime >= 0 && first_prime + n_limbs <= c.K, "prime range out of the basis");
+    KS_CUDA(cudaSetDevice(c.device));
+    const long long total = (long long)n_limbs * batch;
+    const NttTables T = c.tables();
+    for (long long off = 0; off < total; off += 65535) {
+      const int cnt = (int)std::min<long long>(65535, total - off);
+      // keep the prime pattern aligned: chunks start at multiples of n_limbs
+      LimbMap m{data + off * c.N, c.N, nullptr, nullptr, first_prime, n_limbs};
+      if (off % n_limbs != 0) throw KsError{KS_ERR_UNSUPPORTED, "internal chunking error"};
+      KS_CUDA(fwd ? ntt_forward(m, cnt, T, (cudaStream_t)stream)
+                  : ntt_inverse(m, cnt, T, (cudaStream_t)stream));
+      c.launches += 2;
+    }
+  });
+}
+
+int ks_ntt_forward(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,
+                   void *stream) {
+  return ntt_api(ctx, data, n_limbs, first_prime, batch, stream, true);
+}
+int ks_ntt_inverse(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,
+                   void *stream) {
+  return ntt_api(ctx, data, n_limbs, first_prime, batch, stream, false);
+}
+
+int ks_scatter_limbs(ks_ctx *ctx, const uint64_t *global_buf, uint64_t *local_buf, int n_polys,
+                     int total_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(global_buf && local_buf && aligned16(global_buf) && aligned16(local_buf),
+               "buffers must be non-null and 16-byte aligned");
+    KS_REQUIRE(n_polys >= 0 && total_limbs >= 0, "bad sizes");
+    KS_CUDA(cudaSetDevice(c.device));
+    KS_CUDA(scatter_limbs(global_buf, local_buf, n_polys, total_limbs, c.log_n, c.rank, c.world,
+                          (cudaStream_t)stream));
+  });
+}
+
+int ks_gather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *global_buf, int n_polys,
+                    int total_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(global_buf && local_buf && aligned16(global_buf) && aligned16(local_buf),
+               "buffers must be non-null and 16-byte aligned");
+    KS_REQUIRE(n_polys >= 0 && total_limbs >= 0, "bad sizes");
+    KS_CUDA(cudaSetDevice(c.device));
+    KS_CUDA(gather_limbs(local_buf, global_buf, n_polys, total_limbs, c.log_n, c.rank, c.world,
+                         (cudaStream_t)stream));
+  });
+}
+
+int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_buf,
+                       int total_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(local_buf && full_buf && aligned16(local_buf) && aligned16(full_buf),
+               "buffers must be non-null and 16-byte aligned");
+    KS_REQUIRE(total_limbs >= 1, "bad sizes");
+    KS_CUDA(cudaSetDevice(c.device));
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t N = c.N, G = c.world, ml = (total_limbs + G - 1) / G;
+    if (G == 1) {
+      KS_CUDA(cudaMemcpyAsync(full_buf, local_buf, total_limbs * N * 8, cudaMemcpyDeviceToDevice, s));
+      return;
+    }
+    // pad to ml limbs, gather rank-grouped, then reorder to limb order
+    u64 *send = dev_alloc<u64>(ml * N), *recv = dev_alloc<u64>(G * ml * N);
+    const int nl = n_local(c.rank, c.world, total_limbs);
+    KS_CUDA(cudaMemsetAsync(send, 0, ml * N * 8, s));
+    if (nl > 0) KS_CUDA(cudaMemcpyAsync(send, local_buf, nl * N * 8, cudaMemcpyDeviceToDevice, s));
+    allgather(c, send, recv, ml * N, s);
+    // rank-grouped [G][ml] -> sequential: limb j at (j % G, j / G)
+    for (int j = 0; j < total_limbs; ++j)
+      KS_CUDA(cudaMemcpyAsync(full_buf + (size_t)j * N, recv + ((j % G) * ml + j / G) * N, N * 8,
+                              cudaMemcpyDeviceToDevice, s));
+    KS_CUDA(cudaStreamSynchronize(s));
+    cudaFree(send);
+    cudaFree(recv);
+  });
+}
+
+int ks_last_launch_count(const ks_ctx *ctx) { return ctx ? ctx->c.launches : KS_ERR_INVALID; }
+
+int ks_profile_enable(ks_ctx *ctx, int on) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.profile = on != 0;
+  return KS_OK;
+}
+
+int ks_profile_stage_count(void) { return ST_COUNT; }
+
+const char *ks_profile_stage_name(int i) { return (i >= 0 && i < ST_COUNT) ? kStageNames[i] : ""; }
+
+int ks_profile_read(ks_ctx *ctx, double *ms, int *calls, int n) {
+  if (!ctx || !ms || !calls || n < ST_COUNT) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_CUDA(cudaSetDevice(c.device));
+    for (int i = 0; i < ST_COUNT; ++i) {
+      ms[i] = 0;
+      calls[i] = 0;
+    }
+    for (auto &pe : c.prof_events) {
+      KS_CUDA(cudaEventSynchronize(pe.second.second));
+      float t = 0;
+      KS_CUDA(cudaEventElapsedTime(&t, pe.second.first, pe.second.second));
+      ms[pe.first] += t;
+      calls[pe.first] += 1;
+      c.event_pool.push_back(pe.second.first);
+      c.event_pool.push_back(pe.second.second);
+    }
+    c.prof_events.clear();
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,99 @@
+// ks_context.hpp -- the per-device key-switching context behind the C ABI.
+//
+// One context drives one GPU (one rank).  It owns the NTT/base-conversion
+// tables, the evaluation-key shards, the scratch arena (sized once at
+// creation for the top level, never grown on the hot path) and, for
+// world > 1, an NCCL communicator.  The reference keeps the same state in
+// PhantomContext + MultiGpuContext and grows thread_local scratch per call
+// (input_broadcast.cu:133-152); here every buffer exists before the first call.
+#pragma once
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "ks_kernels.cuh"
+#include "ks_ntt.cuh"
+
+namespace ksb {
+
+// Host copy + device copy of an int table.
+struct DevInts {
+  std::vector<int> h;
+  int *d = nullptr;
+};
+struct DevI64 {
+  std::vector<long long> h;
+  long long *d = nullptr;
+};
+
+// Everything the key switch needs at one level (Ql Q limbs) on this rank.
+struct Level {
+  int Ql = 0, QlP = 0, beta = 0;
+  int n_out = 0;      // owned output limbs (Q first, then P)
+  int n_q = 0;        // owned Q limbs
+  int n_p = 0;        // owned P limbs
+  int coef_ml = 0;    // ceil(Ql / G): all-gather slot count per rank
+  DevInts prime_of;   // [QlP]
+  DevInts out_j, key_slot, c_slot;  // [n_out]
+  DevInts t_jobs;     // [beta * n_out] prime of t slot or -1
+  DevInts q_index;    // [n_q] global Q limb of local Q slot
+  DevInts z_jobs;     // [2 * n_q] prime of z slot
+  DevInts cx_slot_q;  // [n_q]
+  DevInts p_jobs;     // [2 * n_p] primes of the owned P slots being inverse-transformed
+  DevI64 p_offsets;   // [2 * n_p] word offsets of those slots (in cx for G=1, in ysend otherwise)
+  DevI64 y_off;       // [2 * alpha] offsets of P limb i of poly p in the y buffer
+  ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
+  u64 *w = nullptr;               // [beta][QlP][alpha]
+  ModUpDev mu{};
+  KsLayout lay{};
+};
+
+struct KeyShard {
+  u64 *d = nullptr;
+  int limbs = 0;  // key limbs held (owned key-basis limbs)
+  int beta = 0;
+};
+
+struct Ctx {
+  // parameters
+  int device = 0, rank = 0, world = 1, mode = 0, max_batch = 1;
+  int log_n = 0, N = 0, L = 0, alpha = 0, K = 0;
+  std::vector<u64> primes;  // K = L + alpha
+  // device tables
+  PrimeDev *d_primes = nullptr;
+  ulonglong2 *d_tw_fwd = nullptr, *d_tw_inv = nullptr;
+  u64 *d_gauss = nullptr;
+  ModDownDev md{};
+  ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
+  u64 *d_mdw = nullptr;
+  std::vector<Level> levels;  // index Ql (1..L)
+  // key-basis ownership
+  std::vector<int> own_key;   // owned key-basis limbs, increasing
+  DevInts own_key_prime;      // same, device copy (prime index == key index)
+  // keys
+  std::map<unsigned long long, KeyShard> keys;  // (kind << 32) | elt
+  // scratch arena
+  u64 *arena = nullptr;
+  size_t arena_words = 0;
+  u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr, *s_cx = nullptr,
+      *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr;
+  int max_p_own = 0;
+  // comm
+  ncclComm_t comm = nullptr;
+  bool own_comm = false;
+  int timeout_ms = 60000;
+  // diagnostics
+  std::string err;
+  int launches = 0;
+  // optional per-stage timing: event pairs recorded on the launch stream
+  bool profile = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
+  std::vector<cudaEvent_t> event_pool;
+
+  NttTables tables() const { return NttTables{d_tw_fwd, d_tw_inv, d_primes, log_n}; }
+};
+
+}  // namespace ksb

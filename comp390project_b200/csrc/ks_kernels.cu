@@ -1,0 +1,416 @@
+// ks_kernels.cu -- ModUp base extension, inner product, ModDown finish,
+// automorphism, partition copies and synthetic-key samplers (sm_100a).
+//
+// All kernels stream 128-bit words (two coefficients per thread per access)
+// and keep per-limb constants in registers; the limb index of a CTA is
+// blockIdx.y so every constant load is warp-uniform.
+#include "ks_kernels.cuh"
+
+namespace ksb {
+namespace {
+
+constexpr int kBlk = 256;
+
+__device__ __forceinline__ u64 mix64(u64 z) {
+  z ^= z >> 30;
+  z *= 0xBF58476D1CE4E5B9ull;
+  z ^= z >> 27;
+  z *= 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return z;
+}
+
+__device__ __forceinline__ uint32_t brev_n(uint32_t x, int log_n) { return __brev(x) >> (32 - log_n); }
+
+// Source index of output slot i under X -> X^elt in the bit-reversed NTT order:
+// slot i holds the evaluation at psi^(2 brev(i) + 1).
+__device__ __forceinline__ uint32_t galois_src(uint32_t i, uint32_t elt, int log_n) {
+  const uint32_t mask2n = (2u << log_n) - 1u;
+  const uint32_t e = 2u * brev_n(i, log_n) + 1u;
+  const uint32_t ge = (e * elt) & mask2n;
+  return brev_n((ge - 1u) >> 1, log_n);
+}
+
+__global__ void k_galois_ntt(const u64 *__restrict__ in, u64 *__restrict__ out, int log_n,
+                             uint32_t elt) {
+  const int N = 1 << log_n;
+  const long long limb = blockIdx.y;
+  const uint32_t i = blockIdx.x * kBlk + threadIdx.x;
+  if (i >= (uint32_t)N) return;
+  out[limb * N + i] = __ldg(&in[limb * N + galois_src(i, elt, log_n)]);
+}
+
+// One thread: two adjacent coefficients of one digit, all output limbs.
+__global__ void __launch_bounds__(kBlk) k_modup_bconv(const u64 *__restrict__ coef,
+                                                     u64 *__restrict__ t, ModUpDev mu,
+                                                     KsLayout lay, const PrimeDev *primes,
+                                                     int log_n) {
+  const int N = 1 << log_n;
+  const int d = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const int lo = d * mu.alpha;
+  const int n_src = min(mu.alpha, mu.Ql - lo);
+  u64 v0[KS_MAX_ALPHA], v1[KS_MAX_ALPHA];
+#pragma unroll
+  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
+    if (i < n_src) {
+      const int j = lo + i;
+      const long long slot = (long long)(j % lay.coef_G) * lay.coef_ml + j / lay.coef_G;
+      const ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(coef + slot * N + k);
+      const ulonglong2 c = mu.qhatinv[d * mu.alpha + i];
+      const u64 q = primes[mu.prime_of[j]].q;
+      v0[i] = mul_shoup(x.x, c.x, c.y, q);
+      v1[i] = mul_shoup(x.y, c.x, c.y, q);
+    }
+  }
+  u64 *td = t + (long long)d * lay.n_out * N;
+  for (int s = 0; s < lay.n_out; ++s) {
+    const int j = lay.out_j[s];
+    if (j >= lo && j < lo + n_src) continue;
+    const PrimeDev P = primes[mu.prime_of[j]];
+    const u64 *w = mu.w + ((long long)d * mu.QlP + j) * mu.alpha;
+    u128v a0 = {0, 0}, a1 = {0, 0};
+#pragma unroll
+    for (int i = 0; i < KS_MAX_ALPHA; ++i) {
+      if (i < n_src) {
+        const u64 wi = __ldg(&w[i]);
+        mac(a0, v0[i], wi);
+        mac(a1, v1[i], wi);
+      }
+    }
+    ulonglong2 r;
+    r.x = barrett128(a0, P.q, P.br_hi, P.br_lo);
+    r.y = barrett128(a1, P.q, P.br_hi, P.br_lo);
+    *reinterpret_cast<ulonglong2 *>(td + (long long)s * N + k) = r;
+  }
+}
+
+// One thread: two adjacent coefficients of one output limb, both polys.
+__global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ t,
+                                                       const u64 *__restrict__ c_ntt,
+                                                       const u64 *__restrict__ key,
+                                                       int key_limbs, u64 *__restrict__ cx,
+                                                       ModUpDev mu, KsLayout lay,
+                                                       const PrimeDev *primes, int log_n) {
+  const int N = 1 << log_n;
+  const int s = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const int j = lay.out_j[s];
+  const PrimeDev P = primes[mu.prime_of[j]];
+  const long long ks = lay.key_slot[s];
+  const int dj = j < mu.Ql ? j / mu.alpha : -1;  // digit holding limb j
+  u128v a00 = {0, 0}, a01 = {0, 0}, a10 = {0, 0}, a11 = {0, 0};
+  const long long kstride = (long long)key_limbs * N;
+  for (int d = 0; d < mu.beta; ++d) {
+    const u64 *src = (d == dj) ? c_ntt + (long long)lay.c_slot[s] * N
+                               : t + ((long long)d * lay.n_out + s) * N;
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(src + k);
+    const u64 *kb = key + (long long)(2 * d) * kstride + ks * N + k;
+    const ulonglong2 b = __ldg(reinterpret_cast<const ulonglong2 *>(kb));
+    const ulonglong2 a = __ldg(reinterpret_cast<const ulonglong2 *>(kb + kstride));
+    mac(a00, x.x, b.x);
+    mac(a01, x.y, b.y);
+    mac(a10, x.x, a.x);
+    mac(a11, x.y, a.y);
+  }
+  ulonglong2 r0, r1;
+  r0.x = barrett128(a00, P.q, P.br_hi, P.br_lo);
+  r0.y = barrett128(a01, P.q, P.br_hi, P.br_lo);
+  r1.x = barrett128(a10, P.q, P.br_hi, P.br_lo);
+  r1.y = barrett128(a11, P.q, P.br_hi, P.br_lo);
+  *reinterpret_cast<ulonglong2 *>(cx + (long long)s * N + k) = r0;
+  *reinterpret_cast<ulonglong2 *>(cx + ((long long)lay.n_out + s) * N + k) = r1;
+}
+
+// One thread: two coefficients of one poly, all Q output limbs.
+__global__ void __launch_bounds__(kBlk) k_moddown_bconv(const u64 *__restrict__ y_base,
+                                                       const long long *__restrict__ y_off,
+                                                       u64 *__restrict__ z, int n_q,
+                                                       const int *__restrict__ q_index,
+                                                       ModDownDev md, const PrimeDev *primes,
+                                                       int log_n) {
+  const int N = 1 << log_n;
+  const int p = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  u64 v0[KS_MAX_ALPHA], v1[KS_MAX_ALPHA];
+#pragma unroll
+  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
+    if (i < md.alpha) {
+      const ulonglong2 x =
+          *reinterpret_cast<const ulonglong2 *>(y_base + y_off[p * md.alpha + i] + k);
+      const ulonglong2 c = md.phatinv[i];
+      const u64 q = primes[md.first_p + i].q;
+      v0[i] = mul_shoup(x.x, c.x, c.y, q);
+      v1[i] = mul_shoup(x.y, c.x, c.y, q);
+    }
+  }
+  for (int s = 0; s < n_q; ++s) {
+    const int j = q_index[s];
+    const PrimeDev P = primes[j];
+    const u64 *w = md.w + (long long)j * md.alpha;
+    u128v a0 = {0, 0}, a1 = {0, 0};
+#pragma unroll
+    for (int i = 0; i < KS_MAX_ALPHA; ++i) {
+      if (i < md.alpha) {
+        const u64 wi = __ldg(&w[i]);
+        mac(a0, v0[i], wi);
+        mac(a1, v1[i], wi);
+      }
+    }
+    ulonglong2 r;
+    r.x = barrett128(a0, P.q, P.br_hi, P.br_lo);
+    r.y = barrett128(a1, P.q, P.br_hi, P.br_lo);
+    *reinterpret_cast<ulonglong2 *>(z + ((long long)p * n_q + s) * N + k) = r;
+  }
+}
+
+__global__ void __launch_bounds__(kBlk) k_moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0,
+                                                        const u64 *__restrict__ cx,
+                                                        int cx_stride_poly,
+                                                        const int *__restrict__ cx_slot,
+                                                        const u64 *__restrict__ z, int n_q,
+                                                        const int *__restrict__ q_index,
+                                                        ModDownDev md, const PrimeDev *primes,
+                                                        int log_n, int rotate) {
+  const int N = 1 << log_n;
+  const int s = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const int j = q_index[s];
+  const u64 q = primes[j].q;
+  const ulonglong2 pi = md.pinv[j];
+  const long long off = (long long)s * N + k;
+  const long long cxo = (long long)cx_slot[s] * N + k;
+  const ulonglong2 c0 = *reinterpret_cast<const ulonglong2 *>(cx + cxo);
+  const ulonglong2 c1 = *reinterpret_cast<const ulonglong2 *>(cx + cx_stride_poly + cxo);
+  const ulonglong2 z0 = *reinterpret_cast<const ulonglong2 *>(z + off);
+  const ulonglong2 z1 = *reinterpret_cast<const ulonglong2 *>(z + (long long)n_q * N + off);
+  ulonglong2 o0, o1;
+  o0.x = mul_shoup(c0.x + q - z0.x, pi.x, pi.y, q);
+  o0.y = mul_shoup(c0.y + q - z0.y, pi.x, pi.y, q);
+  o1.x = mul_shoup(c1.x + q - z1.x, pi.x, pi.y, q);
+  o1.y = mul_shoup(c1.y + q - z1.y, pi.x, pi.y, q);
+  ulonglong2 base0 = *reinterpret_cast<const ulonglong2 *>((rotate ? g0 : ct0) + off);
+  ulonglong2 r0, r1;
+  r0.x = add_mod(base0.x, o0.x, q);
+  r0.y = add_mod(base0.y, o0.y, q);
+  if (rotate) {
+    r1 = o1;
+  } else {
+    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2 *>(ct1 + off);
+    r1.x = add_mod(b1.x, o1.x, q);
+    r1.y = add_mod(b1.y, o1.y, q);
+  }
+  *reinterpret_cast<ulonglong2 *>(ct0 + off) = r0;
+  *reinterpret_cast<ulonglong2 *>(ct1 + off) = r1;
+}
+
+__global__ void k_mod_reduce(u64 *x, const int *prime_of_slot, const PrimeDev *primes,
+                             int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = blockIdx.x * kBlk + threadIdx.x;
+  if (k >= N) return;
+  const u64 q = primes[prime_of_slot[l]].q;
+  x[(long long)l * N + k] %= q;
+}
+
+__global__ void k_scatter(const u64 *__restrict__ gbuf, u64 *__restrict__ lbuf, int total,
+                          int n_local, int log_n, int g, int G, int to_local) {
+  const int N = 1 << log_n;
+  const int poly = blockIdx.z, loc = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const long long glimb = (long long)loc * G + g;
+  if (glimb >= total) return;
+  ulonglong2 *gp = reinterpret_cast<ulonglong2 *>(const_cast<u64 *>(gbuf) +
+                                                  ((long long)poly * total + glimb) * N + k);
+  ulonglong2 *lp = reinterpret_cast<ulonglong2 *>(lbuf + ((long long)poly * n_local + loc) * N + k);
+  if (to_local) *lp = *gp;
+  else *gp = *lp;
+}
+
+__global__ void k_keygen(u64 *key_b, u64 *key_a, const u64 *__restrict__ s_ntt,
+                         const u64 *__restrict__ snew_ntt, const u64 *__restrict__ e_ntt,
+                         const int *key_index, const int *prime_of_slot, const int *in_digit,
+                         const u64 *p_mod_q, u64 key_a_stream, int d, int K,
+                         const PrimeDev *primes, int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = blockIdx.x * kBlk + threadIdx.x;
+  if (k >= N) return;
+  const PrimeDev P = primes[prime_of_slot[l]];
+  const long long o = (long long)l * N + k;
+  const u64 idx = ((u64)d * K + (u64)key_index[l]) * N + k;
+  const u64 r = mix64(key_a_stream + (idx + 1) * 0x9E3779B97F4A7C15ull);
+  const u64 a = __umul64hi(r, P.q);
+  u128v prod = {0, 0};
+  mac(prod, a, s_ntt[o]);
+  const u64 as = barrett128(prod, P.q, P.br_hi, P.br_lo);
+  u64 v = sub_mod(e_ntt[o], as, P.q);
+  if (in_digit[l]) {
+    u128v g = {0, 0};
+    mac(g, p_mod_q[l], snew_ntt[o]);
+    v = add_mod(v, barrett128(g, P.q, P.br_hi, P.br_lo), P.q);
+  }
+  key_a[o] = a;
+  key_b[o] = v;
+}
+
+__global__ void k_gauss(u64 *e, const int *prime_of_slot, const PrimeDev *primes,
+                        const u64 *__restrict__ table, u64 stream, u64 idx0, int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = blockIdx.x * kBlk + threadIdx.x;
+  if (k >= N) return;
+  const u64 r = mix64(stream + (idx0 + k + 1) * 0x9E3779B97F4A7C15ull);
+  const u64 u = r >> 1;
+  int mag = 0;
+  while (mag < 19 && u >= table[mag]) ++mag;
+  const u64 q = primes[prime_of_slot[l]].q;
+  u64 v = (u64)mag;
+  if ((r & 1) && mag) v = q - v;
+  e[(long long)l * N + k] = v;
+}
+
+__global__ void k_ternary(const int8_t *s, u64 *out, const int *prime_of_slot,
+                          const PrimeDev *primes, int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = blockIdx.x * kBlk + threadIdx.x;
+  if (k >= N) return;
+  const u64 q = primes[prime_of_slot[l]].q;
+  const int v = s[k];
+  out[(long long)l * N + k] = v >= 0 ? (u64)v : q - (u64)(-v);
+}
+
+__global__ void k_mul(const u64 *a, const u64 *b, u64 *out, const int *prime_of_slot,
+                      const PrimeDev *primes, int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = blockIdx.x * kBlk + threadIdx.x;
+  if (k >= N) return;
+  const PrimeDev P = primes[prime_of_slot[l]];
+  const long long o = (long long)l * N + k;
+  u128v p = {0, 0};
+  mac(p, a[o], b[o]);
+  out[o] = barrett128(p, P.q, P.br_hi, P.br_lo);
+}
+
+inline dim3 grid2(int log_n, int y, int per_thread) {
+  const int N = 1 << log_n;
+  return dim3((N / per_thread + kBlk - 1) / kBlk, y);
+}
+
+}  // namespace
+
+cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
+                       cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_galois_ntt<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(in, out, log_n, elt);
+  return cudaGetLastError();
+}
+
+cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLayout &lay,
+                        const PrimeDev *primes, int log_n, cudaStream_t s) {
+  if (mu.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
+  k_modup_bconv<<<grid2(log_n, mu.beta, 2), kBlk, 0, s>>>(coef, t, mu, lay, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
+                          u64 *cx, const ModUpDev &mu, const KsLayout &lay,
+                          const PrimeDev *primes, int log_n, cudaStream_t s) {
+  if (lay.n_out <= 0) return cudaSuccess;
+  k_inner_product<<<grid2(log_n, lay.n_out, 2), kBlk, 0, s>>>(t, c_ntt, key, key_limbs, cx, mu,
+                                                              lay, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t moddown_bconv(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
+                          const int *q_index, const ModDownDev &md, const PrimeDev *primes,
+                          int log_n, cudaStream_t s) {
+  if (md.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
+  if (n_q <= 0) return cudaSuccess;
+  k_moddown_bconv<<<grid2(log_n, 2, 2), kBlk, 0, s>>>(y_base, y_off, z, n_q, q_index, md, primes,
+                                                      log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0, const u64 *cx, int cx_stride_poly,
+                           const int *cx_slot, const u64 *z, int n_q, const int *q_index,
+                           const ModDownDev &md, const PrimeDev *primes, int log_n, bool rotate,
+                           cudaStream_t s) {
+  if (n_q <= 0) return cudaSuccess;
+  k_moddown_finish<<<grid2(log_n, n_q, 2), kBlk, 0, s>>>(ct0, ct1, g0, cx, cx_stride_poly,
+                                                         cx_slot, z, n_q, q_index, md, primes,
+                                                         log_n, rotate ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
+                       int log_n, cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_mod_reduce<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(x, prime_of_slot, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t scatter_limbs(const u64 *global_buf, u64 *local_buf, int n_polys, int total_limbs,
+                          int log_n, int g, int G, cudaStream_t s) {
+  const int n_local = g < total_limbs ? (total_limbs - g - 1) / G + 1 : 0;
+  if (n_local == 0 || n_polys == 0) return cudaSuccess;
+  dim3 grid(((1 << log_n) / 2 + kBlk - 1) / kBlk, n_local, n_polys);
+  k_scatter<<<grid, kBlk, 0, s>>>(global_buf, local_buf, total_limbs, n_local, log_n, g, G, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t gather_limbs(const u64 *local_buf, u64 *global_buf, int n_polys, int total_limbs,
+                         int log_n, int g, int G, cudaStream_t s) {
+  const int n_local = g < total_limbs ? (total_limbs - g - 1) / G + 1 : 0;
+  if (n_local == 0 || n_polys == 0) return cudaSuccess;
+  dim3 grid(((1 << log_n) / 2 + kBlk - 1) / kBlk, n_local, n_polys);
+  k_scatter<<<grid, kBlk, 0, s>>>(global_buf, const_cast<u64 *>(local_buf), total_limbs, n_local,
+                                  log_n, g, G, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t keygen_digit(u64 *key_b, u64 *key_a, const u64 *s_ntt, const u64 *snew_ntt,
+                         const u64 *e_ntt, int n_limbs, const int *key_index,
+                         const int *prime_of_slot, const int *in_digit, const u64 *p_mod_q,
+                         uint64_t key_a_stream, int d, int K, const PrimeDev *primes, int log_n,
+                         cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_keygen<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(key_b, key_a, s_ntt, snew_ntt, e_ntt,
+                                                     key_index, prime_of_slot, in_digit, p_mod_q,
+                                                     key_a_stream, d, K, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t sample_gauss(u64 *e, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
+                         const u64 *table, uint64_t stream, uint64_t idx0, int log_n,
+                         cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_gauss<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(e, prime_of_slot, primes, table, stream, idx0,
+                                                    log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t expand_ternary(const int8_t *sk, u64 *out, int n_limbs, const int *prime_of_slot,
+                           const PrimeDev *primes, int log_n, cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_ternary<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(sk, out, prime_of_slot, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t mul_pointwise(const u64 *a, const u64 *b, u64 *out, int n_limbs,
+                          const int *prime_of_slot, const PrimeDev *primes, int log_n,
+                          cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  k_mul<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(a, b, out, prime_of_slot, primes, log_n);
+  return cudaGetLastError();
+}
+
+}  // namespace ksb

@@ -1,0 +1,101 @@
+// ks_kernels.cuh -- element-wise and base-conversion kernels of the hybrid
+// key switch (ModUp base extension, evaluation-key inner product, ModDown
+// finish, NTT-domain automorphism), the limb scatter/gather of the cyclic
+// partition, and the synthetic-key samplers.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "ks_arith.cuh"
+
+namespace ksb {
+
+constexpr int KS_MAX_ALPHA = 8;
+
+// Per-level constants of the base extension Q_d -> (Ql+alpha) basis, in
+// device memory.  Digit d covers the Q limbs [d*alpha, min((d+1)*alpha, Ql)).
+struct ModUpDev {
+  int Ql, QlP, beta, alpha;
+  const int *prime_of;        // [QlP] prime index of QlP limb j (Q limbs, then P)
+  const ulonglong2 *qhatinv;  // [beta][alpha] {[(Q_d/q_i)^-1]_{q_i}, Shoup}
+  const u64 *w;               // [beta][QlP][alpha] [Q_d/q_i]_{m_j}
+};
+
+// Constants of the conversion P -> Q (ModDown), indexed by Q limb j.
+struct ModDownDev {
+  int alpha;
+  int first_p;                // prime index of p_0
+  const ulonglong2 *phatinv;  // [alpha] {[(P/p_i)^-1]_{p_i}, Shoup}
+  const u64 *w;               // [L][alpha] [P/p_i]_{q_j}
+  const ulonglong2 *pinv;     // [L] {[P^-1]_{q_j}, Shoup}
+};
+
+// Which QlP limbs this device produces and where its inputs live.
+struct KsLayout {
+  int n_out;                  // number of output limbs (owned QlP limbs)
+  const int *out_j;           // [n_out] QlP index of output slot s
+  const int *key_slot;        // [n_out] limb slot of that limb in the key shard
+  const int *c_slot;          // [n_out] local slot of Q limb j in the NTT-form input, or -1
+  int coef_G, coef_ml;        // coefficient-form Q limb j at slot (j % G) * ml + j / G
+};
+
+// out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
+cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
+                       cudaStream_t s);
+
+// ModUp base extension for all digits:
+//   t[d][s][k] = sum_i [x_i[k] * qhatinv_{d,i}]_{q_i} * w[d][j][i] mod m_j,  j = out_j[s],
+// for every output slot s with j outside digit d (those slots are left untouched).
+cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLayout &lay,
+                        const PrimeDev *primes, int log_n, cudaStream_t s);
+
+// cx[p][s][k] = sum_d src_d[s][k] * key[d][p][key_slot[s]][k]  mod m_j,
+// src_d = c_ntt[c_slot[s]] when limb j lies in digit d, else t[d][s].
+// key: [beta_key][2][key_limbs][N].
+cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
+                          u64 *cx, const ModUpDev &mu, const KsLayout &lay,
+                          const PrimeDev *primes, int log_n, cudaStream_t s);
+
+// z[p][s][k] = sum_i [y_i[k] * phatinv_i]_{p_i} * w[j][i] mod q_j for the Q limbs
+// j = q_index[s], s < n_q; y: pointers to the alpha P-limb coefficient arrays
+// of poly p at y_off[p*alpha + i] (word offsets from y_base).
+cudaError_t moddown_bconv(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
+                          const int *q_index, const ModDownDev &md, const PrimeDev *primes,
+                          int log_n, cudaStream_t s);
+
+// Final ModDown step and the add to the ciphertext, for the Q slots s < n_q:
+//   o_p = (cx[p][cx_slot[s]] - z[p][s]) * P^-1 mod q_j
+//   relin:  ct0 += o_0, ct1 += o_1;   rotate: ct0 = g0 + o_0, ct1 = o_1.
+cudaError_t moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0, const u64 *cx, int cx_stride_poly,
+                           const int *cx_slot, const u64 *z, int n_q, const int *q_index,
+                           const ModDownDev &md, const PrimeDev *primes, int log_n, bool rotate,
+                           cudaStream_t s);
+
+// x %= q for each limb (after an integer all-reduce / reduce-scatter of partial sums).
+cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
+                       int log_n, cudaStream_t s);
+
+// Cyclic partition copies: global [poly][total][N] <-> local [poly][n_local][N]
+// for the limbs j = local*G + g (reference rns_partition.cu:26-80).
+cudaError_t scatter_limbs(const u64 *global_buf, u64 *local_buf, int n_polys, int total_limbs,
+                          int log_n, int g, int G, cudaStream_t s);
+cudaError_t gather_limbs(const u64 *local_buf, u64 *global_buf, int n_polys, int total_limbs,
+                         int log_n, int g, int G, cudaStream_t s);
+
+// Synthetic evaluation-key generation for one digit d over n_limbs key limbs
+// (not a secure generator; the sampler is the counter-based hash shared with
+// the CPU oracle).  key_a_stream = the per-(seed, domain) hash key.
+cudaError_t keygen_digit(u64 *key_b, u64 *key_a, const u64 *s_ntt, const u64 *snew_ntt,
+                         const u64 *e_ntt, int n_limbs, const int *key_index,
+                         const int *prime_of_slot, const int *in_digit, const u64 *p_mod_q,
+                         uint64_t key_a_stream, int d, int K, const PrimeDev *primes, int log_n,
+                         cudaStream_t s);
+cudaError_t sample_gauss(u64 *e, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
+                         const u64 *table, uint64_t stream, uint64_t idx0, int log_n,
+                         cudaStream_t s);
+cudaError_t expand_ternary(const int8_t *sk, u64 *out, int n_limbs, const int *prime_of_slot,
+                           const PrimeDev *primes, int log_n, cudaStream_t s);
+cudaError_t mul_pointwise(const u64 *a, const u64 *b, u64 *out, int n_limbs,
+                          const int *prime_of_slot, const PrimeDev *primes, int log_n,
+                          cudaStream_t s);
+
+}  // namespace ksb

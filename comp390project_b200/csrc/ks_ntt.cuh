@@ -1,0 +1,38 @@
+// ks_ntt.cuh -- batched negacyclic NTT / INTT over RNS limbs (sm_100a).
+//
+// Convention (the same as the CPU oracle): forward = Cooley-Tukey with the
+// table psi^brev(i), natural order in, bit-reversed order out; inverse =
+// Gentleman-Sande with psi^-brev(i), bit-reversed in, natural out, N^-1
+// folded into the last stage.  Replaces Phantom's nwt_2d_radix8_forward /
+// backward_inplace (paper/code_study.tex:493-506 of the reference).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "ks_arith.cuh"
+
+namespace ksb {
+
+// Where limb i of a batch lives and which prime it uses.
+struct LimbMap {
+  u64 *base;
+  long long stride;          // words between consecutive limbs (normally N)
+  const long long *offsets;  // device array; if set, limb i is at base + offsets[i]
+  const int *prime_tab;      // device array; if null: first_prime + (i % period)
+  int first_prime, period;
+};
+
+struct NttTables {
+  const ulonglong2 *fwd;  // [n_primes][N] {w, w_shoup}, w = psi^brev(i)
+  const ulonglong2 *inv;  // [n_primes][N] {w, w_shoup}, w = psi^-brev(i)
+  const PrimeDev *primes; // [n_primes]
+  int log_n;
+};
+
+// Transforms n_limbs limbs in place; outputs are canonical in [0, q).
+// Inputs must be < q (canonical).  Limbs whose prime index is negative are
+// skipped.  Supported ring degrees: 2^12 .. 2^16.
+cudaError_t ntt_forward(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s);
+cudaError_t ntt_inverse(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s);
+bool ntt_supported_log_n(int log_n);
+
+}  // namespace ksb

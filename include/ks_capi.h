@@ -1,0 +1,172 @@
+/*
+ * ks_capi.h -- C ABI of the B200-native CKKS hybrid key-switching library
+ * (libks_b200.so).
+ *
+ * This is the drop-in boundary for the reference's key-switching layer
+ * (hkanpak21/Comp390Project, namespace nexus_multi_gpu):
+ *   src/multi_gpu/keyswitching/input_broadcast.cuh:68-114
+ *   src/multi_gpu/keyswitching/output_aggregation.cuh:69-92
+ *   src/multi_gpu/comm/nccl_comm.cuh:42-195
+ *   src/multi_gpu/partition/rns_partition.cuh:29-191
+ * and of the Phantom entry points those files call (keyswitch_inplace,
+ * apply_galois_inplace, rotate_vector, relinearize, nwt_2d_radix8_*).
+ *
+ * Conventions
+ *  - C linkage, no exceptions cross the boundary.  Every function returns an
+ *    int status: KS_OK (0) or a negative KS_ERR_* code; ks_last_error()
+ *    describes the last failure on that context.
+ *  - Ciphertexts are caller-owned device arrays of uint64 words in the
+ *    PhantomCiphertext layout [poly][limb][N] (reference
+ *    paper/code_study.tex:371-372).  With world > 1 each rank holds only the
+ *    limbs it owns under the cyclic partition (limb j on rank j % world, at
+ *    local slot j / world; rns_partition.cuh:29-60), i.e. [poly][n_local][N].
+ *  - NTT values are canonical residues in [0, q); NTT order is bit-reversed.
+ *  - `level_limbs` is the number of Q limbs of the ciphertext (Phantom's
+ *    coeff_modulus_size; chain_index c corresponds to L - c + 1 limbs).
+ *  - Streams are passed as `void *` holding a cudaStream_t (NULL = legacy
+ *    default stream).  Calls are asynchronous on that stream.
+ *  - One host thread drives one context; contexts are independent.
+ *  - All device pointers must be 16-byte aligned.
+ */
+#ifndef KS_CAPI_H
+#define KS_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KS_OK 0
+#define KS_ERR_INVALID (-1)     /* bad argument: null/misaligned pointer, size, level */
+#define KS_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define KS_ERR_NCCL (-3)        /* an NCCL call failed */
+#define KS_ERR_NO_KEY (-4)      /* no evaluation key for the requested element */
+#define KS_ERR_UNSUPPORTED (-5) /* parameter set outside what the kernels support */
+#define KS_ERR_ALLOC (-6)       /* device allocation failed */
+#define KS_ERR_TIMEOUT (-7)     /* a collective did not complete within the deadline */
+
+#define KS_KEY_RELIN 0
+#define KS_KEY_GALOIS 1
+
+#define KS_MODE_INPUT_BROADCAST 0   /* all-gather c2 limbs, limb-local extension */
+#define KS_MODE_OUTPUT_AGGREGATION 1 /* digit-split inner product + reduce-scatter */
+
+typedef struct ks_ctx ks_ctx;
+
+typedef struct ks_params {
+  uint32_t log_n;       /* ring degree N = 2^log_n (12..16) */
+  int n_q;              /* L: number of ciphertext (Q) primes */
+  const uint64_t *q;    /* Q primes, q_0 first */
+  int n_p;              /* alpha: number of special (P) primes = digit size (0..8) */
+  const uint64_t *p;    /* P primes */
+  int mode;             /* KS_MODE_* (ignored when world == 1) */
+  int max_batch;        /* ciphertexts per batched call the scratch is sized for (>=1) */
+} ks_params;
+
+/* Phantom/SEAL CoeffModulus::Create: the largest primes below 2^bits that are
+ * 1 mod 2N, smaller ones first within one bit size. */
+int ks_gen_primes(uint32_t log_n, const int *bit_sizes, int n, uint64_t *out);
+
+/* Synthetic ternary secret [N] from a seed: uniform ternary (hamming_weight
+ * <= 0) or exactly hamming_weight entries of +-1.  Host function; the
+ * sampler is a counter hash, NOT a secure RNG. */
+int ks_secret_generate(uint32_t log_n, uint64_t seed, int hamming_weight, int8_t *out);
+
+/* NCCL bootstrap: rank 0 calls ks_nccl_unique_id and shares the bytes
+ * (KS_NCCL_ID_BYTES) with the other ranks by any means (e.g. a torch store). */
+#define KS_NCCL_ID_BYTES 128
+int ks_nccl_unique_id(void *out, size_t n);
+
+/* One context per (device, rank).  world == 1 needs no NCCL id.
+ * Replaces MultiGpuContext::create (reference nccl_comm.cu:41-58). */
+int ks_ctx_create(const ks_params *prm, int device, int rank, int world,
+                  const void *nccl_id, ks_ctx **out);
+/* Single-process, all devices (ncclCommInitAll); outs[i] drives devices[i]. */
+int ks_ctx_create_all(const ks_params *prm, const int *devices, int n, ks_ctx **outs);
+int ks_ctx_destroy(ks_ctx *ctx);
+/* Copies the last error message of ctx (or the global one if ctx is NULL). */
+int ks_last_error(const ks_ctx *ctx, char *buf, size_t n);
+/* Collective deadline in milliseconds (0 = wait forever); default 60000. */
+int ks_set_timeout_ms(ks_ctx *ctx, int ms);
+
+/* Partition queries (reference rns_partition.cuh:29-60). */
+int ks_n_local_limbs(const ks_ctx *ctx, int total_limbs);
+int ks_owner_of_limb(const ks_ctx *ctx, int limb);
+int ks_num_digits(const ks_ctx *ctx, int level_limbs);
+int ks_galois_elt(const ks_ctx *ctx, int step, uint32_t *elt);
+/* Words of one full (unsharded) key: ceil(L/alpha) * 2 * (L+alpha) * N. */
+size_t ks_key_words(const ks_ctx *ctx);
+
+/* Evaluation keys, full layout [ceil(L/alpha)][2][L+alpha][N] (NTT form,
+ * key[d][0] = b_d, key[d][1] = a_d; reference output_aggregation.cu:115-118).
+ * The context keeps the shard its partition needs. */
+int ks_key_upload(ks_ctx *ctx, int kind, uint32_t galois_elt, const uint64_t *host_key,
+                  size_t n_words);
+/* Same, from a device array of the same full layout. */
+int ks_key_upload_device(ks_ctx *ctx, int kind, uint32_t galois_elt,
+                         const uint64_t *dev_key, size_t n_words, void *stream);
+/* Generates a synthetic key on the device from an int8 ternary secret [N]
+ * (host array) and a seed.  The sampler is a counter hash, NOT a secure RNG. */
+int ks_key_generate(ks_ctx *ctx, int kind, uint32_t galois_elt, const int8_t *secret,
+                    uint64_t seed, void *stream);
+/* Copies the (local shard of the) key back to host memory (for tests). */
+int ks_key_download(ks_ctx *ctx, int kind, uint32_t galois_elt, uint64_t *host_key,
+                    size_t n_words);
+int ks_key_drop(ks_ctx *ctx, int kind, uint32_t galois_elt);
+
+/* Relinearisation of ct [3][n_local][N] in place: polys 0, 1 receive the
+ * result.  Replaces keyswitching_input_broadcast / keyswitching_output_
+ * aggregation (input_broadcast.cu:117-176, output_aggregation.cu:197-294). */
+int ks_relinearize(ks_ctx *ctx, uint64_t *ct, int level_limbs, void *stream);
+/* X -> X^galois_elt on ct [2][n_local][N] in place plus key switch with the
+ * Galois key of that element (Phantom apply_galois_inplace;
+ * rotation_input_broadcast, input_broadcast.cu:182-202). */
+int ks_apply_galois(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t galois_elt,
+                    void *stream);
+/* Left rotation of the slots by `step` (galois element 3^step mod 2N). */
+int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream);
+/* n rotations of n independent ciphertexts (cts[i] rotated by steps[i]). */
+int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n,
+                    int level_limbs, void *stream);
+/* Hoisted rotations: one ModUp of ct's c1 shared by n rotations; outs[i]
+ * [2][n_local][N] receives ct rotated by steps[i].  ct is not modified. */
+int ks_rotate_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs, const int *steps,
+                      int n, uint64_t *const *outs, void *stream);
+
+/* Batched negacyclic NTT in place over data [batch][n_limbs][N]; limb i uses
+ * prime first_prime + i of the context's basis (Q primes then P primes).
+ * Replaces nwt_2d_radix8_forward_inplace / backward_inplace. */
+int ks_ntt_forward(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,
+                   void *stream);
+int ks_ntt_inverse(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,
+                   void *stream);
+
+/* Cyclic partition copies global [n_polys][total][N] <-> local
+ * [n_polys][n_local][N] for this context's rank (rns_partition.cu:86-128). */
+int ks_scatter_limbs(ks_ctx *ctx, const uint64_t *global_buf, uint64_t *local_buf,
+                     int n_polys, int total_limbs, void *stream);
+int ks_gather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *global_buf,
+                    int n_polys, int total_limbs, void *stream);
+/* All-gather of local limbs [n_local][N] into sequential order [total][N]
+ * on every rank (allgather_c2_limbs + reorder, input_broadcast.cu:45-111). */
+int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_buf,
+                       int total_limbs, void *stream);
+
+/* Number of kernels the last hot-path call launched (for bench accounting). */
+int ks_last_launch_count(const ks_ctx *ctx);
+
+/* Optional per-stage timing of the key switch with CUDA events recorded on
+ * the launch stream (bench accounting; off by default).  ks_profile_read
+ * waits for the recorded events, returns the summed milliseconds and the
+ * number of timed calls per stage, and clears the record. */
+int ks_profile_enable(ks_ctx *ctx, int on);
+int ks_profile_stage_count(void);
+const char *ks_profile_stage_name(int i);
+int ks_profile_read(ks_ctx *ctx, double *ms, int *calls, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KS_CAPI_H */

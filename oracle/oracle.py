@@ -1,0 +1,268 @@
+"""ctypes/numpy wrapper of the CPU oracle (test infrastructure only).
+
+Only tests/, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` leg of
+bench.py may import this module; the product library never does.  See
+oracle/ckks_oracle.h for what the oracle restates, which reference lines it
+follows, and its parity status (bit-level parity with Phantom is unpinned;
+primes, partition math and decode-level semantics are pinned).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "build", "libckks_oracle.so")
+_lib = None
+
+u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
+i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with its Makefile (g++, OpenMP)."""
+    if force or not os.path.exists(_LIB_PATH):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(_LIB_PATH)
+        V, P, I, U32, U64, D = None, C.c_void_p, C.c_int, C.c_uint32, C.c_uint64, C.c_double
+        sig = {
+            "ork_gen_primes": (I, [U32, i32p, I, u64p]),
+            "ork_is_prime": (I, [U64]),
+            "ork_create": (P, [U32, u64p, I, u64p, I]),
+            "ork_destroy": (V, [P]),
+            "ork_set_threads": (V, [I]),
+            "ork_get_threads": (I, []),
+            "ork_num_digits": (I, [P, I]),
+            "ork_psi": (U64, [P, I]),
+            "ork_ntt_forward": (V, [P, u64p, I, i32p]),
+            "ork_ntt_inverse": (V, [P, u64p, I, i32p]),
+            "ork_galois_elt": (U32, [P, I]),
+            "ork_galois_ntt": (V, [P, U32, u64p, u64p, I]),
+            "ork_galois_coeff": (V, [P, U32, u64p, u64p, I, i32p]),
+            "ork_bconv": (V, [P, u64p, i32p, I, u64p, i32p, I]),
+            "ork_modup": (V, [P, u64p, I, u64p]),
+            "ork_inner_product": (V, [P, u64p, I, u64p, u64p]),
+            "ork_moddown": (V, [P, u64p, I, u64p]),
+            "ork_keyswitch": (V, [P, u64p, I, u64p, u64p]),
+            "ork_apply_galois": (V, [P, u64p, I, U32, u64p, u64p]),
+            "ork_relinearize": (V, [P, u64p, I, u64p, u64p]),
+            "ork_rotate_hoisted": (V, [P, u64p, I, I, C.POINTER(C.c_uint32), C.POINTER(C.c_void_p), u64p]),
+            "ork_prng": (U64, [U64, U64, U64]),
+            "ork_gauss": (I, [U64]),
+            "ork_gauss_table": (V, [u64p]),
+            "ork_secret": (V, [P, U64, I, i8p]),
+            "ork_secret_ntt": (V, [P, i8p, I, u64p]),
+            "ork_keygen_galois": (V, [P, i8p, U32, U64, u64p]),
+            "ork_keygen_relin": (V, [P, i8p, U64, u64p]),
+            "ork_encode": (V, [P, f64p, f64p, I, D, I, u64p]),
+            "ork_decode": (V, [P, u64p, I, D, f64p, f64p, I]),
+            "ork_encrypt": (V, [P, i8p, u64p, I, U64, u64p]),
+            "ork_decrypt": (V, [P, i8p, u64p, I, I, u64p]),
+            "ork_multiply": (V, [P, u64p, u64p, I, u64p]),
+            "ork_ks_noise_log2": (D, [P, i8p, u64p, u64p, u64p, I]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def gen_primes(log_n: int, bit_sizes) -> np.ndarray:
+    bits = np.ascontiguousarray(bit_sizes, dtype=np.int32)
+    out = np.zeros(len(bits), dtype=np.uint64)
+    if lib().ork_gen_primes(log_n, bits, len(bits), out) != 0:
+        raise ValueError("not enough primes")
+    return out
+
+
+def set_threads(n: int) -> None:
+    lib().ork_set_threads(int(n))
+
+
+def prng(seed: int, domain: int, idx: int) -> int:
+    return int(lib().ork_prng(seed, domain, idx))
+
+
+class Oracle:
+    """One parameter set: N = 2^log_n, L Q primes, alpha P primes."""
+
+    def __init__(self, log_n: int, q, p):
+        self.log_n = int(log_n)
+        self.N = 1 << self.log_n
+        self.q = np.ascontiguousarray(q, dtype=np.uint64)
+        self.p = np.ascontiguousarray(p, dtype=np.uint64)
+        self.L, self.alpha = len(self.q), len(self.p)
+        self.h = lib().ork_create(self.log_n, self.q, self.L, self.p, self.alpha)
+        self.moduli = np.concatenate([self.q, self.p])
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h and _lib is not None:
+            _lib.ork_destroy(h)
+            self.h = None
+
+    # -- helpers -------------------------------------------------------------
+    def digits(self, Ql: int) -> int:
+        return int(lib().ork_num_digits(self.h, Ql))
+
+    def key_words(self) -> int:
+        return self.digits(self.L) * 2 * (self.L + self.alpha) * self.N
+
+    def psi(self, k: int) -> int:
+        return int(lib().ork_psi(self.h, k))
+
+    def galois_elt(self, step: int) -> int:
+        return int(lib().ork_galois_elt(self.h, int(step)))
+
+    # -- transforms ----------------------------------------------------------
+    def ntt(self, data: np.ndarray, key_idx, inverse: bool = False) -> np.ndarray:
+        a = np.ascontiguousarray(data, dtype=np.uint64).copy()
+        idx = np.ascontiguousarray(key_idx, dtype=np.int32)
+        n = a.size // self.N
+        assert len(idx) == n
+        f = lib().ork_ntt_inverse if inverse else lib().ork_ntt_forward
+        f(self.h, a.reshape(-1), n, idx)
+        return a
+
+    def galois_ntt(self, data: np.ndarray, elt: int) -> np.ndarray:
+        a = np.ascontiguousarray(data, dtype=np.uint64)
+        out = np.empty_like(a)
+        lib().ork_galois_ntt(self.h, elt, a.reshape(-1), out.reshape(-1), a.size // self.N)
+        return out
+
+    def galois_coeff(self, data: np.ndarray, elt: int, key_idx) -> np.ndarray:
+        a = np.ascontiguousarray(data, dtype=np.uint64)
+        out = np.empty_like(a)
+        idx = np.ascontiguousarray(key_idx, dtype=np.int32)
+        lib().ork_galois_coeff(self.h, elt, a.reshape(-1), out.reshape(-1), a.size // self.N, idx)
+        return out
+
+    def bconv(self, x: np.ndarray, in_idx, out_idx) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.uint64)
+        ii = np.ascontiguousarray(in_idx, dtype=np.int32)
+        oi = np.ascontiguousarray(out_idx, dtype=np.int32)
+        out = np.zeros((len(oi), self.N), dtype=np.uint64)
+        lib().ork_bconv(self.h, x.reshape(-1), ii, len(ii), out.reshape(-1), oi, len(oi))
+        return out
+
+    # -- key switching -------------------------------------------------------
+    def modup(self, c: np.ndarray, Ql: int) -> np.ndarray:
+        c = np.ascontiguousarray(c, dtype=np.uint64)
+        t = np.zeros((self.digits(Ql), Ql + self.alpha, self.N), dtype=np.uint64)
+        lib().ork_modup(self.h, c.reshape(-1), Ql, t.reshape(-1))
+        return t
+
+    def inner_product(self, t: np.ndarray, Ql: int, key: np.ndarray) -> np.ndarray:
+        cx = np.zeros((2, Ql + self.alpha, self.N), dtype=np.uint64)
+        lib().ork_inner_product(self.h, np.ascontiguousarray(t).reshape(-1), Ql,
+                                np.ascontiguousarray(key).reshape(-1), cx.reshape(-1))
+        return cx
+
+    def moddown(self, cx_poly: np.ndarray, Ql: int) -> np.ndarray:
+        out = np.zeros((Ql, self.N), dtype=np.uint64)
+        lib().ork_moddown(self.h, np.ascontiguousarray(cx_poly).reshape(-1), Ql, out.reshape(-1))
+        return out
+
+    def keyswitch(self, c: np.ndarray, Ql: int, key: np.ndarray) -> np.ndarray:
+        out = np.zeros((2, Ql, self.N), dtype=np.uint64)
+        lib().ork_keyswitch(self.h, np.ascontiguousarray(c).reshape(-1), Ql,
+                            np.ascontiguousarray(key).reshape(-1), out.reshape(-1))
+        return out
+
+    def apply_galois(self, ct: np.ndarray, Ql: int, elt: int, key: np.ndarray) -> np.ndarray:
+        out = np.zeros((2, Ql, self.N), dtype=np.uint64)
+        lib().ork_apply_galois(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, elt,
+                               np.ascontiguousarray(key).reshape(-1), out.reshape(-1))
+        return out
+
+    def rotate(self, ct: np.ndarray, Ql: int, step: int, key: np.ndarray) -> np.ndarray:
+        return self.apply_galois(ct, Ql, self.galois_elt(step), key)
+
+    def relinearize(self, ct3: np.ndarray, Ql: int, key: np.ndarray) -> np.ndarray:
+        out = np.zeros((2, Ql, self.N), dtype=np.uint64)
+        lib().ork_relinearize(self.h, np.ascontiguousarray(ct3).reshape(-1), Ql,
+                              np.ascontiguousarray(key).reshape(-1), out.reshape(-1))
+        return out
+
+    def rotate_hoisted(self, ct: np.ndarray, Ql: int, elts, keys) -> np.ndarray:
+        n = len(elts)
+        out = np.zeros((n, 2, Ql, self.N), dtype=np.uint64)
+        e = (C.c_uint32 * n)(*[int(x) for x in elts])
+        ks = [np.ascontiguousarray(k) for k in keys]
+        kp = (C.c_void_p * n)(*[k.ctypes.data for k in ks])
+        lib().ork_rotate_hoisted(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, n, e, kp,
+                                 out.reshape(-1))
+        return out
+
+    # -- keys, encoding, encryption -------------------------------------------
+    def secret(self, seed: int, hamming_weight: int = 0) -> np.ndarray:
+        s = np.zeros(self.N, dtype=np.int8)
+        lib().ork_secret(self.h, seed, hamming_weight, s)
+        return s
+
+    def secret_ntt(self, s: np.ndarray, n_limbs: int) -> np.ndarray:
+        out = np.zeros((n_limbs, self.N), dtype=np.uint64)
+        lib().ork_secret_ntt(self.h, s, n_limbs, out.reshape(-1))
+        return out
+
+    def keygen_galois(self, s: np.ndarray, elt: int, seed: int) -> np.ndarray:
+        key = np.zeros((self.digits(self.L), 2, self.L + self.alpha, self.N), dtype=np.uint64)
+        lib().ork_keygen_galois(self.h, s, elt, seed, key.reshape(-1))
+        return key
+
+    def keygen_relin(self, s: np.ndarray, seed: int) -> np.ndarray:
+        key = np.zeros((self.digits(self.L), 2, self.L + self.alpha, self.N), dtype=np.uint64)
+        lib().ork_keygen_relin(self.h, s, seed, key.reshape(-1))
+        return key
+
+    def encode(self, z: np.ndarray, scale: float, Ql: int) -> np.ndarray:
+        z = np.asarray(z)
+        re = np.ascontiguousarray(z.real, dtype=np.float64)
+        im = np.ascontiguousarray(np.imag(z) if np.iscomplexobj(z) else np.zeros(len(z)),
+                                  dtype=np.float64)
+        pt = np.zeros((Ql, self.N), dtype=np.uint64)
+        lib().ork_encode(self.h, re, im, len(re), scale, Ql, pt.reshape(-1))
+        return pt
+
+    def decode(self, pt: np.ndarray, Ql: int, scale: float, n_slots: int | None = None) -> np.ndarray:
+        n = n_slots or self.N // 2
+        re = np.zeros(n)
+        im = np.zeros(n)
+        lib().ork_decode(self.h, np.ascontiguousarray(pt).reshape(-1), Ql, scale, re, im, n)
+        return re + 1j * im
+
+    def encrypt(self, s: np.ndarray, pt: np.ndarray, Ql: int, seed: int) -> np.ndarray:
+        ct = np.zeros((2, Ql, self.N), dtype=np.uint64)
+        lib().ork_encrypt(self.h, s, np.ascontiguousarray(pt).reshape(-1), Ql, seed, ct.reshape(-1))
+        return ct
+
+    def decrypt(self, s: np.ndarray, ct: np.ndarray, Ql: int) -> np.ndarray:
+        ct = np.ascontiguousarray(ct)
+        pt = np.zeros((Ql, self.N), dtype=np.uint64)
+        lib().ork_decrypt(self.h, s, ct.reshape(-1), ct.shape[0], Ql, pt.reshape(-1))
+        return pt
+
+    def multiply(self, a: np.ndarray, b: np.ndarray, Ql: int) -> np.ndarray:
+        out = np.zeros((3, Ql, self.N), dtype=np.uint64)
+        lib().ork_multiply(self.h, np.ascontiguousarray(a).reshape(-1),
+                           np.ascontiguousarray(b).reshape(-1), Ql, out.reshape(-1))
+        return out
+
+    def ks_noise_log2(self, s, c_in, snew_ntt, ks, Ql) -> float:
+        return float(lib().ork_ks_noise_log2(self.h, s, np.ascontiguousarray(c_in).reshape(-1),
+                                              np.ascontiguousarray(snew_ntt).reshape(-1),
+                                              np.ascontiguousarray(ks).reshape(-1), Ql))

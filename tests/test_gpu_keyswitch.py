@@ -1,0 +1,134 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle, bit-exact."""
+import numpy as np
+import pytest
+
+from tests.ksparams import CFG1, CFG3, SMALL, oracle_for, split
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _ctx(cfg, **kw):
+    from comp390project_b200 import KsContext
+    log_n, q, p = split(cfg)
+    return KsContext(log_n, q, p, device=0, **kw)
+
+
+def _to_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+
+
+def _to_host(t):
+    return t.cpu().numpy().view(np.uint64)
+
+
+@pytest.mark.parametrize("name,cfg", [("cfg1", CFG1), ("small", SMALL), ("cfg3", CFG3)])
+def test_ntt_roundtrip_bitexact(name, cfg, cuda_device):
+    o = oracle_for(name)
+    ctx = _ctx(cfg)
+    K = o.L + o.alpha
+    rng = np.random.default_rng(1)
+    x = np.stack([rng.integers(0, int(m), size=o.N, dtype=np.uint64) for m in o.moduli])
+    d = _to_dev(x)
+    ctx.ntt_forward(d, K, 0, 1)
+    fwd = _to_host(d)
+    ref = o.ntt(x, list(range(K)))
+    assert np.array_equal(fwd, ref)
+    ctx.ntt_inverse(d, K, 0, 1)
+    assert np.array_equal(_to_host(d), x)
+
+
+def test_ntt_batch_prime_pattern(cuda_device):
+    o = oracle_for("small")
+    ctx = _ctx(SMALL)
+    rng = np.random.default_rng(2)
+    batch, nl, first = 3, 4, 2
+    x = np.stack([rng.integers(0, int(o.moduli[first + (i % nl)]), size=o.N, dtype=np.uint64)
+                  for i in range(batch * nl)])
+    d = _to_dev(x)
+    ctx.ntt_forward(d, nl, first, batch)
+    ref = o.ntt(x, [first + (i % nl) for i in range(batch * nl)])
+    assert np.array_equal(_to_host(d), ref)
+
+
+def _encrypted(o, Ql, seed, s):
+    rng = np.random.default_rng(seed)
+    z = rng.uniform(-1, 1, o.N // 2)
+    pt = o.encode(z, 2.0 ** 40, Ql)
+    return z, o.encrypt(s, pt, Ql, seed + 100)
+
+
+@pytest.mark.parametrize("name,cfg,Ql,step", [("cfg1", CFG1, 3, 1), ("small", SMALL, 7, 5),
+                                              ("small", SMALL, 5, -3), ("small", SMALL, 1, 2)])
+def test_rotate_bitexact(name, cfg, Ql, step, cuda_device):
+    o = oracle_for(name)
+    ctx = _ctx(cfg)
+    s = o.secret(0)
+    elt = o.galois_elt(step)
+    assert ctx.galois_elt(step) == elt
+    key = o.keygen_galois(s, elt, 11)
+    ctx.key_upload(1, elt, key)
+    z, ct = _encrypted(o, Ql, 3, s)
+    ref = o.apply_galois(ct, Ql, elt, key)
+    d = _to_dev(ct)
+    ctx.rotate(d, Ql, step)
+    out = _to_host(d).reshape(2, Ql, o.N)
+    assert np.array_equal(out, ref)
+    dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 40)
+    assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
+
+
+@pytest.mark.parametrize("name,cfg,Ql", [("cfg1", CFG1, 3), ("small", SMALL, 7), ("small", SMALL, 4)])
+def test_relinearize_bitexact(name, cfg, Ql, cuda_device):
+    o = oracle_for(name)
+    ctx = _ctx(cfg)
+    s = o.secret(1)
+    key = o.keygen_relin(s, 21)
+    ctx.key_upload(0, 0, key)
+    z1, c1 = _encrypted(o, Ql, 5, s)
+    z2, c2 = _encrypted(o, Ql, 6, s)
+    m = o.multiply(c1, c2, Ql)
+    ref = o.relinearize(m, Ql, key)
+    d = _to_dev(m)
+    ctx.relinearize(d, Ql)
+    out = _to_host(d).reshape(3, Ql, o.N)[:2]
+    assert np.array_equal(out, ref)
+    if Ql >= 2:
+        dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 80)
+        assert np.abs(dec - z1 * z2).mean() < 1e-3
+
+
+@pytest.mark.parametrize("name,cfg,kind", [("cfg1", CFG1, 1), ("small", SMALL, 1), ("small", SMALL, 0)])
+def test_gpu_keygen_matches_oracle(name, cfg, kind, cuda_device):
+    o = oracle_for(name)
+    ctx = _ctx(cfg)
+    from comp390project_b200 import secret_generate
+    s = secret_generate(o.log_n, 7, 0)
+    assert np.array_equal(s, o.secret(7))
+    elt = o.galois_elt(3) if kind == 1 else 0
+    ctx.key_generate(kind, elt, s, 99)
+    torch.cuda.synchronize()
+    got = ctx.key_download(kind, elt)
+    ref = o.keygen_galois(s, elt, 99) if kind == 1 else o.keygen_relin(s, 99)
+    assert np.array_equal(got, ref)
+
+
+def test_config3_rotation_bitexact(cuda_device):
+    o = oracle_for("cfg3")
+    ctx = _ctx(CFG3)
+    from comp390project_b200 import secret_generate
+    s = secret_generate(o.log_n, 3, 192)
+    assert np.array_equal(s, o.secret(3, 192))
+    step = 5
+    elt = o.galois_elt(step)
+    ctx.key_generate(1, elt, s, 17)
+    z, ct = _encrypted(o, 35, 9, s)
+    d = _to_dev(ct)
+    ctx.rotate(d, 35, step)
+    out = _to_host(d).reshape(2, 35, o.N)
+    key = o.keygen_galois(s, elt, 17)
+    ref = o.apply_galois(ct, 35, elt, key)
+    assert np.array_equal(out, ref)
+    dec = o.decode(o.decrypt(s, out, 35), 35, 2.0 ** 40)
+    assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
