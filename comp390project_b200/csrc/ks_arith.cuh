@@ -17,7 +17,15 @@ struct __align__(16) PrimeDev {
   u64 br_hi, br_lo;      // floor(2^128 / q)
   u64 ninv, ninv_sh;     // N^-1 and its Shoup companion
   u64 w1ninv, w1ninv_sh; // psi^-brev(1) * N^-1 (last inverse stage, N^-1 folded in)
+  u64 mu, pad_;          // floor(2^64 / q)
 };
+
+// Forward butterflies skip every conditional subtraction when q < 2^58:
+// each Cooley-Tukey stage grows the bound by 2q, so 16 stages from inputs
+// < q end below 33q < 2^64.  Inverse butterflies skip them when q < 2^46:
+// each Gentleman-Sande stage at most doubles the bound, 2^16 * q < 2^62.
+constexpr u64 kFwdLazyBound = 1ull << 58;
+constexpr u64 kInvLazyBound = 1ull << 46;
 
 constexpr int KS_MAX_PRIMES = 96;
 
@@ -86,5 +94,33 @@ __device__ __forceinline__ void gs_bfly_last(u64 &X, u64 &Y, const PrimeDev &P) 
 
 // [0, 4q) -> [0, q)
 __device__ __forceinline__ u64 reduce4(u64 x, u64 q, u64 two_q) { return csub(csub(x, two_q), q); }
+
+// Any x < 2^64 -> [0, q): qhat = floor(x * mu / 2^64) >= floor(x/q) - 1.
+__device__ __forceinline__ u64 reduce_full(u64 x, u64 q, u64 mu) {
+  return csub(x - __umul64hi(x, mu) * q, q);
+}
+
+// Forward butterfly without reductions (q < kFwdLazyBound): bound grows by 2q.
+__device__ __forceinline__ void ct_bfly_lazy(u64 &X, u64 &Y, u64 w, u64 wp, u64 q, u64 two_q) {
+  const u64 t = mul_shoup_lazy(Y, w, wp, q);
+  const u64 x = X;
+  X = x + t;
+  Y = x - t + two_q;
+}
+
+// Inverse butterfly without reductions (q < kInvLazyBound).  K is a multiple
+// of q no smaller than the bound on Y, so X + K - Y never wraps.
+__device__ __forceinline__ void gs_bfly_lazy(u64 &X, u64 &Y, u64 w, u64 wp, u64 q, u64 K) {
+  const u64 s = X + Y;
+  const u64 d = X + K - Y;
+  X = s;
+  Y = mul_shoup_lazy(d, w, wp, q);
+}
+__device__ __forceinline__ void gs_bfly_last_lazy(u64 &X, u64 &Y, const PrimeDev &P, u64 K) {
+  const u64 s = X + Y;
+  const u64 d = X + K - Y;
+  X = mul_shoup_lazy(s, P.ninv, P.ninv_sh, P.q);
+  Y = mul_shoup_lazy(d, P.w1ninv, P.w1ninv_sh, P.q);
+}
 
 }  // namespace ksb

@@ -26,6 +26,7 @@
 
 #include "../../include/ks_capi.h"
 #include "ks_context.hpp"
+#include "ks_fused.cuh"
 #include "ks_hostmath.hpp"
 
 using namespace ksb;
@@ -153,6 +154,8 @@ void build_tables(Ctx &c) {
     P.ninv_sh = h_shoup(P.ninv, q);
     P.w1ninv = h_mulmod(pwi[N / 2], P.ninv, q);
     P.w1ninv_sh = h_shoup(P.w1ninv, q);
+    P.mu = (u64)((~(u128)0 >> 64) / q);  // floor((2^64 - 1) / q) == floor(2^64 / q)
+    P.pad_ = 0;
   };
   const int nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
   for (int t0 = 0; t0 < nth; ++t0)
@@ -160,6 +163,7 @@ void build_tables(Ctx &c) {
       for (int k = t0; k < K; k += nth) work(k);
     });
   for (auto &t : th) t.join();
+  c.h_primes = pd;
   c.d_primes = upload(pd);
   c.d_tw_fwd = upload(fwd);
   c.d_tw_inv = upload(inv);
@@ -291,6 +295,49 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       }
     }
   }
+  // fused ModUp jobs and the scaled-INTT constants
+  auto scale_pair = [&](int prime, u64 cst, std::vector<ulonglong2> &out) {
+    const PrimeDev &P = c.h_primes[prime];
+    const u64 q = P.q;
+    const u64 a0 = h_mulmod(P.ninv, cst, q), a1 = h_mulmod(P.w1ninv, cst, q);
+    out.push_back(make_ulonglong2(a0, h_shoup(a0, q)));
+    out.push_back(make_ulonglong2(a1, h_shoup(a1, q)));
+  };
+  for (int d = 0; d < lv.beta; ++d)
+    for (int i = 0; i < a; ++i) {
+      const int j = d * a + i;
+      lv.src_slot.h.push_back(j < Ql ? (j % G) * lv.coef_ml + j / G : 0);
+    }
+  for (int d = 0; d < lv.beta; ++d)
+    for (int s = 0; s < lv.n_out; ++s)
+      if (lv.t_jobs.h[(size_t)d * lv.n_out + s] >= 0) {
+        lv.job_d.h.push_back(d);
+        lv.job_s.h.push_back(s);
+        lv.job_prime.h.push_back(lv.t_jobs.h[(size_t)d * lv.n_out + s]);
+        lv.job_off.h.push_back(((long long)d * lv.n_out + s) * N);
+      }
+  lv.n_jobs = (int)lv.job_d.h.size();
+  std::vector<ulonglong2> sin, sp;
+  for (int s = 0; s < lv.n_q; ++s) {
+    const int j = lv.out_j.h[s], d = j / a;
+    scale_pair(j, qhi[(size_t)d * a + (j - d * a)].x, sin);
+  }
+  for (int p = 0; p < 2; ++p)
+    for (int k = 0; k < lv.n_p; ++k) {
+      const int i = own_p[k];
+      const u64 pi = c.primes[L + i];
+      u64 prod = 1;
+      for (int t = 0; t < a; ++t)
+        if (t != i) prod = h_mulmod(prod, c.primes[L + t] % pi, pi);
+      scale_pair(L + i, h_invmod(prod, pi), sp);
+    }
+  up_ints(lv.src_slot);
+  up_ints(lv.job_d);
+  up_ints(lv.job_s);
+  up_ints(lv.job_prime);
+  up_i64(lv.job_off);
+  lv.scale_in = upload(sin);
+  lv.scale_p = upload(sp);
   up_ints(lv.prime_of);
   up_ints(lv.out_j);
   up_ints(lv.key_slot);
@@ -407,6 +454,10 @@ void ctx_free(Ctx &c) {
     f(lv.p_offsets.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
+    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime}) f(t->d);
+    f(lv.job_off.d);
+    f(lv.scale_in);
+    f(lv.scale_p);
     f(lv.w);
   }
   f(c.own_key_prime.d);
@@ -545,10 +596,9 @@ enum Stage {
   ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_BCONV, ST_MODUP_NTT, ST_INNER_PROD, ST_INTT_P,
   ST_MODDOWN_BCONV, ST_MODDOWN_NTT, ST_FINISH, ST_COMM, ST_COUNT
 };
-static const char *kStageNames[ST_COUNT] = {"galois",       "intt_input",      "modup_bconv",
-                                            "modup_ntt",    "inner_product",   "intt_p",
-                                            "moddown_bconv", "moddown_ntt",    "moddown_finish",
-                                            "collective"};
+static const char *kStageNames[ST_COUNT] = {
+    "galois",       "intt_input",   "modup_cols", "modup_rows",   "inner_product",
+    "intt_p",       "moddown_cols", "moddown_rows", "moddown_finish", "collective"};
 
 cudaEvent_t pool_event(Ctx &c) {
   if (!c.event_pool.empty()) {
@@ -597,30 +647,31 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
                     u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
   const size_t N = c.N;
   const NttTables T = c.tables();
-  // 2. coefficient form of the input, all-gathered
+  // 2. scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the input, all-gathered
   {
     StageTimer tm(c, ST_INTT_IN, s);
     KS_CUDA(cudaMemcpyAsync(c.s_coef, in_ntt, (size_t)lv.n_q * N * 8, cudaMemcpyDeviceToDevice,
                             s));
     LimbMap mc{c.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
-    KS_CUDA(ntt_inverse(mc, lv.n_q, T, s));
+    KS_CUDA(ntt_inverse_scaled(mc, lv.n_q, lv.scale_in, T, s));
     c.launches += 2;
   }
   if (c.world > 1) {
     StageTimer tm(c, ST_COMM, s);
     allgather(c, c.s_coef, c.s_coef_all, (size_t)lv.coef_ml * N, s);
   }
-  // 3. ModUp: base extension + NTT
+  // 3. ModUp: base extension fused into the column pass, then the row pass
   {
     StageTimer tm(c, ST_MODUP_BCONV, s);
-    KS_CUDA(modup_bconv(c.s_coef_all, c.s_t, lv.mu, lv.lay, c.d_primes, c.log_n, s));
+    KS_CUDA(modup_fused_cols(c.s_coef_all, lv.src_slot.d, c.s_t, lv.mu, lv.lay, lv.job_d.d,
+                             lv.job_s.d, lv.n_jobs, T, s));
     c.launches += 1;
   }
   {
     StageTimer tm(c, ST_MODUP_NTT, s);
-    LimbMap mt{c.s_t, (long long)N, nullptr, lv.t_jobs.d, 0, 1};
-    KS_CUDA(ntt_forward(mt, lv.beta * lv.n_out, T, s));
-    c.launches += 2;
+    LimbMap mt{c.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
+    KS_CUDA(ntt_forward_rows_only(mt, lv.n_jobs, T, s));
+    c.launches += 1;
   }
   // 4. inner product
   {
@@ -629,12 +680,12 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
                           c.log_n, s));
     c.launches += 1;
   }
-  // 5. P part to coefficient form
+  // 5. P part to scaled coefficient form [y_i (P/p_i)^-1]_{p_i}
   const u64 *y_base;
   if (c.world == 1) {
     StageTimer tm(c, ST_INTT_P, s);
     LimbMap mp{c.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-    KS_CUDA(ntt_inverse(mp, 2 * lv.n_p, T, s));
+    KS_CUDA(ntt_inverse_scaled(mp, 2 * lv.n_p, lv.scale_p, T, s));
     c.launches += 2;
     y_base = c.s_cx;
   } else {
@@ -647,7 +698,7 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
                                   cudaMemcpyDeviceToDevice, s));
       if (lv.n_p > 0) {
         LimbMap mp{c.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-        KS_CUDA(ntt_inverse(mp, 2 * lv.n_p, T, s));
+        KS_CUDA(ntt_inverse_scaled(mp, 2 * lv.n_p, lv.scale_p, T, s));
         c.launches += 2;
       }
     }
@@ -655,24 +706,17 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
     allgather(c, c.s_ysend, c.s_yall, (size_t)c.max_p_own * 2 * N, s);
     y_base = c.s_yall;
   }
-  // 6. P -> Q conversion and NTT
+  // 6. P -> Q conversion fused into the column pass
   {
     StageTimer tm(c, ST_MODDOWN_BCONV, s);
-    KS_CUDA(moddown_bconv(y_base, lv.y_off.d, c.s_z, lv.n_q, lv.q_index.d, c.md, c.d_primes,
-                          c.log_n, s));
+    KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, c.s_z, lv.n_q, lv.q_index.d, c.md, T, s));
     c.launches += 1;
   }
+  // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {
     StageTimer tm(c, ST_MODDOWN_NTT, s);
-    LimbMap mz{c.s_z, (long long)N, nullptr, lv.z_jobs.d, 0, 1};
-    KS_CUDA(ntt_forward(mz, 2 * lv.n_q, T, s));
-    c.launches += 2;
-  }
-  // 7. finish
-  {
-    StageTimer tm(c, ST_FINISH, s);
-    KS_CUDA(moddown_finish(ct0, ct1, g0, c.s_cx, (int)(lv.n_out * N), lv.cx_slot_q.d, c.s_z,
-                           lv.n_q, lv.q_index.d, c.md, c.d_primes, c.log_n, rotate, s));
+    KS_CUDA(moddown_fused_rows(c.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, c.s_cx,
+                               (long long)lv.n_out * N, ct0, ct1, g0, rotate, c.md, T, s));
     c.launches += 1;
   }
 }

@@ -47,6 +47,13 @@ struct Level {
   DevI64 y_off;       // [2 * alpha] offsets of P limb i of poly p in the y buffer
   ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
   u64 *w = nullptr;               // [beta][QlP][alpha]
+  // fused ModUp: one job per (digit d, output slot s) with limb j outside digit d
+  int n_jobs = 0;
+  DevInts src_slot;               // [beta * alpha] slot of Q limb d*alpha+i in the gathered input
+  DevInts job_d, job_s, job_prime;  // [n_jobs]
+  DevI64 job_off;                 // [n_jobs] word offset of t[d][s]
+  ulonglong2 *scale_in = nullptr; // [2 * n_q] last-stage INTT scales with (Q_d/q_j)^-1 folded in
+  ulonglong2 *scale_p = nullptr;  // [2 * 2 * n_p] same with (P/p_i)^-1 for the owned P limbs
   ModUpDev mu{};
   KsLayout lay{};
 };
@@ -62,7 +69,8 @@ struct Ctx {
   int device = 0, rank = 0, world = 1, mode = 0, max_batch = 1;
   int log_n = 0, N = 0, L = 0, alpha = 0, K = 0;
   std::vector<u64> primes;  // K = L + alpha
-  // device tables
+  // device tables (and the host copy of the per-prime constants)
+  std::vector<PrimeDev> h_primes;
   PrimeDev *d_primes = nullptr;
   ulonglong2 *d_tw_fwd = nullptr, *d_tw_inv = nullptr;
   u64 *d_gauss = nullptr;

@@ -1,0 +1,39 @@
+// ks_fused.cuh -- key-switch kernels that fuse a base conversion into the
+// NTT column pass and the ModDown finish into the NTT row pass.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "ks_kernels.cuh"
+#include "ks_ntt.cuh"
+
+namespace ksb {
+
+// Inverse NTT whose last stage multiplies by a per-limb constant c (on top
+// of N^-1): scale[i] = {N^-1 c, Shoup}, {psi^-brev(1) N^-1 c, Shoup}.
+cudaError_t ntt_inverse_scaled(const LimbMap &m, int n_limbs, const ulonglong2 *scale,
+                               const NttTables &T, cudaStream_t s);
+
+// ModUp: for each job (digit d, output slot s) the column pass of the
+// forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
+// where v_i are the digit's scaled coefficient limbs (v_all at limb slot
+// src_slot[d*alpha + i]).  Result (column pass done) -> t[d][s].
+cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
+                             const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
+                             const NttTables &T, cudaStream_t s);
+
+// ModDown: for each job (poly p, Q slot s) the column pass of the forward
+// NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
+// scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].
+cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
+                               const int *q_index, const ModDownDev &md, const NttTables &T,
+                               cudaStream_t s);
+
+// Row pass of z[p][s] with the ModDown finish in the epilogue:
+//   o = (cx[p][cx_slot[s]] - z) * P^-1 mod q_j;
+//   p = 0: ct0 = (rotate ? g0 : ct0) + o;   p = 1: ct1 = rotate ? o : ct1 + o.
+cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,
+                               const u64 *cx, long long cx_stride_poly, u64 *ct0, u64 *ct1,
+                               const u64 *g0, bool rotate, const ModDownDev &md,
+                               const NttTables &T, cudaStream_t s);
+
+}  // namespace ksb

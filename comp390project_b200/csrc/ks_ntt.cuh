@@ -34,5 +34,11 @@ struct NttTables {
 cudaError_t ntt_forward(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s);
 cudaError_t ntt_inverse(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s);
 bool ntt_supported_log_n(int log_n);
+// Only the second pass of a forward transform (the first pass of an inverse
+// one), for callers that run a fused first/second pass of their own.
+cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
+                                  cudaStream_t s);
+cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
+                                  cudaStream_t s);
 
 }  // namespace ksb

@@ -1,0 +1,202 @@
+// ks_ntt_impl.cuh -- the device building blocks of the two-pass NTT, shared
+// by the plain batched transform (ks_ntt.cu) and the fused key-switch
+// kernels (ks_fused.cu).
+//
+// The length-N transform is split as N = M1 * M2 (M1 = 2^(logN/2)).  The
+// column pass runs the stages whose butterflies span the high index bits
+// (each column of M1 elements at stride M2 is an independent sub-transform);
+// the row pass runs the remaining stages inside contiguous rows of M2
+// elements.  Every thread keeps 16 elements in registers and runs four
+// butterfly stages on them (a radix-16 step); one shared-memory exchange
+// re-partitions the sub-transform for the next four stages.
+//
+// Column-pass tiles are 4096/M1 adjacent columns wide with the lane index
+// running along the contiguous column direction, so every global access is
+// a full row segment (128 bytes for M1 = 256).  Row-pass tiles are 4096
+// contiguous words.
+#pragma once
+#include "ks_arith.cuh"
+
+namespace ksb {
+namespace ntt {
+
+constexpr int kThreads = 256;
+constexpr int kEpt = 16;                // elements per thread
+constexpr int kTile = kThreads * kEpt;  // 4096 words per CTA
+
+// Register e = (g << NB) | v holds the local index
+//   ((u >> LO) << (LO + NB)) | (v << LO) | (u & ((1 << LO) - 1)),  u = (g << LOG_T) | t.
+template <int LOG_M, int LO, int NB>
+__device__ __forceinline__ int lidx(int t, int e) {
+  constexpr int LOG_T = LOG_M - 4;
+  const int g = e >> NB, v = e & ((1 << NB) - 1);
+  const int u = (g << LOG_T) | t;
+  return ((u >> LO) << (LO + NB)) | (v << LO) | (u & ((1 << LO) - 1));
+}
+
+// Forward stages on local bits [LO, LO+NB), high bit first.  Global bit of
+// local bit b is b + gofs; the twiddle of the pair whose lower element has
+// local index i is tw[(1 << (logN-1-b-gofs)) + (((prefix << LOG_M) | i) >> (b+1))].
+template <int LOG_M, int LO, int NB, bool LAZY>
+__device__ __forceinline__ void fwd_round(u64 (&x)[kEpt], int t, long long prefix, int gofs,
+                                          int log_n, const ulonglong2 *__restrict__ tw, u64 q,
+                                          u64 two_q) {
+#pragma unroll
+  for (int k = NB - 1; k >= 0; --k) {
+    const int b = LO + k;
+    const int base = 1 << (log_n - 1 - b - gofs);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
+      const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+      if (LAZY) ct_bfly_lazy(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
+      else ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
+    }
+  }
+}
+
+// Inverse stages on local bits [LO, LO+NB), low bit first.  If LAST, the top
+// stage of this round is the final stage of the transform, with the output
+// scale folded in (scale = N^-1 and psi^-brev(1) N^-1, Shoup pairs).
+template <int LOG_M, int LO, int NB, bool LAZY, bool LAST>
+__device__ __forceinline__ void inv_round(u64 (&x)[kEpt], int t, long long prefix, int gofs,
+                                          int log_n, const ulonglong2 *__restrict__ tw,
+                                          const PrimeDev &P, ulonglong2 s0, ulonglong2 s1) {
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int b = LO + k;
+    const int gb = b + gofs;
+    const int base = 1 << (log_n - 1 - gb);
+    const u64 K = P.q << gb;  // >= bound of the operands entering this stage (lazy path)
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      u64 &X = x[e], &Y = x[e | (1 << k)];
+      if (LAST && k == NB - 1) {
+        const u64 s = LAZY ? X + Y : X + Y;  // < 2^64 on both paths
+        const u64 d = LAZY ? X + K - Y : X - Y + P.two_q;
+        X = mul_shoup_lazy(s, s0.x, s0.y, P.q);
+        Y = mul_shoup_lazy(d, s1.x, s1.y, P.q);
+      } else {
+        const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
+        const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+        if (LAZY) gs_bfly_lazy(X, Y, w.x, w.y, P.q, K);
+        else gs_bfly(X, Y, w.x, w.y, P.q, P.two_q);
+      }
+    }
+  }
+}
+
+template <int LOG_M>
+__device__ __forceinline__ int padx(int r, int i) {
+  constexpr int M = 1 << LOG_M;
+  return r * (M + M / 16) + i + (i >> 4);
+}
+
+template <int LOG_M>
+struct ColGeom {
+  static constexpr int M = 1 << LOG_M, LOG_T = LOG_M - 4, TT = 1 << LOG_T, C = kThreads / TT;
+  static constexpr int HI = LOG_M - 4, NLO = LOG_M - 4;
+  static constexpr int SMEM = M * C;  // words
+};
+template <int LOG_M>
+struct RowGeom {
+  static constexpr int M = 1 << LOG_M, LOG_T = LOG_M - 4, TT = 1 << LOG_T, R = kThreads / TT;
+  static constexpr int HI = LOG_M - 4, NLO = LOG_M - 4;
+  static constexpr int SMEM = R * (M + M / 16);
+};
+
+// ---------------------------------------------------------------------------
+// Forward column pass.  load(r, col) gives the input of row r (< q for the
+// lazy path, < 4q otherwise); store(r, col, v) receives the output (< 17q lazy,
+// < 4q Harvey).  Rows r index the column sub-transform, col < M2.
+// ---------------------------------------------------------------------------
+template <int LOG_M, bool LAZY, class Load, class Store>
+__device__ __forceinline__ void fwd_cols(u64 *sm, int col, int t, int c, int log_n,
+                                         const ulonglong2 *tw, const PrimeDev &P, Load &&load,
+                                         Store &&store) {
+  using G = ColGeom<LOG_M>;
+  const int gofs = log_n - LOG_M;
+  u64 x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = load(lidx<LOG_M, G::HI, 4>(t, e), col);
+  fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, 0, gofs, log_n, tw, P.q, P.two_q);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = x[e];
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c];
+  fwd_round<LOG_M, 0, G::NLO, LAZY>(x, t, 0, gofs, log_n, tw, P.q, P.two_q);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) store(lidx<LOG_M, 0, G::NLO>(t, e), col, x[e]);
+}
+
+// Inverse column pass (the second pass of an inverse transform); outputs are
+// canonical and multiplied by the scale of the last stage.
+template <int LOG_M, bool LAZY, class Load, class Store>
+__device__ __forceinline__ void inv_cols(u64 *sm, int col, int t, int c, int log_n,
+                                         const ulonglong2 *tw, const PrimeDev &P, ulonglong2 s0,
+                                         ulonglong2 s1, Load &&load, Store &&store) {
+  using G = ColGeom<LOG_M>;
+  const int gofs = log_n - LOG_M;
+  u64 x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = load(lidx<LOG_M, 0, G::NLO>(t, e), col);
+  inv_round<LOG_M, 0, G::NLO, LAZY, false>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c] = x[e];
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c];
+  inv_round<LOG_M, G::HI, 4, LAZY, true>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) store(lidx<LOG_M, G::HI, 4>(t, e), col, csub(x[e], P.q));
+}
+
+// ---------------------------------------------------------------------------
+// Forward row pass over one 4096-word tile (R rows of M).  The thread's
+// 16 outputs (canonical) are handed to finish(rr, i, v) for local row rr,
+// index i in the row; the tile is then written by the caller from smem.
+// ---------------------------------------------------------------------------
+template <int LOG_M, bool LAZY>
+__device__ __forceinline__ void fwd_rows_regs(u64 (&x)[kEpt], u64 *sm, const u64 *tile, int t,
+                                              int rr, long long row, int log_n,
+                                              const ulonglong2 *tw, const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)];
+  fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))] = x[e];
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))];
+  fwd_round<LOG_M, 0, G::NLO, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e)
+    x[e] = LAZY ? reduce_full(x[e], P.q, P.mu) : reduce4(x[e], P.q, P.two_q);
+  __syncwarp();
+}
+
+// Inverse row pass (the first pass of an inverse transform) over one tile
+// already staged in smem (padx layout); outputs in registers, pattern HI.
+template <int LOG_M, bool LAZY>
+__device__ __forceinline__ void inv_rows_regs(u64 (&x)[kEpt], u64 *sm, int t, int rr,
+                                              long long row, int log_n, const ulonglong2 *tw,
+                                              const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
+  const ulonglong2 none = make_ulonglong2(0, 0);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))];
+  inv_round<LOG_M, 0, G::NLO, LAZY, false>(x, t, row, 0, log_n, tw, P, none, none);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))];
+  inv_round<LOG_M, G::HI, 4, LAZY, false>(x, t, row, 0, log_n, tw, P, none, none);
+}
+
+}  // namespace ntt
+}  // namespace ksb
