@@ -18,7 +18,17 @@ struct __align__(16) PrimeDev {
   u64 ninv, ninv_sh;     // N^-1 and its Shoup companion
   u64 w1ninv, w1ninv_sh; // psi^-brev(1) * N^-1 (last inverse stage, N^-1 folded in)
   u64 mu, pad_;          // floor(2^64 / q)
+  // FP64 representation (primes below kFpBound): q, 1/q, and the last
+  // inverse-stage scales as {s, s/q} pairs.
+  double qd, qinv;
+  double ninv_d, ninv_q, w1ninv_d, w1ninv_q;
 };
+
+// Primes below 2^43 run their NTT butterflies on the FP64 pipe: values are
+// exact signed integers in doubles, products split exactly with an FMA
+// (Dekker/Ogita two-product), the quotient estimate round(y*w/q) comes from
+// the precomputed w/q, and every intermediate stays below 2^53.
+constexpr u64 kFpBound = 1ull << 43;
 
 // Forward butterflies skip every conditional subtraction when q < 2^58:
 // each Cooley-Tukey stage grows the bound by 2q, so 16 stages from inputs
@@ -116,6 +126,55 @@ __device__ __forceinline__ void gs_bfly_lazy(u64 &X, u64 &Y, u64 w, u64 wp, u64 
   X = s;
   Y = mul_shoup_lazy(d, w, wp, q);
 }
+// ---------------------------------------------------------------------------
+// FP64 modular arithmetic for q < kFpBound.  Operands are integers held in
+// doubles, |y| <= 2^50.  fp_mulmod returns r = y*w - qt*q exactly with
+// qt = rint(y * fl(w/q)):  h + l = y*w exactly (FMA two-product);
+// |y*fl(w/q) - y*w/q| <= 2^50 * 2^-54, so |y*w/q - qt| < 0.57 and |r| < 0.57q;
+// h - qt*q and the final sum are integers below 2^53, hence exact.
+// ---------------------------------------------------------------------------
+constexpr double kRound = 6755399441055744.0;  // 1.5 * 2^52: x + kRound - kRound = rint(x)
+constexpr double kTwo52 = 4503599627370496.0;
+
+__device__ __forceinline__ double fp_mulmod(double y, double w, double wq, double q) {
+  const double h = __dmul_rn(y, w);
+  const double l = __fma_rn(y, w, -h);
+  const double qt = __dsub_rn(__fma_rn(y, wq, kRound), kRound);
+  return __dadd_rn(__fma_rn(-qt, q, h), l);
+}
+// Cooley-Tukey: |X|,|Y| < B -> < B + 0.57q.
+__device__ __forceinline__ void fp_ct_bfly(double &X, double &Y, double w, double wq, double q) {
+  const double r = fp_mulmod(Y, w, wq, q);
+  const double x = X;
+  X = __dadd_rn(x, r);
+  Y = __dsub_rn(x, r);
+}
+// Gentleman-Sande: |X|,|Y| < B -> |X| < 2B, |Y| < 0.57q.
+__device__ __forceinline__ void fp_gs_bfly(double &X, double &Y, double w, double wq, double q) {
+  const double s = __dadd_rn(X, Y);
+  const double d = __dsub_rn(X, Y);
+  X = s;
+  Y = fp_mulmod(d, w, wq, q);
+}
+// (With |y| <= 2^50 the estimate error is below 2^-4, so |r| < 0.57q.)
+// x - round(x/q) q, |result| <= 0.5q (+1), for |x| < 2^51.
+__device__ __forceinline__ double fp_reduce_sym(double x, double q, double qinv) {
+  const double t = __dsub_rn(__fma_rn(x, qinv, kRound), kRound);
+  return __fma_rn(-t, q, x);
+}
+// Canonical [0, q) as a uint64, for |x| < 64q: floor(x/q) = rint(x/q - 1/2)
+// because x/q - 1/2 is never within 1/(2q) of an integer.
+__device__ __forceinline__ u64 fp_to_canon(double x, double q, double qinv) {
+  const double u = __fma_rn(x, qinv, -0.5);
+  const double t = __dsub_rn(__dadd_rn(u, kRound), kRound);
+  const double r = __fma_rn(-t, q, x);
+  return (u64)__double_as_longlong(__dadd_rn(r, kTwo52)) & 0xFFFFFFFFFFFFFull;
+}
+// Exact uint64 -> double for x < 2^52.
+__device__ __forceinline__ double u64_to_fp(u64 x) {
+  return __dsub_rn(__longlong_as_double((long long)(x | 0x4330000000000000ull)), kTwo52);
+}
+
 __device__ __forceinline__ void gs_bfly_last_lazy(u64 &X, u64 &Y, const PrimeDev &P, u64 K) {
   const u64 s = X + Y;
   const u64 d = X + K - Y;

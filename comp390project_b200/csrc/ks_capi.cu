@@ -131,6 +131,7 @@ void build_tables(Ctx &c) {
   const int N = c.N, K = c.K;
   std::vector<PrimeDev> pd(K);
   std::vector<ulonglong2> fwd((size_t)K * N), inv((size_t)K * N);
+  std::vector<double2> fwd_fp((size_t)K * N, make_double2(0, 0)), inv_fp((size_t)K * N, make_double2(0, 0));
   std::vector<std::thread> th;
   auto work = [&](int k) {
     const u64 q = c.primes[k];
@@ -145,6 +146,10 @@ void build_tables(Ctx &c) {
       const uint32_t r = h_brev((uint32_t)i, c.log_n);
       fwd[(size_t)k * N + i] = make_ulonglong2(pw[r], h_shoup(pw[r], q));
       inv[(size_t)k * N + i] = make_ulonglong2(pwi[r], h_shoup(pwi[r], q));
+      if (q < kFpBound) {
+        fwd_fp[(size_t)k * N + i] = make_double2((double)pw[r], (double)pw[r] / (double)q);
+        inv_fp[(size_t)k * N + i] = make_double2((double)pwi[r], (double)pwi[r] / (double)q);
+      }
     }
     PrimeDev &P = pd[k];
     P.q = q;
@@ -156,6 +161,12 @@ void build_tables(Ctx &c) {
     P.w1ninv_sh = h_shoup(P.w1ninv, q);
     P.mu = (u64)((~(u128)0 >> 64) / q);  // floor((2^64 - 1) / q) == floor(2^64 / q)
     P.pad_ = 0;
+    P.qd = (double)q;
+    P.qinv = 1.0 / (double)q;
+    P.ninv_d = (double)P.ninv;
+    P.ninv_q = (double)P.ninv / (double)q;
+    P.w1ninv_d = (double)P.w1ninv;
+    P.w1ninv_q = (double)P.w1ninv / (double)q;
   };
   const int nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
   for (int t0 = 0; t0 < nth; ++t0)
@@ -167,6 +178,8 @@ void build_tables(Ctx &c) {
   c.d_primes = upload(pd);
   c.d_tw_fwd = upload(fwd);
   c.d_tw_inv = upload(inv);
+  c.d_tw_fwd_fp = upload(fwd_fp);
+  c.d_tw_inv_fp = upload(inv_fp);
 
   // Discrete Gaussian CDT (sigma 3.2, |e| <= 19) for the synthetic keys.
   std::vector<u64> T(20);
@@ -300,8 +313,18 @@ void build_level(Ctx &c, Level &lv, int Ql) {
     const PrimeDev &P = c.h_primes[prime];
     const u64 q = P.q;
     const u64 a0 = h_mulmod(P.ninv, cst, q), a1 = h_mulmod(P.w1ninv, cst, q);
-    out.push_back(make_ulonglong2(a0, h_shoup(a0, q)));
-    out.push_back(make_ulonglong2(a1, h_shoup(a1, q)));
+    if (q < kFpBound) {  // FP64 primes: the bits of {s, fl(s/q)}
+      auto bits = [](double d) {
+        u64 b;
+        std::memcpy(&b, &d, 8);
+        return b;
+      };
+      out.push_back(make_ulonglong2(bits((double)a0), bits((double)a0 / (double)q)));
+      out.push_back(make_ulonglong2(bits((double)a1), bits((double)a1 / (double)q)));
+    } else {
+      out.push_back(make_ulonglong2(a0, h_shoup(a0, q)));
+      out.push_back(make_ulonglong2(a1, h_shoup(a1, q)));
+    }
   };
   for (int d = 0; d < lv.beta; ++d)
     for (int i = 0; i < a; ++i) {
@@ -464,6 +487,8 @@ void ctx_free(Ctx &c) {
   f(c.d_primes);
   f(c.d_tw_fwd);
   f(c.d_tw_inv);
+  f(c.d_tw_fwd_fp);
+  f(c.d_tw_inv_fp);
   f(c.d_gauss);
   f(c.d_phatinv);
   f(c.d_pinv);

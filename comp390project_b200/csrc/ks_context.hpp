@@ -73,6 +73,7 @@ struct Ctx {
   std::vector<PrimeDev> h_primes;
   PrimeDev *d_primes = nullptr;
   ulonglong2 *d_tw_fwd = nullptr, *d_tw_inv = nullptr;
+  double2 *d_tw_fwd_fp = nullptr, *d_tw_inv_fp = nullptr;
   u64 *d_gauss = nullptr;
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
@@ -101,7 +102,9 @@ struct Ctx {
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
   std::vector<cudaEvent_t> event_pool;
 
-  NttTables tables() const { return NttTables{d_tw_fwd, d_tw_inv, d_primes, log_n}; }
+  NttTables tables() const {
+    return NttTables{d_tw_fwd, d_tw_inv, d_primes, log_n, d_tw_fwd_fp, d_tw_inv_fp};
+  }
 };
 
 }  // namespace ksb

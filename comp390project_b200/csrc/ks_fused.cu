@@ -36,8 +36,16 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   const ulonglong2 s0 = scale[2 * li], s1 = scale[2 * li + 1];
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
-  if (P.q < kInvLazyBound) inv_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
-  else inv_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
+  if (P.q < kFpBound) {
+    // scale entries of FP64 primes hold the bits of {s, fl(s/q)}
+    inv_cols_fp<LOG_M>(sm, col, t, c, log_n, T.inv_fp + (long long)prime * N, P,
+                       make_double2(as_fp(s0.x), as_fp(s0.y)), make_double2(as_fp(s1.x), as_fp(s1.y)),
+                       load, store);
+  } else if (P.q < kInvLazyBound) {
+    inv_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
+  } else {
+    inv_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -78,7 +86,9 @@ __global__ void __launch_bounds__(kThreads)
   };
   u64 *out = t + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
+  if (P.q < kFpBound)
+    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, load, store);
+  else if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
   else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, load, store);
 }
 
@@ -117,7 +127,9 @@ __global__ void __launch_bounds__(kThreads)
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
+  if (P.q < kFpBound)
+    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, load, store);
+  else if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
   else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, load, store);
 }
 
@@ -140,7 +152,9 @@ __global__ void __launch_bounds__(kThreads)
   const u64 *tile = z + ((long long)p * n_q + s) * N + tile0;
   const long long row = (long long)blockIdx.x * G::R + rr;
   u64 x[kEpt];
-  if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
+  if (P.q < kFpBound)
+    fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, T.fwd_fp + (long long)j * N, P);
+  else if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
   else fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
   const ulonglong2 pinv = md.pinv[j];
   const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N;

@@ -32,7 +32,15 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   const int col = blockIdx.x * G::C + c;
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
-  if (FWD) {
+  if (P.q < kFpBound) {
+    const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
+    if (FWD) {
+      fwd_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, load, store);
+    } else {
+      const double2 s0 = make_double2(P.ninv_d, P.ninv_q), s1 = make_double2(P.w1ninv_d, P.w1ninv_q);
+      inv_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, s0, s1, load, store);
+    }
+  } else if (FWD) {
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, load, store);
     else fwd_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, load, store);
   } else {
@@ -58,8 +66,11 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, NttTables T) {
   u64 *tile = a + (long long)blockIdx.x * kTile;
   const long long row = (long long)blockIdx.x * G::R + rr;
   u64 x[kEpt];
+  const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
+  const bool fp = P.q < kFpBound;
   if (FWD) {
-    if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
+    if (fp) fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, twf, P);
+    else if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
     else fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
@@ -76,7 +87,8 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, NttTables T) {
       sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))] = tile[lin];
     }
     __syncthreads();
-    if (P.q < kInvLazyBound) inv_rows_regs<LOG_M, true>(x, sm, t, rr, row, log_n, tw, P);
+    if (fp) inv_rows_regs_fp<LOG_M>(x, sm, t, rr, row, log_n, twf, P);
+    else if (P.q < kInvLazyBound) inv_rows_regs<LOG_M, true>(x, sm, t, rr, row, log_n, tw, P);
     else inv_rows_regs<LOG_M, false>(x, sm, t, rr, row, log_n, tw, P);
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)] = x[e];

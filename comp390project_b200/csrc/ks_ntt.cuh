@@ -26,6 +26,8 @@ struct NttTables {
   const ulonglong2 *inv;  // [n_primes][N] {w, w_shoup}, w = psi^-brev(i)
   const PrimeDev *primes; // [n_primes]
   int log_n;
+  const double2 *fwd_fp;  // [n_primes][N] {w, fl(w/q)} (used for primes below kFpBound)
+  const double2 *inv_fp;
 };
 
 // Transforms n_limbs limbs in place; outputs are canonical in [0, q).

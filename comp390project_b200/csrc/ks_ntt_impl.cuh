@@ -198,5 +198,149 @@ __device__ __forceinline__ void inv_rows_regs(u64 (&x)[kEpt], u64 *sm, int t, in
   inv_round<LOG_M, G::HI, 4, LAZY, false>(x, t, row, 0, log_n, tw, P, none, none);
 }
 
+// ===========================================================================
+// FP64 variants (primes below kFpBound).  Values travel between the passes as
+// the bits of signed integer-valued doubles; the pass inputs and the final
+// outputs are canonical uint64.  Twiddle tables hold {w, fl(w/q)} doubles.
+// ===========================================================================
+__device__ __forceinline__ double as_fp(u64 b) { return __longlong_as_double((long long)b); }
+__device__ __forceinline__ u64 fp_bits(double d) { return (u64)__double_as_longlong(d); }
+
+// Bound: operands < B on entry -> < B + 4 * 0.57q on exit (additive growth).
+template <int LOG_M, int LO, int NB>
+__device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long prefix, int gofs,
+                                             int log_n, const double2 *__restrict__ tw, double q) {
+#pragma unroll
+  for (int k = NB - 1; k >= 0; --k) {
+    const int b = LO + k;
+    const int base = 1 << (log_n - 1 - b - gofs);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
+      const double2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+      fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
+    }
+  }
+}
+
+// Every operand is reduced to |x| <= q/2 (+1) on entry, so within the round
+// the sums stay below 2^NB * 0.57q and every product input below 2^50.
+template <int LOG_M, int LO, int NB, bool LAST>
+__device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long prefix, int gofs,
+                                             int log_n, const double2 *__restrict__ tw,
+                                             const PrimeDev &P, double2 s0, double2 s1) {
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = fp_reduce_sym(x[e], P.qd, P.qinv);
+#pragma unroll
+  for (int k = 0; k < NB; ++k) {
+    const int b = LO + k;
+    const int gb = b + gofs;
+    const int base = 1 << (log_n - 1 - gb);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      double &X = x[e], &Y = x[e | (1 << k)];
+      if (LAST && k == NB - 1) {
+        const double s = __dadd_rn(X, Y), d = __dsub_rn(X, Y);
+        X = fp_mulmod(s, s0.x, s0.y, P.qd);
+        Y = fp_mulmod(d, s1.x, s1.y, P.qd);
+      } else {
+        const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
+        const double2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+        fp_gs_bfly(X, Y, w.x, w.y, P.qd);
+      }
+    }
+  }
+}
+
+// Forward column pass; load() gives canonical uint64, store() receives the
+// bits of the pass result (|x| < q + 8 * 0.57q).
+template <int LOG_M, class Load, class Store>
+__device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
+                                            const double2 *tw, const PrimeDev &P, Load &&load,
+                                            Store &&store) {
+  using G = ColGeom<LOG_M>;
+  const int gofs = log_n - LOG_M;
+  double x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(load(lidx<LOG_M, G::HI, 4>(t, e), col));
+  fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, gofs, log_n, tw, P.qd);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = fp_bits(x[e]);
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c]);
+  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, 0, gofs, log_n, tw, P.qd);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) store(lidx<LOG_M, 0, G::NLO>(t, e), col, fp_bits(x[e]));
+}
+
+// Inverse column pass (second pass); load() gives the bits of the first
+// pass result, store() receives canonical uint64 times the last-stage scale.
+template <int LOG_M, class Load, class Store>
+__device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int log_n,
+                                            const double2 *tw, const PrimeDev &P, double2 s0,
+                                            double2 s1, Load &&load, Store &&store) {
+  using G = ColGeom<LOG_M>;
+  const int gofs = log_n - LOG_M;
+  double x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(load(lidx<LOG_M, 0, G::NLO>(t, e), col));
+  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c] = fp_bits(x[e]);
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c]);
+  inv_round_fp<LOG_M, G::HI, 4, true>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e)
+    store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
+}
+
+// Forward row pass; the tile holds first-pass bits; canonical outputs in x.
+template <int LOG_M>
+__device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const u64 *tile, int t,
+                                                 int rr, long long row, int log_n,
+                                                 const double2 *tw, const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
+  double x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)]);
+  fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, 0, log_n, tw, P.qd);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))] = fp_bits(x[e]);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))]);
+  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, 0, log_n, tw, P.qd);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) xo[e] = fp_to_canon(x[e], P.qd, P.qinv);
+  __syncwarp();
+}
+
+// Inverse row pass (first pass) over a tile staged in smem as canonical
+// uint64; outputs (bits of doubles) in xo, pattern HI.
+template <int LOG_M>
+__device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, int t, int rr,
+                                                 long long row, int log_n, const double2 *tw,
+                                                 const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
+  const double2 none = make_double2(0, 0);
+  double x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))]);
+  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, row, 0, log_n, tw, P, none, none);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = fp_bits(x[e]);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))]);
+  inv_round_fp<LOG_M, G::HI, 4, false>(x, t, row, 0, log_n, tw, P, none, none);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) xo[e] = fp_bits(fp_reduce_sym(x[e], P.qd, P.qinv));
+}
+
 }  // namespace ntt
 }  // namespace ksb

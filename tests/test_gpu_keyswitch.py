@@ -39,6 +39,34 @@ def test_ntt_roundtrip_bitexact(name, cfg, cuda_device):
     assert np.array_equal(_to_host(d), x)
 
 
+@pytest.mark.parametrize("pattern", ["max", "zero", "alt", "one", "ramp"])
+def test_ntt_extreme_inputs(pattern, cuda_device):
+    """Inputs at the ends of [0, q) stress the lazy-reduction bounds of every
+    butterfly path (FP64 for 42-bit primes, integer Shoup for 58/60-bit)."""
+    o = oracle_for("cfg3")
+    ctx = _ctx(CFG3)
+    K = o.L + o.alpha
+    x = np.empty((K, o.N), dtype=np.uint64)
+    for i, m in enumerate(o.moduli):
+        m = int(m)
+        if pattern == "max":
+            x[i] = m - 1
+        elif pattern == "zero":
+            x[i] = 0
+        elif pattern == "alt":
+            x[i] = np.where(np.arange(o.N) % 2 == 0, m - 1, 0)
+        elif pattern == "one":
+            x[i] = 1
+        else:
+            x[i] = (np.arange(o.N, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15 % m)) % np.uint64(m)
+    d = _to_dev(x)
+    ctx.ntt_forward(d, K, 0, 1)
+    assert np.array_equal(_to_host(d), o.ntt(x, list(range(K))))
+    d = _to_dev(x)
+    ctx.ntt_inverse(d, K, 0, 1)
+    assert np.array_equal(_to_host(d), o.ntt(x, list(range(K)), inverse=True))
+
+
 def test_ntt_batch_prime_pattern(cuda_device):
     o = oracle_for("small")
     ctx = _ctx(SMALL)
