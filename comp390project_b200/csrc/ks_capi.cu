@@ -226,8 +226,12 @@ void build_moddown(Ctx &c) {
   }
   c.d_phatinv = upload(phatinv);
   c.d_pinv = upload(pinv);
+  std::vector<u64> wsh(w.size());
+  for (int j = 0; j < L; ++j)
+    for (int i = 0; i < a; ++i) wsh[(size_t)j * a + i] = h_shoup(w[(size_t)j * a + i], c.primes[j]);
   c.d_mdw = upload(w);
-  c.md = ModDownDev{a, L, c.d_phatinv, c.d_mdw, c.d_pinv};
+  c.d_mdwsh = upload(wsh);
+  c.md = ModDownDev{a, L, c.d_phatinv, c.d_mdw, c.d_pinv, c.d_mdwsh};
 }
 
 void build_level(Ctx &c, Level &lv, int Ql) {
@@ -373,8 +377,16 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   up_i64(lv.p_offsets);
   up_i64(lv.y_off);
   lv.qhatinv = upload(qhi);
+  std::vector<u64> wsh(w.size());
+  for (int d = 0; d < lv.beta; ++d)
+    for (int j = 0; j < lv.QlP; ++j)
+      for (int i = 0; i < a; ++i) {
+        const size_t o = ((size_t)d * lv.QlP + j) * a + i;
+        wsh[o] = h_shoup(w[o], c.primes[lv.prime_of.h[j]]);
+      }
   lv.w = upload(w);
-  lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w};
+  lv.wsh = upload(wsh);
+  lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh};
   lv.lay = KsLayout{lv.n_out, lv.out_j.d, lv.key_slot.d, lv.c_slot.d, G, lv.coef_ml};
 }
 
@@ -482,6 +494,7 @@ void ctx_free(Ctx &c) {
     f(lv.scale_in);
     f(lv.scale_p);
     f(lv.w);
+    f(lv.wsh);
   }
   f(c.own_key_prime.d);
   f(c.d_primes);
@@ -493,6 +506,7 @@ void ctx_free(Ctx &c) {
   f(c.d_phatinv);
   f(c.d_pinv);
   f(c.d_mdw);
+  f(c.d_mdwsh);
   f(c.arena);
   for (auto &pe : c.prof_events) {
     cudaEventDestroy(pe.second.first);
@@ -675,10 +689,9 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
   // 2. scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the input, all-gathered
   {
     StageTimer tm(c, ST_INTT_IN, s);
-    KS_CUDA(cudaMemcpyAsync(c.s_coef, in_ntt, (size_t)lv.n_q * N * 8, cudaMemcpyDeviceToDevice,
-                            s));
+    LimbMap min{const_cast<u64 *>(in_ntt), (long long)N, nullptr, lv.q_index.d, 0, 1};
     LimbMap mc{c.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(mc, lv.n_q, lv.scale_in, T, s));
+    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_q, lv.scale_in, T, s));
     c.launches += 2;
   }
   if (c.world > 1) {
@@ -710,7 +723,7 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
   if (c.world == 1) {
     StageTimer tm(c, ST_INTT_P, s);
     LimbMap mp{c.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(mp, 2 * lv.n_p, lv.scale_p, T, s));
+    KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
     c.launches += 2;
     y_base = c.s_cx;
   } else {
@@ -723,7 +736,7 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
                                   cudaMemcpyDeviceToDevice, s));
       if (lv.n_p > 0) {
         LimbMap mp{c.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-        KS_CUDA(ntt_inverse_scaled(mp, 2 * lv.n_p, lv.scale_p, T, s));
+        KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
         c.launches += 2;
       }
     }

@@ -47,6 +47,7 @@ struct Level {
   DevI64 y_off;       // [2 * alpha] offsets of P limb i of poly p in the y buffer
   ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
   u64 *w = nullptr;               // [beta][QlP][alpha]
+  u64 *wsh = nullptr;             // Shoup companions of w
   // fused ModUp: one job per (digit d, output slot s) with limb j outside digit d
   int n_jobs = 0;
   DevInts src_slot;               // [beta * alpha] slot of Q limb d*alpha+i in the gathered input
@@ -77,7 +78,7 @@ struct Ctx {
   u64 *d_gauss = nullptr;
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
-  u64 *d_mdw = nullptr;
+  u64 *d_mdw = nullptr, *d_mdwsh = nullptr;
   std::vector<Level> levels;  // index Ql (1..L)
   // key-basis ownership
   std::vector<int> own_key;   // owned key-basis limbs, increasing

@@ -1,16 +1,19 @@
 // ks_fused.cu -- fused key-switch kernels (sm_100a).
 //
-// ModUp base extension fused into the first NTT pass: every element of a
-// column tile is produced from the alpha scaled coefficient limbs of its
-// digit (5 L2-resident loads + 5 multiply-accumulates + one Barrett
-// reduction) and fed straight into the butterflies, so the extended limbs in
-// coefficient form never touch HBM.  The scaled inputs
-// v_i = [x_i * (Q_d/q_i)^-1]_{q_i} come out of the input INTT, whose last
-// stage already multiplies by N^-1 and now also by (Q_d/q_i)^-1.
+// ModUp base extension fused into the first NTT pass: the inputs of a column
+// tile are produced from the alpha scaled coefficient limbs of their digit,
+//   y = sum_i v_i * [Q_d/q_i]_{m_j}  mod m_j,
+// one source limb at a time (16 independent coalesced loads per thread per
+// source, Shoup products against the per-(digit, limb) constants accumulated
+// in 64 bits), and fed straight into the butterflies, so the extended limbs
+// in coefficient form never touch HBM.  The scaled inputs
+// v_i = [x_i (Q_d/q_i)^-1]_{q_i} come out of the input INTT, whose last stage
+// multiplies by N^-1 (Q_d/q_i)^-1 instead of N^-1.
 //
 // ModDown: the P -> Q conversion is fused the same way into the first pass,
-// and the second pass ends with (cx - z) * P^-1 and the add to the
-// ciphertext, so the converted limbs never reach HBM in NTT form either.
+// and the second pass ends with (cx - z) P^-1 mod q_j and the add to the
+// ciphertext, staged through shared memory so every global access of the
+// epilogue is coalesced.
 #include "ks_fused.cuh"
 #include "ks_ntt_impl.cuh"
 
@@ -39,13 +42,39 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   if (P.q < kFpBound) {
     // scale entries of FP64 primes hold the bits of {s, fl(s/q)}
     inv_cols_fp<LOG_M>(sm, col, t, c, log_n, T.inv_fp + (long long)prime * N, P,
-                       make_double2(as_fp(s0.x), as_fp(s0.y)), make_double2(as_fp(s1.x), as_fp(s1.y)),
-                       load, store);
+                       make_double2(as_fp(s0.x), as_fp(s0.y)),
+                       make_double2(as_fp(s1.x), as_fp(s1.y)), load, store);
   } else if (P.q < kInvLazyBound) {
     inv_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
   } else {
     inv_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
   }
+}
+
+// Fills the 16 column inputs of this thread with
+//   y = sum_{i < n_src} [v_i * w_i]_{q}  (each term canonical, sum < 8q),
+// reduced to [0, q).  src(i) points at source limb i.
+template <int LOG_M, class Src>
+__device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M2, int n_src,
+                                           Src &&src, const u64 *w, const u64 *wsh,
+                                           const PrimeDev &P) {
+  using G = ColGeom<LOG_M>;
+  u64 acc[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) acc[e] = 0;
+#pragma unroll 1
+  for (int i = 0; i < n_src; ++i) {
+    const u64 *s = src(i);
+    const u64 wi = __ldg(&w[i]), wp = __ldg(&wsh[i]);
+    u64 v[kEpt];
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e)
+      v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) acc[e] += mul_shoup(v[e], wi, wp, P.q);
+  }
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = reduce_full(acc[e], P.q, P.mu);
 }
 
 // ---------------------------------------------------------------------------
@@ -63,33 +92,23 @@ __global__ void __launch_bounds__(kThreads)
   const int prime = mu.prime_of[j];
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
-  const ulonglong2 *tw = T.fwd + (long long)prime * N;
   const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
   const int col = blockIdx.x * G::C + c;
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
-  const u64 *src[KS_MAX_ALPHA];
-  u64 w[KS_MAX_ALPHA];
-#pragma unroll
-  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-    if (i < n_src) {
-      src[i] = v_all + (long long)src_slot[d * mu.alpha + i] * N;
-      w[i] = mu.w[((long long)d * mu.QlP + j) * mu.alpha + i];
-    }
-  }
-  auto load = [&](int r, int cl) {
-    const long long k = (long long)r * M2 + cl;
-    u128v acc = {0, 0};
-#pragma unroll
-    for (int i = 0; i < KS_MAX_ALPHA; ++i)
-      if (i < n_src) mac(acc, __ldg(src[i] + k), w[i]);
-    return barrett128(acc, P.q, P.br_hi, P.br_lo);
+  const long long wo = ((long long)d * mu.QlP + j) * mu.alpha;
+  auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
+  auto fill = [&](u64 (&x)[kEpt]) {
+    bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, mu.w + wo, mu.wsh + wo, P);
   };
   u64 *out = t + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFpBound)
-    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, load, store);
-  else if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
-  else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, load, store);
+  if (P.q < kFpBound) {
+    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, fill, store);
+  } else {
+    const ulonglong2 *tw = T.fwd + (long long)prime * N;
+    if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
+    else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, fill, store);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -105,32 +124,22 @@ __global__ void __launch_bounds__(kThreads)
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
-  const ulonglong2 *tw = T.fwd + (long long)j * N;
   const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
   const int col = blockIdx.x * G::C + c;
-  const u64 *src[KS_MAX_ALPHA];
-  u64 w[KS_MAX_ALPHA];
-#pragma unroll
-  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-    if (i < md.alpha) {
-      src[i] = y_base + y_off[p * md.alpha + i];
-      w[i] = md.w[(long long)j * md.alpha + i];
-    }
-  }
-  auto load = [&](int r, int cl) {
-    const long long k = (long long)r * M2 + cl;
-    u128v acc = {0, 0};
-#pragma unroll
-    for (int i = 0; i < KS_MAX_ALPHA; ++i)
-      if (i < md.alpha) mac(acc, __ldg(src[i] + k), w[i]);
-    return barrett128(acc, P.q, P.br_hi, P.br_lo);
+  const long long wo = (long long)j * md.alpha;
+  auto src = [&](int i) { return y_base + y_off[p * md.alpha + i]; };
+  auto fill = [&](u64 (&x)[kEpt]) {
+    bconv_fill<LOG_M>(x, tt, col, M2, md.alpha, src, md.w + wo, md.wsh + wo, P);
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFpBound)
-    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, load, store);
-  else if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, load, store);
-  else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, load, store);
+  if (P.q < kFpBound) {
+    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, fill, store);
+  } else {
+    const ulonglong2 *tw = T.fwd + (long long)j * N;
+    if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
+    else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, fill, store);
+  }
 }
 
 // Row pass of z with the ModDown finish fused into the epilogue.
@@ -146,25 +155,32 @@ __global__ void __launch_bounds__(kThreads)
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
   const int log_n = T.log_n, N = 1 << log_n;
-  const ulonglong2 *tw = T.fwd + (long long)j * N;
   const int t = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const long long tile0 = (long long)blockIdx.x * kTile;
   const u64 *tile = z + ((long long)p * n_q + s) * N + tile0;
   const long long row = (long long)blockIdx.x * G::R + rr;
   u64 x[kEpt];
-  if (P.q < kFpBound)
+  if (P.q < kFpBound) {
     fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, T.fwd_fp + (long long)j * N, P);
-  else if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
-  else fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
-  const ulonglong2 pinv = md.pinv[j];
-  const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N;
-  u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N;
-  const u64 *base = (p == 0) ? (rotate ? g0 + (long long)s * N : dst) : (rotate ? nullptr : dst);
+  } else {
+    const ulonglong2 *tw = T.fwd + (long long)j * N;
+    if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
+    else fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
+  }
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) {
-    const long long k = row * G::M + lidx<LOG_M, 0, G::NLO>(t, e);
-    const u64 o = mul_shoup(cxp[k] + P.q - x[e], pinv.x, pinv.y, P.q);
-    dst[k] = base ? add_mod(base[k], o, P.q) : o;
+  for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
+  __syncthreads();
+  const ulonglong2 pinv = md.pinv[j];
+  const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N + tile0;
+  u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N + tile0;
+  const u64 *base =
+      (p == 0) ? (rotate ? g0 + (long long)s * N + tile0 : dst) : (rotate ? nullptr : dst);
+#pragma unroll 4
+  for (int i = 0; i < kEpt; ++i) {
+    const int lin = threadIdx.x + i * kThreads;
+    const u64 zv = sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))];
+    const u64 o = mul_shoup(cxp[lin] + P.q - zv, pinv.x, pinv.y, P.q);
+    dst[lin] = base ? add_mod(base[lin], o, P.q) : o;
   }
 }
 
@@ -175,19 +191,19 @@ inline int col_tiles(int log_n, int log_m) {
 
 }  // namespace
 
-cudaError_t ntt_inverse_scaled(const LimbMap &m, int n_limbs, const ulonglong2 *scale,
-                               const NttTables &T, cudaStream_t s) {
+cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
+                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
   if (n_limbs == 0) return cudaSuccess;
-  // first pass: the ordinary inverse row pass
-  cudaError_t e = ntt_inverse_rows_only(m, n_limbs, T, s);
+  // first pass: the ordinary inverse row pass, src -> dst
+  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst);
   if (e != cudaSuccess) return e;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_limbs);
   switch (s1) {
-    case 6: k_inv_cols_scaled<6><<<grid, kThreads, 0, s>>>(m, T, scale); break;
-    case 7: k_inv_cols_scaled<7><<<grid, kThreads, 0, s>>>(m, T, scale); break;
-    case 8: k_inv_cols_scaled<8><<<grid, kThreads, 0, s>>>(m, T, scale); break;
+    case 6: k_inv_cols_scaled<6><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 7: k_inv_cols_scaled<7><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 8: k_inv_cols_scaled<8><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -10,8 +10,9 @@ namespace ksb {
 
 // Inverse NTT whose last stage multiplies by a per-limb constant c (on top
 // of N^-1): scale[i] = {N^-1 c, Shoup}, {psi^-brev(1) N^-1 c, Shoup}.
-cudaError_t ntt_inverse_scaled(const LimbMap &m, int n_limbs, const ulonglong2 *scale,
-                               const NttTables &T, cudaStream_t s);
+// Reads src, writes dst (which may alias src).
+cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
+                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s);
 
 // ModUp: for each job (digit d, output slot s) the column pass of the
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),

@@ -18,6 +18,7 @@ struct ModUpDev {
   const int *prime_of;        // [QlP] prime index of QlP limb j (Q limbs, then P)
   const ulonglong2 *qhatinv;  // [beta][alpha] {[(Q_d/q_i)^-1]_{q_i}, Shoup}
   const u64 *w;               // [beta][QlP][alpha] [Q_d/q_i]_{m_j}
+  const u64 *wsh;             // same layout: Shoup companions of w w.r.t. m_j
 };
 
 // Constants of the conversion P -> Q (ModDown), indexed by Q limb j.
@@ -27,6 +28,7 @@ struct ModDownDev {
   const ulonglong2 *phatinv;  // [alpha] {[(P/p_i)^-1]_{p_i}, Shoup}
   const u64 *w;               // [L][alpha] [P/p_i]_{q_j}
   const ulonglong2 *pinv;     // [L] {[P^-1]_{q_j}, Shoup}
+  const u64 *wsh;             // [L][alpha] Shoup companions of w w.r.t. q_j
 };
 
 // Which QlP limbs this device produces and where its inputs live.

@@ -31,18 +31,19 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   const int c = threadIdx.x % G::C, t = threadIdx.x / G::C;
   const int col = blockIdx.x * G::C + c;
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
+  auto fill = [&](u64 (&x)[kEpt]) { fill_cols<LOG_M>(x, t, col, load); };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
     const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
     if (FWD) {
-      fwd_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, load, store);
+      fwd_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, fill, store);
     } else {
       const double2 s0 = make_double2(P.ninv_d, P.ninv_q), s1 = make_double2(P.w1ninv_d, P.w1ninv_q);
       inv_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, s0, s1, load, store);
     }
   } else if (FWD) {
-    if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, load, store);
-    else fwd_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, load, store);
+    if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, fill, store);
+    else fwd_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, fill, store);
   } else {
     const ulonglong2 s0 = make_ulonglong2(P.ninv, P.ninv_sh);
     const ulonglong2 s1 = make_ulonglong2(P.w1ninv, P.w1ninv_sh);
@@ -52,18 +53,20 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
 }
 
 template <int LOG_M, bool FWD>
-__global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, NttTables T) {
+__global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T) {
   using G = RowGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
-  u64 *a;
-  int prime;
+  u64 *a, *o;
+  int prime, prime_o;
   limb_of(m, blockIdx.y, a, prime);
+  limb_of(mo, blockIdx.y, o, prime_o);  // output limb (== input limb when in place)
   if (prime < 0) return;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
   const ulonglong2 *tw = (FWD ? T.fwd : T.inv) + (long long)prime * N;
   const int t = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
-  u64 *tile = a + (long long)blockIdx.x * kTile;
+  const u64 *tile = a + (long long)blockIdx.x * kTile;
+  u64 *otile = o + (long long)blockIdx.x * kTile;
   const long long row = (long long)blockIdx.x * G::R + rr;
   u64 x[kEpt];
   const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, NttTables T) {
 #pragma unroll
     for (int i = 0; i < kEpt; ++i) {
       const int lin = threadIdx.x + i * kThreads;
-      tile[lin] = sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))];
+      otile[lin] = sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))];
     }
   } else {
 #pragma unroll
@@ -91,7 +94,7 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, NttTables T) {
     else if (P.q < kInvLazyBound) inv_rows_regs<LOG_M, true>(x, sm, t, rr, row, log_n, tw, P);
     else inv_rows_regs<LOG_M, false>(x, sm, t, rr, row, log_n, tw, P);
 #pragma unroll
-    for (int e = 0; e < kEpt; ++e) tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)] = x[e];
+    for (int e = 0; e < kEpt; ++e) otile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)] = x[e];
   }
 }
 
@@ -103,19 +106,21 @@ cudaError_t launch_cols(const LimbMap &m, int n_limbs, const NttTables &T, cudaS
   return cudaGetLastError();
 }
 template <int LOG_M, bool FWD>
-cudaError_t launch_rows(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s) {
+cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
+                        cudaStream_t s) {
   dim3 grid((1 << T.log_n) / kTile, n_limbs);
-  ntt_rows<LOG_M, FWD><<<grid, kThreads, 0, s>>>(m, T);
+  ntt_rows<LOG_M, FWD><<<grid, kThreads, 0, s>>>(m, mo, T);
   return cudaGetLastError();
 }
 
 template <bool FWD>
 cudaError_t launch_pass(bool cols, int log_m, const LimbMap &m, int n, const NttTables &T,
-                        cudaStream_t s) {
+                        cudaStream_t s, const LimbMap *mo = nullptr) {
+  const LimbMap &o = mo ? *mo : m;
   switch (log_m) {
-    case 6: return cols ? launch_cols<6, FWD>(m, n, T, s) : launch_rows<6, FWD>(m, n, T, s);
-    case 7: return cols ? launch_cols<7, FWD>(m, n, T, s) : launch_rows<7, FWD>(m, n, T, s);
-    case 8: return cols ? launch_cols<8, FWD>(m, n, T, s) : launch_rows<8, FWD>(m, n, T, s);
+    case 6: return cols ? launch_cols<6, FWD>(m, n, T, s) : launch_rows<6, FWD>(m, o, n, T, s);
+    case 7: return cols ? launch_cols<7, FWD>(m, n, T, s) : launch_rows<7, FWD>(m, o, n, T, s);
+    case 8: return cols ? launch_cols<8, FWD>(m, n, T, s) : launch_rows<8, FWD>(m, o, n, T, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -141,10 +146,10 @@ cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables
 }
 
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
-                                  cudaStream_t s) {
+                                  cudaStream_t s, const LimbMap *out) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
   if (n_limbs == 0) return cudaSuccess;
-  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s);
+  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s, out);
 }
 
 cudaError_t ntt_inverse(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s) {

@@ -40,7 +40,8 @@ bool ntt_supported_log_n(int log_n);
 // one), for callers that run a fused first/second pass of their own.
 cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
                                   cudaStream_t s);
+// out: optional separate destination (same limb order and primes as m).
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
-                                  cudaStream_t s);
+                                  cudaStream_t s, const LimbMap *out = nullptr);
 
 }  // namespace ksb

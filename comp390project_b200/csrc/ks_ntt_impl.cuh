@@ -112,15 +112,21 @@ struct RowGeom {
 // lazy path, < 4q otherwise); store(r, col, v) receives the output (< 17q lazy,
 // < 4q Harvey).  Rows r index the column sub-transform, col < M2.
 // ---------------------------------------------------------------------------
-template <int LOG_M, bool LAZY, class Load, class Store>
+// fill(x) sets x[e] to the input of column row lidx<LOG_M, HI, 4>(t, e).
+template <int LOG_M, class Load>
+__device__ __forceinline__ void fill_cols(u64 (&x)[kEpt], int t, int col, Load &&load) {
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = load(lidx<LOG_M, ColGeom<LOG_M>::HI, 4>(t, e), col);
+}
+
+template <int LOG_M, bool LAZY, class Fill, class Store>
 __device__ __forceinline__ void fwd_cols(u64 *sm, int col, int t, int c, int log_n,
-                                         const ulonglong2 *tw, const PrimeDev &P, Load &&load,
+                                         const ulonglong2 *tw, const PrimeDev &P, Fill &&fill,
                                          Store &&store) {
   using G = ColGeom<LOG_M>;
   const int gofs = log_n - LOG_M;
   u64 x[kEpt];
-#pragma unroll
-  for (int e = 0; e < kEpt; ++e) x[e] = load(lidx<LOG_M, G::HI, 4>(t, e), col);
+  fill(x);
   fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, 0, gofs, log_n, tw, P.q, P.two_q);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = x[e];
@@ -256,15 +262,19 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
 
 // Forward column pass; load() gives canonical uint64, store() receives the
 // bits of the pass result (|x| < q + 8 * 0.57q).
-template <int LOG_M, class Load, class Store>
+template <int LOG_M, class Fill, class Store>
 __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double2 *tw, const PrimeDev &P, Load &&load,
+                                            const double2 *tw, const PrimeDev &P, Fill &&fill,
                                             Store &&store) {
   using G = ColGeom<LOG_M>;
   const int gofs = log_n - LOG_M;
   double x[kEpt];
+  {
+    u64 xin[kEpt];
+    fill(xin);
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(load(lidx<LOG_M, G::HI, 4>(t, e), col));
+    for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(xin[e]);
+  }
   fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, gofs, log_n, tw, P.qd);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = fp_bits(x[e]);
