@@ -449,16 +449,26 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     size_t w_ya = world > 1 ? (size_t)world * c.max_p_own * 2 * N : 0;
     size_t w_z = 2 * nq * N;
     c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z;
-    c.arena = dev_alloc<u64>(c.arena_words);
-    u64 *p = c.arena;
-    c.s_g = p; p += w_g;
-    c.s_coef = p; p += w_coef;
-    c.s_coef_all = world > 1 ? p : c.s_coef; p += w_coef_all;
-    c.s_t = p; p += w_t;
-    c.s_cx = p; p += w_cx;
-    c.s_ysend = p; p += w_ys;
-    c.s_yall = p; p += w_ya;
-    c.s_z = p; p += w_z;
+    // one scratch arena per lane; lanes = max_batch (1..8)
+    // (contexts made by ks_ctx_create_all are set up one after another on one
+    // thread, where splitting communicators would block, so they keep one lane)
+    c.lanes.resize(comm ? 1 : std::min(8, c.max_batch));
+    for (size_t li = 0; li < c.lanes.size(); ++li) {
+      Ctx::Lane &ln = c.lanes[li];
+      ln.arena = dev_alloc<u64>(c.arena_words);
+      u64 *p = ln.arena;
+      ln.s_g = p; p += w_g;
+      ln.s_coef = p; p += w_coef;
+      ln.s_coef_all = world > 1 ? p : ln.s_coef; p += w_coef_all;
+      ln.s_t = p; p += w_t;
+      ln.s_cx = p; p += w_cx;
+      ln.s_ysend = p; p += w_ys;
+      ln.s_yall = p; p += w_ya;
+      ln.s_z = p; p += w_z;
+      if (li > 0) KS_CUDA(cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking));
+      KS_CUDA(cudaEventCreateWithFlags(&ln.done, cudaEventDisableTiming));
+    }
+    KS_CUDA(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
   }
   if (world > 1) {
     if (comm) {
@@ -470,6 +480,12 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       KS_NCCL(ncclCommInitRank(&c.comm, world, id, rank));
     }
     c.own_comm = true;
+    // every lane gets its own communicator so collectives of different key
+    // switches never share one (all ranks create them in the same order)
+    for (size_t li = 0; li < c.lanes.size(); ++li) {
+      if (li == 0) c.lanes[li].comm = c.comm;
+      else KS_NCCL(ncclCommSplit(c.comm, 0, rank, &c.lanes[li].comm, nullptr));
+    }
   }
   KS_CUDA(cudaDeviceSynchronize());
 }
@@ -507,7 +523,15 @@ void ctx_free(Ctx &c) {
   f(c.d_pinv);
   f(c.d_mdw);
   f(c.d_mdwsh);
-  f(c.arena);
+  for (size_t li = 0; li < c.lanes.size(); ++li) {
+    Ctx::Lane &ln = c.lanes[li];
+    f(ln.arena);
+    if (ln.stream) cudaStreamDestroy(ln.stream);
+    if (ln.done) cudaEventDestroy(ln.done);
+    if (li > 0 && ln.comm) ncclCommDestroy(ln.comm);
+  }
+  c.lanes.clear();
+  if (c.ev_fork) cudaEventDestroy(c.ev_fork);
   for (auto &pe : c.prof_events) {
     cudaEventDestroy(pe.second.first);
     cudaEventDestroy(pe.second.second);
@@ -587,7 +611,8 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
   const NttTables T = c.tables();
   int8_t *d_sk = dev_alloc<int8_t>(N);
   KS_CUDA(cudaMemcpyAsync(d_sk, sk_host, N, cudaMemcpyHostToDevice, s));
-  u64 *s_ntt = c.s_t, *snew = c.s_t + (size_t)n * N, *e = c.s_t + 2 * (size_t)n * N;
+  u64 *st = c.lanes[0].s_t;
+  u64 *s_ntt = st, *snew = st + (size_t)n * N, *e = st + 2 * (size_t)n * N;
   const int *prime = c.own_key_prime.d;
   KS_CUDA(expand_ternary(d_sk, s_ntt, n, prime, c.d_primes, c.log_n, s));
   LimbMap ms{s_ntt, N, nullptr, prime, 0, 1};
@@ -673,8 +698,8 @@ struct StageTimer {
 // ---------------------------------------------------------------------------
 // Collectives
 // ---------------------------------------------------------------------------
-void allgather(Ctx &c, const u64 *send, u64 *recv, size_t words, cudaStream_t s) {
-  KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, c.comm, s));
+void allgather(ncclComm_t comm, const u64 *send, u64 *recv, size_t words, cudaStream_t s) {
+  KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, comm, s));
 }
 
 // ---------------------------------------------------------------------------
@@ -682,7 +707,7 @@ void allgather(Ctx &c, const u64 *send, u64 *recv, size_t words, cudaStream_t s)
 // ---------------------------------------------------------------------------
 // in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]).
 // rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
-void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_ntt, u64 *ct0,
+void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt, u64 *ct0,
                     u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
   const size_t N = c.N;
   const NttTables T = c.tables();
@@ -690,31 +715,31 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
   {
     StageTimer tm(c, ST_INTT_IN, s);
     LimbMap min{const_cast<u64 *>(in_ntt), (long long)N, nullptr, lv.q_index.d, 0, 1};
-    LimbMap mc{c.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
+    LimbMap mc{L.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
     KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_q, lv.scale_in, T, s));
     c.launches += 2;
   }
   if (c.world > 1) {
     StageTimer tm(c, ST_COMM, s);
-    allgather(c, c.s_coef, c.s_coef_all, (size_t)lv.coef_ml * N, s);
+    allgather(L.comm, L.s_coef, L.s_coef_all, (size_t)lv.coef_ml * N, s);
   }
   // 3. ModUp: base extension fused into the column pass, then the row pass
   {
     StageTimer tm(c, ST_MODUP_BCONV, s);
-    KS_CUDA(modup_fused_cols(c.s_coef_all, lv.src_slot.d, c.s_t, lv.mu, lv.lay, lv.job_d.d,
+    KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
                              lv.job_s.d, lv.n_jobs, T, s));
     c.launches += 1;
   }
   {
     StageTimer tm(c, ST_MODUP_NTT, s);
-    LimbMap mt{c.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
+    LimbMap mt{L.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
     KS_CUDA(ntt_forward_rows_only(mt, lv.n_jobs, T, s));
     c.launches += 1;
   }
   // 4. inner product
   {
     StageTimer tm(c, ST_INNER_PROD, s);
-    KS_CUDA(inner_product(c.s_t, in_ntt, key.d, key.limbs, c.s_cx, lv.mu, lv.lay, c.d_primes,
+    KS_CUDA(inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay, c.d_primes,
                           c.log_n, s));
     c.launches += 1;
   }
@@ -722,38 +747,38 @@ void keyswitch_core(Ctx &c, const Level &lv, const KeyShard &key, const u64 *in_
   const u64 *y_base;
   if (c.world == 1) {
     StageTimer tm(c, ST_INTT_P, s);
-    LimbMap mp{c.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
+    LimbMap mp{L.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
     KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
     c.launches += 2;
-    y_base = c.s_cx;
+    y_base = L.s_cx;
   } else {
     {
       StageTimer tm(c, ST_INTT_P, s);
       for (int p = 0; p < 2; ++p)
         for (int k = 0; k < lv.n_p; ++k)
-          KS_CUDA(cudaMemcpyAsync(c.s_ysend + ((size_t)k * 2 + p) * N,
-                                  c.s_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N, N * 8,
+          KS_CUDA(cudaMemcpyAsync(L.s_ysend + ((size_t)k * 2 + p) * N,
+                                  L.s_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N, N * 8,
                                   cudaMemcpyDeviceToDevice, s));
       if (lv.n_p > 0) {
-        LimbMap mp{c.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
+        LimbMap mp{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
         KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
         c.launches += 2;
       }
     }
     StageTimer tm(c, ST_COMM, s);
-    allgather(c, c.s_ysend, c.s_yall, (size_t)c.max_p_own * 2 * N, s);
-    y_base = c.s_yall;
+    allgather(L.comm, L.s_ysend, L.s_yall, (size_t)c.max_p_own * 2 * N, s);
+    y_base = L.s_yall;
   }
   // 6. P -> Q conversion fused into the column pass
   {
     StageTimer tm(c, ST_MODDOWN_BCONV, s);
-    KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, c.s_z, lv.n_q, lv.q_index.d, c.md, T, s));
+    KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md, T, s));
     c.launches += 1;
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {
     StageTimer tm(c, ST_MODDOWN_NTT, s);
-    KS_CUDA(moddown_fused_rows(c.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, c.s_cx,
+    KS_CUDA(moddown_fused_rows(L.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, L.s_cx,
                                (long long)lv.n_out * N, ct0, ct1, g0, rotate, c.md, T, s));
     c.launches += 1;
   }
@@ -765,7 +790,7 @@ const Level &level_of(Ctx &c, int Ql) {
   return c.levels[Ql];
 }
 
-void do_apply_galois(Ctx &c, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
+void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
   KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
   check_elt(c, elt);
   const Level &lv = level_of(c, Ql);
@@ -775,19 +800,24 @@ void do_apply_galois(Ctx &c, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
   // 1. automorphism of both polys -> g0, g1
   {
     StageTimer tm(c, ST_GALOIS, s);
-    KS_CUDA(galois_ntt(ct, c.s_g, 2 * (int)nq, c.log_n, elt, s));
+    KS_CUDA(galois_ntt(ct, L.s_g, 2 * (int)nq, c.log_n, elt, s));
     c.launches += 1;
   }
-  keyswitch_core(c, lv, key, c.s_g + nq * N, ct, ct + nq * N, c.s_g, true, s);
+  keyswitch_core(c, L, lv, key, L.s_g + nq * N, ct, ct + nq * N, L.s_g, true, s);
 }
 
-void do_relin(Ctx &c, u64 *ct, int Ql, cudaStream_t s) {
+void do_relin(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, cudaStream_t s) {
   KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
   const Level &lv = level_of(c, Ql);
   const KeyShard &key = key_get(c, KS_KEY_RELIN, 0);
   const size_t nq = lv.n_q, N = c.N;
   KS_CUDA(cudaSetDevice(c.device));
-  keyswitch_core(c, lv, key, ct + 2 * nq * N, ct, ct + nq * N, nullptr, false, s);
+  keyswitch_core(c, L, lv, key, ct + 2 * nq * N, ct, ct + nq * N, nullptr, false, s);
+}
+
+Ctx::Lane &lane0(Ctx &c) {
+  KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
+  return c.lanes[0];
 }
 
 uint32_t elt_of_step(const Ctx &c, int step) {
@@ -990,20 +1020,23 @@ int ks_key_drop(ks_ctx *ctx, int kind, uint32_t elt) {
 int ks_relinearize(ks_ctx *ctx, uint64_t *ct, int level_limbs, void *stream) {
   if (!ctx) return KS_ERR_INVALID;
   ctx->c.launches = 0;
-  return guarded(ctx, [&] { do_relin(ctx->c, ct, level_limbs, (cudaStream_t)stream); });
+  return guarded(ctx, [&] { do_relin(ctx->c, lane0(ctx->c), ct, level_limbs, (cudaStream_t)stream); });
 }
 
 int ks_apply_galois(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t elt, void *stream) {
   if (!ctx) return KS_ERR_INVALID;
   ctx->c.launches = 0;
-  return guarded(ctx, [&] { do_apply_galois(ctx->c, ct, level_limbs, elt, (cudaStream_t)stream); });
+  return guarded(ctx, [&] {
+    do_apply_galois(ctx->c, lane0(ctx->c), ct, level_limbs, elt, (cudaStream_t)stream);
+  });
 }
 
 int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream) {
   if (!ctx) return KS_ERR_INVALID;
   ctx->c.launches = 0;
   return guarded(ctx, [&] {
-    do_apply_galois(ctx->c, ct, level_limbs, elt_of_step(ctx->c, step), (cudaStream_t)stream);
+    do_apply_galois(ctx->c, lane0(ctx->c), ct, level_limbs, elt_of_step(ctx->c, step),
+                    (cudaStream_t)stream);
   });
 }
 
@@ -1013,9 +1046,32 @@ int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, 
   ctx->c.launches = 0;
   return guarded(ctx, [&] {
     KS_REQUIRE(cts != nullptr && steps != nullptr && n >= 0, "bad batch arguments");
-    for (int i = 0; i < n; ++i)
-      do_apply_galois(ctx->c, cts[i], level_limbs, elt_of_step(ctx->c, steps[i]),
-                      (cudaStream_t)stream);
+    Ctx &c = ctx->c;
+    KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int nl = std::min<int>((int)c.lanes.size(), n);
+    if (nl <= 1) {
+      for (int i = 0; i < n; ++i)
+        do_apply_galois(c, c.lanes[0], cts[i], level_limbs, elt_of_step(c, steps[i]), s);
+      return;
+    }
+    // fork: every lane waits for the work already queued on the caller's stream
+    KS_CUDA(cudaSetDevice(c.device));
+    KS_CUDA(cudaEventRecord(c.ev_fork, s));
+    for (int li = 0; li < nl; ++li) {
+      cudaStream_t ls = li == 0 ? s : c.lanes[li].stream;
+      if (li > 0) KS_CUDA(cudaStreamWaitEvent(ls, c.ev_fork, 0));
+    }
+    for (int i = 0; i < n; ++i) {
+      const int li = i % nl;
+      cudaStream_t ls = li == 0 ? s : c.lanes[li].stream;
+      do_apply_galois(c, c.lanes[li], cts[i], level_limbs, elt_of_step(c, steps[i]), ls);
+    }
+    // join: the caller's stream waits for every lane
+    for (int li = 1; li < nl; ++li) {
+      KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
+      KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));
+    }
   });
 }
 
@@ -1108,7 +1164,7 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
     const int nl = n_local(c.rank, c.world, total_limbs);
     KS_CUDA(cudaMemsetAsync(send, 0, ml * N * 8, s));
     if (nl > 0) KS_CUDA(cudaMemcpyAsync(send, local_buf, nl * N * 8, cudaMemcpyDeviceToDevice, s));
-    allgather(c, send, recv, ml * N, s);
+    allgather(c.comm, send, recv, ml * N, s);
     // rank-grouped [G][ml] -> sequential: limb j at (j % G, j / G)
     for (int j = 0; j < total_limbs; ++j)
       KS_CUDA(cudaMemcpyAsync(full_buf + (size_t)j * N, recv + ((j % G) * ml + j / G) * N, N * 8,

@@ -85,13 +85,23 @@ struct Ctx {
   DevInts own_key_prime;      // same, device copy (prime index == key index)
   // keys
   std::map<unsigned long long, KeyShard> keys;  // (kind << 32) | elt
-  // scratch arena
-  u64 *arena = nullptr;
+  // Execution lanes: lane 0 runs single calls on the caller's stream; a batch
+  // of independent key switches is spread over all lanes, each with its own
+  // stream, scratch arena and (world > 1) communicator, so memory-bound and
+  // compute-bound stages of different key switches overlap.
+  struct Lane {
+    cudaStream_t stream = nullptr;  // null for lane 0 (uses the caller's stream)
+    cudaEvent_t done = nullptr;
+    u64 *arena = nullptr;
+    u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr,
+        *s_cx = nullptr, *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr;
+    ncclComm_t comm = nullptr;
+  };
+  std::vector<Lane> lanes;
+  cudaEvent_t ev_fork = nullptr;
   size_t arena_words = 0;
-  u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr, *s_cx = nullptr,
-      *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr;
   int max_p_own = 0;
-  // comm
+  // comm (lane 0's communicator)
   ncclComm_t comm = nullptr;
   bool own_comm = false;
   int timeout_ms = 60000;

@@ -160,3 +160,25 @@ def test_config3_rotation_bitexact(cuda_device):
     assert np.array_equal(out, ref)
     dec = o.decode(o.decrypt(s, out, 35), 35, 2.0 ** 40)
     assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
+
+
+@pytest.mark.parametrize("lanes", [1, 3])
+def test_rotate_batch_lanes(lanes, cuda_device):
+    """Batched rotations spread over several execution lanes (streams with
+    their own scratch) give the same words as the oracle for every member."""
+    o = oracle_for("small")
+    ctx = _ctx(SMALL, max_batch=lanes)
+    s = o.secret(4)
+    steps = [1, 2, 3, -1, 5]
+    keys = {}
+    for st in steps:
+        elt = o.galois_elt(st)
+        keys[st] = o.keygen_galois(s, elt, 40 + st)
+        ctx.key_upload(1, elt, keys[st])
+    cts = [_encrypted(o, 7, 50 + i, s)[1] for i in range(len(steps))]
+    devs = [_to_dev(ct) for ct in cts]
+    ctx.rotate_batch(devs, steps, 7)
+    torch.cuda.synchronize()
+    for ct, d, st in zip(cts, devs, steps):
+        ref = o.apply_galois(ct, 7, o.galois_elt(st), keys[st])
+        assert np.array_equal(_to_host(d).reshape(2, 7, o.N), ref)
