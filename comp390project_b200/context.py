@@ -205,6 +205,13 @@ class KsContext:
         self._check(self.lib.ks_relinearize(self.h, self._ptr(ct), int(level_limbs),
                                             _stream_ptr(stream, self.device)))
 
+    def keyswitch_add(self, c, ct, level_limbs: int, kind: int = KS_KEY_RELIN, elt: int = 0,
+                      stream=None):
+        """ct[0] += ks0(c), ct[1] += ks1(c) for the key (kind, elt)."""
+        self._check(self.lib.ks_keyswitch_add(self.h, self._ptr(c), self._ptr(ct),
+                                              int(level_limbs), int(kind), int(elt),
+                                              _stream_ptr(stream, self.device)))
+
     def apply_galois(self, ct, level_limbs: int, elt: int, stream=None):
         self._check(self.lib.ks_apply_galois(self.h, self._ptr(ct), int(level_limbs), int(elt),
                                              _stream_ptr(stream, self.device)))

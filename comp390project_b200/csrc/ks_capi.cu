@@ -1023,6 +1023,24 @@ int ks_relinearize(ks_ctx *ctx, uint64_t *ct, int level_limbs, void *stream) {
   return guarded(ctx, [&] { do_relin(ctx->c, lane0(ctx->c), ct, level_limbs, (cudaStream_t)stream); });
 }
 
+int ks_keyswitch_add(ks_ctx *ctx, const uint64_t *cin, uint64_t *ct, int level_limbs, int kind,
+                     uint32_t elt, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(cin != nullptr && ct != nullptr && aligned16(cin) && aligned16(ct),
+               "pointers must be non-null and 16-byte aligned");
+    KS_REQUIRE(kind == KS_KEY_RELIN || kind == KS_KEY_GALOIS, "unknown key kind");
+    const Level &lv = level_of(c, level_limbs);
+    const KeyShard &key = key_get(c, kind, kind == KS_KEY_RELIN ? 0u : elt);
+    const size_t nq = lv.n_q, N = c.N;
+    KS_CUDA(cudaSetDevice(c.device));
+    keyswitch_core(c, lane0(c), lv, key, cin, ct, ct + nq * N, nullptr, false,
+                   (cudaStream_t)stream);
+  });
+}
+
 int ks_apply_galois(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t elt, void *stream) {
   if (!ctx) return KS_ERR_INVALID;
   ctx->c.launches = 0;

@@ -120,6 +120,13 @@ int ks_key_drop(ks_ctx *ctx, int kind, uint32_t galois_elt);
  * result.  Replaces keyswitching_input_broadcast / keyswitching_output_
  * aggregation (input_broadcast.cu:117-176, output_aggregation.cu:197-294). */
 int ks_relinearize(ks_ctx *ctx, uint64_t *ct, int level_limbs, void *stream);
+/* Generic key switch of one polynomial c [n_local][N] (NTT form) with the key
+ * (kind, galois_elt), added into ct [2][n_local][N]: ct0 += ks0(c),
+ * ct1 += ks1(c).  With the relinearisation key this is the reference's
+ * keyswitching_input_broadcast(encrypted, local_c2, relin_keys)
+ * (input_broadcast.cuh:68-78), c and ct in separate buffers. */
+int ks_keyswitch_add(ks_ctx *ctx, const uint64_t *c, uint64_t *ct, int level_limbs, int kind,
+                     uint32_t galois_elt, void *stream);
 /* X -> X^galois_elt on ct [2][n_local][N] in place plus key switch with the
  * Galois key of that element (Phantom apply_galois_inplace;
  * rotation_input_broadcast, input_broadcast.cu:182-202). */
