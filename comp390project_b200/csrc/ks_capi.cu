@@ -335,15 +335,26 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       const int j = d * a + i;
       lv.src_slot.h.push_back(j < Ql ? (j % G) * lv.coef_ml + j / G : 0);
     }
-  for (int d = 0; d < lv.beta; ++d)
-    for (int s = 0; s < lv.n_out; ++s)
-      if (lv.t_jobs.h[(size_t)d * lv.n_out + s] >= 0) {
+  // jobs whose target prime takes the FP64 path first, then the integer ones
+  for (int pass = 0; pass < 2; ++pass)
+    for (int d = 0; d < lv.beta; ++d)
+      for (int s = 0; s < lv.n_out; ++s) {
+        const int pj = lv.t_jobs.h[(size_t)d * lv.n_out + s];
+        if (pj < 0 || (c.primes[pj] < kFpBound) != (pass == 0)) continue;
         lv.job_d.h.push_back(d);
         lv.job_s.h.push_back(s);
-        lv.job_prime.h.push_back(lv.t_jobs.h[(size_t)d * lv.n_out + s]);
+        lv.job_prime.h.push_back(pj);
         lv.job_off.h.push_back(((long long)d * lv.n_out + s) * N);
+        if (pass == 0) ++lv.n_jobs_fp;
       }
   lv.n_jobs = (int)lv.job_d.h.size();
+  for (int pass = 0; pass < 2; ++pass)
+    for (int p = 0; p < 2; ++p)
+      for (int s = 0; s < lv.n_q; ++s) {
+        if ((c.primes[lv.out_j.h[s]] < kFpBound) != (pass == 0)) continue;
+        lv.md_job_ps.h.push_back(p * lv.n_q + s);
+        if (pass == 0) ++lv.n_md_fp;
+      }
   std::vector<ulonglong2> sin, sp;
   for (int s = 0; s < lv.n_q; ++s) {
     const int j = lv.out_j.h[s], d = j / a;
@@ -359,6 +370,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       scale_pair(L + i, h_invmod(prod, pi), sp);
     }
   up_ints(lv.src_slot);
+  up_ints(lv.md_job_ps);
   up_ints(lv.job_d);
   up_ints(lv.job_s);
   up_ints(lv.job_prime);
@@ -378,15 +390,19 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   up_i64(lv.y_off);
   lv.qhatinv = upload(qhi);
   std::vector<u64> wsh(w.size());
+  std::vector<double> wq(w.size(), 0.0);
   for (int d = 0; d < lv.beta; ++d)
     for (int j = 0; j < lv.QlP; ++j)
       for (int i = 0; i < a; ++i) {
         const size_t o = ((size_t)d * lv.QlP + j) * a + i;
-        wsh[o] = h_shoup(w[o], c.primes[lv.prime_of.h[j]]);
+        const u64 m = c.primes[lv.prime_of.h[j]];
+        wsh[o] = h_shoup(w[o], m);
+        if (m < kFpBound) wq[o] = (double)w[o] / (double)m;
       }
   lv.w = upload(w);
   lv.wsh = upload(wsh);
-  lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh};
+  lv.wq = upload(wq);
+  lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh, lv.wq};
   lv.lay = KsLayout{lv.n_out, lv.out_j.d, lv.key_slot.d, lv.c_slot.d, G, lv.coef_ml};
 }
 
@@ -505,12 +521,13 @@ void ctx_free(Ctx &c) {
     f(lv.p_offsets.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
-    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime}) f(t->d);
+    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps}) f(t->d);
     f(lv.job_off.d);
     f(lv.scale_in);
     f(lv.scale_p);
     f(lv.w);
     f(lv.wsh);
+    f(lv.wq);
   }
   f(c.own_key_prime.d);
   f(c.d_primes);
@@ -727,8 +744,8 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
   {
     StageTimer tm(c, ST_MODUP_BCONV, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
-                             lv.job_s.d, lv.n_jobs, T, s));
-    c.launches += 1;
+                             lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s));
+    c.launches += (lv.n_jobs_fp > 0) + (lv.n_jobs > lv.n_jobs_fp);
   }
   {
     StageTimer tm(c, ST_MODUP_NTT, s);
@@ -772,8 +789,9 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
   // 6. P -> Q conversion fused into the column pass
   {
     StageTimer tm(c, ST_MODDOWN_BCONV, s);
-    KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md, T, s));
-    c.launches += 1;
+    KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md,
+                               lv.md_job_ps.d, lv.n_md_fp, T, s));
+    c.launches += (lv.n_md_fp > 0) + (2 * lv.n_q > lv.n_md_fp);
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {

@@ -48,8 +48,11 @@ struct Level {
   ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
   u64 *w = nullptr;               // [beta][QlP][alpha]
   u64 *wsh = nullptr;             // Shoup companions of w
+  double *wq = nullptr;           // fl(w / m_j) for FP64 primes
   // fused ModUp: one job per (digit d, output slot s) with limb j outside digit d
-  int n_jobs = 0;
+  int n_jobs = 0, n_jobs_fp = 0;  // jobs with FP64 targets come first
+  DevInts md_job_ps;              // [2 * n_q] ModDown jobs p*n_q + s, FP64 targets first
+  int n_md_fp = 0;
   DevInts src_slot;               // [beta * alpha] slot of Q limb d*alpha+i in the gathered input
   DevInts job_d, job_s, job_prime;  // [n_jobs]
   DevI64 job_off;                 // [n_jobs] word offset of t[d][s]

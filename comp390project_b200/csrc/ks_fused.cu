@@ -77,17 +77,50 @@ __device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M
   for (int e = 0; e < kEpt; ++e) x[e] = reduce_full(acc[e], P.q, P.mu);
 }
 
+// FP64 variant for targets q < kFpBound: x = sum_i fp_mulmod(v_i, w_i, w_i/q),
+// |x| < 0.57 q n_src < 4.6q.  A source limb whose prime is not below 2^50
+// (the 58-bit q_0) is first reduced mod q with the integer Barrett-style
+// reduce_full so that every product input stays below 2^50.
+template <int LOG_M, class Src>
+__device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col, int M2,
+                                              int n_src, Src &&src, const int *src_prime,
+                                              const u64 *w, const double *wq,
+                                              const PrimeDev *primes, const PrimeDev &P) {
+  using G = ColGeom<LOG_M>;
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = 0.0;
+#pragma unroll 1
+  for (int i = 0; i < n_src; ++i) {
+    const u64 *s = src(i);
+    const double wd = (double)__ldg(&w[i]), wqd = __ldg(&wq[i]);
+    const bool big = primes[src_prime[i]].q >= (1ull << 50);
+    u64 v[kEpt];
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e)
+      v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
+    if (big) {
+#pragma unroll
+      for (int e = 0; e < kEpt; ++e) v[e] = reduce_full(v[e], P.q, P.mu);
+    }
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e)
+      x[e] = __dadd_rn(x[e], fp_mulmod(u64_to_fp(v[e]), wd, wqd, P.qd));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // ModUp: base conversion + forward column pass
 // ---------------------------------------------------------------------------
-template <int LOG_M>
-__global__ void __launch_bounds__(kThreads)
+// One instantiation per arithmetic path keeps the register count of each at
+// what that path needs: FP = jobs whose target prime is below kFpBound.
+template <int LOG_M, bool FP>
+__global__ void __launch_bounds__(kThreads, 2)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
-                 const int *__restrict__ job_s, NttTables T) {
+                 const int *__restrict__ job_s, int job0, NttTables T) {
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
-  const int d = job_d[blockIdx.y], s = job_s[blockIdx.y];
+  const int d = job_d[job0 + blockIdx.y], s = job_s[job0 + blockIdx.y];
   const int j = lay.out_j[s];
   const int prime = mu.prime_of[j];
   const PrimeDev P = T.primes[prime];
@@ -97,14 +130,20 @@ __global__ void __launch_bounds__(kThreads)
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
   const long long wo = ((long long)d * mu.QlP + j) * mu.alpha;
   auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
-  auto fill = [&](u64 (&x)[kEpt]) {
-    bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, mu.w + wo, mu.wsh + wo, P);
-  };
   u64 *out = t + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFpBound) {
-    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, fill, store);
+  if constexpr (FP) {
+    const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
+    auto filld = [&](double (&x)[kEpt]) {
+      bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src, src_prime, mu.w + wo, mu.wq + wo,
+                           T.primes, P);
+    };
+    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, filld,
+                        store);
   } else {
+    auto fill = [&](u64 (&x)[kEpt]) {
+      bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, mu.w + wo, mu.wsh + wo, P);
+    };
     const ulonglong2 *tw = T.fwd + (long long)prime * N;
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
     else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, fill, store);
@@ -114,13 +153,15 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
-template <int LOG_M>
-__global__ void __launch_bounds__(kThreads)
+template <int LOG_M, bool FP>
+__global__ void __launch_bounds__(kThreads, 2)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
-                   int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T) {
+                   int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
+                   const int *__restrict__ job_ps, int job0) {
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
-  const int p = blockIdx.y / n_q, s = blockIdx.y % n_q;
+  const int ps = job_ps[job0 + blockIdx.y];
+  const int p = ps / n_q, s = ps % n_q;
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
@@ -133,7 +174,7 @@ __global__ void __launch_bounds__(kThreads)
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (P.q < kFpBound) {
+  if constexpr (FP) {
     fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, fill, store);
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
@@ -159,6 +200,17 @@ __global__ void __launch_bounds__(kThreads)
   const long long tile0 = (long long)blockIdx.x * kTile;
   const u64 *tile = z + ((long long)p * n_q + s) * N + tile0;
   const long long row = (long long)blockIdx.x * G::R + rr;
+  const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N + tile0;
+  u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N + tile0;
+  const u64 *base =
+      (p == 0) ? (rotate ? g0 + (long long)s * N + tile0 : dst) : (rotate ? nullptr : dst);
+  // Pull the epilogue operands into L2 while the butterflies run: one
+  // prefetch per 128-byte line of the tile (4096 words = 256 lines).
+  {
+    const int line = threadIdx.x * 16;  // words; kThreads * 16 == kTile
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(cxp + line));
+    if (base) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + line));
+  }
   u64 x[kEpt];
   if (P.q < kFpBound) {
     fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, T.fwd_fp + (long long)j * N, P);
@@ -171,10 +223,6 @@ __global__ void __launch_bounds__(kThreads)
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
   __syncthreads();
   const ulonglong2 pinv = md.pinv[j];
-  const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N + tile0;
-  u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N + tile0;
-  const u64 *base =
-      (p == 0) ? (rotate ? g0 + (long long)s * N + tile0 : dst) : (rotate ? nullptr : dst);
 #pragma unroll 4
   for (int i = 0; i < kEpt; ++i) {
     const int lin = threadIdx.x + i * kThreads;
@@ -209,38 +257,64 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
   return cudaGetLastError();
 }
 
+template <int LOG_M>
+void launch_modup_cols(dim3 grid, bool fp, int job0, cudaStream_t s, const u64 *v_all,
+                       const int *src_slot, u64 *t, const ModUpDev &mu, const KsLayout &lay,
+                       const int *job_d, const int *job_s, const NttTables &T) {
+  if (fp) k_modup_cols<LOG_M, true><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, job0, T);
+  else k_modup_cols<LOG_M, false><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, job0, T);
+}
+
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
-                             const NttTables &T, cudaStream_t s) {
+                             int n_fp, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_jobs < 0 || n_jobs > 65535) return cudaErrorInvalidValue;
-  if (mu.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
-  if (n_jobs == 0) return cudaSuccess;
+  if (mu.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > n_jobs) return cudaErrorInvalidValue;
   const int s1 = T.log_n / 2;
-  dim3 grid(col_tiles(T.log_n, s1), n_jobs);
-  switch (s1) {
-    case 6: k_modup_cols<6><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-    case 7: k_modup_cols<7><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-    case 8: k_modup_cols<8><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-    default: return cudaErrorInvalidValue;
+  for (int part = 0; part < 2; ++part) {
+    const int job0 = part == 0 ? 0 : n_fp, cnt = part == 0 ? n_fp : n_jobs - n_fp;
+    if (cnt == 0) continue;
+    dim3 grid(col_tiles(T.log_n, s1), cnt);
+    switch (s1) {
+      case 6: launch_modup_cols<6>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
+      case 7: launch_modup_cols<7>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
+      case 8: launch_modup_cols<8>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
+      default: return cudaErrorInvalidValue;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
   }
-  return cudaGetLastError();
+  return cudaSuccess;
+}
+
+template <int LOG_M>
+void launch_moddown_cols(dim3 grid, bool fp, int job0, cudaStream_t s, const u64 *y_base,
+                         const long long *y_off, u64 *z, int n_q, const int *q_index,
+                         const ModDownDev &md, const NttTables &T, const int *job_ps) {
+  if (fp) k_moddown_cols<LOG_M, true><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, job0);
+  else k_moddown_cols<LOG_M, false><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, job0);
 }
 
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
-                               const int *q_index, const ModDownDev &md, const NttTables &T,
-                               cudaStream_t s) {
+                               const int *q_index, const ModDownDev &md, const int *job_ps,
+                               int n_fp, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
-  if (md.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
-  if (n_q == 0) return cudaSuccess;
+  if (md.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > 2 * n_q) return cudaErrorInvalidValue;
   const int s1 = T.log_n / 2;
-  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
-  switch (s1) {
-    case 6: k_moddown_cols<6><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T); break;
-    case 7: k_moddown_cols<7><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T); break;
-    case 8: k_moddown_cols<8><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T); break;
-    default: return cudaErrorInvalidValue;
+  for (int part = 0; part < 2; ++part) {
+    const int job0 = part == 0 ? 0 : n_fp, cnt = part == 0 ? n_fp : 2 * n_q - n_fp;
+    if (cnt == 0) continue;
+    dim3 grid(col_tiles(T.log_n, s1), cnt);
+    switch (s1) {
+      case 6: launch_moddown_cols<6>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
+      case 7: launch_moddown_cols<7>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
+      case 8: launch_moddown_cols<8>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
+      default: return cudaErrorInvalidValue;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
   }
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,

@@ -18,16 +18,19 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
 // where v_i are the digit's scaled coefficient limbs (v_all at limb slot
 // src_slot[d*alpha + i]).  Result (column pass done) -> t[d][s].
+// The first n_fp jobs have targets below kFpBound (FP64 kernel), the rest
+// run the integer kernel.
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
-                             const NttTables &T, cudaStream_t s);
+                             int n_fp, const NttTables &T, cudaStream_t s);
 
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
 // scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].
+// job_ps[2*n_q] lists p*n_q + s, the first n_fp with q_j below kFpBound.
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
-                               const int *q_index, const ModDownDev &md, const NttTables &T,
-                               cudaStream_t s);
+                               const int *q_index, const ModDownDev &md, const int *job_ps,
+                               int n_fp, const NttTables &T, cudaStream_t s);
 
 // Row pass of z[p][s] with the ModDown finish in the epilogue:
 //   o = (cx[p][cx_slot[s]] - z) * P^-1 mod q_j;

@@ -19,6 +19,7 @@ struct ModUpDev {
   const ulonglong2 *qhatinv;  // [beta][alpha] {[(Q_d/q_i)^-1]_{q_i}, Shoup}
   const u64 *w;               // [beta][QlP][alpha] [Q_d/q_i]_{m_j}
   const u64 *wsh;             // same layout: Shoup companions of w w.r.t. m_j
+  const double *wq;           // same layout: fl(w / m_j) for FP64 primes m_j
 };
 
 // Constants of the conversion P -> Q (ModDown), indexed by Q limb j.

@@ -262,19 +262,16 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
 
 // Forward column pass; load() gives canonical uint64, store() receives the
 // bits of the pass result (|x| < q + 8 * 0.57q).
-template <int LOG_M, class Fill, class Store>
-__device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double2 *tw, const PrimeDev &P, Fill &&fill,
-                                            Store &&store) {
+// filld(x) fills signed integer-valued doubles (|x| < 8q keeps every later
+// product input below 2^50 for q < kFpBound).
+template <int LOG_M, class FillD, class Store>
+__device__ __forceinline__ void fwd_cols_fpd(u64 *sm, int col, int t, int c, int log_n,
+                                             const double2 *tw, const PrimeDev &P, FillD &&filld,
+                                             Store &&store) {
   using G = ColGeom<LOG_M>;
   const int gofs = log_n - LOG_M;
   double x[kEpt];
-  {
-    u64 xin[kEpt];
-    fill(xin);
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(xin[e]);
-  }
+  filld(x);
   fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, gofs, log_n, tw, P.qd);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = fp_bits(x[e]);
@@ -284,6 +281,19 @@ __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int 
   fwd_round_fp<LOG_M, 0, G::NLO>(x, t, 0, gofs, log_n, tw, P.qd);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) store(lidx<LOG_M, 0, G::NLO>(t, e), col, fp_bits(x[e]));
+}
+
+template <int LOG_M, class Fill, class Store>
+__device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
+                                            const double2 *tw, const PrimeDev &P, Fill &&fill,
+                                            Store &&store) {
+  auto filld = [&](double (&x)[kEpt]) {
+    u64 xin[kEpt];
+    fill(xin);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(xin[e]);
+  };
+  fwd_cols_fpd<LOG_M>(sm, col, t, c, log_n, tw, P, filld, store);
 }
 
 // Inverse column pass (second pass); load() gives the bits of the first
