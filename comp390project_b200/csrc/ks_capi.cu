@@ -745,7 +745,7 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
     StageTimer tm(c, ST_MODUP_BCONV, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
                              lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s));
-    c.launches += (lv.n_jobs_fp > 0) + (lv.n_jobs > lv.n_jobs_fp);
+    c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
   {
     StageTimer tm(c, ST_MODUP_NTT, s);
@@ -791,7 +791,7 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
     StageTimer tm(c, ST_MODDOWN_BCONV, s);
     KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md,
                                lv.md_job_ps.d, lv.n_md_fp, T, s));
-    c.launches += (lv.n_md_fp > 0) + (2 * lv.n_q > lv.n_md_fp);
+    c.launches += lv.n_q > 0 ? 1 : 0;
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {

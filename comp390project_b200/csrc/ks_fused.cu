@@ -111,9 +111,9 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
 // ---------------------------------------------------------------------------
 // ModUp: base conversion + forward column pass
 // ---------------------------------------------------------------------------
-// One instantiation per arithmetic path keeps the register count of each at
-// what that path needs: FP = jobs whose target prime is below kFpBound.
-template <int LOG_M, bool FP>
+// The arithmetic path is chosen per CTA from the target prime (FP64 below
+// kFpBound, integer above); jobs are ordered FP64 first.
+template <int LOG_M>
 __global__ void __launch_bounds__(kThreads, 2)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
   u64 *out = t + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if constexpr (FP) {
+  if (P.q < kFpBound) {
     const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
     auto filld = [&](double (&x)[kEpt]) {
       bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src, src_prime, mu.w + wo, mu.wq + wo,
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
-template <int LOG_M, bool FP>
+template <int LOG_M>
 __global__ void __launch_bounds__(kThreads, 2)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
                    int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if constexpr (FP) {
+  if (P.q < kFpBound) {
     fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, fill, store);
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
@@ -257,42 +257,21 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
   return cudaGetLastError();
 }
 
-template <int LOG_M>
-void launch_modup_cols(dim3 grid, bool fp, int job0, cudaStream_t s, const u64 *v_all,
-                       const int *src_slot, u64 *t, const ModUpDev &mu, const KsLayout &lay,
-                       const int *job_d, const int *job_s, const NttTables &T) {
-  if (fp) k_modup_cols<LOG_M, true><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, job0, T);
-  else k_modup_cols<LOG_M, false><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, job0, T);
-}
-
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
                              int n_fp, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_jobs < 0 || n_jobs > 65535) return cudaErrorInvalidValue;
   if (mu.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > n_jobs) return cudaErrorInvalidValue;
+  if (n_jobs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  for (int part = 0; part < 2; ++part) {
-    const int job0 = part == 0 ? 0 : n_fp, cnt = part == 0 ? n_fp : n_jobs - n_fp;
-    if (cnt == 0) continue;
-    dim3 grid(col_tiles(T.log_n, s1), cnt);
-    switch (s1) {
-      case 6: launch_modup_cols<6>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-      case 7: launch_modup_cols<7>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-      case 8: launch_modup_cols<8>(grid, part == 0, job0, s, v_all, src_slot, t, mu, lay, job_d, job_s, T); break;
-      default: return cudaErrorInvalidValue;
-    }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  dim3 grid(col_tiles(T.log_n, s1), n_jobs);
+  switch (s1) {
+    case 6: k_modup_cols<6><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 7: k_modup_cols<7><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 8: k_modup_cols<8><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    default: return cudaErrorInvalidValue;
   }
-  return cudaSuccess;
-}
-
-template <int LOG_M>
-void launch_moddown_cols(dim3 grid, bool fp, int job0, cudaStream_t s, const u64 *y_base,
-                         const long long *y_off, u64 *z, int n_q, const int *q_index,
-                         const ModDownDev &md, const NttTables &T, const int *job_ps) {
-  if (fp) k_moddown_cols<LOG_M, true><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, job0);
-  else k_moddown_cols<LOG_M, false><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, job0);
+  return cudaGetLastError();
 }
 
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
@@ -300,21 +279,16 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
                                int n_fp, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
   if (md.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > 2 * n_q) return cudaErrorInvalidValue;
+  if (n_q == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  for (int part = 0; part < 2; ++part) {
-    const int job0 = part == 0 ? 0 : n_fp, cnt = part == 0 ? n_fp : 2 * n_q - n_fp;
-    if (cnt == 0) continue;
-    dim3 grid(col_tiles(T.log_n, s1), cnt);
-    switch (s1) {
-      case 6: launch_moddown_cols<6>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
-      case 7: launch_moddown_cols<7>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
-      case 8: launch_moddown_cols<8>(grid, part == 0, job0, s, y_base, y_off, z, n_q, q_index, md, T, job_ps); break;
-      default: return cudaErrorInvalidValue;
-    }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
+  switch (s1) {
+    case 6: k_moddown_cols<6><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 7: k_moddown_cols<7><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 8: k_moddown_cols<8><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    default: return cudaErrorInvalidValue;
   }
-  return cudaSuccess;
+  return cudaGetLastError();
 }
 
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,

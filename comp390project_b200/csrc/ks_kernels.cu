@@ -103,32 +103,17 @@ __global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ 
   const int dj = j < mu.Ql ? j / mu.alpha : -1;  // digit holding limb j
   u128v a00 = {0, 0}, a01 = {0, 0}, a10 = {0, 0}, a11 = {0, 0};
   const long long kstride = (long long)key_limbs * N;
-  // Digits in groups of four with every load of a group issued before its
-  // multiply-accumulates (memory-level parallelism); key words are streamed
-  // once, so they bypass L1 and are marked evict-first in L2.
-  for (int d0 = 0; d0 < mu.beta; d0 += 4) {
-    ulonglong2 xv[4], bv[4], av[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int d = d0 + u;
-      if (d < mu.beta) {
-        const u64 *src = (d == dj) ? c_ntt + (long long)lay.c_slot[s] * N
-                                   : t + ((long long)d * lay.n_out + s) * N;
-        xv[u] = *reinterpret_cast<const ulonglong2 *>(src + k);
-        const u64 *kb = key + (long long)(2 * d) * kstride + ks * N + k;
-        bv[u] = __ldcs(reinterpret_cast<const ulonglong2 *>(kb));
-        av[u] = __ldcs(reinterpret_cast<const ulonglong2 *>(kb + kstride));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (d0 + u < mu.beta) {
-        mac(a00, xv[u].x, bv[u].x);
-        mac(a01, xv[u].y, bv[u].y);
-        mac(a10, xv[u].x, av[u].x);
-        mac(a11, xv[u].y, av[u].y);
-      }
-    }
+  for (int d = 0; d < mu.beta; ++d) {
+    const u64 *src = (d == dj) ? c_ntt + (long long)lay.c_slot[s] * N
+                               : t + ((long long)d * lay.n_out + s) * N;
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(src + k);
+    const u64 *kb = key + (long long)(2 * d) * kstride + ks * N + k;
+    const ulonglong2 b = __ldg(reinterpret_cast<const ulonglong2 *>(kb));
+    const ulonglong2 a = __ldg(reinterpret_cast<const ulonglong2 *>(kb + kstride));
+    mac(a00, x.x, b.x);
+    mac(a01, x.y, b.y);
+    mac(a10, x.x, a.x);
+    mac(a11, x.y, a.y);
   }
   ulonglong2 r0, r1;
   r0.x = barrett128(a00, P.q, P.br_hi, P.br_lo);
