@@ -131,7 +131,7 @@ void build_tables(Ctx &c) {
   const int N = c.N, K = c.K;
   std::vector<PrimeDev> pd(K);
   std::vector<ulonglong2> fwd((size_t)K * N), inv((size_t)K * N);
-  std::vector<double2> fwd_fp((size_t)K * N, make_double2(0, 0)), inv_fp((size_t)K * N, make_double2(0, 0));
+  std::vector<double> fwd_fp((size_t)K * N, 0.0), inv_fp((size_t)K * N, 0.0);
   std::vector<std::thread> th;
   auto work = [&](int k) {
     const u64 q = c.primes[k];
@@ -147,8 +147,8 @@ void build_tables(Ctx &c) {
       fwd[(size_t)k * N + i] = make_ulonglong2(pw[r], h_shoup(pw[r], q));
       inv[(size_t)k * N + i] = make_ulonglong2(pwi[r], h_shoup(pwi[r], q));
       if (q < kFpBound) {
-        fwd_fp[(size_t)k * N + i] = make_double2((double)pw[r], (double)pw[r] / (double)q);
-        inv_fp[(size_t)k * N + i] = make_double2((double)pwi[r], (double)pwi[r] / (double)q);
+        fwd_fp[(size_t)k * N + i] = (double)pw[r];
+        inv_fp[(size_t)k * N + i] = (double)pwi[r];
       }
     }
     PrimeDev &P = pd[k];

@@ -77,7 +77,7 @@ struct Ctx {
   std::vector<PrimeDev> h_primes;
   PrimeDev *d_primes = nullptr;
   ulonglong2 *d_tw_fwd = nullptr, *d_tw_inv = nullptr;
-  double2 *d_tw_fwd_fp = nullptr, *d_tw_inv_fp = nullptr;
+  double *d_tw_fwd_fp = nullptr, *d_tw_inv_fp = nullptr;
   u64 *d_gauss = nullptr;
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;

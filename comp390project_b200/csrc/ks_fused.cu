@@ -191,7 +191,9 @@ __global__ void __launch_bounds__(kThreads)
                    long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0, int rotate,
                    ModDownDev md, NttTables T) {
   using G = RowGeom<LOG_M>;
-  __shared__ u64 sm[G::SMEM];
+  extern __shared__ __align__(16) u64 dsm[];
+  u64 *sm = dsm;
+  double *smtw = reinterpret_cast<double *>(dsm + G::SMEM);
   const int p = blockIdx.y / n_q, s = blockIdx.y % n_q;
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
@@ -199,11 +201,13 @@ __global__ void __launch_bounds__(kThreads)
   const int t = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const long long tile0 = (long long)blockIdx.x * kTile;
   const u64 *tile = z + ((long long)p * n_q + s) * N + tile0;
-  const long long row = (long long)blockIdx.x * G::R + rr;
+  const long long row0 = (long long)blockIdx.x * G::R, row = row0 + rr;
   const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N + tile0;
   u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N + tile0;
   const u64 *base =
       (p == 0) ? (rotate ? g0 + (long long)s * N + tile0 : dst) : (rotate ? nullptr : dst);
+  const bool fp = P.q < kFpBound;
+  if (fp) stage_row_twiddles<LOG_M, G::R>(smtw, T.fwd_fp + (long long)j * N, log_n, row0);
   // Pull the epilogue operands into L2 while the butterflies run: one
   // prefetch per 128-byte line of the tile (4096 words = 256 lines).
   {
@@ -212,8 +216,10 @@ __global__ void __launch_bounds__(kThreads)
     if (base) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + line));
   }
   u64 x[kEpt];
-  if (P.q < kFpBound) {
-    fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, T.fwd_fp + (long long)j * N, P);
+  if (fp) {
+    cp_async_wait_all();
+    __syncthreads();
+    fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
     if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
@@ -230,6 +236,24 @@ __global__ void __launch_bounds__(kThreads)
     const u64 o = mul_shoup(cxp[lin] + P.q - zv, pinv.x, pinv.y, P.q);
     dst[lin] = base ? add_mod(base[lin], o, P.q) : o;
   }
+}
+
+template <int LOG_M>
+cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q,
+                               const int *q_index, const int *cx_slot, const u64 *cx,
+                               long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0,
+                               int rot, const ModDownDev &md, const NttTables &T) {
+  constexpr size_t smem = row_smem_bytes<LOG_M>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_moddown_rows<LOG_M>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  k_moddown_rows<LOG_M><<<grid, kThreads, smem, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly,
+                                                     ct0, ct1, g0, rot, md, T);
+  return cudaGetLastError();
 }
 
 inline int col_tiles(int log_n, int log_m) {
@@ -301,12 +325,11 @@ cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const 
   dim3 grid((1 << T.log_n) / kTile, 2 * n_q);
   const int rot = rotate ? 1 : 0;
   switch (s2) {
-    case 6: k_moddown_rows<6><<<grid, kThreads, 0, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T); break;
-    case 7: k_moddown_rows<7><<<grid, kThreads, 0, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T); break;
-    case 8: k_moddown_rows<8><<<grid, kThreads, 0, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T); break;
+    case 6: return launch_moddown_rows<6>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
+    case 7: return launch_moddown_rows<7>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
+    case 8: return launch_moddown_rows<8>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace ksb

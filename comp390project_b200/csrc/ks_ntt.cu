@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   auto fill = [&](u64 (&x)[kEpt]) { fill_cols<LOG_M>(x, t, col, load); };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
-    const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
+    const double *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
     if (FWD) {
       fwd_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, fill, store);
     } else {
@@ -55,7 +55,9 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
 template <int LOG_M, bool FWD>
 __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T) {
   using G = RowGeom<LOG_M>;
-  __shared__ u64 sm[G::SMEM];
+  extern __shared__ __align__(16) u64 dsm[];
+  u64 *sm = dsm;
+  double *smtw = reinterpret_cast<double *>(dsm + G::SMEM);
   u64 *a, *o;
   int prime, prime_o;
   limb_of(m, blockIdx.y, a, prime);
@@ -67,14 +69,23 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
   const int t = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const u64 *tile = a + (long long)blockIdx.x * kTile;
   u64 *otile = o + (long long)blockIdx.x * kTile;
-  const long long row = (long long)blockIdx.x * G::R + rr;
+  const long long row0 = (long long)blockIdx.x * G::R, row = row0 + rr;
   u64 x[kEpt];
-  const double2 *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
   const bool fp = P.q < kFpBound;
+  if (fp) {
+    stage_row_twiddles<LOG_M, G::R>(smtw, (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N,
+                                    log_n, row0);
+  }
   if (FWD) {
-    if (fp) fwd_rows_regs_fp<LOG_M>(x, sm, tile, t, rr, row, log_n, twf, P);
-    else if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
-    else fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
+    if (fp) {
+      cp_async_wait_all();
+      __syncthreads();
+      fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
+    } else if (P.q < kFwdLazyBound) {
+      fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
+    } else {
+      fwd_rows_regs<LOG_M, false>(x, sm, tile, t, rr, row, log_n, tw, P);
+    }
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
     __syncthreads();
@@ -89,8 +100,9 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
       const int lin = threadIdx.x + i * kThreads;
       sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))] = tile[lin];
     }
+    if (fp) cp_async_wait_all();
     __syncthreads();
-    if (fp) inv_rows_regs_fp<LOG_M>(x, sm, t, rr, row, log_n, twf, P);
+    if (fp) inv_rows_regs_fp<LOG_M>(x, sm, smtw, t, rr, row, row0, P);
     else if (P.q < kInvLazyBound) inv_rows_regs<LOG_M, true>(x, sm, t, rr, row, log_n, tw, P);
     else inv_rows_regs<LOG_M, false>(x, sm, t, rr, row, log_n, tw, P);
 #pragma unroll
@@ -108,8 +120,16 @@ cudaError_t launch_cols(const LimbMap &m, int n_limbs, const NttTables &T, cudaS
 template <int LOG_M, bool FWD>
 cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
                         cudaStream_t s) {
+  constexpr size_t smem = row_smem_bytes<LOG_M>();
+  static bool attr_set = false;  // idempotent; one call per instantiation suffices
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(ntt_rows<LOG_M, FWD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
   dim3 grid((1 << T.log_n) / kTile, n_limbs);
-  ntt_rows<LOG_M, FWD><<<grid, kThreads, 0, s>>>(m, mo, T);
+  ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T);
   return cudaGetLastError();
 }
 

@@ -26,8 +26,8 @@ struct NttTables {
   const ulonglong2 *inv;  // [n_primes][N] {w, w_shoup}, w = psi^-brev(i)
   const PrimeDev *primes; // [n_primes]
   int log_n;
-  const double2 *fwd_fp;  // [n_primes][N] {w, fl(w/q)} (used for primes below kFpBound)
-  const double2 *inv_fp;
+  const double *fwd_fp;   // [n_primes][N] w as a double (primes below kFpBound)
+  const double *inv_fp;
 };
 
 // Transforms n_limbs limbs in place; outputs are canonical in [0, q).

@@ -207,42 +207,90 @@ __device__ __forceinline__ void inv_rows_regs(u64 (&x)[kEpt], u64 *sm, int t, in
 // ===========================================================================
 // FP64 variants (primes below kFpBound).  Values travel between the passes as
 // the bits of signed integer-valued doubles; the pass inputs and the final
-// outputs are canonical uint64.  Twiddle tables hold {w, fl(w/q)} doubles.
+// outputs are canonical uint64.  Twiddle tables hold w (a double); the
+// quotient factor fl(w/q) is formed as w * fl(1/q) next to its use, which
+// keeps the estimate error below |y| 2^-52 <= 2^-4 for |y| <= 2^48 (every
+// product input of these passes stays below 2^48 for q < kFpBound).
+//
+// A twiddle getter tw(b, H) returns psi^(+-brev) of the pair at local bit b
+// whose lower element has extended index H = (prefix << LOG_M) | local.
 // ===========================================================================
 __device__ __forceinline__ double as_fp(u64 b) { return __longlong_as_double((long long)b); }
 __device__ __forceinline__ u64 fp_bits(double d) { return (u64)__double_as_longlong(d); }
 
+// Global-table getter (column passes: every column of a CTA shares them).
+struct TwGlobal {
+  const double *tw;
+  int log_n, gofs;
+  __device__ __forceinline__ double operator()(int b, long long H) const {
+    return __ldg(&tw[(1 << (log_n - 1 - b - gofs)) + (int)(H >> (b + 1))]);
+  }
+};
+
+// Shared-memory getter for a row pass over rows [row0, row0 + R): the block
+// of local bit b holds R * 2^u twiddles, u = LOG_M - 1 - b, at offset
+// R (2^u - 1).
+template <int LOG_M, int R>
+struct TwRowsSmem {
+  const double *sm;
+  long long row0;
+  __device__ __forceinline__ double operator()(int b, long long H) const {
+    const int u = LOG_M - 1 - b;
+    return sm[R * ((1 << u) - 1) + (int)((H >> (b + 1)) - (row0 << u))];
+  }
+};
+
+// Issues cp.async copies of the row-pass twiddle block (R (M - 1) doubles)
+// of rows [row0, row0 + R) into sm; the caller waits with cp_async_wait_all.
+// Block u (u = 0..LOG_M-1) is tw[2^(logN-LOG_M+u) + row0 2^u, +R 2^u); with R
+// even every block starts and ends on a 16-byte boundary.
+template <int LOG_M, int R>
+__device__ __forceinline__ void stage_row_twiddles(double *sm, const double *tw, int log_n,
+                                                   long long row0) {
+  constexpr int M = 1 << LOG_M, TOTAL = R * (M - 1);
+  static_assert(R % 2 == 0, "row blocks must be 16-byte multiples");
+  for (int ch = threadIdx.x; ch < TOTAL / 2; ch += kThreads) {
+    const int e = 2 * ch;
+    const int u = 31 - __clz(e / R + 1);
+    const int o = e - R * ((1 << u) - 1);
+    const double *g = tw + (1ll << (log_n - LOG_M + u)) + (row0 << u) + o;
+    const unsigned s = (unsigned)__cvta_generic_to_shared(sm + e);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(g) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Bound: operands < B on entry -> < B + 4 * 0.57q on exit (additive growth).
-template <int LOG_M, int LO, int NB>
-__device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long prefix, int gofs,
-                                             int log_n, const double2 *__restrict__ tw, double q) {
+template <int LOG_M, int LO, int NB, class Tw>
+__device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long prefix,
+                                             const Tw &tw, double q, double qinv) {
 #pragma unroll
   for (int k = NB - 1; k >= 0; --k) {
     const int b = LO + k;
-    const int base = 1 << (log_n - 1 - b - gofs);
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
       const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
-      const double2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
-      fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
+      const double w = tw(b, H);
+      fp_ct_bfly(x[e], x[e | (1 << k)], w, __dmul_rn(w, qinv), q);
     }
   }
 }
 
 // Every operand is reduced to |x| <= q/2 (+1) on entry, so within the round
-// the sums stay below 2^NB * 0.57q and every product input below 2^50.
-template <int LOG_M, int LO, int NB, bool LAST>
-__device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long prefix, int gofs,
-                                             int log_n, const double2 *__restrict__ tw,
-                                             const PrimeDev &P, double2 s0, double2 s1) {
+// the sums stay below 2^NB * 0.57q and every product input below 2^48.
+template <int LOG_M, int LO, int NB, bool LAST, class Tw>
+__device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long prefix,
+                                             const Tw &tw, const PrimeDev &P, double2 s0,
+                                             double2 s1) {
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = fp_reduce_sym(x[e], P.qd, P.qinv);
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
     const int b = LO + k;
-    const int gb = b + gofs;
-    const int base = 1 << (log_n - 1 - gb);
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
@@ -253,39 +301,36 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
         Y = fp_mulmod(d, s1.x, s1.y, P.qd);
       } else {
         const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
-        const double2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
-        fp_gs_bfly(X, Y, w.x, w.y, P.qd);
+        const double w = tw(b, H);
+        fp_gs_bfly(X, Y, w, __dmul_rn(w, P.qinv), P.qd);
       }
     }
   }
 }
 
-// Forward column pass; load() gives canonical uint64, store() receives the
-// bits of the pass result (|x| < q + 8 * 0.57q).
-// filld(x) fills signed integer-valued doubles (|x| < 8q keeps every later
-// product input below 2^50 for q < kFpBound).
+// filld(x) fills signed integer-valued doubles (|x| < 8q).
 template <int LOG_M, class FillD, class Store>
 __device__ __forceinline__ void fwd_cols_fpd(u64 *sm, int col, int t, int c, int log_n,
-                                             const double2 *tw, const PrimeDev &P, FillD &&filld,
+                                             const double *tw, const PrimeDev &P, FillD &&filld,
                                              Store &&store) {
   using G = ColGeom<LOG_M>;
-  const int gofs = log_n - LOG_M;
+  const TwGlobal twg{tw, log_n, log_n - LOG_M};
   double x[kEpt];
   filld(x);
-  fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, gofs, log_n, tw, P.qd);
+  fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, twg, P.qd, P.qinv);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c] = fp_bits(x[e]);
   __syncthreads();
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c]);
-  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, 0, gofs, log_n, tw, P.qd);
+  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, 0, twg, P.qd, P.qinv);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) store(lidx<LOG_M, 0, G::NLO>(t, e), col, fp_bits(x[e]));
 }
 
 template <int LOG_M, class Fill, class Store>
 __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double2 *tw, const PrimeDev &P, Fill &&fill,
+                                            const double *tw, const PrimeDev &P, Fill &&fill,
                                             Store &&store) {
   auto filld = [&](double (&x)[kEpt]) {
     u64 xin[kEpt];
@@ -300,66 +345,77 @@ __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int 
 // pass result, store() receives canonical uint64 times the last-stage scale.
 template <int LOG_M, class Load, class Store>
 __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double2 *tw, const PrimeDev &P, double2 s0,
+                                            const double *tw, const PrimeDev &P, double2 s0,
                                             double2 s1, Load &&load, Store &&store) {
   using G = ColGeom<LOG_M>;
-  const int gofs = log_n - LOG_M;
+  const TwGlobal twg{tw, log_n, log_n - LOG_M};
   double x[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(load(lidx<LOG_M, 0, G::NLO>(t, e), col));
-  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, 0, twg, P, s0, s1);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c] = fp_bits(x[e]);
   __syncthreads();
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c]);
-  inv_round_fp<LOG_M, G::HI, 4, true>(x, t, 0, gofs, log_n, tw, P, s0, s1);
+  inv_round_fp<LOG_M, G::HI, 4, true>(x, t, 0, twg, P, s0, s1);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e)
     store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
 }
 
-// Forward row pass; the tile holds first-pass bits; canonical outputs in x.
+// Forward row pass; the tile holds first-pass bits; canonical outputs in xo.
+// smtw: this CTA's twiddle block, staged by stage_row_twiddles (the caller
+// waits for it and synchronises before calling).
 template <int LOG_M>
-__device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const u64 *tile, int t,
-                                                 int rr, long long row, int log_n,
-                                                 const double2 *tw, const PrimeDev &P) {
+__device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
+                                                 const u64 *tile, int t, int rr, long long row,
+                                                 long long row0, const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
+  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0};
   double x[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)]);
-  fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, 0, log_n, tw, P.qd);
+  fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, tw, P.qd, P.qinv);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))] = fp_bits(x[e]);
   __syncwarp();
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))]);
-  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, 0, log_n, tw, P.qd);
+  fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, tw, P.qd, P.qinv);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) xo[e] = fp_to_canon(x[e], P.qd, P.qinv);
   __syncwarp();
 }
 
 // Inverse row pass (first pass) over a tile staged in smem as canonical
-// uint64; outputs (bits of doubles) in xo, pattern HI.
+// uint64; outputs (bits of doubles, |x| <= q/2 + 1) in xo, pattern HI.
 template <int LOG_M>
-__device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, int t, int rr,
-                                                 long long row, int log_n, const double2 *tw,
+__device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
+                                                 int t, int rr, long long row, long long row0,
                                                  const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
+  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0};
   const double2 none = make_double2(0, 0);
   double x[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = u64_to_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))]);
-  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, row, 0, log_n, tw, P, none, none);
+  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, row, tw, P, none, none);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = fp_bits(x[e]);
   __syncwarp();
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))]);
-  inv_round_fp<LOG_M, G::HI, 4, false>(x, t, row, 0, log_n, tw, P, none, none);
+  inv_round_fp<LOG_M, G::HI, 4, false>(x, t, row, tw, P, none, none);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) xo[e] = fp_bits(fp_reduce_sym(x[e], P.qd, P.qinv));
+}
+
+// Shared memory of a row-pass CTA: the exchange buffer then (FP64 path) the
+// twiddle block.
+template <int LOG_M>
+constexpr size_t row_smem_bytes() {
+  return (size_t)RowGeom<LOG_M>::SMEM * 8 + (size_t)RowGeom<LOG_M>::R * ((1 << LOG_M) - 1) * 8;
 }
 
 }  // namespace ntt
