@@ -1,0 +1,130 @@
+"""Multi-GPU key switching through the C ABI: one process per GPU, NCCL
+communicators created by the library from an id broadcast over a gloo
+process group; every rank holds its cyclic share of the limbs.  The gathered
+result must equal the single-process CPU oracle bit for bit.  Skipped when
+fewer than two GPUs are visible."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, name, q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from comp390project_b200 import KS_KEY_GALOIS, KS_KEY_RELIN, KsContext
+        from tests.ksparams import oracle_for, split, CFG3, SMALL
+        cfg = {"small": SMALL, "cfg3": CFG3}[name]
+        o = oracle_for(name)
+        log_n, qs, ps = split(cfg)
+        N, L = o.N, o.L
+        Ql = L
+        ctx = KsContext.from_process_group(log_n, qs, ps, device=rank, max_batch=2)
+        ctx.set_timeout_ms(60000)
+        s = o.secret(11, 64 if name == "small" else 192)
+        steps = [1, 3]
+        keys = {}
+        for st in steps:
+            e = o.galois_elt(st)
+            keys[st] = o.keygen_galois(s, e, 500 + st)
+        ctx.key_upload(KS_KEY_GALOIS, o.galois_elt(1), keys[1])  # host upload of the shard
+        ctx.key_generate(KS_KEY_GALOIS, o.galois_elt(3), s, 503)  # device generation of the shard
+        rk = o.keygen_relin(s, 600)
+        ctx.key_upload(KS_KEY_RELIN, 0, rk)
+        rng = np.random.default_rng(77)
+        cts = [np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
+                                   for j in range(Ql)]) for _ in range(2)]) for _ in steps]
+        c3 = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
+                                 for j in range(Ql)]) for _ in range(3)])
+        mine = list(range(rank, Ql, world))
+
+        def local(ct):
+            return torch.from_numpy(np.ascontiguousarray(ct[:, mine]).view(np.int64)).cuda()
+
+        def gather(t, n_polys):
+            h = torch.zeros((n_polys, (Ql + world - 1) // world, N), dtype=torch.int64)
+            h[:, :len(mine)] = t.cpu()[:n_polys]
+            out = [torch.zeros_like(h) for _ in range(world)]
+            dist.all_gather(out, h)
+            full = np.zeros((n_polys, Ql, N), dtype=np.uint64)
+            for j in range(Ql):
+                full[:, j] = out[j % world][:, j // world].numpy().view(np.uint64)
+            return full
+
+        ok = True
+        # single rotation
+        d = local(cts[0])
+        ctx.rotate(d, Ql, steps[0])
+        torch.cuda.synchronize()
+        ok &= np.array_equal(gather(d, 2), o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
+        # batch over two lanes (each with its own split communicator)
+        ds = [local(c) for c in cts]
+        ctx.rotate_batch(ds, steps, Ql)
+        torch.cuda.synchronize()
+        for c, dd, st in zip(cts, ds, steps):
+            ok &= np.array_equal(gather(dd, 2), o.apply_galois(c, Ql, o.galois_elt(st), keys[st]))
+        # relinearisation
+        d3 = local(c3)
+        ctx.relinearize(d3, Ql)
+        torch.cuda.synchronize()
+        ok &= np.array_equal(gather(d3, 2), o.relinearize(c3, Ql, rk))
+        # a lower level (short last digit)
+        Ql2 = Ql - 3
+        c2 = cts[0][:, :Ql2]
+        mine2 = list(range(rank, Ql2, world))
+        d2 = torch.from_numpy(np.ascontiguousarray(c2[:, mine2]).view(np.int64)).cuda()
+        ctx.rotate(d2, Ql2, 1)
+        torch.cuda.synchronize()
+        h = torch.zeros((2, (Ql2 + world - 1) // world, N), dtype=torch.int64)
+        h[:, :len(mine2)] = d2.cpu()
+        outs = [torch.zeros_like(h) for _ in range(world)]
+        dist.all_gather(outs, h)
+        full2 = np.zeros((2, Ql2, N), dtype=np.uint64)
+        for j in range(Ql2):
+            full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
+        ok &= np.array_equal(full2, o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
+        ctx.close()
+        q.put((rank, bool(ok)))
+    except Exception as e:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name", ["small", "cfg3"])
+def test_two_gpu_keyswitch_bitexact(name, cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    assert all(v is True for v in res.values()), res
