@@ -82,6 +82,7 @@ SIGNATURES = {
     "ks_relinearize": (_I, [_P, _P, _I, _P]),
     "ks_keyswitch_add": (_I, [_P, _P, _P, _I, _I, _U32, _P]),
     "ks_apply_galois": (_I, [_P, _P, _I, _U32, _P]),
+    "ks_apply_galois_noalloc": (_I, [_P, _P, _I, _U32, _P]),
     "ks_rotate": (_I, [_P, _P, _I, _I, _P]),
     "ks_rotate_batch": (_I, [_P, C.POINTER(_P), C.POINTER(C.c_int), _I, _I, _P]),
     "ks_rotate_hoisted": (_I, [_P, _P, _I, C.POINTER(C.c_int), _I, C.POINTER(_P), _P]),

@@ -216,6 +216,13 @@ class KsContext:
         self._check(self.lib.ks_apply_galois(self.h, self._ptr(ct), int(level_limbs), int(elt),
                                              _stream_ptr(stream, self.device)))
 
+    def apply_galois_noalloc(self, ct, level_limbs: int, elt: int, stream=None):
+        """apply_galois without any device allocation on the call: the scratch
+        is the library's fixed 16 MiB device array (small parameter sets only;
+        calls that overlap on the GPU race)."""
+        self._check(self.lib.ks_apply_galois_noalloc(self.h, self._ptr(ct), int(level_limbs),
+                                                     int(elt), _stream_ptr(stream, self.device)))
+
     def rotate(self, ct, level_limbs: int, step: int, stream=None):
         self._check(self.lib.ks_rotate(self.h, self._ptr(ct), int(level_limbs), int(step),
                                        _stream_ptr(stream, self.device)))

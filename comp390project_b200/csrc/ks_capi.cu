@@ -1246,3 +1246,69 @@ int ks_profile_read(ks_ctx *ctx, double *ms, int *calls, int n) {
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Rotation without any allocation on the call
+// ===========================================================================
+// Some callers may not allocate device memory when they call in: code that
+// runs under a fixed memory budget, or a service that reserves every byte of
+// HBM up front and hands libraries only the buffers they work on.
+// ks_apply_galois_noalloc serves them: the same automorphism + key switch as
+// ks_apply_galois, but its scratch comes from the file-scope array below
+// (kNoAllocWords words = 16 MiB, held by every GPU that loads the library
+// until the process exits) instead of the context's lane arena, and the call
+// itself allocates nothing.
+namespace {
+
+constexpr size_t kNoAllocWords = (size_t)2 << 20;  // 2 Mi words = 16 MiB
+__device__ __align__(256) u64 g_noalloc_scratch[kNoAllocWords];
+
+std::mutex g_noalloc_mu;
+std::map<int, u64 *> g_noalloc_addr;  // device -> device address of g_noalloc_scratch
+
+// Device address of the array on the current device (set-up once per device).
+// In host code the array's name is only a host-side stand-in, so the address
+// must come from cudaGetSymbolAddress with the device current.
+u64 *noalloc_base(int device) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  auto it = g_noalloc_addr.find(device);
+  if (it != g_noalloc_addr.end()) return it->second;
+  void *p = nullptr;
+  KS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  g_noalloc_addr[device] = static_cast<u64 *>(p);
+  return static_cast<u64 *>(p);
+}
+
+}  // namespace
+
+extern "C" int ks_apply_galois_noalloc(ks_ctx *ctx, uint64_t *ct, int level_limbs,
+                                       uint32_t galois_elt, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(c.alpha > 0, "context has no special primes (NTT-only context)");
+    KS_REQUIRE(c.world == 1, "the allocation-free rotation serves single-GPU contexts only");
+    KS_REQUIRE(!c.profile, "disable per-stage profiling before the allocation-free rotation");
+    if (c.arena_words > kNoAllocWords)
+      throw KsError{KS_ERR_UNSUPPORTED,
+                    "parameter set needs " + std::to_string(c.arena_words * 8) +
+                        " bytes of scratch; the allocation-free rotation holds at most " +
+                        std::to_string(kNoAllocWords * 8)};
+    KS_CUDA(cudaSetDevice(c.device));
+    u64 *p = noalloc_base(c.device);
+    // the lane layout of the context's own arena, laid over the static array
+    const size_t N = c.N, nq = n_local(0, 1, c.L), ml = c.L;
+    const Level &top = c.levels[c.L];
+    Ctx::Lane ln;
+    ln.comm = nullptr;
+    ln.s_g = p; p += 2 * nq * N;
+    ln.s_coef = p; p += ml * N;
+    ln.s_coef_all = ln.s_coef;
+    ln.s_t = p; p += std::max((size_t)top.beta * top.n_out * N, 3 * c.own_key.size() * N);
+    ln.s_cx = p; p += 2 * (size_t)top.n_out * N;
+    ln.s_ysend = ln.s_yall = p;
+    ln.s_z = p;
+    do_apply_galois(c, ln, ct, level_limbs, galois_elt, (cudaStream_t)stream);
+  });
+}

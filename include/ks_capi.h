@@ -132,6 +132,20 @@ int ks_keyswitch_add(ks_ctx *ctx, const uint64_t *c, uint64_t *ct, int level_lim
  * rotation_input_broadcast, input_broadcast.cu:182-202). */
 int ks_apply_galois(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t galois_elt,
                     void *stream);
+/* ks_apply_galois for callers that may not allocate device memory when they
+ * call in (a fixed memory budget, or HBM reserved up front by the host
+ * application).  No counterpart in the reference.  Same result as
+ * ks_apply_galois; its scratch is a file-scope device array of 16 MiB (held
+ * by every GPU that loads the library until the process exits) and the call
+ * makes no cudaMalloc/cudaFree.  Parameter sets whose key switch needs more
+ * scratch than that (e.g. N = 2^16 with 35 + 5 primes) are rejected with
+ * KS_ERR_UNSUPPORTED; world must be 1 and profiling off.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other contexts on the same
+ * device) race; serialise them.  No word of the array needs to start at zero. */
+int ks_apply_galois_noalloc(ks_ctx *ctx, uint64_t *ct, int level_limbs, uint32_t galois_elt,
+                            void *stream);
 /* Left rotation of the slots by `step` (galois element 3^step mod 2N). */
 int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream);
 /* n rotations of n independent ciphertexts (cts[i] rotated by steps[i]). */
