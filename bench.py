@@ -37,6 +37,9 @@ PBITS = [60] * 5
 BATCH = 64
 SCALE = 2.0 ** 40
 METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
+# DRAM bytes per launch (read + write) of each key-switch kernel at config 3,
+# one key switch, from `ncu --set full` (profiles/keyswitch_config3.md).
+PROFILED_TRAFFIC = {}
 
 
 def parse():
@@ -355,19 +358,25 @@ def run_ours(args, rank, world):
     U = 8 * N
     n_out = len(range(rank, L, world)) + sum(1 for i in range(len(p)) if (L + i) % world == rank)
     n_q = nloc
+    # Algorithmic bytes per key switch on this rank (U = one limb): compulsory
+    # inputs once + outputs once of each stage (twiddle/constant tables excluded).
+    n_jobs = beta * n_out - n_q  # extended limbs produced by ModUp (own digit limbs are copies)
+    n_p_own = n_out - n_q
     alg = {
-        "modup_ntt": (beta * n_out - sum(1 for j in range(rank, L, world))) * 2 * U,
-        "inner_product": (beta * n_out * 3 + 2 * n_out) * U,
-        "modup_bconv": (beta * 0 + L) * U + (beta * n_out - n_q) * U,
-        "moddown_ntt": 2 * n_q * 2 * U,
-        "intt_input": n_q * 2 * U,
         "galois": 4 * n_q * U,
-        "moddown_finish": (2 * n_out + 2 * n_q + 3 * n_q) * U,
-        "moddown_bconv": (2 * len(p) + 2 * n_q) * U,
-        "intt_p": 2 * len(p) * 2 * U,
+        "intt_input": 2 * n_q * U,
+        "modup_cols": (L + n_jobs) * U,
+        "modup_rows": 2 * n_jobs * U,
+        "inner_product": (beta * n_out + 2 * beta * n_out + 2 * n_out) * U,
+        "intt_p": 4 * n_p_own * U,
+        "moddown_cols": (2 * len(p) + 2 * n_q) * U,
+        "moddown_rows": 7 * n_q * U,
     }
     peak, peak_kind = measured_peaks()
-    achieved = alg.get(dom, 0) / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
+    achieved = alg[dom] / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
+    # DRAM traffic per launch of the dominant kernel from one ncu capture
+    # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/keyswitch_config3.md)
+    traffic = PROFILED_TRAFFIC.get(dom) if world == 1 else None
 
     # end to end through the C ABI with host buffers (pinned), copies timed
     e2e = None
@@ -414,7 +423,8 @@ def run_ours(args, rank, world):
                        "l2": "inputs (2.3 GB cts + 18.8 GB keys) exceed L2; no flush"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
-                         "traffic": None, "peak_kind": peak_kind,
+                         "traffic": traffic, "peak_kind": peak_kind,
+                         "alg_bytes": alg.get(dom),
                          "launch_ms": per_launch_ms},
             "stages_ms_per_ks_serial": {k: v[0] / prof_ks for k, v in stages.items()},
             "cpu_baseline": cpu,
