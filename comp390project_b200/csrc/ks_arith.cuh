@@ -78,6 +78,16 @@ __device__ __forceinline__ u64 barrett128(u128v x, u64 q, u64 rh, u64 rl) {
   return csub(r, q);
 }
 
+// (acc + x * k) mod q for acc < q, x, k < 2^62 (x * k + acc < 2^125).
+__device__ __forceinline__ u64 mac_reduce(u64 acc, u64 x, u64 k, u64 q, u64 rh, u64 rl) {
+  u128v m;
+  m.lo = x * k;
+  m.hi = __umul64hi(x, k);
+  m.lo += acc;
+  m.hi += m.lo < acc ? 1ull : 0ull;
+  return barrett128(m, q, rh, rl);
+}
+
 // Harvey's forward (Cooley-Tukey) butterfly: X, Y in [0, 4q) -> [0, 4q).
 __device__ __forceinline__ void ct_bfly(u64 &X, u64 &Y, u64 w, u64 wp, u64 q, u64 two_q) {
   u64 x = csub(X, two_q);

@@ -146,9 +146,21 @@ void build_tables(Ctx &c) {
       const uint32_t r = h_brev((uint32_t)i, c.log_n);
       fwd[(size_t)k * N + i] = make_ulonglong2(pw[r], h_shoup(pw[r], q));
       inv[(size_t)k * N + i] = make_ulonglong2(pwi[r], h_shoup(pwi[r], q));
-      if (q < kFpBound) {
-        fwd_fp[(size_t)k * N + i] = (double)pw[r];
-        inv_fp[(size_t)k * N + i] = (double)pwi[r];
+    }
+    if (q < kFpBound) {
+      // FP64 tables: w as a double, row-pass blocks permuted by row_tw_pos
+      const int lm = c.log_n - c.log_n / 2;
+      for (int i = 0; i < N; ++i) {
+        size_t dst = (size_t)i;
+        const int b = c.log_n - 1 - (31 - __builtin_clz((unsigned)std::max(i, 1)));
+        if (i > 0 && b < lm) {  // row-pass local bit b: i = 2^(logN-1-b) + row 2^u + kk
+          const int u = lm - 1 - b;
+          const size_t off = (size_t)i - ((size_t)1 << (c.log_n - 1 - b));
+          const int kk = (int)(off & (((size_t)1 << u) - 1));
+          dst = ((size_t)1 << (c.log_n - 1 - b)) + (off >> u << u) + row_tw_pos(lm, b, kk);
+        }
+        fwd_fp[(size_t)k * N + dst] = (double)fwd[(size_t)k * N + i].x;
+        inv_fp[(size_t)k * N + dst] = (double)inv[(size_t)k * N + i].x;
       }
     }
     PrimeDev &P = pd[k];
@@ -674,12 +686,12 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
 // Optional per-stage timing (bench accounting; off by default)
 // ---------------------------------------------------------------------------
 enum Stage {
-  ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_BCONV, ST_MODUP_NTT, ST_INNER_PROD, ST_INTT_P,
-  ST_MODDOWN_BCONV, ST_MODDOWN_NTT, ST_FINISH, ST_COMM, ST_COUNT
+  ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_COLS, ST_MODUP_ROWS_IP, ST_INTT_P, ST_MODDOWN_COLS,
+  ST_MODDOWN_ROWS, ST_COMM, ST_COUNT
 };
 static const char *kStageNames[ST_COUNT] = {
-    "galois",       "intt_input",   "modup_cols", "modup_rows",   "inner_product",
-    "intt_p",       "moddown_cols", "moddown_rows", "moddown_finish", "collective"};
+    "galois",       "intt_input",   "modup_cols",  "modup_rows_ip",
+    "intt_p",       "moddown_cols", "moddown_rows", "collective"};
 
 cudaEvent_t pool_event(Ctx &c) {
   if (!c.event_pool.empty()) {
@@ -742,23 +754,17 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
   }
   // 3. ModUp: base extension fused into the column pass, then the row pass
   {
-    StageTimer tm(c, ST_MODUP_BCONV, s);
+    StageTimer tm(c, ST_MODUP_COLS, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
                              lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s));
     c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
+  // 4. row pass of every extended limb fused with the inner product
   {
-    StageTimer tm(c, ST_MODUP_NTT, s);
-    LimbMap mt{L.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
-    KS_CUDA(ntt_forward_rows_only(mt, lv.n_jobs, T, s));
-    c.launches += 1;
-  }
-  // 4. inner product
-  {
-    StageTimer tm(c, ST_INNER_PROD, s);
-    KS_CUDA(inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay, c.d_primes,
-                          c.log_n, s));
-    c.launches += 1;
+    StageTimer tm(c, ST_MODUP_ROWS_IP, s);
+    KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay, T,
+                                     s));
+    c.launches += lv.lay.n_out > 0 ? 1 : 0;
   }
   // 5. P part to scaled coefficient form [y_i (P/p_i)^-1]_{p_i}
   const u64 *y_base;
@@ -788,14 +794,14 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
   }
   // 6. P -> Q conversion fused into the column pass
   {
-    StageTimer tm(c, ST_MODDOWN_BCONV, s);
+    StageTimer tm(c, ST_MODDOWN_COLS, s);
     KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md,
                                lv.md_job_ps.d, lv.n_md_fp, T, s));
     c.launches += lv.n_q > 0 ? 1 : 0;
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {
-    StageTimer tm(c, ST_MODDOWN_NTT, s);
+    StageTimer tm(c, ST_MODDOWN_ROWS, s);
     KS_CUDA(moddown_fused_rows(L.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, L.s_cx,
                                (long long)lv.n_out * N, ct0, ct1, g0, rotate, c.md, T, s));
     c.launches += 1;

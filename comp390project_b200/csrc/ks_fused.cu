@@ -16,6 +16,7 @@
 // epilogue is coalesced.
 #include "ks_fused.cuh"
 #include "ks_ntt_impl.cuh"
+#include "ks_tmem.cuh"
 
 namespace ksb {
 namespace {
@@ -150,6 +151,213 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// One digit's contribution to an accumulator: acc + y * k mod m_j.  FP:
+// y and acc are the bits of doubles, every term |.| < 0.57 m_j, re-centred
+// every 32 digits; integer: Barrett reduction of y * k + acc.
+template <bool FP>
+__device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool recentre,
+                                       const PrimeDev &P) {
+  if (FP) {
+    const double kd = u64_to_fp(k);
+    double a = first ? 0.0 : as_fp(acc);
+    a = __dadd_rn(a, fp_mulmod(as_fp(y), kd, __dmul_rn(kd, P.qinv), P.qd));
+    if (recentre) a = fp_reduce_sym(a, P.qd, P.qinv);
+    return fp_bits(a);
+  }
+  return mac_reduce(first ? 0ull : acc, y, k, P.q, P.br_hi, P.br_lo);
+}
+
+// ---------------------------------------------------------------------------
+// ModUp row pass fused with the evaluation-key inner product
+// ---------------------------------------------------------------------------
+// One CTA: one 4096-word tile of one output limb s (prime m_j), all digits.
+// For each digit d the tile of t[d][s] gets its row pass in registers (the
+// digit that contains q_j instead reads the NTT-form input limb), goes
+// through shared memory into a warp-coalesced order (warp w owns tile words
+// [512w, 512w + 512), lane l the pairs 2l + 64i, i < 8), and is multiplied
+// into the two accumulators against the key limbs of digit d:
+//   cx[0][s] = sum_d t[d][s] * key[d][0][j],   cx[1][s] = sum_d t[d][s] * key[d][1][j].
+// The key pairs of a lane are copied into shared memory with cp.async when
+// the digit starts, so they arrive while the butterflies run; the next
+// digit's value tile is prefetched into L2.  The 32 accumulators of a
+// thread live in TMEM (64 columns: poly 0 in [0, 32), poly 1 in [32, 64),
+// one u64 as two columns), not in registers.  The extended limbs never
+// return to HBM.
+struct RowsIpArgs {
+  const u64 *t, *c_ntt, *key;
+  u64 *cx;
+  int key_limbs;
+};
+
+template <int LOG_M>
+__host__ __device__ constexpr size_t rows_ip_smem_bytes() {
+  // exchange buffer + per-warp key stage [8 warps][2 polys][8 pairs][32 lanes] x 16 B
+  return (size_t)RowGeom<LOG_M>::SMEM * 8 + (size_t)(kThreads / 32) * 2 * 8 * 32 * 16;
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// FP: prime below kFpBound (FP64 butterflies); else LAZY selects the
+// integer butterflies without reductions.
+template <int LOG_M, bool FP, bool LAZY>
+__device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
+                                             const KsLayout &lay, const NttTables &T, int s,
+                                             int prime, u64 *sm, ulonglong2 *kst, uint32_t tacc) {
+  using G = RowGeom<LOG_M>;
+  const PrimeDev P = T.primes[prime];
+  const int log_n = T.log_n, N = 1 << log_n;
+  const int j = lay.out_j[s];
+  const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long tile0 = (long long)blockIdx.x * kTile;
+  const long long row = (long long)blockIdx.x * G::R + rr;
+  const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's pairs in the tile
+  const int dj = j < mu.Ql ? j / mu.alpha : -1;
+  const long long kstride = (long long)A.key_limbs * N;
+  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0 + wofs;
+  const u64 *tbase = A.t + (long long)s * N + tile0;
+  const long long tstride = (long long)lay.n_out * N;
+  const u64 *cown = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N + tile0 : nullptr;
+  const ulonglong2 *tw = T.fwd + (long long)prime * N;
+  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n};
+  kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
+  // L2 prefetch of digit d's value tile: one 128-byte line per thread.
+  auto prefetch = [&](int d) {
+    const int line = threadIdx.x * 16;
+    const u64 *v = d == dj ? cown + line : tbase + d * tstride + line;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(v));
+  };
+  prefetch(0);
+#pragma unroll 1
+  for (int d = 0; d < mu.beta; ++d) {
+    const bool own = d == dj;
+    {
+      const u64 *kb = kbase + (long long)(2 * d) * kstride;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        cp_async16(kst + i * 32, kb + 64 * i);
+        cp_async16(kst + (8 + i) * 32, kb + kstride + 64 * i);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    if (d + 1 < mu.beta) prefetch(d + 1);
+    if (!own) {
+      u64 x[kEpt];
+      const u64 *tile = tbase + d * tstride;
+      if (FP) fwd_rows_regs_fp_tw<LOG_M, false>(x, sm, twf, tile, tt, rr, row, P);
+      else fwd_rows_regs<LOG_M, LAZY>(x, sm, tile, tt, rr, row, log_n, tw, P);
+#pragma unroll
+      for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(tt, e))] = x[e];
+      __syncwarp();
+    }
+    cp_async_wait_all();  // this lane's own key pairs
+    const u64 *cb = own ? cown + wofs : nullptr;
+    const bool first = d == 0, recentre = (d & 31) == 31;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      u64 y[4];
+      ulonglong2 k0[2], k1[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = 2 * h + q;
+        k0[q] = kst[i * 32];
+        k1[q] = kst[(8 + i) * 32];
+        if (own) {
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(cb + 64 * i);
+          y[2 * q] = FP ? fp_bits(u64_to_fp(v.x)) : v.x;
+          y[2 * q + 1] = FP ? fp_bits(u64_to_fp(v.y)) : v.y;
+        } else {
+          const int w = wofs + 64 * i;
+          const int a = padx<LOG_M>(w >> LOG_M, w & (G::M - 1));  // pair's second word: a + 1
+          y[2 * q] = sm[a];
+          y[2 * q + 1] = sm[a + 1];
+        }
+      }
+      uint32_t r0[8], r1[8];
+      if (!first) {
+        tmem::ld8(tacc + 8 * h, r0);
+        tmem::ld8(tacc + 32 + 8 * h, r1);
+        tmem::wait_ld(r0, r1);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const u64 b = (u & 1) ? k0[u >> 1].y : k0[u >> 1].x;
+        const u64 a = (u & 1) ? k1[u >> 1].y : k1[u >> 1].x;
+        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], b, first, recentre, P);
+        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], a, first, recentre, P);
+        r0[2 * u] = (uint32_t)v0;
+        r0[2 * u + 1] = (uint32_t)(v0 >> 32);
+        r1[2 * u] = (uint32_t)v1;
+        r1[2 * u + 1] = (uint32_t)(v1 >> 32);
+      }
+      tmem::st8(tacc + 8 * h, r0);
+      tmem::st8(tacc + 32 + 8 * h, r1);
+    }
+    tmem::wait_st();
+    __syncwarp();  // exchange buffer and key stage are reused by the next digit
+  }
+  u64 *o0 = A.cx + (long long)s * N + tile0 + wofs;
+  u64 *o1 = o0 + (long long)lay.n_out * N;
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    uint32_t r0[8], r1[8];
+    tmem::ld8(tacc + 8 * h, r0);
+    tmem::ld8(tacc + 32 + 8 * h, r1);
+    tmem::wait_ld(r0, r1);
+    u64 v0[4], v1[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v0[u] = tmem::pack(r0[2 * u], r0[2 * u + 1]);
+      v1[u] = tmem::pack(r1[2 * u], r1[2 * u + 1]);
+      if (FP) {
+        v0[u] = fp_to_canon(as_fp(v0[u]), P.qd, P.qinv);
+        v1[u] = fp_to_canon(as_fp(v1[u]), P.qd, P.qinv);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = 2 * h + q;
+      *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0[2 * q], v0[2 * q + 1]);
+      *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
+    }
+  }
+}
+
+template <int LOG_M>
+__global__ void __launch_bounds__(kThreads, 2)
+    k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
+  // Shared memory caps residency at 2 CTAs per SM (at most 4 would still
+  // fit): 4 x 128 TMEM columns fit the 512 of an SM, so tmem::alloc never waits.
+  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / 5, "TMEM columns could be oversubscribed");
+  constexpr uint32_t kCols = 128;
+  extern __shared__ __align__(16) u64 dsm[];
+  __shared__ uint32_t tmem_slot;
+  u64 *sm = dsm;
+  ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(dsm + RowGeom<LOG_M>::SMEM);
+  const int s = blockIdx.y;
+  const int prime = mu.prime_of[lay.out_j[s]];
+  const u64 q = T.primes[prime].q;
+  const int warp = threadIdx.x >> 5;
+  if (warp == 0) tmem::alloc(&tmem_slot, kCols);
+  tmem::fence_before_sync();
+  __syncthreads();
+  tmem::fence_after_sync();
+  // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
+  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
+  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  tmem::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tmem::fence_after_sync();
+    tmem::dealloc(tmem_slot, kCols);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
@@ -256,6 +464,24 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
   return cudaGetLastError();
 }
 
+template <int LOG_M>
+cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt, const u64 *key,
+                                 int key_limbs, u64 *cx, const ModUpDev &mu, const KsLayout &lay,
+                                 const NttTables &T) {
+  constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_modup_rows_ip<LOG_M>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const dim3 grid((1 << T.log_n) / kTile, lay.n_out);
+  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs};
+  k_modup_rows_ip<LOG_M><<<grid, kThreads, smem, s>>>(A, mu, lay, T);
+  return cudaGetLastError();
+}
+
 inline int col_tiles(int log_n, int log_m) {
   const int M2 = (1 << log_n) >> log_m;
   return M2 / (kThreads / ((1 << log_m) / 16));
@@ -296,6 +522,21 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
+                                     int key_limbs, u64 *cx, const ModUpDev &mu,
+                                     const KsLayout &lay, const NttTables &T, cudaStream_t s) {
+  if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
+    return cudaErrorInvalidValue;
+  if (lay.n_out == 0) return cudaSuccess;
+  const int s2 = T.log_n - T.log_n / 2;
+  switch (s2) {
+    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
+    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
+    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,

@@ -24,6 +24,14 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
                              int n_fp, const NttTables &T, cudaStream_t s);
 
+// ModUp row pass (t[d][s] from modup_fused_cols, d outside the digit of
+// out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner
+// product against the key shard ([beta][2][key_limbs][N], limb key_slot[s]):
+//   cx[p][s] = sum_d NTT_rows(t[d][s]) * key[d][p][key_slot[s]]  (p = 0, 1).
+cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
+                                     int key_limbs, u64 *cx, const ModUpDev &mu,
+                                     const KsLayout &lay, const NttTables &T, cudaStream_t s);
+
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
 // scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].

@@ -21,13 +21,28 @@ struct LimbMap {
   int first_prime, period;
 };
 
+// The FP64 tables hold w as a double at the same index as the integer
+// tables, except inside the row-pass region: for row-pass local bit b < LM-4
+// (LM = row length log2 = logN - logN/2) the 2^u twiddles of each row
+// (u = LM-1-b) are stored at row_tw_pos(LM, b, k) instead of k.  In the
+// second radix-16 round of a row pass thread t needs k = (t << s) | m
+// (s = LM-5-b, m < 2^s); the position puts t in the low bits, so the lanes
+// of a warp read consecutive words (no shared-memory bank conflicts, one
+// 128-byte line per row from global memory).
+__host__ __device__ constexpr int row_tw_pos(int lm, int b, int k) {
+  return b >= lm - 4 ? k
+                     : (k & ~((1 << (lm - 5 - b + lm - 4)) - 1)) |
+                           ((k & ((1 << (lm - 5 - b + lm - 4)) - 1)) >> (lm - 5 - b)) |
+                           ((k & ((1 << (lm - 5 - b)) - 1)) << (lm - 4));
+}
+
 struct NttTables {
   const ulonglong2 *fwd;  // [n_primes][N] {w, w_shoup}, w = psi^brev(i)
   const ulonglong2 *inv;  // [n_primes][N] {w, w_shoup}, w = psi^-brev(i)
   const PrimeDev *primes; // [n_primes]
   int log_n;
-  const double *fwd_fp;   // [n_primes][N] w as a double (primes below kFpBound)
-  const double *inv_fp;
+  const double *fwd_fp;   // [n_primes][N] w as a double (primes below kFpBound),
+  const double *inv_fp;   // row-pass region permuted by row_tw_pos
 };
 
 // Transforms n_limbs limbs in place; outputs are canonical in [0, q).

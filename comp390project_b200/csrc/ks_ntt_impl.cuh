@@ -236,7 +236,23 @@ struct TwRowsSmem {
   long long row0;
   __device__ __forceinline__ double operator()(int b, long long H) const {
     const int u = LOG_M - 1 - b;
-    return sm[R * ((1 << u) - 1) + (int)((H >> (b + 1)) - (row0 << u))];
+    const long long hk = H >> (b + 1);
+    const int k = (int)hk & ((1 << u) - 1);
+    return sm[R * ((1 << u) - 1) + (int)(((hk >> u) - row0) << u) + row_tw_pos(LOG_M, b, k)];
+  }
+};
+
+// Global-table getter for a row pass (rows of 2^LOG_M words, permuted
+// row-pass region of the FP64 table).
+template <int LOG_M>
+struct TwRowsGlobal {
+  const double *tw;
+  int log_n;
+  __device__ __forceinline__ double operator()(int b, long long H) const {
+    const int u = LOG_M - 1 - b;
+    const long long hk = H >> (b + 1);
+    const int k = (int)hk & ((1 << u) - 1);
+    return __ldg(&tw[(1ll << (log_n - 1 - b)) + ((hk >> u) << u) + row_tw_pos(LOG_M, b, k)]);
   }
 };
 
@@ -364,15 +380,14 @@ __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int 
     store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
 }
 
-// Forward row pass; the tile holds first-pass bits; canonical outputs in xo.
-// smtw: this CTA's twiddle block, staged by stage_row_twiddles (the caller
-// waits for it and synchronises before calling).
-template <int LOG_M>
-__device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
-                                                 const u64 *tile, int t, int rr, long long row,
-                                                 long long row0, const PrimeDev &P) {
+// Forward row pass; the tile holds first-pass bits; canonical outputs in xo
+// (CANON), else the bits of the unreduced doubles (|x| < 12q < 2^47).
+// tw: twiddle getter (TwRowsSmem over a staged block, or TwRowsGlobal).
+template <int LOG_M, bool CANON, class Tw>
+__device__ __forceinline__ void fwd_rows_regs_fp_tw(u64 (&xo)[kEpt], u64 *sm, const Tw &tw,
+                                                    const u64 *tile, int t, int rr, long long row,
+                                                    const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
-  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0};
   double x[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)]);
@@ -384,8 +399,18 @@ __device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))]);
   fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, tw, P.qd, P.qinv);
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) xo[e] = fp_to_canon(x[e], P.qd, P.qinv);
+  for (int e = 0; e < kEpt; ++e) xo[e] = CANON ? fp_to_canon(x[e], P.qd, P.qinv) : fp_bits(x[e]);
   __syncwarp();
+}
+
+// smtw: this CTA's twiddle block, staged by stage_row_twiddles (the caller
+// waits for it and synchronises before calling).
+template <int LOG_M, bool CANON = true>
+__device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
+                                                 const u64 *tile, int t, int rr, long long row,
+                                                 long long row0, const PrimeDev &P) {
+  const TwRowsSmem<LOG_M, RowGeom<LOG_M>::R> tw{smtw, row0};
+  fwd_rows_regs_fp_tw<LOG_M, CANON>(xo, sm, tw, tile, t, rr, row, P);
 }
 
 // Inverse row pass (first pass) over a tile staged in smem as canonical
@@ -414,7 +439,7 @@ __device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const
 // Shared memory of a row-pass CTA: the exchange buffer then (FP64 path) the
 // twiddle block.
 template <int LOG_M>
-constexpr size_t row_smem_bytes() {
+__host__ __device__ constexpr size_t row_smem_bytes() {
   return (size_t)RowGeom<LOG_M>::SMEM * 8 + (size_t)RowGeom<LOG_M>::R * ((1 << LOG_M) - 1) * 8;
 }
 
