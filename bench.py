@@ -38,8 +38,11 @@ BATCH = 64
 SCALE = 2.0 ** 40
 METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
 # DRAM bytes per launch (read + write) of each key-switch kernel at config 3,
-# one key switch, from `ncu --set full` (profiles/keyswitch_config3.md).
-PROFILED_TRAFFIC = {}
+# one key switch, from `ncu --set full` (profiles/keyswitch_config3_kernels.md).
+PROFILED_TRAFFIC = {
+    "galois": 38.1e6, "intt_input": 55.7e6, "modup_cols": 100.9e6, "modup_rows_ip": 508.8e6,
+    "intt_p": 15.9e6, "moddown_cols": 5.4e6, "moddown_rows": 140.2e6,
+}
 
 
 def parse():
@@ -372,8 +375,9 @@ def run_ours(args, rank, world):
         "galois": 4 * n_q * U,
         "intt_input": 2 * n_q * U,
         "modup_cols": (L + n_jobs) * U,
-        "modup_rows": 2 * n_jobs * U,
-        "inner_product": (beta * n_out + 2 * beta * n_out + 2 * n_out) * U,
+        # extended limbs (column pass done) + own-digit input limbs, both key
+        # polys of every digit, cx out
+        "modup_rows_ip": (beta * n_out + 2 * beta * n_out + 2 * n_out) * U,
         "intt_p": 4 * n_p_own * U,
         "moddown_cols": (2 * len(p) + 2 * n_q) * U,
         "moddown_rows": 7 * n_q * U,
@@ -381,7 +385,7 @@ def run_ours(args, rank, world):
     peak, peak_kind = measured_peaks()
     achieved = alg[dom] / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
     # DRAM traffic per launch of the dominant kernel from one ncu capture
-    # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/keyswitch_config3.md)
+    # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/keyswitch_config3_kernels.md)
     traffic = PROFILED_TRAFFIC.get(dom) if world == 1 else None
 
     # end to end through the C ABI with host buffers (pinned), copies timed

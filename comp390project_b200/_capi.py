@@ -92,6 +92,10 @@ SIGNATURES = {
     "ks_gather_limbs": (_I, [_P, _P, _P, _I, _I, _P]),
     "ks_allgather_limbs": (_I, [_P, _P, _P, _I, _P]),
     "ks_last_launch_count": (_I, [_P]),
+    "ks_graph_capture_begin": (_I, [_P, _P]),
+    "ks_graph_capture_end": (_I, [_P, _P, C.POINTER(_P)]),
+    "ks_graph_launch": (_I, [_P, _P]),
+    "ks_graph_destroy": (_I, [_P]),
     "ks_profile_enable": (_I, [_P, _I]),
     "ks_profile_stage_count": (_I, []),
     "ks_profile_stage_name": (C.c_char_p, [_I]),

@@ -12,7 +12,8 @@ from typing import Optional, Sequence
 import numpy as np
 
 from . import _capi
-from ._capi import (KS_KEY_GALOIS, KS_KEY_RELIN, KS_MODE_INPUT_BROADCAST, KS_NCCL_ID_BYTES,
+from ._capi import (KS_KEY_GALOIS, KS_KEY_RELIN, KS_MODE_INPUT_BROADCAST,
+                    KS_MODE_OUTPUT_AGGREGATION, KS_NCCL_ID_BYTES,
                     check, ks_params)
 
 
@@ -50,6 +51,27 @@ def nccl_unique_id() -> bytes:
     buf = C.create_string_buffer(KS_NCCL_ID_BYTES)
     check(_capi.load().ks_nccl_unique_id(buf, KS_NCCL_ID_BYTES))
     return buf.raw
+
+
+class KsGraph:
+    """A captured sequence of hot-path calls (ks_graph_*)."""
+
+    def __init__(self, lib, handle):
+        self.lib, self.h = lib, handle
+
+    def launch(self, stream=None, device: int = 0):
+        check(self.lib.ks_graph_launch(self.h, _stream_ptr(stream, device)), None)
+
+    def close(self):
+        if self.h:
+            self.lib.ks_graph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class KsContext:
@@ -150,6 +172,18 @@ class KsContext:
     def last_launch_count(self) -> int:
         return int(self.lib.ks_last_launch_count(self.h))
 
+    # -- CUDA graphs -----------------------------------------------------------
+    def graph_capture_begin(self, stream):
+        """Starts recording the hot-path calls made on ``stream`` (a torch
+        stream or a raw handle; not the legacy default stream)."""
+        self._check(self.lib.ks_graph_capture_begin(self.h, _stream_ptr(stream, self.device)))
+
+    def graph_capture_end(self, stream) -> "KsGraph":
+        g = C.c_void_p()
+        self._check(self.lib.ks_graph_capture_end(self.h, _stream_ptr(stream, self.device),
+                                                  C.byref(g)))
+        return KsGraph(self.lib, g.value)
+
     def profile_enable(self, on: bool = True):
         self._check(self.lib.ks_profile_enable(self.h, 1 if on else 0))
 
@@ -179,9 +213,15 @@ class KsContext:
                                              _stream_ptr(stream, self.device)))
 
     def key_download(self, kind: int, elt: int) -> np.ndarray:
+        """The key shard this context holds: [digits][2][limbs][N].  Input
+        broadcast (or one GPU): all digits, the cyclic key-basis limbs j % G ==
+        rank; output aggregation: the digits d % G == rank, all limbs."""
         beta = (self.L + self.alpha - 1) // self.alpha
-        limbs = len(range(self.rank, self.L + self.alpha, self.world))
-        out = np.zeros((beta, 2, limbs, self.N), dtype=np.uint64)
+        if self.world > 1 and self.mode == KS_MODE_OUTPUT_AGGREGATION:
+            digits, limbs = len(range(self.rank, beta, self.world)), self.L + self.alpha
+        else:
+            digits, limbs = beta, len(range(self.rank, self.L + self.alpha, self.world))
+        out = np.zeros((digits, 2, limbs, self.N), dtype=np.uint64)
         self._check(self.lib.ks_key_download(self.h, kind, int(elt), out.ctypes.data, out.size))
         return out
 

@@ -35,6 +35,12 @@ struct ks_ctx {
   Ctx c;
 };
 
+struct ks_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int device = 0;
+};
+
 namespace {
 
 std::mutex g_err_mu;
@@ -67,6 +73,17 @@ struct KsError {
     if (!(cond)) throw KsError{KS_ERR_INVALID, msg};                                      \
   } while (0)
 
+// A failed call during a graph capture ends (and discards) the capture, so
+// the caller's stream is usable again.
+inline void abort_capture(ks_ctx *ctx) {
+  if (!ctx || !ctx->c.capturing) return;
+  cudaGraph_t g = nullptr;
+  cudaStreamEndCapture(ctx->c.capture_stream, &g);
+  if (g) cudaGraphDestroy(g);
+  cudaGetLastError();
+  ctx->c.capturing = false;
+}
+
 template <class F>
 int guarded(ks_ctx *ctx, F &&f) {
   try {
@@ -75,10 +92,12 @@ int guarded(ks_ctx *ctx, F &&f) {
   } catch (const KsError &e) {
     if (ctx) ctx->c.err = e.msg;
     set_global_err(e.msg);
+    abort_capture(ctx);
     return e.code;
   } catch (const std::exception &e) {
     if (ctx) ctx->c.err = e.what();
     set_global_err(e.what());
+    abort_capture(ctx);
     return KS_ERR_INVALID;
   }
 }
@@ -247,7 +266,11 @@ void build_moddown(Ctx &c) {
 }
 
 void build_level(Ctx &c, Level &lv, int Ql) {
-  const int a = c.alpha, L = c.L, G = c.world, g = c.rank;
+  // Output aggregation keeps the whole ciphertext on every rank: its limb
+  // layout is the single-GPU one, and only the digits (d % world == rank)
+  // are split.
+  const bool oa = c.oa();
+  const int a = c.alpha, L = c.L, G = oa ? 1 : c.world, g = oa ? 0 : c.rank;
   lv.Ql = Ql;
   lv.QlP = Ql + a;
   lv.beta = (Ql + a - 1) / a;
@@ -268,16 +291,29 @@ void build_level(Ctx &c, Level &lv, int Ql) {
     lv.c_slot.h.push_back(j < Ql ? j / G : -1);
   }
   lv.coef_ml = (Ql + G - 1) / G;
+  auto my_digit = [&](int d) { return !oa || d % c.world == c.rank; };
+  for (int d = 0; d < lv.beta; ++d)
+    if (my_digit(d)) lv.digits.h.push_back(d);
   for (int d = 0; d < lv.beta; ++d)
     for (int s = 0; s < lv.n_out; ++s) {
       const int j = lv.out_j.h[s];
       const bool in_digit = j < Ql && j / a == d;
-      lv.t_jobs.h.push_back(in_digit ? -1 : lv.prime_of.h[j]);
+      lv.t_jobs.h.push_back(in_digit || !my_digit(d) ? -1 : lv.prime_of.h[j]);
     }
   for (int s = 0; s < lv.n_q; ++s) {
     lv.q_index.h.push_back(lv.out_j.h[s]);
     lv.cx_slot_q.h.push_back(s);
   }
+  for (int p = 0; p < 2; ++p)
+    for (int s = 0; s < lv.n_out; ++s) lv.cx_prime.h.push_back(lv.prime_of.h[lv.out_j.h[s]]);
+  // input INTT: owned Q limbs, or (output aggregation) the limbs of this rank's digits
+  for (int s = 0; s < lv.n_q; ++s) {
+    const int j = lv.out_j.h[s];
+    if (!my_digit(j / a)) continue;
+    lv.intt_off.h.push_back((long long)s * c.N);
+    lv.intt_prime.h.push_back(j);
+  }
+  lv.n_intt = (int)lv.intt_prime.h.size();
   for (int p = 0; p < 2; ++p)
     for (int s = 0; s < lv.n_q; ++s) lv.z_jobs.h.push_back(lv.out_j.h[s]);
   // P part: offsets of the owned P slots that get inverse-transformed
@@ -368,8 +404,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
         if (pass == 0) ++lv.n_md_fp;
       }
   std::vector<ulonglong2> sin, sp;
-  for (int s = 0; s < lv.n_q; ++s) {
-    const int j = lv.out_j.h[s], d = j / a;
+  for (int i = 0; i < lv.n_intt; ++i) {
+    const int j = lv.intt_prime.h[i], d = j / a;
     scale_pair(j, qhi[(size_t)d * a + (j - d * a)].x, sin);
   }
   for (int p = 0; p < 2; ++p)
@@ -382,6 +418,10 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       scale_pair(L + i, h_invmod(prod, pi), sp);
     }
   up_ints(lv.src_slot);
+  up_ints(lv.digits);
+  up_ints(lv.cx_prime);
+  up_ints(lv.intt_prime);
+  up_i64(lv.intt_off);
   up_ints(lv.md_job_ps);
   up_ints(lv.job_d);
   up_ints(lv.job_s);
@@ -415,7 +455,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   lv.wsh = upload(wsh);
   lv.wq = upload(wq);
   lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh, lv.wq};
-  lv.lay = KsLayout{lv.n_out, lv.out_j.d, lv.key_slot.d, lv.c_slot.d, G, lv.coef_ml};
+  lv.lay = KsLayout{lv.n_out,  lv.out_j.d,    lv.key_slot.d,          lv.c_slot.d, G,
+                    lv.coef_ml, lv.digits.d, (int)lv.digits.h.size()};
 }
 
 void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncclComm_t comm,
@@ -433,8 +474,6 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
   c.mode = world > 1 ? prm->mode : KS_MODE_INPUT_BROADCAST;
   KS_REQUIRE(c.mode == KS_MODE_INPUT_BROADCAST || c.mode == KS_MODE_OUTPUT_AGGREGATION,
              "unknown mode");
-  if (c.mode == KS_MODE_OUTPUT_AGGREGATION)
-    throw KsError{KS_ERR_UNSUPPORTED, "output-aggregation mode is not built yet"};
   c.max_batch = std::max(1, prm->max_batch);
   c.log_n = (int)prm->log_n;
   c.N = 1 << c.log_n;
@@ -452,9 +491,16 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
   }
   KS_CUDA(cudaSetDevice(device));
   build_tables(c);
-  for (int kj = rank; kj < c.K; kj += world) c.own_key.push_back(kj);
+  // key shard: cyclic key-basis limbs of all digits (input broadcast), or
+  // all limbs of the digits d % world == rank (output aggregation)
+  for (int kj = c.oa() ? 0 : rank; kj < c.K; kj += c.oa() ? 1 : world) c.own_key.push_back(kj);
   c.own_key_prime.h = c.own_key;
   up_ints(c.own_key_prime);
+  if (c.alpha > 0) {
+    const int beta = (c.L + c.alpha - 1) / c.alpha;
+    for (int d = 0; d < beta; ++d)
+      if (!c.oa() || d % world == rank) c.key_digits.push_back(d);
+  }
   if (c.alpha > 0) {
     for (int g = 0; g < world; ++g) {
       int cnt = 0;
@@ -468,13 +514,15 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     // scratch, sized for the top level
     const Level &top = c.levels[c.L];
     const size_t N = c.N;
-    const size_t nq = n_local(rank, world, c.L), ml = (c.L + world - 1) / world;
+    const bool ib = !c.replicated();  // input broadcast over world > 1 ranks
+    const size_t nq = ib ? n_local(rank, world, c.L) : c.L;
+    const size_t ml = ib ? (c.L + world - 1) / world : c.L;
     const size_t n_key_own = c.own_key.size();
-    size_t w_g = 2 * nq * N, w_coef = ml * N, w_coef_all = world > 1 ? world * ml * N : 0;
+    size_t w_g = 2 * nq * N, w_coef = ml * N, w_coef_all = ib ? world * ml * N : 0;
     size_t w_t = std::max((size_t)top.beta * top.n_out * N, 3 * n_key_own * N);
     size_t w_cx = 2 * (size_t)top.n_out * N;
-    size_t w_ys = world > 1 ? (size_t)c.max_p_own * 2 * N : 0;
-    size_t w_ya = world > 1 ? (size_t)world * c.max_p_own * 2 * N : 0;
+    size_t w_ys = ib ? (size_t)c.max_p_own * 2 * N : 0;
+    size_t w_ya = ib ? (size_t)world * c.max_p_own * 2 * N : 0;
     size_t w_z = 2 * nq * N;
     c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z;
     // one scratch arena per lane; lanes = max_batch (1..8)
@@ -487,7 +535,7 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       u64 *p = ln.arena;
       ln.s_g = p; p += w_g;
       ln.s_coef = p; p += w_coef;
-      ln.s_coef_all = world > 1 ? p : ln.s_coef; p += w_coef_all;
+      ln.s_coef_all = ib ? p : ln.s_coef; p += w_coef_all;
       ln.s_t = p; p += w_t;
       ln.s_cx = p; p += w_cx;
       ln.s_ysend = p; p += w_ys;
@@ -533,8 +581,11 @@ void ctx_free(Ctx &c) {
     f(lv.p_offsets.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
-    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps}) f(t->d);
+    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
+                       &lv.digits, &lv.cx_prime, &lv.intt_prime})
+      f(t->d);
     f(lv.job_off.d);
+    f(lv.intt_off.d);
     f(lv.scale_in);
     f(lv.scale_p);
     f(lv.w);
@@ -591,8 +642,8 @@ KeyShard &key_alloc(Ctx &c, int kind, uint32_t elt) {
   if (it != c.keys.end()) return it->second;
   KeyShard k;
   k.limbs = (int)c.own_key.size();
-  k.beta = (c.L + c.alpha - 1) / c.alpha;
-  k.d = dev_alloc<u64>((size_t)k.beta * 2 * k.limbs * c.N);
+  k.beta = (int)c.key_digits.size();
+  k.d = dev_alloc<u64>(std::max<size_t>(1, (size_t)k.beta * 2 * k.limbs * c.N));
   return c.keys[id] = k;
 }
 
@@ -620,6 +671,12 @@ void key_upload(Ctx &c, int kind, uint32_t elt, const u64 *src, size_t n_words, 
   const cudaMemcpyKind dir = from_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   if (c.world == 1) {
     KS_CUDA(cudaMemcpyAsync(k.d, src, n_words * 8, dir, s));
+  } else if (c.oa()) {
+    // digits d % G == g of the full layout [d][p][K], all limbs
+    for (int di = 0; di < k.beta; ++di)
+      KS_CUDA(cudaMemcpyAsync(k.d + (size_t)2 * di * k.limbs * N,
+                              src + (size_t)2 * c.key_digits[di] * c.K * N,
+                              (size_t)2 * c.K * N * 8, dir, s));
   } else {
     // rows of the full layout [d][p][K] -> shard [d][p][own]
     for (int d = 0; d < k.beta; ++d)
@@ -663,16 +720,17 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
   KS_CUDA(cudaMemcpyAsync(d_pmq, pmodq.data(), n * 8, cudaMemcpyHostToDevice, s));
   const u64 sa = prng_stream(seed, DOM_KEY_A), se = prng_stream(seed, DOM_KEY_E);
   std::vector<std::vector<int>> flags(k.beta, std::vector<int>(n));
-  for (int d = 0; d < k.beta; ++d) {
+  for (int di = 0; di < k.beta; ++di) {
+    const int d = c.key_digits[di];  // the digit's samples do not depend on the shard
     for (int sl = 0; sl < n; ++sl) {
       const int kj = c.own_key[sl];
-      flags[d][sl] = (kj < c.L && kj / c.alpha == d) ? 1 : 0;
+      flags[di][sl] = (kj < c.L && kj / c.alpha == d) ? 1 : 0;
     }
-    KS_CUDA(cudaMemcpyAsync(d_in, flags[d].data(), n * sizeof(int), cudaMemcpyHostToDevice, s));
+    KS_CUDA(cudaMemcpyAsync(d_in, flags[di].data(), n * sizeof(int), cudaMemcpyHostToDevice, s));
     KS_CUDA(sample_gauss(e, n, prime, c.d_primes, c.d_gauss, se, (u64)d * N, c.log_n, s));
     LimbMap me{e, N, nullptr, prime, 0, 1};
     KS_CUDA(ntt_forward(me, n, T, s));
-    u64 *kb = k.d + (size_t)(2 * d) * n * N, *ka = k.d + (size_t)(2 * d + 1) * n * N;
+    u64 *kb = k.d + (size_t)(2 * di) * n * N, *ka = k.d + (size_t)(2 * di + 1) * n * N;
     KS_CUDA(keygen_digit(kb, ka, s_ntt, snew, e, n, prime, prime, d_in, d_pmq, sa, d, c.K,
                          c.d_primes, c.log_n, s));
     KS_CUDA(cudaStreamSynchronize(s));  // flags buffer is reused per digit
@@ -734,41 +792,53 @@ void allgather(ncclComm_t comm, const u64 *send, u64 *recv, size_t words, cudaSt
 // ---------------------------------------------------------------------------
 // The key switch
 // ---------------------------------------------------------------------------
-// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]).
-// rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
-void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt, u64 *ct0,
-                    u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
+// Steps 2-3: scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the
+// input limbs this rank extends (input broadcast all-gathers them), then the
+// base extension fused into the column pass -> L.s_t.
+void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const u64 *in_ntt, cudaStream_t s) {
   const size_t N = c.N;
   const NttTables T = c.tables();
-  // 2. scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the input, all-gathered
   {
     StageTimer tm(c, ST_INTT_IN, s);
-    LimbMap min{const_cast<u64 *>(in_ntt), (long long)N, nullptr, lv.q_index.d, 0, 1};
-    LimbMap mc{L.s_coef, (long long)N, nullptr, lv.q_index.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_q, lv.scale_in, T, s));
-    c.launches += 2;
+    LimbMap min{const_cast<u64 *>(in_ntt), 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
+    LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
+    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s));
+    c.launches += lv.n_intt > 0 ? 2 : 0;
   }
-  if (c.world > 1) {
+  if (!c.replicated()) {
     StageTimer tm(c, ST_COMM, s);
     allgather(L.comm, L.s_coef, L.s_coef_all, (size_t)lv.coef_ml * N, s);
   }
-  // 3. ModUp: base extension fused into the column pass, then the row pass
   {
     StageTimer tm(c, ST_MODUP_COLS, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
                              lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s));
     c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
-  // 4. row pass of every extended limb fused with the inner product
+}
+
+// Output aggregation: sum the partial inner products of all ranks (every
+// rank then holds all of cx; G q < 2^64) and reduce mod the limb primes.
+void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, cudaStream_t s) {
+  if (!c.oa()) return;
   {
-    StageTimer tm(c, ST_MODUP_ROWS_IP, s);
-    KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay, T,
-                                     s));
-    c.launches += lv.lay.n_out > 0 ? 1 : 0;
+    StageTimer tm(c, ST_COMM, s);
+    KS_NCCL(ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum,
+                          L.comm, s));
   }
+  KS_CUDA(mod_reduce(L.s_cx, 2 * lv.n_out, lv.cx_prime.d, c.d_primes, c.log_n, s));
+  c.launches += 1;
+}
+
+// Steps 5-7: ModDown of L.s_cx into the ciphertext (see moddown_fused_rows
+// for rotate / diag).
+void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, u64 *ct0, u64 *ct1, const u64 *g0,
+                bool rotate, const u64 *diag, cudaStream_t s) {
+  const size_t N = c.N;
+  const NttTables T = c.tables();
   // 5. P part to scaled coefficient form [y_i (P/p_i)^-1]_{p_i}
   const u64 *y_base;
-  if (c.world == 1) {
+  if (c.replicated()) {
     StageTimer tm(c, ST_INTT_P, s);
     LimbMap mp{L.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
     KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
@@ -803,9 +873,30 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
   {
     StageTimer tm(c, ST_MODDOWN_ROWS, s);
     KS_CUDA(moddown_fused_rows(L.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, L.s_cx,
-                               (long long)lv.n_out * N, ct0, ct1, g0, rotate, c.md, T, s));
+                               (long long)lv.n_out * N, ct0, ct1, g0, rotate, diag, c.md, T, s));
     c.launches += 1;
   }
+}
+
+// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]).
+// rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
+void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt,
+                    u64 *ct0, u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
+  const NttTables T = c.tables();
+  ks_modup_cols(c, L, lv, in_ntt, s);
+  // 4. row pass of every extended limb fused with the inner product
+  {
+    StageTimer tm(c, ST_MODUP_ROWS_IP, s);
+    if (lv.lay.n_digits > 0) {
+      KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay,
+                                       T, s));
+      c.launches += lv.lay.n_out > 0 ? 1 : 0;
+    } else {  // output aggregation with more ranks than digits: a zero partial sum
+      KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));
+    }
+  }
+  ks_aggregate(c, L, lv, s);
+  ks_moddown(c, L, lv, ct0, ct1, g0, rotate, nullptr, s);
 }
 
 const Level &level_of(Ctx &c, int Ql) {
@@ -1115,6 +1206,57 @@ int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, 
       KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));
     }
   });
+}
+
+int ks_graph_capture_begin(ks_ctx *ctx, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(stream != nullptr, "graph capture needs a non-default stream");
+    KS_REQUIRE(!c.profile, "profiling must be off during graph capture");
+    KS_REQUIRE(!c.capturing, "a capture is already open on this context");
+    KS_CUDA(cudaSetDevice(c.device));
+    KS_CUDA(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal));
+    c.capturing = true;
+    c.capture_stream = (cudaStream_t)stream;
+  });
+}
+
+int ks_graph_capture_end(ks_ctx *ctx, void *stream, ks_graph **out) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    KS_REQUIRE(out != nullptr && stream != nullptr, "bad arguments");
+    KS_REQUIRE(c.capturing, "no capture is open on this context");
+    KS_REQUIRE((cudaStream_t)stream == c.capture_stream, "not the capturing stream");
+    KS_CUDA(cudaSetDevice(c.device));
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture((cudaStream_t)stream, &g);
+    c.capturing = false;
+    KS_CUDA(e);
+    cudaGraphExec_t x = nullptr;
+    const cudaError_t e2 = cudaGraphInstantiate(&x, g, 0);
+    if (e2 != cudaSuccess) cudaGraphDestroy(g);
+    KS_CUDA(e2);
+    *out = new ks_graph{g, x, c.device};
+  });
+}
+
+int ks_graph_launch(ks_graph *graph, void *stream) {
+  if (!graph || !graph->exec) return KS_ERR_INVALID;
+  return guarded(nullptr, [&] {
+    KS_CUDA(cudaSetDevice(graph->device));
+    KS_CUDA(cudaGraphLaunch(graph->exec, (cudaStream_t)stream));
+  });
+}
+
+int ks_graph_destroy(ks_graph *graph) {
+  if (!graph) return KS_OK;
+  cudaSetDevice(graph->device);
+  if (graph->exec) cudaGraphExecDestroy(graph->exec);
+  if (graph->graph) cudaGraphDestroy(graph->graph);
+  delete graph;
+  return KS_OK;
 }
 
 int ks_rotate_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs, const int *steps, int n,

@@ -14,6 +14,7 @@
 #include <string>
 #include <vector>
 
+#include "../../include/ks_capi.h"
 #include "ks_kernels.cuh"
 #include "ks_ntt.cuh"
 
@@ -56,7 +57,15 @@ struct Level {
   DevInts src_slot;               // [beta * alpha] slot of Q limb d*alpha+i in the gathered input
   DevInts job_d, job_s, job_prime;  // [n_jobs]
   DevI64 job_off;                 // [n_jobs] word offset of t[d][s]
-  ulonglong2 *scale_in = nullptr; // [2 * n_q] last-stage INTT scales with (Q_d/q_j)^-1 folded in
+  // input INTT: the Q limbs this rank extends (owned limbs; in output-aggregation
+  // mode the limbs of its digits), at word offset intt_off of the input and
+  // of the coefficient buffer, prime intt_prime
+  int n_intt = 0;
+  DevI64 intt_off;
+  DevInts intt_prime;
+  DevInts digits;                 // digits of the inner product (all, or this rank's)
+  DevInts cx_prime;               // [2 * n_out] prime of cx slot (post-all-reduce reduction)
+  ulonglong2 *scale_in = nullptr; // [2 * n_intt] last-stage INTT scales with (Q_d/q_j)^-1 folded in
   ulonglong2 *scale_p = nullptr;  // [2 * 2 * n_p] same with (P/p_i)^-1 for the owned P limbs
   ModUpDev mu{};
   KsLayout lay{};
@@ -65,12 +74,14 @@ struct Level {
 struct KeyShard {
   u64 *d = nullptr;
   int limbs = 0;  // key limbs held (owned key-basis limbs)
-  int beta = 0;
+  int beta = 0;   // digits held (Ctx::key_digits)
 };
 
 struct Ctx {
   // parameters
   int device = 0, rank = 0, world = 1, mode = 0, max_batch = 1;
+  bool capturing = false;  // a graph capture is open (ks_graph_capture_begin)
+  cudaStream_t capture_stream = nullptr;
   int log_n = 0, N = 0, L = 0, alpha = 0, K = 0;
   std::vector<u64> primes;  // K = L + alpha
   // device tables (and the host copy of the per-prime constants)
@@ -86,6 +97,13 @@ struct Ctx {
   // key-basis ownership
   std::vector<int> own_key;   // owned key-basis limbs, increasing
   DevInts own_key_prime;      // same, device copy (prime index == key index)
+  std::vector<int> key_digits;  // digits of the key held (all; output aggregation: d % G == g)
+  // Input broadcast (G > 1): every rank holds its cyclic limbs of the
+  // ciphertext and of the key.  Output aggregation: every rank holds the whole
+  // ciphertext and the key digits d % G == g, all limbs.
+  bool oa() const { return world > 1 && mode == KS_MODE_OUTPUT_AGGREGATION; }
+  // all limbs of the ciphertext on this rank (G = 1 or output aggregation)
+  bool replicated() const { return world == 1 || oa(); }
   // keys
   std::map<unsigned long long, KeyShard> keys;  // (kind << 32) | elt
   // Execution lanes: lane 0 runs single calls on the caller's stream; a batch

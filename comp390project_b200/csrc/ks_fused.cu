@@ -230,12 +230,14 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
     const u64 *v = d == dj ? cown + line : tbase + d * tstride + line;
     asm volatile("prefetch.global.L2 [%0];" ::"l"(v));
   };
-  prefetch(0);
+  const int n_dig = lay.n_digits;
+  prefetch(__ldg(&lay.digits[0]));
 #pragma unroll 1
-  for (int d = 0; d < mu.beta; ++d) {
+  for (int di = 0; di < n_dig; ++di) {
+    const int d = __ldg(&lay.digits[di]);  // digit di of the key shard
     const bool own = d == dj;
     {
-      const u64 *kb = kbase + (long long)(2 * d) * kstride;
+      const u64 *kb = kbase + (long long)(2 * di) * kstride;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         cp_async16(kst + i * 32, kb + 64 * i);
@@ -243,7 +245,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    if (d + 1 < mu.beta) prefetch(d + 1);
+    if (di + 1 < n_dig) prefetch(__ldg(&lay.digits[di + 1]));
     if (!own) {
       u64 x[kEpt];
       const u64 *tile = tbase + d * tstride;
@@ -255,7 +257,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
     }
     cp_async_wait_all();  // this lane's own key pairs
     const u64 *cb = own ? cown + wofs : nullptr;
-    const bool first = d == 0, recentre = (d & 31) == 31;
+    const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       u64 y[4];
@@ -397,7 +399,7 @@ __global__ void __launch_bounds__(kThreads)
     k_moddown_rows(const u64 *__restrict__ z, int n_q, const int *__restrict__ q_index,
                    const int *__restrict__ cx_slot, const u64 *__restrict__ cx,
                    long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0, int rotate,
-                   ModDownDev md, NttTables T) {
+                   const u64 *__restrict__ diag, ModDownDev md, NttTables T) {
   using G = RowGeom<LOG_M>;
   extern __shared__ __align__(16) u64 dsm[];
   u64 *sm = dsm;
@@ -437,12 +439,14 @@ __global__ void __launch_bounds__(kThreads)
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(t, e))] = x[e];
   __syncthreads();
   const ulonglong2 pinv = md.pinv[j];
+  const u64 *dg = diag ? diag + (long long)s * N + tile0 : nullptr;
 #pragma unroll 4
   for (int i = 0; i < kEpt; ++i) {
     const int lin = threadIdx.x + i * kThreads;
     const u64 zv = sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))];
     const u64 o = mul_shoup(cxp[lin] + P.q - zv, pinv.x, pinv.y, P.q);
-    dst[lin] = base ? add_mod(base[lin], o, P.q) : o;
+    const u64 v = base ? add_mod(base[lin], o, P.q) : o;
+    dst[lin] = dg ? mac_reduce(dst[lin], v, dg[lin], P.q, P.br_hi, P.br_lo) : v;
   }
 }
 
@@ -450,7 +454,8 @@ template <int LOG_M>
 cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q,
                                const int *q_index, const int *cx_slot, const u64 *cx,
                                long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0,
-                               int rot, const ModDownDev &md, const NttTables &T) {
+                               int rot, const u64 *diag, const ModDownDev &md,
+                               const NttTables &T) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
   static bool attr_set = false;
   if (!attr_set) {
@@ -460,7 +465,7 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
     attr_set = true;
   }
   k_moddown_rows<LOG_M><<<grid, kThreads, smem, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly,
-                                                     ct0, ct1, g0, rot, md, T);
+                                                     ct0, ct1, g0, rot, diag, md, T);
   return cudaGetLastError();
 }
 
@@ -558,17 +563,17 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
 
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,
                                const u64 *cx, long long cx_stride_poly, u64 *ct0, u64 *ct1,
-                               const u64 *g0, bool rotate, const ModDownDev &md,
-                               const NttTables &T, cudaStream_t s) {
+                               const u64 *g0, bool rotate, const u64 *diag,
+                               const ModDownDev &md, const NttTables &T, cudaStream_t s) {
   if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
   if (n_q == 0) return cudaSuccess;
   const int s2 = T.log_n - T.log_n / 2;
   dim3 grid((1 << T.log_n) / kTile, 2 * n_q);
   const int rot = rotate ? 1 : 0;
   switch (s2) {
-    case 6: return launch_moddown_rows<6>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
-    case 7: return launch_moddown_rows<7>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
-    case 8: return launch_moddown_rows<8>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, md, T);
+    case 6: return launch_moddown_rows<6>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
+    case 7: return launch_moddown_rows<7>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
+    case 8: return launch_moddown_rows<8>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -26,8 +26,9 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 
 // ModUp row pass (t[d][s] from modup_fused_cols, d outside the digit of
 // out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner
-// product against the key shard ([beta][2][key_limbs][N], limb key_slot[s]):
-//   cx[p][s] = sum_d NTT_rows(t[d][s]) * key[d][p][key_slot[s]]  (p = 0, 1).
+// product against the key shard ([n_digits][2][key_limbs][N], limb key_slot[s]):
+//   cx[p][s] = sum_i NTT_rows(t[d_i][s]) * key[i][p][key_slot[s]]  (p = 0, 1,
+// d_i = lay.digits[i], lay.n_digits >= 1).
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s);
@@ -42,10 +43,12 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
 
 // Row pass of z[p][s] with the ModDown finish in the epilogue:
 //   o = (cx[p][cx_slot[s]] - z) * P^-1 mod q_j;
-//   p = 0: ct0 = (rotate ? g0 : ct0) + o;   p = 1: ct1 = rotate ? o : ct1 + o.
+//   p = 0: v = (rotate ? g0 : ct0) + o;   p = 1: v = rotate ? o : ct1 + o;
+//   ct_p = v, or with diag ([n_q][N], NTT form): ct_p += diag * v (a plaintext
+//   product accumulated into ct_p).
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,
                                const u64 *cx, long long cx_stride_poly, u64 *ct0, u64 *ct1,
-                               const u64 *g0, bool rotate, const ModDownDev &md,
-                               const NttTables &T, cudaStream_t s);
+                               const u64 *g0, bool rotate, const u64 *diag,
+                               const ModDownDev &md, const NttTables &T, cudaStream_t s);
 
 }  // namespace ksb

@@ -86,13 +86,18 @@ __global__ void __launch_bounds__(kBlk) k_modup_bconv(const u64 *__restrict__ co
   }
 }
 
-// One thread: two adjacent coefficients of one output limb, both polys.
+// One thread: two adjacent output slots (k, k+1) of one output limb, both
+// polys.  Under X -> X^elt the pair reads the aligned source pair
+// galois_src(k) & ~1 (the two sources are galois_src(k) and its neighbour
+// galois_src(k) ^ 1), so every warp still reads whole 256-byte segments.
+// Keys are streamed (__ldcs) so the extended digits stay in L2 across calls.
 __global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ t,
                                                        const u64 *__restrict__ c_ntt,
                                                        const u64 *__restrict__ key,
                                                        int key_limbs, u64 *__restrict__ cx,
                                                        ModUpDev mu, KsLayout lay,
-                                                       const PrimeDev *primes, int log_n) {
+                                                       const PrimeDev *primes, int log_n,
+                                                       uint32_t elt) {
   const int N = 1 << log_n;
   const int s = blockIdx.y;
   const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
@@ -101,15 +106,24 @@ __global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ 
   const PrimeDev P = primes[mu.prime_of[j]];
   const long long ks = lay.key_slot[s];
   const int dj = j < mu.Ql ? j / mu.alpha : -1;  // digit holding limb j
+  const uint32_t src = galois_src((uint32_t)k, elt, log_n);
+  const uint32_t sbase = src & ~1u;
+  const bool swap = (src & 1u) != 0;
   u128v a00 = {0, 0}, a01 = {0, 0}, a10 = {0, 0}, a11 = {0, 0};
   const long long kstride = (long long)key_limbs * N;
-  for (int d = 0; d < mu.beta; ++d) {
-    const u64 *src = (d == dj) ? c_ntt + (long long)lay.c_slot[s] * N
-                               : t + ((long long)d * lay.n_out + s) * N;
-    const ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(src + k);
-    const u64 *kb = key + (long long)(2 * d) * kstride + ks * N + k;
-    const ulonglong2 b = __ldg(reinterpret_cast<const ulonglong2 *>(kb));
-    const ulonglong2 a = __ldg(reinterpret_cast<const ulonglong2 *>(kb + kstride));
+  for (int di = 0; di < lay.n_digits; ++di) {
+    const int d = lay.digits[di];
+    const u64 *T = (d == dj) ? c_ntt + (long long)lay.c_slot[s] * N
+                             : t + ((long long)d * lay.n_out + s) * N;
+    ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(T + sbase);
+    if (swap) {
+      const u64 tmp = x.x;
+      x.x = x.y;
+      x.y = tmp;
+    }
+    const u64 *kb = key + (long long)(2 * di) * kstride + ks * N + k;
+    const ulonglong2 b = __ldcs(reinterpret_cast<const ulonglong2 *>(kb));
+    const ulonglong2 a = __ldcs(reinterpret_cast<const ulonglong2 *>(kb + kstride));
     mac(a00, x.x, b.x);
     mac(a01, x.y, b.y);
     mac(a10, x.x, a.x);
@@ -214,8 +228,9 @@ __global__ void k_mod_reduce(u64 *x, const int *prime_of_slot, const PrimeDev *p
   const int l = blockIdx.y;
   const int k = blockIdx.x * kBlk + threadIdx.x;
   if (k >= N) return;
-  const u64 q = primes[prime_of_slot[l]].q;
-  x[(long long)l * N + k] %= q;
+  const PrimeDev &P = primes[prime_of_slot[l]];
+  u64 &v = x[(long long)l * N + k];
+  v = reduce_full(v, P.q, P.mu);
 }
 
 __global__ void k_scatter(const u64 *__restrict__ gbuf, u64 *__restrict__ lbuf, int total,
@@ -323,10 +338,11 @@ cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLay
 
 cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
                           u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                          const PrimeDev *primes, int log_n, cudaStream_t s) {
+                          const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s) {
   if (lay.n_out <= 0) return cudaSuccess;
+  if (!(elt & 1u) || elt >= (2u << log_n)) return cudaErrorInvalidValue;
   k_inner_product<<<grid2(log_n, lay.n_out, 2), kBlk, 0, s>>>(t, c_ntt, key, key_limbs, cx, mu,
-                                                              lay, primes, log_n);
+                                                              lay, primes, log_n, elt);
   return cudaGetLastError();
 }
 

@@ -39,6 +39,8 @@ struct KsLayout {
   const int *key_slot;        // [n_out] limb slot of that limb in the key shard
   const int *c_slot;          // [n_out] local slot of Q limb j in the NTT-form input, or -1
   int coef_G, coef_ml;        // coefficient-form Q limb j at slot (j % G) * ml + j / G
+  const int *digits;          // [n_digits] digits summed by the inner product, ascending;
+  int n_digits;               // digit digits[i] is digit i of the key shard
 };
 
 // out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
@@ -51,12 +53,14 @@ cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t
 cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLayout &lay,
                         const PrimeDev *primes, int log_n, cudaStream_t s);
 
-// cx[p][s][k] = sum_d src_d[s][k] * key[d][p][key_slot[s]][k]  mod m_j,
-// src_d = c_ntt[c_slot[s]] when limb j lies in digit d, else t[d][s].
-// key: [beta_key][2][key_limbs][N].
+// Inner product of the automorphism X -> X^elt of the extended digits
+// (elt = 1: no automorphism), all in NTT form:
+//   cx[p][s][k] = sum_i src_{d_i}[s][galois_src(k)] * key[i][p][key_slot[s]][k]  mod m_j,
+// d_i = lay.digits[i], src_d = c_ntt[c_slot[s]] when limb j lies in digit d,
+// else t[d][s] (t: [beta][n_out][N]); key: [n_digits][2][key_limbs][N].
 cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
                           u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                          const PrimeDev *primes, int log_n, cudaStream_t s);
+                          const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s);
 
 // z[p][s][k] = sum_i [y_i[k] * phatinv_i]_{p_i} * w[j][i] mod q_j for the Q limbs
 // j = q_index[s], s < n_q; y: pointers to the alpha P-limb coefficient arrays

@@ -178,6 +178,24 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
 /* Number of kernels the last hot-path call launched (for bench accounting). */
 int ks_last_launch_count(const ks_ctx *ctx);
 
+/* CUDA graph capture and replay of hot-path calls (the capture/replay half
+ * of the reference's StreamManager, overlap/stream_manager.cu:25-159).
+ * ks_graph_capture_begin starts a thread-local capture on `stream` (not the
+ * legacy default stream); every hot-path call made on that stream until
+ * ks_graph_capture_end is recorded instead of run (batched calls fork their
+ * lanes from the capturing stream, NCCL collectives are captured too); end
+ * instantiates the graph.  Replay with ks_graph_launch on any stream of the
+ * context's device.  The graph keeps the pointers and keys of the captured
+ * calls: the ciphertext buffers must stay allocated and the keys uploaded
+ * while it is used; a call that fails during capture ends the capture.
+ * Make each kind of call once outside capture first (kernel attributes are
+ * set on first use); profiling must be off. */
+typedef struct ks_graph ks_graph;
+int ks_graph_capture_begin(ks_ctx *ctx, void *stream);
+int ks_graph_capture_end(ks_ctx *ctx, void *stream, ks_graph **out);
+int ks_graph_launch(ks_graph *graph, void *stream);
+int ks_graph_destroy(ks_graph *graph);
+
 /* Optional per-stage timing of the key switch with CUDA events recorded on
  * the launch stream (bench accounting; off by default).  ks_profile_read
  * waits for the recorded events, returns the summed milliseconds and the

@@ -1,8 +1,10 @@
 """Multi-GPU key switching through the C ABI: one process per GPU, NCCL
 communicators created by the library from an id broadcast over a gloo
-process group; every rank holds its cyclic share of the limbs.  The gathered
-result must equal the single-process CPU oracle bit for bit.  Skipped when
-fewer than two GPUs are visible."""
+process group.  Input broadcast: every rank holds its cyclic share of the
+limbs and the gathered result must equal the single-process CPU oracle bit
+for bit.  Output aggregation: every rank holds the whole ciphertext and its
+digits of the key, and every rank's result must equal the oracle.  Skipped
+when fewer than two GPUs are visible."""
 import os
 import socket
 import sys
@@ -24,7 +26,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, name, q):
+def _worker(rank, world, port, name, mode, q):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import torch
@@ -32,14 +34,17 @@ def _worker(rank, world, port, name, q):
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from comp390project_b200 import KS_KEY_GALOIS, KS_KEY_RELIN, KsContext
+        from comp390project_b200 import (KS_KEY_GALOIS, KS_KEY_RELIN, KsContext,
+                                         KS_MODE_OUTPUT_AGGREGATION)
         from tests.ksparams import oracle_for, split, CFG3, SMALL
         cfg = {"small": SMALL, "cfg3": CFG3}[name]
         o = oracle_for(name)
         log_n, qs, ps = split(cfg)
         N, L = o.N, o.L
         Ql = L
-        ctx = KsContext.from_process_group(log_n, qs, ps, device=rank, max_batch=2)
+        oa = mode == "oa"
+        ctx = KsContext.from_process_group(log_n, qs, ps, device=rank, max_batch=2,
+                                           mode=KS_MODE_OUTPUT_AGGREGATION if oa else 0)
         ctx.set_timeout_ms(60000)
         s = o.secret(11, 64 if name == "small" else 192)
         steps = [1, 3]
@@ -56,12 +61,14 @@ def _worker(rank, world, port, name, q):
                                    for j in range(Ql)]) for _ in range(2)]) for _ in steps]
         c3 = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
                                  for j in range(Ql)]) for _ in range(3)])
-        mine = list(range(rank, Ql, world))
+        mine = list(range(rank, Ql, world)) if not oa else list(range(Ql))
 
         def local(ct):
             return torch.from_numpy(np.ascontiguousarray(ct[:, mine]).view(np.int64)).cuda()
 
         def gather(t, n_polys):
+            if oa:  # every rank holds the whole result
+                return t.cpu()[:n_polys].numpy().view(np.uint64)
             h = torch.zeros((n_polys, (Ql + world - 1) // world, N), dtype=torch.int64)
             h[:, :len(mine)] = t.cpu()[:n_polys]
             out = [torch.zeros_like(h) for _ in range(world)]
@@ -91,17 +98,20 @@ def _worker(rank, world, port, name, q):
         # a lower level (short last digit)
         Ql2 = Ql - 3
         c2 = cts[0][:, :Ql2]
-        mine2 = list(range(rank, Ql2, world))
+        mine2 = list(range(rank, Ql2, world)) if not oa else list(range(Ql2))
         d2 = torch.from_numpy(np.ascontiguousarray(c2[:, mine2]).view(np.int64)).cuda()
         ctx.rotate(d2, Ql2, 1)
         torch.cuda.synchronize()
-        h = torch.zeros((2, (Ql2 + world - 1) // world, N), dtype=torch.int64)
-        h[:, :len(mine2)] = d2.cpu()
-        outs = [torch.zeros_like(h) for _ in range(world)]
-        dist.all_gather(outs, h)
-        full2 = np.zeros((2, Ql2, N), dtype=np.uint64)
-        for j in range(Ql2):
-            full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
+        if oa:
+            full2 = d2.cpu().numpy().view(np.uint64)
+        else:
+            h = torch.zeros((2, (Ql2 + world - 1) // world, N), dtype=torch.int64)
+            h[:, :len(mine2)] = d2.cpu()
+            outs = [torch.zeros_like(h) for _ in range(world)]
+            dist.all_gather(outs, h)
+            full2 = np.zeros((2, Ql2, N), dtype=np.uint64)
+            for j in range(Ql2):
+                full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
         ok &= np.array_equal(full2, o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
         ctx.close()
         q.put((rank, bool(ok)))
@@ -112,8 +122,9 @@ def _worker(rank, world, port, name, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["ib", "oa"])
 @pytest.mark.parametrize("name", ["small", "cfg3"])
-def test_two_gpu_keyswitch_bitexact(name, cuda_device):
+def test_two_gpu_keyswitch_bitexact(name, mode, cuda_device):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -121,7 +132,8 @@ def test_two_gpu_keyswitch_bitexact(name, cuda_device):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, mode, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in range(world))
