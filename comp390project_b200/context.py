@@ -281,6 +281,17 @@ class KsContext:
         self._check(self.lib.ks_rotate_hoisted(self.h, self._ptr(ct), int(level_limbs), st, n,
                                                ptrs, _stream_ptr(stream, self.device)))
 
+    def linear_transform_hoisted(self, ct, level_limbs: int, steps: Sequence[int], diags, out,
+                                 stream=None):
+        """out = sum_i diags[i] * rotate(ct, steps[i]) with one shared ModUp
+        (diags: NTT-form plaintexts [n_local][N])."""
+        n = len(steps)
+        dp = (C.c_void_p * n)(*[self._ptr(t) for t in diags])
+        st = (C.c_int * n)(*[int(s) for s in steps])
+        self._check(self.lib.ks_linear_transform_hoisted(self.h, self._ptr(ct), int(level_limbs),
+                                                         st, n, dp, self._ptr(out),
+                                                         _stream_ptr(stream, self.device)))
+
     def ntt_forward(self, data, n_limbs: int, first_prime: int = 0, batch: int = 1, stream=None):
         self._check(self.lib.ks_ntt_forward(self.h, self._ptr(data), int(n_limbs),
                                             int(first_prime), int(batch),

@@ -257,6 +257,14 @@ void build_moddown(Ctx &c) {
   }
   c.d_phatinv = upload(phatinv);
   c.d_pinv = upload(pinv);
+  std::vector<ulonglong2> pmodq(L);
+  for (int j = 0; j < L; ++j) {
+    const u64 q = c.primes[j];
+    u64 P = 1;
+    for (int t = 0; t < a; ++t) P = h_mulmod(P, c.primes[L + t] % q, q);
+    pmodq[j] = make_ulonglong2(P, h_shoup(P, q));
+  }
+  c.d_pmodq = upload(pmodq);
   std::vector<u64> wsh(w.size());
   for (int j = 0; j < L; ++j)
     for (int i = 0; i < a; ++i) wsh[(size_t)j * a + i] = h_shoup(w[(size_t)j * a + i], c.primes[j]);
@@ -601,6 +609,7 @@ void ctx_free(Ctx &c) {
   f(c.d_gauss);
   f(c.d_phatinv);
   f(c.d_pinv);
+  f(c.d_pmodq);
   f(c.d_mdw);
   f(c.d_mdwsh);
   for (size_t li = 0; li < c.lanes.size(); ++li) {
@@ -745,11 +754,13 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
 // ---------------------------------------------------------------------------
 enum Stage {
   ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_COLS, ST_MODUP_ROWS_IP, ST_INTT_P, ST_MODDOWN_COLS,
-  ST_MODDOWN_ROWS, ST_COMM, ST_COUNT
+  ST_MODDOWN_ROWS, ST_COMM, ST_MODUP_ROWS, ST_INNER_PROD, ST_COUNT
 };
+// modup_rows and inner_product are the two halves of modup_rows_ip that the
+// hoisted path runs apart (one row pass, one inner product per rotation).
 static const char *kStageNames[ST_COUNT] = {
-    "galois",       "intt_input",   "modup_cols",  "modup_rows_ip",
-    "intt_p",       "moddown_cols", "moddown_rows", "collective"};
+    "galois",       "intt_input",   "modup_cols",   "modup_rows_ip", "intt_p",
+    "moddown_cols", "moddown_rows", "collective",   "modup_rows",    "inner_product"};
 
 cudaEvent_t pool_event(Ctx &c) {
   if (!c.event_pool.empty()) {
@@ -921,6 +932,104 @@ void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaSt
   keyswitch_core(c, L, lv, key, L.s_g + nq * N, ct, ct + nq * N, L.s_g, true, s);
 }
 
+uint32_t elt_of_step(const Ctx &c, int step) {
+  const long long slots = c.N / 2;
+  long long st = ((step % slots) + slots) % slots;
+  return (uint32_t)h_powmod(3, (u64)st, 2ull * c.N);
+}
+
+// Hoisted rotations of one ciphertext ct [2][n_q][N] (not modified):
+//   shared by all rotations: INTT of c1, base extension + column pass, and
+//   the row pass of every extended limb -> lane 0's t (NTT form);
+//   outs != null, rotation i (galois element g_i): the inner product reads the
+//     extended digits through the automorphism (k_inner_product with elt g_i),
+//     all-reduce (output aggregation), ModDown: outs[i] = (c0 o g_i + ks0, ks1).
+//     Rotations run on the lanes round-robin (each lane has its own cx /
+//     ModDown scratch and communicator).  This is the hoisting of Halevi-Shoup
+//     (decompose and extend once, permute the extended digits per rotation).
+//   diags != null (linear transform, double hoisting as in Bossuat et al.,
+//     Eurocrypt 2021): every rotation's inner product, plus [P] c0 o g_i on the
+//     Q limbs, is multiplied by diags[i] (extended basis, [n_out][N]) and
+//     accumulated in lane 0's cx; one all-reduce (output aggregation) and one
+//     ModDown at the end: out = sum_i diags[i] * rot_i(ct).
+void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *const *outs,
+                const u64 *const *diags, u64 *out, cudaStream_t s) {
+  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  KS_REQUIRE(steps != nullptr && n >= 0, "bad rotation list");
+  KS_REQUIRE((outs != nullptr) != (out != nullptr), "give either outs or out");
+  const Level &lv = level_of(c, Ql);
+  const size_t nq = lv.n_q, N = c.N;
+  std::vector<uint32_t> elts(n);
+  std::vector<const KeyShard *> keys(n);
+  for (int i = 0; i < n; ++i) {
+    elts[i] = elt_of_step(c, steps[i]);
+    keys[i] = &key_get(c, KS_KEY_GALOIS, elts[i]);
+    if (outs) KS_REQUIRE(outs[i] && aligned16(outs[i]), "output pointer null or misaligned");
+    else KS_REQUIRE(diags && diags[i] && aligned16(diags[i]), "diagonal pointer null or misaligned");
+  }
+  KS_CUDA(cudaSetDevice(c.device));
+  if (out) KS_CUDA(cudaMemsetAsync(out, 0, 2 * nq * N * 8, s));
+  if (n == 0) return;
+  const NttTables T = c.tables();
+  Ctx::Lane &L0 = c.lanes[0];
+  const u64 *c1 = ct + nq * N;
+  ks_modup_cols(c, L0, lv, c1, s);
+  {
+    StageTimer tm(c, ST_MODUP_ROWS, s);
+    LimbMap mt{L0.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
+    KS_CUDA(ntt_forward_rows_only(mt, lv.n_jobs, T, s));
+    c.launches += lv.n_jobs > 0 ? 1 : 0;
+  }
+  if (!outs) {
+    const bool add_c0 = !c.oa() || c.rank == 0;  // the c0 term once over the ranks
+    for (int i = 0; i < n; ++i) {
+      StageTimer tm(c, ST_INNER_PROD, s);
+      if (lv.lay.n_digits > 0) {
+        KS_CUDA(inner_product_acc(L0.s_t, c1, keys[i]->d, keys[i]->limbs, L0.s_cx, diags[i], ct,
+                                  c.d_pmodq, add_c0, i == 0, lv.mu, lv.lay, c.d_primes,
+                                  c.log_n, elts[i], s));
+        c.launches += lv.lay.n_out > 0 ? 1 : 0;
+      } else if (i == 0) {
+        KS_CUDA(cudaMemsetAsync(L0.s_cx, 0, (size_t)2 * lv.n_out * N * 8, s));
+      }
+    }
+    ks_aggregate(c, L0, lv, s);
+    ks_moddown(c, L0, lv, out, out + nq * N, nullptr, true, nullptr, s);
+    return;
+  }
+  const int nl = std::min<int>((int)c.lanes.size(), n);
+  if (nl > 1) {
+    KS_CUDA(cudaEventRecord(c.ev_fork, s));
+    for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
+  }
+  for (int i = 0; i < n; ++i) {
+    const int li = i % nl;
+    Ctx::Lane &L = c.lanes[li];
+    const cudaStream_t ls = li == 0 ? s : L.stream;
+    {
+      StageTimer tm(c, ST_GALOIS, ls);
+      KS_CUDA(galois_ntt(ct, L.s_g, (int)nq, c.log_n, elts[i], ls));
+      c.launches += 1;
+    }
+    {
+      StageTimer tm(c, ST_INNER_PROD, ls);
+      if (lv.lay.n_digits > 0) {
+        KS_CUDA(inner_product(L0.s_t, c1, keys[i]->d, keys[i]->limbs, L.s_cx, lv.mu, lv.lay,
+                              c.d_primes, c.log_n, elts[i], ls));
+        c.launches += lv.lay.n_out > 0 ? 1 : 0;
+      } else {
+        KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * N * 8, ls));
+      }
+    }
+    ks_aggregate(c, L, lv, ls);
+    ks_moddown(c, L, lv, outs[i], outs[i] + nq * N, L.s_g, true, nullptr, ls);
+  }
+  for (int li = 1; li < nl; ++li) {
+    KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
+    KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));
+  }
+}
+
 void do_relin(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, cudaStream_t s) {
   KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
   const Level &lv = level_of(c, Ql);
@@ -935,11 +1044,6 @@ Ctx::Lane &lane0(Ctx &c) {
   return c.lanes[0];
 }
 
-uint32_t elt_of_step(const Ctx &c, int step) {
-  const long long slots = c.N / 2;
-  long long st = ((step % slots) + slots) % slots;
-  return (uint32_t)h_powmod(3, (u64)st, 2ull * c.N);
-}
 
 }  // namespace
 
@@ -1261,10 +1365,26 @@ int ks_graph_destroy(ks_graph *graph) {
 
 int ks_rotate_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs, const int *steps, int n,
                       uint64_t *const *outs, void *stream) {
-  (void)ct; (void)level_limbs; (void)steps; (void)n; (void)outs; (void)stream;
   if (!ctx) return KS_ERR_INVALID;
-  ctx->c.err = "hoisted rotations are not built yet";
-  return KS_ERR_UNSUPPORTED;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    KS_REQUIRE(outs != nullptr, "outs is null");
+    KS_REQUIRE(!ctx->c.lanes.empty(), "context has no special primes (NTT-only context)");
+    do_hoisted(ctx->c, ct, level_limbs, steps, n, outs, nullptr, nullptr, (cudaStream_t)stream);
+  });
+}
+
+int ks_linear_transform_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs,
+                                const int *steps, int n, const uint64_t *const *diags,
+                                uint64_t *out, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    KS_REQUIRE(out != nullptr && aligned16(out), "output pointer null or misaligned");
+    KS_REQUIRE(out != ct, "out must not alias ct");
+    KS_REQUIRE(!ctx->c.lanes.empty(), "context has no special primes (NTT-only context)");
+    do_hoisted(ctx->c, ct, level_limbs, steps, n, nullptr, diags, out, (cudaStream_t)stream);
+  });
 }
 
 static int ntt_api(ks_ctx *ctx, uint64_t *data, int n_limbs, int first_prime, int batch,

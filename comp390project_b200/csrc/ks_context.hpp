@@ -92,6 +92,7 @@ struct Ctx {
   u64 *d_gauss = nullptr;
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
+  ulonglong2 *d_pmodq = nullptr;  // [L] {[P]_{q_j}, Shoup}
   u64 *d_mdw = nullptr, *d_mdwsh = nullptr;
   std::vector<Level> levels;  // index Ql (1..L)
   // key-basis ownership

@@ -414,8 +414,9 @@ __global__ void __launch_bounds__(kThreads)
   const long long row0 = (long long)blockIdx.x * G::R, row = row0 + rr;
   const u64 *cxp = cx + p * cx_stride_poly + (long long)cx_slot[s] * N + tile0;
   u64 *dst = (p == 0 ? ct0 : ct1) + (long long)s * N + tile0;
-  const u64 *base =
-      (p == 0) ? (rotate ? g0 + (long long)s * N + tile0 : dst) : (rotate ? nullptr : dst);
+  // rotate with g0 == null: ct0 = o (no c0 term; the hoisted linear transform)
+  const u64 *g0t = g0 ? g0 + (long long)s * N + tile0 : nullptr;
+  const u64 *base = (p == 0) ? (rotate ? g0t : dst) : (rotate ? nullptr : dst);
   const bool fp = P.q < kFpBound;
   if (fp) stage_row_twiddles<LOG_M, G::R>(smtw, T.fwd_fp + (long long)j * N, log_n, row0);
   // Pull the epilogue operands into L2 while the butterflies run: one

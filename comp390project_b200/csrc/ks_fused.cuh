@@ -43,7 +43,8 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
 
 // Row pass of z[p][s] with the ModDown finish in the epilogue:
 //   o = (cx[p][cx_slot[s]] - z) * P^-1 mod q_j;
-//   p = 0: v = (rotate ? g0 : ct0) + o;   p = 1: v = rotate ? o : ct1 + o;
+//   p = 0: v = (rotate ? g0 : ct0) + o (rotate with g0 null: v = o);
+//   p = 1: v = rotate ? o : ct1 + o;
 //   ct_p = v, or with diag ([n_q][N], NTT form): ct_p += diag * v (a plaintext
 //   product accumulated into ct_p).
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,

@@ -86,29 +86,23 @@ __global__ void __launch_bounds__(kBlk) k_modup_bconv(const u64 *__restrict__ co
   }
 }
 
-// One thread: two adjacent output slots (k, k+1) of one output limb, both
-// polys.  Under X -> X^elt the pair reads the aligned source pair
-// galois_src(k) & ~1 (the two sources are galois_src(k) and its neighbour
-// galois_src(k) ^ 1), so every warp still reads whole 256-byte segments.
-// Keys are streamed (__ldcs) so the extended digits stay in L2 across calls.
-__global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ t,
-                                                       const u64 *__restrict__ c_ntt,
-                                                       const u64 *__restrict__ key,
-                                                       int key_limbs, u64 *__restrict__ cx,
-                                                       ModUpDev mu, KsLayout lay,
-                                                       const PrimeDev *primes, int log_n,
-                                                       uint32_t elt) {
-  const int N = 1 << log_n;
-  const int s = blockIdx.y;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
+// Inner product of the automorphism X -> X^elt of the extended digits for
+// the two adjacent output slots (k, k+1) of output limb s, both polys
+// (canonical).  The pair reads the aligned source pair galois_src(k) & ~1 (the
+// two sources are galois_src(k) and its neighbour galois_src(k) ^ 1), so every
+// warp still reads whole 256-byte segments.  Keys are streamed (__ldcs) so the
+// extended digits stay in L2 across calls.
+struct IpPair {
+  ulonglong2 r0, r1;
+};
+__device__ __forceinline__ IpPair ip_pair(const u64 *__restrict__ t, const u64 *__restrict__ c_ntt,
+                                          const u64 *__restrict__ key, int key_limbs,
+                                          const ModUpDev &mu, const KsLayout &lay,
+                                          const PrimeDev &P, int N, int s, int k, uint32_t sbase,
+                                          bool swap) {
   const int j = lay.out_j[s];
-  const PrimeDev P = primes[mu.prime_of[j]];
   const long long ks = lay.key_slot[s];
   const int dj = j < mu.Ql ? j / mu.alpha : -1;  // digit holding limb j
-  const uint32_t src = galois_src((uint32_t)k, elt, log_n);
-  const uint32_t sbase = src & ~1u;
-  const bool swap = (src & 1u) != 0;
   u128v a00 = {0, 0}, a01 = {0, 0}, a10 = {0, 0}, a11 = {0, 0};
   const long long kstride = (long long)key_limbs * N;
   for (int di = 0; di < lay.n_digits; ++di) {
@@ -129,13 +123,74 @@ __global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ 
     mac(a10, x.x, a.x);
     mac(a11, x.y, a.y);
   }
-  ulonglong2 r0, r1;
-  r0.x = barrett128(a00, P.q, P.br_hi, P.br_lo);
-  r0.y = barrett128(a01, P.q, P.br_hi, P.br_lo);
-  r1.x = barrett128(a10, P.q, P.br_hi, P.br_lo);
-  r1.y = barrett128(a11, P.q, P.br_hi, P.br_lo);
-  *reinterpret_cast<ulonglong2 *>(cx + (long long)s * N + k) = r0;
-  *reinterpret_cast<ulonglong2 *>(cx + ((long long)lay.n_out + s) * N + k) = r1;
+  IpPair r;
+  r.r0.x = barrett128(a00, P.q, P.br_hi, P.br_lo);
+  r.r0.y = barrett128(a01, P.q, P.br_hi, P.br_lo);
+  r.r1.x = barrett128(a10, P.q, P.br_hi, P.br_lo);
+  r.r1.y = barrett128(a11, P.q, P.br_hi, P.br_lo);
+  return r;
+}
+
+// One thread: two adjacent output slots of one output limb, both polys.
+__global__ void __launch_bounds__(kBlk) k_inner_product(const u64 *__restrict__ t,
+                                                       const u64 *__restrict__ c_ntt,
+                                                       const u64 *__restrict__ key,
+                                                       int key_limbs, u64 *__restrict__ cx,
+                                                       ModUpDev mu, KsLayout lay,
+                                                       const PrimeDev *primes, int log_n,
+                                                       uint32_t elt) {
+  const int N = 1 << log_n;
+  const int s = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const PrimeDev P = primes[mu.prime_of[lay.out_j[s]]];
+  const uint32_t src = galois_src((uint32_t)k, elt, log_n);
+  const IpPair r = ip_pair(t, c_ntt, key, key_limbs, mu, lay, P, N, s, k, src & ~1u, src & 1u);
+  *reinterpret_cast<ulonglong2 *>(cx + (long long)s * N + k) = r.r0;
+  *reinterpret_cast<ulonglong2 *>(cx + ((long long)lay.n_out + s) * N + k) = r.r1;
+}
+
+// Linear-transform accumulation in the extended basis (double hoisting):
+//   acc[0][s] (+)= diag[s] * (ip0 + [P]_{q_j} * c0[galois_src])   (Q limbs; c0 term if add_c0)
+//   acc[1][s] (+)= diag[s] * ip1
+// first: acc starts at zero instead of being read.
+__global__ void __launch_bounds__(kBlk) k_inner_product_acc(
+    const u64 *__restrict__ t, const u64 *__restrict__ c_ntt, const u64 *__restrict__ key,
+    int key_limbs, u64 *__restrict__ acc, const u64 *__restrict__ diag,
+    const u64 *__restrict__ c0, const ulonglong2 *__restrict__ pmodq, int add_c0, int first,
+    ModUpDev mu, KsLayout lay, const PrimeDev *primes, int log_n, uint32_t elt) {
+  const int N = 1 << log_n;
+  const int s = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const int j = lay.out_j[s];
+  const PrimeDev P = primes[mu.prime_of[j]];
+  const uint32_t src = galois_src((uint32_t)k, elt, log_n);
+  const uint32_t sbase = src & ~1u;
+  const bool swap = (src & 1u) != 0;
+  IpPair r = ip_pair(t, c_ntt, key, key_limbs, mu, lay, P, N, s, k, sbase, swap);
+  if (add_c0 && j < mu.Ql) {
+    ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(c0 + (long long)lay.c_slot[s] * N + sbase);
+    if (swap) {
+      const u64 tmp = x.x;
+      x.x = x.y;
+      x.y = tmp;
+    }
+    const ulonglong2 pq = pmodq[j];
+    r.r0.x = add_mod(r.r0.x, mul_shoup(x.x, pq.x, pq.y, P.q), P.q);
+    r.r0.y = add_mod(r.r0.y, mul_shoup(x.y, pq.x, pq.y, P.q), P.q);
+  }
+  const ulonglong2 dg = *reinterpret_cast<const ulonglong2 *>(diag + (long long)s * N + k);
+  u64 *a0 = acc + (long long)s * N + k;
+  u64 *a1 = acc + ((long long)lay.n_out + s) * N + k;
+  ulonglong2 v0 = first ? make_ulonglong2(0, 0) : *reinterpret_cast<const ulonglong2 *>(a0);
+  ulonglong2 v1 = first ? make_ulonglong2(0, 0) : *reinterpret_cast<const ulonglong2 *>(a1);
+  v0.x = mac_reduce(v0.x, r.r0.x, dg.x, P.q, P.br_hi, P.br_lo);
+  v0.y = mac_reduce(v0.y, r.r0.y, dg.y, P.q, P.br_hi, P.br_lo);
+  v1.x = mac_reduce(v1.x, r.r1.x, dg.x, P.q, P.br_hi, P.br_lo);
+  v1.y = mac_reduce(v1.y, r.r1.y, dg.y, P.q, P.br_hi, P.br_lo);
+  *reinterpret_cast<ulonglong2 *>(a0) = v0;
+  *reinterpret_cast<ulonglong2 *>(a1) = v1;
 }
 
 // One thread: two coefficients of one poly, all Q output limbs.
@@ -333,6 +388,18 @@ cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLay
                         const PrimeDev *primes, int log_n, cudaStream_t s) {
   if (mu.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
   k_modup_bconv<<<grid2(log_n, mu.beta, 2), kBlk, 0, s>>>(coef, t, mu, lay, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
+                              u64 *acc, const u64 *diag, const u64 *c0, const ulonglong2 *pmodq,
+                              bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
+                              const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s) {
+  if (lay.n_out <= 0) return cudaSuccess;
+  if (!(elt & 1u) || elt >= (2u << log_n)) return cudaErrorInvalidValue;
+  k_inner_product_acc<<<grid2(log_n, lay.n_out, 2), kBlk, 0, s>>>(
+      t, c_ntt, key, key_limbs, acc, diag, c0, pmodq, add_c0 ? 1 : 0, first ? 1 : 0, mu, lay,
+      primes, log_n, elt);
   return cudaGetLastError();
 }
 

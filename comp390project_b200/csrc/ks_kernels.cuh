@@ -61,6 +61,15 @@ cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLay
 cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
                           u64 *cx, const ModUpDev &mu, const KsLayout &lay,
                           const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s);
+// The same inner product accumulated into a linear transform in the extended
+// basis (double hoisting): with ip_p the inner product above,
+//   acc[0][s] = (first ? 0 : acc[0][s]) + diag[s] * (ip_0 + [P]_{q_j} c0[c_slot[s]] o elt)
+//   acc[1][s] = (first ? 0 : acc[1][s]) + diag[s] * ip_1
+// (the c0 term only for Q limbs and when add_c0; pmodq[j] = {[P]_{q_j}, Shoup}).
+cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
+                              u64 *acc, const u64 *diag, const u64 *c0, const ulonglong2 *pmodq,
+                              bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
+                              const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s);
 
 // z[p][s][k] = sum_i [y_i[k] * phatinv_i]_{p_i} * w[j][i] mod q_j for the Q limbs
 // j = q_index[s], s < n_q; y: pointers to the alpha P-limb coefficient arrays

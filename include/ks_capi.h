@@ -151,10 +151,24 @@ int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream
 /* n rotations of n independent ciphertexts (cts[i] rotated by steps[i]). */
 int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n,
                     int level_limbs, void *stream);
-/* Hoisted rotations: one ModUp of ct's c1 shared by n rotations; outs[i]
- * [2][n_local][N] receives ct rotated by steps[i].  ct is not modified. */
+/* Hoisted rotations: one ModUp of ct's c1 shared by n rotations (the
+ * extended digits are permuted per rotation inside the inner product); outs[i]
+ * [2][n_local][N] receives ct rotated by steps[i].  ct is not modified.  Keys
+ * for every step must be uploaded. */
 int ks_rotate_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs, const int *steps,
                       int n, uint64_t *const *outs, void *stream);
+/* Hoisted linear transform (BSGS / CoeffToSlot style):
+ *   out = sum_i diags[i] * rotate(ct, steps[i])
+ * with one ModUp of c1 and one ModDown for all rotations (double hoisting:
+ * the products are accumulated in the extended basis Q_l * P).  diags[i]
+ * is the plaintext diagonal in NTT form in the extended basis, one word per
+ * output limb of this rank: [Ql + alpha][N] (Q limbs then P limbs) on one
+ * GPU or in output aggregation, the owned Q limbs then the owned P limbs in
+ * input broadcast.  No rescale.  out [2][n_local][N] is overwritten and must
+ * not alias ct. */
+int ks_linear_transform_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs,
+                                const int *steps, int n, const uint64_t *const *diags,
+                                uint64_t *out, void *stream);
 
 /* Batched negacyclic NTT in place over data [batch][n_limbs][N]; limb i uses
  * prime first_prime + i of the context's basis (Q primes then P primes).

@@ -524,6 +524,50 @@ void ork_rotate_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
   }
 }
 
+// Hoisted linear transform with one ModDown ("double hoisting", Bossuat,
+// Mouchet, Troncoso-Pastoriza, Hubaux, Eurocrypt 2021; the reference has no
+// counterpart -- its bootstrapping lives in the absent NEXUS Bootstrapper):
+//   t = ModUp(c1) once; for each rotation r (element g_r):
+//     acc_0 += d_r * (IP_0(g_r(t), key_r) + [P]_{q_j} g_r(c0))   (Q limbs; P limbs: no c0)
+//     acc_1 += d_r * IP_1(g_r(t), key_r)
+//   out_p = ModDown(acc_p).
+// d_r: the plaintext diagonal in the extended basis, [Ql + alpha][N] NTT form
+// (Q limbs, then the alpha P limbs).  P * x has zero residues mod every p_i,
+// so ModDown(P * x + y) = x + ModDown(y) exactly: out = sum_r d_r * rot_r(ct)
+// up to the rounding of one ModDown instead of one per rotation.
+void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
+                                  const uint32_t *elts, const uint64_t *const *keys,
+                                  const uint64_t *const *diags, uint64_t *out) {
+  size_t N = c->N, QN = (size_t)Ql * N;
+  int QlP = Ql + c->alpha, beta = ork_num_digits(c, Ql);
+  std::vector<u64> t((size_t)beta * QlP * N), tg(t.size()), cx((size_t)2 * QlP * N);
+  std::vector<u64> acc((size_t)2 * QlP * N, 0), g0(QN);
+  std::vector<u64> Pq(Ql);
+  for (int j = 0; j < Ql; ++j) {
+    u64 P = 1;
+    for (int i = 0; i < c->alpha; ++i) P = mulmod(P, c->m[c->L + i] % c->m[j], c->m[j]);
+    Pq[j] = P;
+  }
+  ork_modup(c, ct + QN, Ql, t.data());
+  for (int r = 0; r < n; ++r) {
+    ork_galois_ntt(c, elts[r], t.data(), tg.data(), beta * QlP);
+    ork_inner_product(c, tg.data(), Ql, keys[r], cx.data());
+    ork_galois_ntt(c, elts[r], ct, g0.data(), Ql);
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < QlP; ++j) {
+      u64 q = c->m[qlp_key_index(c, Ql, j)];
+      for (int p = 0; p < 2; ++p)
+        for (size_t k = 0; k < N; ++k) {
+          u64 v = cx[((size_t)p * QlP + j) * N + k];
+          if (p == 0 && j < Ql) v = addmod(v, mulmod(Pq[j], g0[(size_t)j * N + k], q), q);
+          u64 &a = acc[((size_t)p * QlP + j) * N + k];
+          a = addmod(a, mulmod(diags[r][(size_t)j * N + k], v, q), q);
+        }
+    }
+  }
+  for (int p = 0; p < 2; ++p) ork_moddown(c, acc.data() + (size_t)p * QlP * N, Ql, out + (size_t)p * QN);
+}
+
 // ---------------------------------------------------------------------------
 // Deterministic sampling (synthetic keys and ciphertexts; NOT a secure RNG)
 // ---------------------------------------------------------------------------
@@ -677,6 +721,15 @@ void fft(std::vector<cd> &a, int sign) {
 
 void ork_encode(const ork_ctx *c, const double *re, const double *im, int n_slots, double scale,
                 int Ql, uint64_t *pt) {
+  std::vector<int> idx(Ql);
+  for (int j = 0; j < Ql; ++j) idx[j] = j;
+  ork_encode_basis(c, re, im, n_slots, scale, idx.data(), Ql, pt);
+}
+
+// Same encoding into the primes idx[0..n_idx) of the key basis (Q primes,
+// then P primes): pt [n_idx][N], NTT form.
+void ork_encode_basis(const ork_ctx *c, const double *re, const double *im, int n_slots,
+                      double scale, const int *key_idx, int n_idx, uint64_t *pt) {
   size_t N = c->N, slots = N / 2;
   std::vector<cd> V(N, cd(0, 0));
   u64 e = 1, twoN = 2 * N;
@@ -692,16 +745,15 @@ void ork_encode(const ork_ctx *c, const double *re, const double *im, int n_slot
     cd x = V[n] / (double)N * std::polar(1.0, -M_PI * (double)n / (double)N);
     coef[n] = std::llround(x.real() * scale);
   }
-  std::vector<int> idx(Ql);
-  for (int j = 0; j < Ql; ++j) {
-    idx[j] = j;
-    u64 q = c->m[j];
+  std::vector<int> idx(key_idx, key_idx + n_idx);
+  for (int j = 0; j < n_idx; ++j) {
+    u64 q = c->m[idx[j]];
     for (size_t n = 0; n < N; ++n) {
       long long v = coef[n];
       pt[j * N + n] = v >= 0 ? (u64)v % q : (q - ((u64)(-v) % q)) % q;
     }
   }
-  ntt_batch(c, pt, Ql, idx.data(), true);
+  ntt_batch(c, pt, n_idx, idx.data(), true);
 }
 
 void ork_decode(const ork_ctx *c, const uint64_t *pt, int Ql, double scale, double *re, double *im,

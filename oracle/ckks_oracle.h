@@ -94,6 +94,11 @@ void ork_relinearize(const ork_ctx *c, const uint64_t *ct, int Ql,
 void ork_rotate_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
                         const uint32_t *elts, const uint64_t *const *keys,
                         uint64_t *out);
+/* out = sum_r diags[r] * rotate(ct, elts[r]) with one ModUp and one ModDown
+ * (double hoisting); diags[r] [Ql + alpha][N] NTT form in the extended basis. */
+void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
+                                  const uint32_t *elts, const uint64_t *const *keys,
+                                  const uint64_t *const *diags, uint64_t *out);
 
 /* Deterministic sampling shared with the product's synthetic-key generator. */
 uint64_t ork_prng(uint64_t seed, uint64_t domain, uint64_t idx);
@@ -108,6 +113,8 @@ void ork_keygen_relin(const ork_ctx *c, const int8_t *s, uint64_t seed, uint64_t
 /* CKKS encoding with N/2 slots, slot j <-> root zeta^(3^j). pt: [Ql][N] NTT. */
 void ork_encode(const ork_ctx *c, const double *re, const double *im, int n_slots,
                 double scale, int Ql, uint64_t *pt);
+void ork_encode_basis(const ork_ctx *c, const double *re, const double *im, int n_slots,
+                      double scale, const int *key_idx, int n_idx, uint64_t *pt);
 void ork_decode(const ork_ctx *c, const uint64_t *pt, int Ql, double scale,
                 double *re, double *im, int n_slots);
 void ork_encrypt(const ork_ctx *c, const int8_t *s, const uint64_t *pt, int Ql,

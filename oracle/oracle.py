@@ -59,6 +59,10 @@ def lib():
             "ork_apply_galois": (V, [P, u64p, I, U32, u64p, u64p]),
             "ork_relinearize": (V, [P, u64p, I, u64p, u64p]),
             "ork_rotate_hoisted": (V, [P, u64p, I, I, C.POINTER(C.c_uint32), C.POINTER(C.c_void_p), u64p]),
+            "ork_linear_transform_hoisted": (V, [P, u64p, I, I, C.POINTER(C.c_uint32),
+                                                 C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                                 u64p]),
+            "ork_encode_basis": (V, [P, f64p, f64p, I, D, i32p, I, u64p]),
             "ork_prng": (U64, [U64, U64, U64]),
             "ork_gauss": (I, [U64]),
             "ork_gauss_table": (V, [u64p]),
@@ -208,6 +212,22 @@ class Oracle:
                                  out.reshape(-1))
         return out
 
+    def linear_transform_hoisted(self, ct: np.ndarray, Ql: int, elts, keys, diags) -> np.ndarray:
+        """sum_r diags[r] * rot_r(ct) with one ModUp and one ModDown; diags[r]:
+        [Ql + alpha][N] NTT-form plaintexts in the extended basis."""
+        n = len(elts)
+        out = np.zeros((2, Ql, self.N), dtype=np.uint64)
+        e = (C.c_uint32 * n)(*[int(x) for x in elts])
+        ks = [np.ascontiguousarray(k) for k in keys]
+        ds = [np.ascontiguousarray(d, dtype=np.uint64) for d in diags]
+        for d in ds:
+            assert d.shape == (Ql + self.alpha, self.N)
+        kp = (C.c_void_p * n)(*[k.ctypes.data for k in ks])
+        dp = (C.c_void_p * n)(*[d.ctypes.data for d in ds])
+        lib().ork_linear_transform_hoisted(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, n,
+                                           e, kp, dp, out.reshape(-1))
+        return out
+
     # -- keys, encoding, encryption -------------------------------------------
     def secret(self, seed: int, hamming_weight: int = 0) -> np.ndarray:
         s = np.zeros(self.N, dtype=np.int8)
@@ -236,6 +256,17 @@ class Oracle:
                                   dtype=np.float64)
         pt = np.zeros((Ql, self.N), dtype=np.uint64)
         lib().ork_encode(self.h, re, im, len(re), scale, Ql, pt.reshape(-1))
+        return pt
+
+    def encode_basis(self, z: np.ndarray, scale: float, key_idx) -> np.ndarray:
+        """encode() into the key-basis primes key_idx (Q primes first, then P)."""
+        z = np.asarray(z)
+        re = np.ascontiguousarray(z.real, dtype=np.float64)
+        im = np.ascontiguousarray(np.imag(z) if np.iscomplexobj(z) else np.zeros(len(z)),
+                                  dtype=np.float64)
+        idx = np.ascontiguousarray(key_idx, dtype=np.int32)
+        pt = np.zeros((len(idx), self.N), dtype=np.uint64)
+        lib().ork_encode_basis(self.h, re, im, len(re), scale, idx, len(idx), pt.reshape(-1))
         return pt
 
     def decode(self, pt: np.ndarray, Ql: int, scale: float, n_slots: int | None = None) -> np.ndarray:

@@ -234,6 +234,36 @@ def test_hoisted_rotations_decode():
         assert np.abs(dec - np.roll(z, -st)).mean() < 1e-3
 
 
+def test_hoisted_linear_transform_decodes():
+    """Double hoisting (one ModUp, products accumulated in the extended basis,
+    one ModDown) decodes to sum_r d_r * roll(z, r)."""
+    o = oracle_for("small")
+    s = o.secret(12, 64)
+    steps = [1, 3, 8]
+    elts = [o.galois_elt(st) for st in steps]
+    keys = [o.keygen_galois(s, e, 60 + i) for i, e in enumerate(elts)]
+    Ql = o.L
+    n = o.N // 2
+    rng = np.random.default_rng(13)
+    z = rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)
+    ct = o.encrypt(s, o.encode(z, 2.0 ** 40, Ql), Ql, 19)
+    dz = [rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n) for _ in steps]
+    basis = list(range(Ql)) + [o.L + i for i in range(o.alpha)]
+    diags = [o.encode_basis(x, 2.0 ** 40, basis) for x in dz]
+    out = o.linear_transform_hoisted(ct, Ql, elts, keys, diags)
+    dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 80)
+    want = sum(x * np.roll(z, -st) for x, st in zip(dz, steps))
+    assert np.abs(dec - want).mean() < 1e-3
+
+
+def test_encode_basis_matches_encode_on_q_limbs():
+    o = oracle_for("small")
+    z = np.random.default_rng(2).uniform(-1, 1, o.N // 2)
+    basis = list(range(o.L)) + [o.L + i for i in range(o.alpha)]
+    ext = o.encode_basis(z, 2.0 ** 40, basis)
+    assert np.array_equal(ext[:o.L], o.encode(z, 2.0 ** 40, o.L))
+
+
 def test_secret_hamming_weight_and_gaussian_support():
     o = oracle_for("small")
     s = o.secret(3, 64)
