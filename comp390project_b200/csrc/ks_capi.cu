@@ -268,9 +268,15 @@ void build_moddown(Ctx &c) {
   std::vector<u64> wsh(w.size());
   for (int j = 0; j < L; ++j)
     for (int i = 0; i < a; ++i) wsh[(size_t)j * a + i] = h_shoup(w[(size_t)j * a + i], c.primes[j]);
+  std::vector<double> wq(w.size(), 0.0);
+  for (int j = 0; j < L; ++j)
+    if (c.primes[j] < kFpBound)
+      for (int i = 0; i < a; ++i)
+        wq[(size_t)j * a + i] = (double)w[(size_t)j * a + i] / (double)c.primes[j];
   c.d_mdw = upload(w);
   c.d_mdwsh = upload(wsh);
-  c.md = ModDownDev{a, L, c.d_phatinv, c.d_mdw, c.d_pinv, c.d_mdwsh};
+  c.d_mdwq = upload(wq);
+  c.md = ModDownDev{a, L, c.d_phatinv, c.d_mdw, c.d_pinv, c.d_mdwsh, c.d_mdwq};
 }
 
 void build_level(Ctx &c, Level &lv, int Ql) {
@@ -612,6 +618,7 @@ void ctx_free(Ctx &c) {
   f(c.d_pmodq);
   f(c.d_mdw);
   f(c.d_mdwsh);
+  f(c.d_mdwq);
   for (size_t li = 0; li < c.lanes.size(); ++li) {
     Ctx::Lane &ln = c.lanes[li];
     f(ln.arena);
@@ -806,14 +813,15 @@ void allgather(ncclComm_t comm, const u64 *send, u64 *recv, size_t words, cudaSt
 // Steps 2-3: scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the
 // input limbs this rank extends (input broadcast all-gathers them), then the
 // base extension fused into the column pass -> L.s_t.
-void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const u64 *in_ntt, cudaStream_t s) {
+void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const u64 *in_ntt, cudaStream_t s,
+                   uint32_t elt = 1) {
   const size_t N = c.N;
   const NttTables T = c.tables();
   {
     StageTimer tm(c, ST_INTT_IN, s);
     LimbMap min{const_cast<u64 *>(in_ntt), 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
     LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s));
+    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s, elt));
     c.launches += lv.n_intt > 0 ? 2 : 0;
   }
   if (!c.replicated()) {
@@ -889,18 +897,20 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, u64 *ct0, u64 *ct1, const
   }
 }
 
-// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]).
+// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]), read
+// through X -> X^elt (elt = 1: as it is).
 // rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
 void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt,
-                    u64 *ct0, u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s) {
+                    u64 *ct0, u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s,
+                    uint32_t elt = 1) {
   const NttTables T = c.tables();
-  ks_modup_cols(c, L, lv, in_ntt, s);
+  ks_modup_cols(c, L, lv, in_ntt, s, elt);
   // 4. row pass of every extended limb fused with the inner product
   {
     StageTimer tm(c, ST_MODUP_ROWS_IP, s);
     if (lv.lay.n_digits > 0) {
       KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay,
-                                       T, s));
+                                       T, s, elt));
       c.launches += lv.lay.n_out > 0 ? 1 : 0;
     } else {  // output aggregation with more ranks than digits: a zero partial sum
       KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));
@@ -923,13 +933,14 @@ void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaSt
   const KeyShard &key = key_get(c, KS_KEY_GALOIS, elt);
   const size_t nq = lv.n_q, N = c.N;
   KS_CUDA(cudaSetDevice(c.device));
-  // 1. automorphism of both polys -> g0, g1
+  // 1. automorphism of c0 -> g0 (c1 is read through the automorphism by the
+  //    input INTT and the inner product; it is overwritten only at the end)
   {
     StageTimer tm(c, ST_GALOIS, s);
-    KS_CUDA(galois_ntt(ct, L.s_g, 2 * (int)nq, c.log_n, elt, s));
+    KS_CUDA(galois_ntt(ct, L.s_g, (int)nq, c.log_n, elt, s));
     c.launches += 1;
   }
-  keyswitch_core(c, L, lv, key, L.s_g + nq * N, ct, ct + nq * N, L.s_g, true, s);
+  keyswitch_core(c, L, lv, key, ct + nq * N, ct, ct + nq * N, L.s_g, true, s, elt);
 }
 
 uint32_t elt_of_step(const Ctx &c, int step) {

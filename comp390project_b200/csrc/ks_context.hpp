@@ -94,6 +94,7 @@ struct Ctx {
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
   ulonglong2 *d_pmodq = nullptr;  // [L] {[P]_{q_j}, Shoup}
   u64 *d_mdw = nullptr, *d_mdwsh = nullptr;
+  double *d_mdwq = nullptr;
   std::vector<Level> levels;  // index Ql (1..L)
   // key-basis ownership
   std::vector<int> own_key;   // owned key-basis limbs, increasing

@@ -15,6 +15,7 @@
 // ciphertext, staged through shared memory so every global access of the
 // epilogue is coalesced.
 #include "ks_fused.cuh"
+#include "ks_galois.cuh"
 #include "ks_ntt_impl.cuh"
 #include "ks_tmem.cuh"
 
@@ -41,8 +42,9 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
-    // scale entries of FP64 primes hold the bits of {s, fl(s/q)}
-    inv_cols_fp<LOG_M>(sm, col, t, c, log_n, T.inv_fp + (long long)prime * N, P,
+    // scale entries of FP64 primes hold the bits of {s, fl(s/q)}; the output
+    // (the ModUp source limbs) stays a double: canonical, as its bits
+    inv_cols_fp<LOG_M, true>(sm, col, t, c, log_n, T.inv_fp + (long long)prime * N, P,
                        make_double2(as_fp(s0.x), as_fp(s0.y)),
                        make_double2(as_fp(s1.x), as_fp(s1.y)), load, store);
   } else if (P.q < kInvLazyBound) {
@@ -52,13 +54,21 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   }
 }
 
+// Source limbs of the base conversions: scaled coefficient limbs from
+// ntt_inverse_scaled, canonical, stored as the bits of a double for primes
+// below kFpBound and as uint64 otherwise.
+__device__ __forceinline__ u64 src_u64(u64 bits, bool fp_src) {
+  return fp_src ? (u64)__double2ull_rn(as_fp(bits)) : bits;
+}
+
 // Fills the 16 column inputs of this thread with
 //   y = sum_{i < n_src} [v_i * w_i]_{q}  (each term canonical, sum < 8q),
-// reduced to [0, q).  src(i) points at source limb i.
-template <int LOG_M, class Src>
+// reduced to [0, q).  src(i) points at source limb i, fp_src(i) tells its
+// storage (src_u64).
+template <int LOG_M, class Src, class SrcFp>
 __device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M2, int n_src,
-                                           Src &&src, const u64 *w, const u64 *wsh,
-                                           const PrimeDev &P) {
+                                           Src &&src, SrcFp &&fp_src, const u64 *w,
+                                           const u64 *wsh, const PrimeDev &P) {
   using G = ColGeom<LOG_M>;
   u64 acc[kEpt];
 #pragma unroll
@@ -67,26 +77,28 @@ __device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M
   for (int i = 0; i < n_src; ++i) {
     const u64 *s = src(i);
     const u64 wi = __ldg(&w[i]), wp = __ldg(&wsh[i]);
+    const bool fs = fp_src(i);
     u64 v[kEpt];
 #pragma unroll
     for (int e = 0; e < kEpt; ++e)
       v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
 #pragma unroll
-    for (int e = 0; e < kEpt; ++e) acc[e] += mul_shoup(v[e], wi, wp, P.q);
+    for (int e = 0; e < kEpt; ++e) acc[e] += mul_shoup(src_u64(v[e], fs), wi, wp, P.q);
   }
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = reduce_full(acc[e], P.q, P.mu);
 }
 
 // FP64 variant for targets q < kFpBound: x = sum_i fp_mulmod(v_i, w_i, w_i/q),
-// |x| < 0.57 q n_src < 4.6q.  A source limb whose prime is not below 2^50
-// (the 58-bit q_0) is first reduced mod q with the integer Barrett-style
-// reduce_full so that every product input stays below 2^50.
-template <int LOG_M, class Src>
+// |x| < 0.57 q n_src < 4.6q.  Sources below kFpBound are read as doubles as
+// stored; a source limb whose prime is not below 2^50 (the 58-bit q_0) is
+// first reduced mod q with the integer Barrett-style reduce_full so that
+// every product input stays below 2^50.
+template <int LOG_M, class Src, class SrcQ>
 __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col, int M2,
-                                              int n_src, Src &&src, const int *src_prime,
+                                              int n_src, Src &&src, SrcQ &&src_q,
                                               const u64 *w, const double *wq,
-                                              const PrimeDev *primes, const PrimeDev &P) {
+                                              const PrimeDev &P) {
   using G = ColGeom<LOG_M>;
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = 0.0;
@@ -94,18 +106,23 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
   for (int i = 0; i < n_src; ++i) {
     const u64 *s = src(i);
     const double wd = (double)__ldg(&w[i]), wqd = __ldg(&wq[i]);
-    const bool big = primes[src_prime[i]].q >= (1ull << 50);
+    const u64 qs = src_q(i);
     u64 v[kEpt];
 #pragma unroll
     for (int e = 0; e < kEpt; ++e)
       v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
-    if (big) {
+    if (qs < kFpBound) {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) v[e] = reduce_full(v[e], P.q, P.mu);
+      for (int e = 0; e < kEpt; ++e) x[e] = __dadd_rn(x[e], fp_mulmod(as_fp(v[e]), wd, wqd, P.qd));
+    } else {
+      if (qs >= (1ull << 50)) {
+#pragma unroll
+        for (int e = 0; e < kEpt; ++e) v[e] = reduce_full(v[e], P.q, P.mu);
+      }
+#pragma unroll
+      for (int e = 0; e < kEpt; ++e)
+        x[e] = __dadd_rn(x[e], fp_mulmod(u64_to_fp(v[e]), wd, wqd, P.qd));
     }
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e)
-      x[e] = __dadd_rn(x[e], fp_mulmod(u64_to_fp(v[e]), wd, wqd, P.qd));
   }
 }
 
@@ -115,7 +132,7 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
 // The arithmetic path is chosen per CTA from the target prime (FP64 below
 // kFpBound, integer above); jobs are ordered FP64 first.
 template <int LOG_M>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
                  const int *__restrict__ job_s, int job0, NttTables T) {
@@ -136,14 +153,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (P.q < kFpBound) {
     const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
     auto filld = [&](double (&x)[kEpt]) {
-      bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src, src_prime, mu.w + wo, mu.wq + wo,
-                           T.primes, P);
+      bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src,
+                           [&](int i) { return T.primes[src_prime[i]].q; }, mu.w + wo,
+                           mu.wq + wo, P);
     };
     fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, filld,
                         store);
   } else {
+    const int *src_prime = mu.prime_of + d * mu.alpha;
+    auto fp_src = [&](int i) { return T.primes[src_prime[i]].q < kFpBound; };
     auto fill = [&](u64 (&x)[kEpt]) {
-      bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, mu.w + wo, mu.wsh + wo, P);
+      bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, fp_src, mu.w + wo, mu.wsh + wo, P);
     };
     const ulonglong2 *tw = T.fwd + (long long)prime * N;
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
@@ -187,12 +207,25 @@ struct RowsIpArgs {
   const u64 *t, *c_ntt, *key;
   u64 *cx;
   int key_limbs;
+  uint32_t elt;  // c_ntt is read through X -> X^elt (1: as it is)
 };
 
+// A CTA is kRipWarps warps; warp w owns the 512 tile words [512w, 512w + 512)
+// (32 / TT rows of M words).  Smaller CTAs than the NTT kernels' 8 warps
+// shorten the wave tail of this long-running kernel.
+constexpr int kRipWarps = 4;
+constexpr int kRipThreads = kRipWarps * 32;
+constexpr int kRipTile = kRipWarps * 512;
+
+template <int LOG_M>
+__host__ __device__ constexpr int rows_ip_rows() {  // rows of M words per CTA
+  return kRipTile >> LOG_M;
+}
 template <int LOG_M>
 __host__ __device__ constexpr size_t rows_ip_smem_bytes() {
-  // exchange buffer + per-warp key stage [8 warps][2 polys][8 pairs][32 lanes] x 16 B
-  return (size_t)RowGeom<LOG_M>::SMEM * 8 + (size_t)(kThreads / 32) * 2 * 8 * 32 * 16;
+  // padded exchange rows + per-warp key stage [warps][2 polys][8 pairs][32 lanes] x 16 B
+  return (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16) * 8 +
+         (size_t)kRipWarps * 2 * 8 * 32 * 16;
 }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -212,23 +245,31 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
   const int j = lay.out_j[s];
   const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long tile0 = (long long)blockIdx.x * kTile;
-  const long long row = (long long)blockIdx.x * G::R + rr;
+  const long long tile0 = (long long)blockIdx.x * kRipTile;
+  const long long row = (long long)blockIdx.x * rows_ip_rows<LOG_M>() + rr;
   const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's pairs in the tile
   const int dj = j < mu.Ql ? j / mu.alpha : -1;
   const long long kstride = (long long)A.key_limbs * N;
   const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0 + wofs;
   const u64 *tbase = A.t + (long long)s * N + tile0;
   const long long tstride = (long long)lay.n_out * N;
-  const u64 *cown = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N + tile0 : nullptr;
+  // own-digit limb, read through the automorphism: the CTA's tile gathers
+  // from the aligned source tile cown, pair (k, k+1) from (src & ~1) (swapped
+  // when src is odd)
+  const u64 *climb = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N : nullptr;
+  const u64 *cown =
+      climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
+            : nullptr;
   const ulonglong2 *tw = T.fwd + (long long)prime * N;
   const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n};
   kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
-  // L2 prefetch of digit d's value tile: one 128-byte line per thread.
+  // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
+  // over the CTA's threads.
   auto prefetch = [&](int d) {
-    const int line = threadIdx.x * 16;
-    const u64 *v = d == dj ? cown + line : tbase + d * tstride + line;
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(v));
+    const u64 *v = d == dj ? cown : tbase + d * tstride;
+#pragma unroll
+    for (int line = threadIdx.x * 16; line < kRipTile; line += kRipThreads * 16)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(v + line));
   };
   const int n_dig = lay.n_digits;
   prefetch(__ldg(&lay.digits[0]));
@@ -256,7 +297,6 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       __syncwarp();
     }
     cp_async_wait_all();  // this lane's own key pairs
-    const u64 *cb = own ? cown + wofs : nullptr;
     const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
@@ -268,7 +308,13 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
         k0[q] = kst[i * 32];
         k1[q] = kst[(8 + i) * 32];
         if (own) {
-          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(cb + 64 * i);
+          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), A.elt, log_n);
+          ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
+          if (src & 1u) {
+            const u64 tmp = v.x;
+            v.x = v.y;
+            v.y = tmp;
+          }
           y[2 * q] = FP ? fp_bits(u64_to_fp(v.x)) : v.x;
           y[2 * q + 1] = FP ? fp_bits(u64_to_fp(v.y)) : v.y;
         } else {
@@ -329,16 +375,21 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
 }
 
 template <int LOG_M>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
-  // Shared memory caps residency at 2 CTAs per SM (at most 4 would still
-  // fit): 4 x 128 TMEM columns fit the 512 of an SM, so tmem::alloc never waits.
-  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / 5, "TMEM columns could be oversubscribed");
-  constexpr uint32_t kCols = 128;
+  // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
+  // needs 64 columns per group of four warps.  Shared memory caps how many
+  // CTAs share an SM so that their columns never exceed the 512 of an SM,
+  // hence tmem::alloc never waits.
+  constexpr uint32_t kCols = kRipWarps > 4 ? 128 : 64;
+  static_assert(kRipWarps == 4 || kRipWarps == 8, "CTA of 4 or 8 warps");
+  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / (512 / kCols + 1),
+                "TMEM columns could be oversubscribed");
   extern __shared__ __align__(16) u64 dsm[];
   __shared__ uint32_t tmem_slot;
   u64 *sm = dsm;
-  ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(dsm + RowGeom<LOG_M>::SMEM);
+  ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
+      dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
   const int s = blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
@@ -379,13 +430,21 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int col = blockIdx.x * G::C + c;
   const long long wo = (long long)j * md.alpha;
   auto src = [&](int i) { return y_base + y_off[p * md.alpha + i]; };
+  auto fp_src = [&](int i) { return T.primes[md.first_p + i].q < kFpBound; };
   auto fill = [&](u64 (&x)[kEpt]) {
-    bconv_fill<LOG_M>(x, tt, col, M2, md.alpha, src, md.w + wo, md.wsh + wo, P);
+    bconv_fill<LOG_M>(x, tt, col, M2, md.alpha, src, fp_src, md.w + wo, md.wsh + wo, P);
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
-    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, fill, store);
+    // FP64 conversion (sources reduced mod q_j first when they do not fit):
+    // spreads the work over the FP64 and integer pipes
+    auto filld = [&](double (&x)[kEpt]) {
+      bconv_fill_fp<LOG_M>(x, tt, col, M2, md.alpha, src,
+                           [&](int i) { return T.primes[md.first_p + i].q; }, md.w + wo,
+                           md.wq + wo, P);
+    };
+    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, filld, store);
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
@@ -473,7 +532,7 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
 template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt, const u64 *key,
                                  int key_limbs, u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                 const NttTables &T) {
+                                 const NttTables &T, uint32_t elt) {
   constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
   static bool attr_set = false;
   if (!attr_set) {
@@ -482,9 +541,9 @@ cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt,
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const dim3 grid((1 << T.log_n) / kTile, lay.n_out);
-  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs};
-  k_modup_rows_ip<LOG_M><<<grid, kThreads, smem, s>>>(A, mu, lay, T);
+  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out);
+  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt};
+  k_modup_rows_ip<LOG_M><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
   return cudaGetLastError();
 }
 
@@ -496,11 +555,12 @@ inline int col_tiles(int log_n, int log_m) {
 }  // namespace
 
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
-                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s) {
+                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
+                               uint32_t elt) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
   if (n_limbs == 0) return cudaSuccess;
-  // first pass: the ordinary inverse row pass, src -> dst
-  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst);
+  // first pass: the ordinary inverse row pass, src (through elt) -> dst
+  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst, elt);
   if (e != cudaSuccess) return e;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_limbs);
@@ -532,15 +592,17 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
-                                     const KsLayout &lay, const NttTables &T, cudaStream_t s) {
+                                     const KsLayout &lay, const NttTables &T, cudaStream_t s,
+                                     uint32_t elt) {
+  if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
   if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
     return cudaErrorInvalidValue;
   if (lay.n_out == 0) return cudaSuccess;
   const int s2 = T.log_n - T.log_n / 2;
   switch (s2) {
-    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
-    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
-    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T);
+    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
+    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
+    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -10,9 +10,13 @@ namespace ksb {
 
 // Inverse NTT whose last stage multiplies by a per-limb constant c (on top
 // of N^-1): scale[i] = {N^-1 c, Shoup}, {psi^-brev(1) N^-1 c, Shoup}.
-// Reads src, writes dst (which may alias src).
+// Reads src, writes dst (which may alias src when elt == 1).  elt != 1
+// transforms the automorphism X -> X^elt of src (read by gathering).
+// Outputs of primes below kFpBound are the bits of the canonical value as a
+// double, the others canonical uint64 (the form the base conversions read).
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
-                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s);
+                               const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
+                               uint32_t elt = 1);
 
 // ModUp: for each job (digit d, output slot s) the column pass of the
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
@@ -29,9 +33,11 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 // product against the key shard ([n_digits][2][key_limbs][N], limb key_slot[s]):
 //   cx[p][s] = sum_i NTT_rows(t[d_i][s]) * key[i][p][key_slot[s]]  (p = 0, 1,
 // d_i = lay.digits[i], lay.n_digits >= 1).
+// elt != 1: the NTT-form input c_ntt is read through X -> X^elt.
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
-                                     const KsLayout &lay, const NttTables &T, cudaStream_t s);
+                                     const KsLayout &lay, const NttTables &T, cudaStream_t s,
+                                     uint32_t elt = 1);
 
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the

@@ -5,6 +5,7 @@
 // and keep per-limb constants in registers; the limb index of a CTA is
 // blockIdx.y so every constant load is warp-uniform.
 #include "ks_kernels.cuh"
+#include "ks_galois.cuh"
 
 namespace ksb {
 namespace {
@@ -20,24 +21,21 @@ __device__ __forceinline__ u64 mix64(u64 z) {
   return z;
 }
 
-__device__ __forceinline__ uint32_t brev_n(uint32_t x, int log_n) { return __brev(x) >> (32 - log_n); }
-
-// Source index of output slot i under X -> X^elt in the bit-reversed NTT order:
-// slot i holds the evaluation at psi^(2 brev(i) + 1).
-__device__ __forceinline__ uint32_t galois_src(uint32_t i, uint32_t elt, int log_n) {
-  const uint32_t mask2n = (2u << log_n) - 1u;
-  const uint32_t e = 2u * brev_n(i, log_n) + 1u;
-  const uint32_t ge = (e * elt) & mask2n;
-  return brev_n((ge - 1u) >> 1, log_n);
-}
-
+// One thread: the output pair (2m, 2m + 1) from the aligned source pair.
 __global__ void k_galois_ntt(const u64 *__restrict__ in, u64 *__restrict__ out, int log_n,
                              uint32_t elt) {
   const int N = 1 << log_n;
   const long long limb = blockIdx.y;
-  const uint32_t i = blockIdx.x * kBlk + threadIdx.x;
+  const uint32_t i = (blockIdx.x * kBlk + threadIdx.x) * 2;
   if (i >= (uint32_t)N) return;
-  out[limb * N + i] = __ldg(&in[limb * N + galois_src(i, elt, log_n)]);
+  const uint32_t src = galois_src(i, elt, log_n);
+  ulonglong2 v = __ldg(reinterpret_cast<const ulonglong2 *>(in + limb * N + (src & ~1u)));
+  if (src & 1u) {
+    const u64 t = v.x;
+    v.x = v.y;
+    v.y = t;
+  }
+  *reinterpret_cast<ulonglong2 *>(out + limb * N + i) = v;
 }
 
 // One thread: two adjacent coefficients of one digit, all output limbs.
@@ -380,7 +378,7 @@ inline dim3 grid2(int log_n, int y, int per_thread) {
 cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
                        cudaStream_t s) {
   if (n_limbs <= 0) return cudaSuccess;
-  k_galois_ntt<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(in, out, log_n, elt);
+  k_galois_ntt<<<grid2(log_n, n_limbs, 2), kBlk, 0, s>>>(in, out, log_n, elt);
   return cudaGetLastError();
 }
 

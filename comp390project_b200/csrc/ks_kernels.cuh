@@ -30,6 +30,7 @@ struct ModDownDev {
   const u64 *w;               // [L][alpha] [P/p_i]_{q_j}
   const ulonglong2 *pinv;     // [L] {[P^-1]_{q_j}, Shoup}
   const u64 *wsh;             // [L][alpha] Shoup companions of w w.r.t. q_j
+  const double *wq;           // [L][alpha] fl(w / q_j) for FP64 primes q_j
 };
 
 // Which QlP limbs this device produces and where its inputs live.

@@ -6,6 +6,7 @@
 // butterflies (60-bit primes) are CTA-uniform.
 #include "ks_ntt.cuh"
 #include "ks_ntt_impl.cuh"
+#include "ks_galois.cuh"
 
 namespace ksb {
 namespace {
@@ -52,8 +53,12 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   }
 }
 
+// elt (inverse direction only): the input is read through the automorphism
+// X -> X^elt (input slot galois_src(i) feeds slot i; the tile gathers from
+// one aligned source tile); elt = 1 reads it as it is.
 template <int LOG_M, bool FWD>
-__global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T) {
+__global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T,
+                                                     uint32_t elt) {
   using G = RowGeom<LOG_M>;
   extern __shared__ __align__(16) u64 dsm[];
   u64 *sm = dsm;
@@ -95,10 +100,21 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
       otile[lin] = sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))];
     }
   } else {
+    if (elt == 1u) {
 #pragma unroll
-    for (int i = 0; i < kEpt; ++i) {
-      const int lin = threadIdx.x + i * kThreads;
-      sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))] = tile[lin];
+      for (int i = 0; i < kEpt; ++i) {
+        const int lin = threadIdx.x + i * kThreads;
+        sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))] = tile[lin];
+      }
+    } else {
+      const uint32_t t0 = (uint32_t)blockIdx.x * kTile;
+      const u64 *stile = a + (galois_src(t0, elt, log_n) & ~(uint32_t)(kTile - 1));
+#pragma unroll
+      for (int i = 0; i < kEpt; ++i) {
+        const int lin = threadIdx.x + i * kThreads;
+        sm[padx<LOG_M>(lin >> LOG_M, lin & (G::M - 1))] =
+            stile[galois_src(t0 + lin, elt, log_n) & (uint32_t)(kTile - 1)];
+      }
     }
     if (fp) cp_async_wait_all();
     __syncthreads();
@@ -119,7 +135,7 @@ cudaError_t launch_cols(const LimbMap &m, int n_limbs, const NttTables &T, cudaS
 }
 template <int LOG_M, bool FWD>
 cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
-                        cudaStream_t s) {
+                        cudaStream_t s, uint32_t elt = 1) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
   static bool attr_set = false;  // idempotent; one call per instantiation suffices
   if (!attr_set) {
@@ -129,18 +145,18 @@ cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const 
     attr_set = true;
   }
   dim3 grid((1 << T.log_n) / kTile, n_limbs);
-  ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T);
+  ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T, elt);
   return cudaGetLastError();
 }
 
 template <bool FWD>
 cudaError_t launch_pass(bool cols, int log_m, const LimbMap &m, int n, const NttTables &T,
-                        cudaStream_t s, const LimbMap *mo = nullptr) {
+                        cudaStream_t s, const LimbMap *mo = nullptr, uint32_t elt = 1) {
   const LimbMap &o = mo ? *mo : m;
   switch (log_m) {
-    case 6: return cols ? launch_cols<6, FWD>(m, n, T, s) : launch_rows<6, FWD>(m, o, n, T, s);
-    case 7: return cols ? launch_cols<7, FWD>(m, n, T, s) : launch_rows<7, FWD>(m, o, n, T, s);
-    case 8: return cols ? launch_cols<8, FWD>(m, n, T, s) : launch_rows<8, FWD>(m, o, n, T, s);
+    case 6: return cols ? launch_cols<6, FWD>(m, n, T, s) : launch_rows<6, FWD>(m, o, n, T, s, elt);
+    case 7: return cols ? launch_cols<7, FWD>(m, n, T, s) : launch_rows<7, FWD>(m, o, n, T, s, elt);
+    case 8: return cols ? launch_cols<8, FWD>(m, n, T, s) : launch_rows<8, FWD>(m, o, n, T, s, elt);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -166,10 +182,12 @@ cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables
 }
 
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
-                                  cudaStream_t s, const LimbMap *out) {
+                                  cudaStream_t s, const LimbMap *out, uint32_t elt) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
+  if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
+  if (elt != 1u && (!out || out->base == m.base)) return cudaErrorInvalidValue;  // gather needs a separate output
   if (n_limbs == 0) return cudaSuccess;
-  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s, out);
+  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s, out, elt);
 }
 
 cudaError_t ntt_inverse(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s) {

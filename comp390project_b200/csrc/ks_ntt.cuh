@@ -56,7 +56,9 @@ bool ntt_supported_log_n(int log_n);
 cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
                                   cudaStream_t s);
 // out: optional separate destination (same limb order and primes as m).
+// elt != 1: the input is read through X -> X^elt (needs a separate out).
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
-                                  cudaStream_t s, const LimbMap *out = nullptr);
+                                  cudaStream_t s, const LimbMap *out = nullptr,
+                                  uint32_t elt = 1);
 
 }  // namespace ksb

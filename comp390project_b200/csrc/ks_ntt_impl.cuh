@@ -358,8 +358,9 @@ __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int 
 }
 
 // Inverse column pass (second pass); load() gives the bits of the first
-// pass result, store() receives canonical uint64 times the last-stage scale.
-template <int LOG_M, class Load, class Store>
+// pass result, store() receives canonical uint64 times the last-stage scale
+// (CANON_FP: the bits of that canonical value as a double instead).
+template <int LOG_M, bool CANON_FP = false, class Load, class Store>
 __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int log_n,
                                             const double *tw, const PrimeDev &P, double2 s0,
                                             double2 s1, Load &&load, Store &&store) {
@@ -376,8 +377,12 @@ __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int 
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c]);
   inv_round_fp<LOG_M, G::HI, 4, true>(x, t, 0, twg, P, s0, s1);
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e)
-    store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
+  for (int e = 0; e < kEpt; ++e) {
+    if (CANON_FP)  // the last stage's fp_mulmod leaves |x| < 0.57q: one add makes it canonical
+      store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_bits(x[e] < 0.0 ? __dadd_rn(x[e], P.qd) : x[e]));
+    else
+      store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
+  }
 }
 
 // Forward row pass; the tile holds first-pass bits; canonical outputs in xo

@@ -122,13 +122,15 @@ def _worker(rank, world, port, name, mode, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 8])
 @pytest.mark.parametrize("mode", ["ib", "oa"])
 @pytest.mark.parametrize("name", ["small", "cfg3"])
-def test_two_gpu_keyswitch_bitexact(name, mode, cuda_device):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def test_multi_gpu_keyswitch_bitexact(name, mode, world, cuda_device):
+    """world 8 at config 3 output aggregation: 7 digits over 8 ranks, rank 7
+    contributes a zero partial sum."""
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     import torch.multiprocessing as mp
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
