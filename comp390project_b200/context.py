@@ -274,6 +274,19 @@ class KsContext:
         self._check(self.lib.ks_rotate_batch(self.h, ptrs, st, n, int(level_limbs),
                                              _stream_ptr(stream, self.device)))
 
+    def rotate_batch_host(self, host_cts, steps: Sequence[int], level_limbs: int, stream=None):
+        """rotate_batch on host tensors (pinned CPU torch tensors or numpy
+        uint64 arrays [2][n_local][N]), rotated in place; asynchronous on the
+        stream (synchronise before reading them)."""
+        n = len(host_cts)
+
+        def hptr(t):
+            return t.ctypes.data if isinstance(t, np.ndarray) else t.data_ptr()
+        ptrs = (C.c_void_p * n)(*[hptr(t) for t in host_cts])
+        st = (C.c_int * n)(*[int(s) for s in steps])
+        self._check(self.lib.ks_rotate_batch_host(self.h, ptrs, st, n, int(level_limbs),
+                                                  _stream_ptr(stream, self.device)))
+
     def rotate_hoisted(self, ct, level_limbs: int, steps: Sequence[int], outs, stream=None):
         n = len(steps)
         ptrs = (C.c_void_p * n)(*[self._ptr(t) for t in outs])

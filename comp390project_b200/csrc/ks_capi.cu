@@ -151,6 +151,8 @@ void build_tables(Ctx &c) {
   std::vector<PrimeDev> pd(K);
   std::vector<ulonglong2> fwd((size_t)K * N), inv((size_t)K * N);
   std::vector<double> fwd_fp((size_t)K * N, 0.0), inv_fp((size_t)K * N, 0.0);
+  const int NC = 1 << (c.log_n / 2);  // column-pass twiddle indices
+  std::vector<double2> fwd_col((size_t)K * NC, make_double2(0, 0)), inv_col(fwd_col);
   std::vector<std::thread> th;
   auto work = [&](int k) {
     const u64 q = c.primes[k];
@@ -180,6 +182,11 @@ void build_tables(Ctx &c) {
         }
         fwd_fp[(size_t)k * N + dst] = (double)fwd[(size_t)k * N + i].x;
         inv_fp[(size_t)k * N + dst] = (double)inv[(size_t)k * N + i].x;
+      }
+      for (int i = 0; i < NC; ++i) {
+        const double wf = (double)fwd[(size_t)k * N + i].x, wi = (double)inv[(size_t)k * N + i].x;
+        fwd_col[(size_t)k * NC + i] = make_double2(wf, wf / (double)q);
+        inv_col[(size_t)k * NC + i] = make_double2(wi, wi / (double)q);
       }
     }
     PrimeDev &P = pd[k];
@@ -211,6 +218,8 @@ void build_tables(Ctx &c) {
   c.d_tw_inv = upload(inv);
   c.d_tw_fwd_fp = upload(fwd_fp);
   c.d_tw_inv_fp = upload(inv_fp);
+  c.d_tw_fwd_col = upload(fwd_col);
+  c.d_tw_inv_col = upload(inv_col);
 
   // Discrete Gaussian CDT (sigma 3.2, |e| <= 19) for the synthetic keys.
   std::vector<u64> T(20);
@@ -538,7 +547,8 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     size_t w_ys = ib ? (size_t)c.max_p_own * 2 * N : 0;
     size_t w_ya = ib ? (size_t)world * c.max_p_own * 2 * N : 0;
     size_t w_z = 2 * nq * N;
-    c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z;
+    size_t w_ct = 2 * nq * N;  // device copy of a host ciphertext (ks_rotate_batch_host)
+    c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z + w_ct;
     // one scratch arena per lane; lanes = max_batch (1..8)
     // (contexts made by ks_ctx_create_all are set up one after another on one
     // thread, where splitting communicators would block, so they keep one lane)
@@ -555,6 +565,7 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       ln.s_ysend = p; p += w_ys;
       ln.s_yall = p; p += w_ya;
       ln.s_z = p; p += w_z;
+      ln.s_ct = p; p += w_ct;
       if (li > 0) KS_CUDA(cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking));
       KS_CUDA(cudaEventCreateWithFlags(&ln.done, cudaEventDisableTiming));
     }
@@ -612,6 +623,8 @@ void ctx_free(Ctx &c) {
   f(c.d_tw_inv);
   f(c.d_tw_fwd_fp);
   f(c.d_tw_inv_fp);
+  f(c.d_tw_fwd_col);
+  f(c.d_tw_inv_col);
   f(c.d_gauss);
   f(c.d_phatinv);
   f(c.d_pinv);
@@ -1316,6 +1329,40 @@ int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, 
       do_apply_galois(c, c.lanes[li], cts[i], level_limbs, elt_of_step(c, steps[i]), ls);
     }
     // join: the caller's stream waits for every lane
+    for (int li = 1; li < nl; ++li) {
+      KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
+      KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));
+    }
+  });
+}
+
+int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *steps, int n,
+                         int level_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    KS_REQUIRE(host_cts != nullptr && steps != nullptr && n >= 0, "bad batch arguments");
+    Ctx &c = ctx->c;
+    KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
+    const Level &lv = level_of(c, level_limbs);
+    const size_t bytes = 2 * (size_t)lv.n_q * c.N * 8;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const int nl = std::min<int>((int)c.lanes.size(), std::max(n, 1));
+    KS_CUDA(cudaSetDevice(c.device));
+    // fork the lanes from the caller's stream; on each lane: copy in, rotate
+    // in the lane's staging buffer, copy out -- the copies of one lane run on
+    // the copy engines while the other lanes compute
+    KS_CUDA(cudaEventRecord(c.ev_fork, s));
+    for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
+    for (int i = 0; i < n; ++i) {
+      KS_REQUIRE(host_cts[i] != nullptr, "host ciphertext pointer is null");
+      const int li = i % nl;
+      Ctx::Lane &L = c.lanes[li];
+      const cudaStream_t ls = li == 0 ? s : L.stream;
+      KS_CUDA(cudaMemcpyAsync(L.s_ct, host_cts[i], bytes, cudaMemcpyHostToDevice, ls));
+      do_apply_galois(c, L, L.s_ct, level_limbs, elt_of_step(c, steps[i]), ls);
+      KS_CUDA(cudaMemcpyAsync(host_cts[i], L.s_ct, bytes, cudaMemcpyDeviceToHost, ls));
+    }
     for (int li = 1; li < nl; ++li) {
       KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
       KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));

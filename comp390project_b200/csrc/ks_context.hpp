@@ -89,6 +89,7 @@ struct Ctx {
   PrimeDev *d_primes = nullptr;
   ulonglong2 *d_tw_fwd = nullptr, *d_tw_inv = nullptr;
   double *d_tw_fwd_fp = nullptr, *d_tw_inv_fp = nullptr;
+  double2 *d_tw_fwd_col = nullptr, *d_tw_inv_col = nullptr;
   u64 *d_gauss = nullptr;
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
@@ -117,7 +118,8 @@ struct Ctx {
     cudaEvent_t done = nullptr;
     u64 *arena = nullptr;
     u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr,
-        *s_cx = nullptr, *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr;
+        *s_cx = nullptr, *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr,
+        *s_ct = nullptr;  // staging of a host ciphertext
     ncclComm_t comm = nullptr;
   };
   std::vector<Lane> lanes;
@@ -137,7 +139,8 @@ struct Ctx {
   std::vector<cudaEvent_t> event_pool;
 
   NttTables tables() const {
-    return NttTables{d_tw_fwd, d_tw_inv, d_primes, log_n, d_tw_fwd_fp, d_tw_inv_fp};
+    return NttTables{d_tw_fwd,    d_tw_inv,    d_primes,     log_n,
+                     d_tw_fwd_fp, d_tw_inv_fp, d_tw_fwd_col, d_tw_inv_col};
   }
 };
 

@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   if (P.q < kFpBound) {
     // scale entries of FP64 primes hold the bits of {s, fl(s/q)}; the output
     // (the ModUp source limbs) stays a double: canonical, as its bits
-    inv_cols_fp<LOG_M, true>(sm, col, t, c, log_n, T.inv_fp + (long long)prime * N, P,
+    inv_cols_fp<LOG_M, true>(sm, col, t, c, log_n, T.inv_col + ((long long)prime << LOG_M), P,
                        make_double2(as_fp(s0.x), as_fp(s0.y)),
                        make_double2(as_fp(s1.x), as_fp(s1.y)), load, store);
   } else if (P.q < kInvLazyBound) {
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 3)
                            [&](int i) { return T.primes[src_prime[i]].q; }, mu.w + wo,
                            mu.wq + wo, P);
     };
-    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)prime * N, P, filld,
+    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_col + ((long long)prime << LOG_M), P, filld,
                         store);
   } else {
     const int *src_prime = mu.prime_of + d * mu.alpha;
@@ -261,7 +261,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
             : nullptr;
   const ulonglong2 *tw = T.fwd + (long long)prime * N;
-  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n};
+  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
   kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
   // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
   // over the CTA's threads.
@@ -444,7 +444,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                            [&](int i) { return T.primes[md.first_p + i].q; }, md.w + wo,
                            md.wq + wo, P);
     };
-    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_fp + (long long)j * N, P, filld, store);
+    fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_col + ((long long)j << LOG_M), P, filld,
+                        store);
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);

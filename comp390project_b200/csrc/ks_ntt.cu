@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   auto fill = [&](u64 (&x)[kEpt]) { fill_cols<LOG_M>(x, t, col, load); };
   auto store = [&](int r, int cl, u64 v) { a[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
-    const double *twf = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
+    const double2 *twf = (FWD ? T.fwd_col : T.inv_col) + ((long long)prime << LOG_M);
     if (FWD) {
       fwd_cols_fp<LOG_M>(sm, col, t, c, log_n, twf, P, fill, store);
     } else {

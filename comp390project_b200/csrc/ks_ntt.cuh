@@ -43,6 +43,8 @@ struct NttTables {
   int log_n;
   const double *fwd_fp;   // [n_primes][N] w as a double (primes below kFpBound),
   const double *inv_fp;   // row-pass region permuted by row_tw_pos
+  // [n_primes][2^(logN/2)] {w, fl(w/q)} of the column-pass indices (FP64 primes)
+  const double2 *fwd_col, *inv_col;
 };
 
 // Transforms n_limbs limbs in place; outputs are canonical in [0, q).

@@ -207,23 +207,25 @@ __device__ __forceinline__ void inv_rows_regs(u64 (&x)[kEpt], u64 *sm, int t, in
 // ===========================================================================
 // FP64 variants (primes below kFpBound).  Values travel between the passes as
 // the bits of signed integer-valued doubles; the pass inputs and the final
-// outputs are canonical uint64.  Twiddle tables hold w (a double); the
-// quotient factor fl(w/q) is formed as w * fl(1/q) next to its use, which
-// keeps the estimate error below |y| 2^-52 <= 2^-4 for |y| <= 2^48 (every
-// product input of these passes stays below 2^48 for q < kFpBound).
-//
-// A twiddle getter tw(b, H) returns psi^(+-brev) of the pair at local bit b
-// whose lower element has extended index H = (prefix << LOG_M) | local.
+// outputs are canonical uint64.  A twiddle getter tw(b, H) returns {w, wq}
+// for the pair at local bit b whose lower element has extended index
+// H = (prefix << LOG_M) | local: w = psi^(+-brev) and wq the quotient factor,
+// either fl(w/q) from the column tables (2^(logN/2) pairs per prime) or
+// w * fl(1/q) formed next to its use from the row tables (w only, to keep the
+// staged row blocks small); both keep the estimate error below
+// |y| 2^-52 <= 2^-4 for |y| <= 2^48 (every product input of these passes
+// stays below 2^48 for q < kFpBound).
 // ===========================================================================
 __device__ __forceinline__ double as_fp(u64 b) { return __longlong_as_double((long long)b); }
 __device__ __forceinline__ u64 fp_bits(double d) { return (u64)__double_as_longlong(d); }
 
-// Global-table getter (column passes: every column of a CTA shares them).
-struct TwGlobal {
-  const double *tw;
-  int log_n, gofs;
-  __device__ __forceinline__ double operator()(int b, long long H) const {
-    return __ldg(&tw[(1 << (log_n - 1 - b - gofs)) + (int)(H >> (b + 1))]);
+// Column-pass getter: the prime's {w, fl(w/q)} column table (index
+// 2^(LOG_M-1-b) + (H >> (b+1)) < 2^LOG_M; every column of a CTA shares them).
+template <int LOG_M>
+struct TwCols {
+  const double2 *tw;
+  __device__ __forceinline__ double2 operator()(int b, long long H) const {
+    return __ldg(&tw[(1 << (LOG_M - 1 - b)) + (int)(H >> (b + 1))]);
   }
 };
 
@@ -234,11 +236,13 @@ template <int LOG_M, int R>
 struct TwRowsSmem {
   const double *sm;
   long long row0;
-  __device__ __forceinline__ double operator()(int b, long long H) const {
+  double qinv;
+  __device__ __forceinline__ double2 operator()(int b, long long H) const {
     const int u = LOG_M - 1 - b;
     const long long hk = H >> (b + 1);
     const int k = (int)hk & ((1 << u) - 1);
-    return sm[R * ((1 << u) - 1) + (int)(((hk >> u) - row0) << u) + row_tw_pos(LOG_M, b, k)];
+    const double w = sm[R * ((1 << u) - 1) + (int)(((hk >> u) - row0) << u) + row_tw_pos(LOG_M, b, k)];
+    return make_double2(w, __dmul_rn(w, qinv));
   }
 };
 
@@ -248,11 +252,14 @@ template <int LOG_M>
 struct TwRowsGlobal {
   const double *tw;
   int log_n;
-  __device__ __forceinline__ double operator()(int b, long long H) const {
+  double qinv;
+  __device__ __forceinline__ double2 operator()(int b, long long H) const {
     const int u = LOG_M - 1 - b;
     const long long hk = H >> (b + 1);
     const int k = (int)hk & ((1 << u) - 1);
-    return __ldg(&tw[(1ll << (log_n - 1 - b)) + ((hk >> u) << u) + row_tw_pos(LOG_M, b, k)]);
+    const double w =
+        __ldg(&tw[(1ll << (log_n - 1 - b)) + ((hk >> u) << u) + row_tw_pos(LOG_M, b, k)]);
+    return make_double2(w, __dmul_rn(w, qinv));
   }
 };
 
@@ -290,8 +297,8 @@ __device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
       const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
-      const double w = tw(b, H);
-      fp_ct_bfly(x[e], x[e | (1 << k)], w, __dmul_rn(w, qinv), q);
+      const double2 w = tw(b, H);
+      fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
     }
   }
 }
@@ -317,8 +324,8 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
         Y = fp_mulmod(d, s1.x, s1.y, P.qd);
       } else {
         const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, e);
-        const double w = tw(b, H);
-        fp_gs_bfly(X, Y, w, __dmul_rn(w, P.qinv), P.qd);
+        const double2 w = tw(b, H);
+        fp_gs_bfly(X, Y, w.x, w.y, P.qd);
       }
     }
   }
@@ -327,10 +334,10 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
 // filld(x) fills signed integer-valued doubles (|x| < 8q).
 template <int LOG_M, class FillD, class Store>
 __device__ __forceinline__ void fwd_cols_fpd(u64 *sm, int col, int t, int c, int log_n,
-                                             const double *tw, const PrimeDev &P, FillD &&filld,
+                                             const double2 *tw, const PrimeDev &P, FillD &&filld,
                                              Store &&store) {
   using G = ColGeom<LOG_M>;
-  const TwGlobal twg{tw, log_n, log_n - LOG_M};
+  const TwCols<LOG_M> twg{tw};
   double x[kEpt];
   filld(x);
   fwd_round_fp<LOG_M, G::HI, 4>(x, t, 0, twg, P.qd, P.qinv);
@@ -346,7 +353,7 @@ __device__ __forceinline__ void fwd_cols_fpd(u64 *sm, int col, int t, int c, int
 
 template <int LOG_M, class Fill, class Store>
 __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double *tw, const PrimeDev &P, Fill &&fill,
+                                            const double2 *tw, const PrimeDev &P, Fill &&fill,
                                             Store &&store) {
   auto filld = [&](double (&x)[kEpt]) {
     u64 xin[kEpt];
@@ -362,10 +369,10 @@ __device__ __forceinline__ void fwd_cols_fp(u64 *sm, int col, int t, int c, int 
 // (CANON_FP: the bits of that canonical value as a double instead).
 template <int LOG_M, bool CANON_FP = false, class Load, class Store>
 __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int log_n,
-                                            const double *tw, const PrimeDev &P, double2 s0,
+                                            const double2 *tw, const PrimeDev &P, double2 s0,
                                             double2 s1, Load &&load, Store &&store) {
   using G = ColGeom<LOG_M>;
-  const TwGlobal twg{tw, log_n, log_n - LOG_M};
+  const TwCols<LOG_M> twg{tw};
   double x[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = as_fp(load(lidx<LOG_M, 0, G::NLO>(t, e), col));
@@ -414,7 +421,7 @@ template <int LOG_M, bool CANON = true>
 __device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
                                                  const u64 *tile, int t, int rr, long long row,
                                                  long long row0, const PrimeDev &P) {
-  const TwRowsSmem<LOG_M, RowGeom<LOG_M>::R> tw{smtw, row0};
+  const TwRowsSmem<LOG_M, RowGeom<LOG_M>::R> tw{smtw, row0, P.qinv};
   fwd_rows_regs_fp_tw<LOG_M, CANON>(xo, sm, tw, tile, t, rr, row, P);
 }
 
@@ -425,7 +432,7 @@ __device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const
                                                  int t, int rr, long long row, long long row0,
                                                  const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
-  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0};
+  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0, P.qinv};
   const double2 none = make_double2(0, 0);
   double x[kEpt];
 #pragma unroll

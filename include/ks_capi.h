@@ -151,6 +151,14 @@ int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream
 /* n rotations of n independent ciphertexts (cts[i] rotated by steps[i]). */
 int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n,
                     int level_limbs, void *stream);
+/* ks_rotate_batch on ciphertexts in HOST memory (pinned memory lets the
+ * copies overlap the compute): host_cts[i] [2][n_local][N] is copied to the
+ * device, rotated by steps[i] and copied back in place.  The ciphertexts are
+ * spread over the lanes, each with its own device staging buffer, so the
+ * copies of one lane overlap the key switches of the others.  Asynchronous
+ * on `stream`: the host buffers may be read only after it completes. */
+int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *steps, int n,
+                         int level_limbs, void *stream);
 /* Hoisted rotations: one ModUp of ct's c1 shared by n rotations (the
  * extended digits are permuted per rotation inside the inner product); outs[i]
  * [2][n_local][N] receives ct rotated by steps[i].  ct is not modified.  Keys

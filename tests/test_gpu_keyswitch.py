@@ -182,3 +182,31 @@ def test_rotate_batch_lanes(lanes, cuda_device):
     for ct, d, st in zip(cts, devs, steps):
         ref = o.apply_galois(ct, 7, o.galois_elt(st), keys[st])
         assert np.array_equal(_to_host(d).reshape(2, 7, o.N), ref)
+
+
+def test_rotate_batch_host_matches_device_batch(cuda_device):
+    """ks_rotate_batch_host (host ciphertexts, copies pipelined over lanes)
+    returns the words of ks_rotate_batch on device copies."""
+    from comp390project_b200 import KS_KEY_GALOIS, KsContext
+    o = oracle_for("small")
+    log_n, q, p = split(SMALL)
+    ctx = KsContext(log_n, q, p, device=0, max_batch=3)
+    s = o.secret(8, 64)
+    steps = [1, 2, 3, 1, 2]
+    for st in sorted(set(steps)):
+        e = o.galois_elt(st)
+        ctx.key_upload(KS_KEY_GALOIS, e, o.keygen_galois(s, e, 80 + st))
+    rng = np.random.default_rng(21)
+    Ql = o.L
+    cts = [np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                               for j in range(Ql)]) for _ in range(2)]) for _ in steps]
+    dev = [torch.from_numpy(c.view(np.int64).copy()).cuda() for c in cts]
+    ctx.rotate_batch(dev, steps, Ql)
+    host = [torch.from_numpy(c.view(np.int64).copy()).pin_memory() for c in cts[:3]]
+    host += [c.copy() for c in cts[3:]]  # pageable numpy arrays work too
+    ctx.rotate_batch_host(host, steps, Ql)
+    torch.cuda.synchronize()
+    for d, h in zip(dev, host):
+        hv = h.numpy().view(np.uint64) if isinstance(h, torch.Tensor) else h
+        assert np.array_equal(d.cpu().numpy().view(np.uint64), hv)
+    ctx.close()
