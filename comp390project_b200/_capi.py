@@ -87,6 +87,7 @@ SIGNATURES = {
     "ks_rotate_batch": (_I, [_P, C.POINTER(_P), C.POINTER(C.c_int), _I, _I, _P]),
     "ks_rotate_hoisted": (_I, [_P, _P, _I, C.POINTER(C.c_int), _I, C.POINTER(_P), _P]),
     "ks_rotate_batch_host": (_I, [_P, C.POINTER(_P), C.POINTER(C.c_int), _I, _I, _P]),
+    "ks_rescale": (_I, [_P, _P, _I, _P, _P]),
     "ks_linear_transform_hoisted": (_I, [_P, _P, _I, C.POINTER(C.c_int), _I, C.POINTER(_P),
                                          _P, _P]),
     "ks_ntt_forward": (_I, [_P, _P, _I, _I, _I, _P]),

@@ -274,6 +274,12 @@ class KsContext:
         self._check(self.lib.ks_rotate_batch(self.h, ptrs, st, n, int(level_limbs),
                                              _stream_ptr(stream, self.device)))
 
+    def rescale(self, ct, level_limbs: int, out, stream=None):
+        """Divide by the last prime and round: ct [2][n_local(Ql)][N] ->
+        out [2][n_local(Ql-1)][N]."""
+        self._check(self.lib.ks_rescale(self.h, self._ptr(ct), int(level_limbs), self._ptr(out),
+                                        _stream_ptr(stream, self.device)))
+
     def rotate_batch_host(self, host_cts, steps: Sequence[int], level_limbs: int, stream=None):
         """rotate_batch on host tensors (pinned CPU torch tensors or numpy
         uint64 arrays [2][n_local][N]), rotated in place; asynchronous on the

@@ -440,6 +440,28 @@ void build_level(Ctx &c, Level &lv, int Ql) {
         if (t != i) prod = h_mulmod(prod, c.primes[L + t] % pi, pi);
       scale_pair(L + i, h_invmod(prod, pi), sp);
     }
+  // rescale by the last prime of this level
+  if (Ql >= 2) {
+    const int last = Ql - 1;
+    const u64 ql = c.primes[last];
+    std::vector<ulonglong2> rpinv(L, make_ulonglong2(0, 0)), rsc;
+    for (int j = 0; j < last; ++j) {
+      const u64 qj = c.primes[j], v = h_invmod(ql % qj, qj);
+      rpinv[j] = make_ulonglong2(v, h_shoup(v, qj));
+    }
+    scale_pair(last, 1, rsc);
+    scale_pair(last, 1, rsc);
+    const bool have_last = (last % G) == g;
+    for (int p = 0; p < 2; ++p) {
+      lv.rs_off.h.push_back(((long long)p * lv.n_q + (have_last ? last / G : 0)) * c.N);
+      lv.rs_prime.h.push_back(last);
+    }
+    lv.rs_pinv = upload(rpinv);
+    lv.rs_scale = upload(rsc);
+    up_i64(lv.rs_off);
+    up_ints(lv.rs_prime);
+    lv.rs_md = ModDownDev{1, last, nullptr, nullptr, lv.rs_pinv, nullptr, nullptr};
+  }
   up_ints(lv.src_slot);
   up_ints(lv.digits);
   up_ints(lv.cx_prime);
@@ -611,6 +633,10 @@ void ctx_free(Ctx &c) {
       f(t->d);
     f(lv.job_off.d);
     f(lv.intt_off.d);
+    f(lv.rs_off.d);
+    f(lv.rs_prime.d);
+    f(lv.rs_pinv);
+    f(lv.rs_scale);
     f(lv.scale_in);
     f(lv.scale_p);
     f(lv.w);
@@ -1054,6 +1080,51 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
   }
 }
 
+// Rescale by the last prime (Phantom rescale_to_next_inplace, reference
+// dist_rescale_to_next_inplace, distributed_eval.cu:265-273, which gathers
+// the ciphertext on GPU 0 for it): the owner of limb Ql-1 INTTs it (both
+// polys) and, with input broadcast, broadcasts the 2N coefficient words;
+// every rank then finishes its own limbs j < Ql-1 with the ModDown column
+// and row kernels, q_{Ql-1} playing the special prime:
+//   out_j = (ct_j - NTT_j([c + h]_{q_last} mod q_j - [h]_{q_j})) * q_last^-1,  h = q_last / 2.
+void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStream_t s) {
+  KS_REQUIRE(ct != nullptr && out != nullptr && aligned16(ct) && aligned16(out),
+             "pointers null or not 16-byte aligned");
+  KS_REQUIRE(ct != out, "out must not alias ct");
+  KS_REQUIRE(Ql >= 2 && Ql <= c.L, "level_limbs must be in [2, L]");
+  const Level &lv = level_of(c, Ql), &lo = level_of(c, Ql - 1);
+  const int last = Ql - 1, G = c.replicated() ? 1 : c.world;
+  const bool have_last = G == 1 || last % G == c.rank;
+  const size_t N = c.N;
+  const NttTables T = c.tables();
+  const u64 ql = c.primes[last];
+  KS_CUDA(cudaSetDevice(c.device));
+  u64 *buf = L.s_t;  // [2][N], coefficient form of the last limb
+  if (have_last) {
+    StageTimer tm(c, ST_INTT_IN, s);
+    LimbMap src{const_cast<u64 *>(ct), 0, lv.rs_off.d, lv.rs_prime.d, 0, 1};
+    LimbMap dst{buf, (long long)N, nullptr, lv.rs_prime.d, 0, 1};
+    KS_CUDA(ntt_inverse_scaled(src, dst, 2, lv.rs_scale, T, s));
+    c.launches += 2;
+  }
+  if (G > 1) {
+    StageTimer tm(c, ST_COMM, s);
+    KS_NCCL(ncclBroadcast(buf, buf, 2 * N, ncclUint64, last % G, L.comm, s));
+  }
+  {
+    StageTimer tm(c, ST_MODDOWN_COLS, s);
+    KS_CUDA(rescale_fused_cols(buf, ql, ql < kFpBound, L.s_z, lo.n_q, lo.q_index.d, T, s));
+    c.launches += lo.n_q > 0 ? 1 : 0;
+  }
+  {
+    StageTimer tm(c, ST_MODDOWN_ROWS, s);
+    KS_CUDA(moddown_fused_rows(L.s_z, lo.n_q, lo.q_index.d, lo.cx_slot_q.d, ct,
+                               (long long)lv.n_q * N, out, out + (size_t)lo.n_q * N, nullptr,
+                               true, nullptr, lv.rs_md, T, s));
+    c.launches += lo.n_q > 0 ? 1 : 0;
+  }
+}
+
 void do_relin(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, cudaStream_t s) {
   KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
   const Level &lv = level_of(c, Ql);
@@ -1333,6 +1404,14 @@ int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, 
       KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
       KS_CUDA(cudaStreamWaitEvent(s, c.lanes[li].done, 0));
     }
+  });
+}
+
+int ks_rescale(ks_ctx *ctx, const uint64_t *ct, int level_limbs, uint64_t *out, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    do_rescale(ctx->c, lane0(ctx->c), ct, level_limbs, out, (cudaStream_t)stream);
   });
 }
 

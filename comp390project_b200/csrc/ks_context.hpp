@@ -69,6 +69,13 @@ struct Level {
   ulonglong2 *scale_p = nullptr;  // [2 * 2 * n_p] same with (P/p_i)^-1 for the owned P limbs
   ModUpDev mu{};
   KsLayout lay{};
+  // rescale by q_{Ql-1} (Ql >= 2): unit-scale INTT pairs of the last limb (both
+  // polys), its word offsets in the input and prime, and q_{Ql-1}^-1 mod q_j
+  ulonglong2 *rs_scale = nullptr;  // [4]
+  DevI64 rs_off;                   // [2]
+  DevInts rs_prime;                // [2]
+  ulonglong2 *rs_pinv = nullptr;   // [L] (j < Ql - 1)
+  ModDownDev rs_md{};
 };
 
 struct KeyShard {

@@ -511,6 +511,46 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Rescale: the last limb (coefficient form, both polys) to the Q limbs + the
+// forward column pass; the row pass is k_moddown_rows with q_last^-1
+// ---------------------------------------------------------------------------
+// Job (p, s), j = q_index[s]: y = ([c_p + h]_{q_last} mod q_j) - [h]_{q_j},
+// h = floor(q_last / 2), c_p the last limb of poly p (last[p * N + k];
+// stored as the bits of a double when q_last < kFpBound).
+template <int LOG_M>
+__global__ void __launch_bounds__(kThreads, 3)
+    k_rescale_cols(const u64 *__restrict__ last, u64 q_last, int last_fp, u64 *z, int n_q,
+                   const int *__restrict__ q_index, NttTables T) {
+  using G = ColGeom<LOG_M>;
+  __shared__ u64 sm[G::SMEM];
+  const int p = blockIdx.y / n_q, s = blockIdx.y % n_q;
+  const int j = q_index[s];
+  const PrimeDev P = T.primes[j];
+  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
+  const int col = blockIdx.x * G::C + c;
+  const u64 h = q_last >> 1, hj = reduce_full(h, P.q, P.mu);
+  const u64 *src = last + (long long)p * N;
+  auto fill = [&](u64 (&x)[kEpt]) {
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      const u64 v = src_u64(__ldg(src + (long long)lidx<LOG_M, G::HI, 4>(tt, e) * M2 + col),
+                            last_fp != 0);
+      x[e] = sub_mod(reduce_full(csub(v + h, q_last), P.q, P.mu), hj, P.q);
+    }
+  };
+  u64 *out = z + ((long long)p * n_q + s) * N;
+  auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
+  if (P.q < kFpBound) {
+    fwd_cols_fp<LOG_M>(sm, col, tt, c, log_n, T.fwd_col + ((long long)j << LOG_M), P, fill, store);
+  } else {
+    const ulonglong2 *tw = T.fwd + (long long)j * N;
+    if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
+    else fwd_cols<LOG_M, false>(sm, col, tt, c, log_n, tw, P, fill, store);
+  }
+}
+
 template <int LOG_M>
 cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q,
                                const int *q_index, const int *cx_slot, const u64 *cx,
@@ -620,6 +660,22 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
     case 6: k_moddown_cols<6><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
     case 7: k_moddown_cols<7><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
     case 8: k_moddown_cols<8><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t rescale_fused_cols(const u64 *last, u64 q_last, bool last_fp, u64 *z, int n_q,
+                               const int *q_index, const NttTables &T, cudaStream_t s) {
+  if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
+  if (n_q == 0) return cudaSuccess;
+  const int s1 = T.log_n / 2;
+  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
+  const int fp = last_fp ? 1 : 0;
+  switch (s1) {
+    case 6: k_rescale_cols<6><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 7: k_rescale_cols<7><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 8: k_rescale_cols<8><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -47,6 +47,14 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
                                const int *q_index, const ModDownDev &md, const int *job_ps,
                                int n_fp, const NttTables &T, cudaStream_t s);
 
+// Rescale, first part: for every job (poly p, Q slot s), j = q_index[s], the
+// column pass of the forward NTT of ([c_p + h]_{q_last} mod q_j) - [h]_{q_j},
+// h = floor(q_last / 2), c_p = last[p * N ..] the coefficient-form last limb
+// (the bits of a double when last_fp) -> z[p][s].  The second part is
+// moddown_fused_rows with q_last^-1 in place of P^-1.
+cudaError_t rescale_fused_cols(const u64 *last, u64 q_last, bool last_fp, u64 *z, int n_q,
+                               const int *q_index, const NttTables &T, cudaStream_t s);
+
 // Row pass of z[p][s] with the ModDown finish in the epilogue:
 //   o = (cx[p][cx_slot[s]] - z) * P^-1 mod q_j;
 //   p = 0: v = (rotate ? g0 : ct0) + o (rotate with g0 null: v = o);

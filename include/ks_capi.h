@@ -151,6 +151,14 @@ int ks_rotate(ks_ctx *ctx, uint64_t *ct, int level_limbs, int step, void *stream
 /* n rotations of n independent ciphertexts (cts[i] rotated by steps[i]). */
 int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n,
                     int level_limbs, void *stream);
+/* Rescale by the last prime of the level (divide by q_{Ql-1} and round;
+ * Phantom rescale_to_next_inplace as called by the reference's
+ * dist_rescale_to_next_inplace, distributed_eval.cu:265-273): ct
+ * [2][n_local(Ql)][N] -> out [2][n_local(Ql-1)][N], out must not alias ct.
+ * With input broadcast only the owner's last limb crosses NVLink (one
+ * broadcast of 2N words); the reference gathers the whole ciphertext on
+ * GPU 0 instead. */
+int ks_rescale(ks_ctx *ctx, const uint64_t *ct, int level_limbs, uint64_t *out, void *stream);
 /* ks_rotate_batch on ciphertexts in HOST memory (pinned memory lets the
  * copies overlap the compute): host_cts[i] [2][n_local][N] is copied to the
  * device, rotated by steps[i] and copied back in place.  The ciphertexts are

@@ -524,6 +524,35 @@ void ork_rotate_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
   }
 }
 
+// Rescale by the last prime (Phantom rescale_to_next_inplace, called by the
+// reference's dist_rescale_to_next_inplace, distributed_eval.cu:265-273; the
+// SEAL/Phantom divide-and-round of the RNS literature):
+//   c = INTT_{q_last}(ct_last) + floor(q_last / 2)  (mod q_last), per poly;
+//   out_j = (ct_j - NTT_j([c]_{q_j} - [floor(q_last / 2)]_{q_j})) * q_last^-1  mod q_j,
+// j < Ql - 1: out = round(ct / q_last) at level Ql - 1.
+void ork_rescale(const ork_ctx *c, const uint64_t *ct, int Ql, uint64_t *out) {
+  size_t N = c->N;
+  const int last = Ql - 1;
+  const u64 ql = c->m[last], half = ql >> 1;
+  for (int p = 0; p < 2; ++p) {
+    std::vector<u64> v(ct + ((size_t)p * Ql + last) * N, ct + ((size_t)p * Ql + last + 1) * N);
+    int li = last;
+    ntt_batch(c, v.data(), 1, &li, false);
+    for (size_t k = 0; k < N; ++k) v[k] = addmod(v[k], half, ql);
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < last; ++j) {
+      const u64 q = c->m[j], hj = half % q, inv = invmod(ql % q, q);
+      std::vector<u64> t(N);
+      for (size_t k = 0; k < N; ++k) t[k] = submod(v[k] % q, hj, q);
+      int jj = j;
+      ntt_batch(c, t.data(), 1, &jj, true);
+      const u64 *src = ct + ((size_t)p * Ql + j) * N;
+      u64 *dst = out + ((size_t)p * last + j) * N;
+      for (size_t k = 0; k < N; ++k) dst[k] = mulmod(submod(src[k], t[k], q), inv, q);
+    }
+  }
+}
+
 // Hoisted linear transform with one ModDown ("double hoisting", Bossuat,
 // Mouchet, Troncoso-Pastoriza, Hubaux, Eurocrypt 2021; the reference has no
 // counterpart -- its bootstrapping lives in the absent NEXUS Bootstrapper):

@@ -96,6 +96,8 @@ void ork_rotate_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
                         uint64_t *out);
 /* out = sum_r diags[r] * rotate(ct, elts[r]) with one ModUp and one ModDown
  * (double hoisting); diags[r] [Ql + alpha][N] NTT form in the extended basis. */
+/* ct [2][Ql][N] -> out [2][Ql-1][N]: divide by the last prime and round. */
+void ork_rescale(const ork_ctx *c, const uint64_t *ct, int Ql, uint64_t *out);
 void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
                                   const uint32_t *elts, const uint64_t *const *keys,
                                   const uint64_t *const *diags, uint64_t *out);

@@ -63,6 +63,7 @@ def lib():
                                                  C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                                  u64p]),
             "ork_encode_basis": (V, [P, f64p, f64p, I, D, i32p, I, u64p]),
+            "ork_rescale": (V, [P, u64p, I, u64p]),
             "ork_prng": (U64, [U64, U64, U64]),
             "ork_gauss": (I, [U64]),
             "ork_gauss_table": (V, [u64p]),
@@ -226,6 +227,12 @@ class Oracle:
         dp = (C.c_void_p * n)(*[d.ctypes.data for d in ds])
         lib().ork_linear_transform_hoisted(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, n,
                                            e, kp, dp, out.reshape(-1))
+        return out
+
+    def rescale(self, ct: np.ndarray, Ql: int) -> np.ndarray:
+        """[2][Ql][N] -> [2][Ql-1][N]: divide by q_{Ql-1} and round."""
+        out = np.zeros((2, Ql - 1, self.N), dtype=np.uint64)
+        lib().ork_rescale(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, out.reshape(-1))
         return out
 
     # -- keys, encoding, encryption -------------------------------------------

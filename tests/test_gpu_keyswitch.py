@@ -210,3 +210,24 @@ def test_rotate_batch_host_matches_device_batch(cuda_device):
         hv = h.numpy().view(np.uint64) if isinstance(h, torch.Tensor) else h
         assert np.array_equal(d.cpu().numpy().view(np.uint64), hv)
     ctx.close()
+
+
+@pytest.mark.parametrize("name,Ql", [("small", 7), ("small", 4), ("small", 2), ("cfg1", 3),
+                                     ("cfg3", 35)])
+def test_rescale_matches_oracle(name, Ql, cuda_device):
+    """ks_rescale (divide by the last prime and round) equals the oracle word
+    for word at several levels."""
+    from comp390project_b200 import KsContext
+    cfg = {"small": SMALL, "cfg1": CFG1, "cfg3": CFG3}[name]
+    o = oracle_for(name)
+    log_n, q, p = split(cfg)
+    ctx = KsContext(log_n, q, p, device=0)
+    rng = np.random.default_rng(40 + Ql)
+    ct = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                             for j in range(Ql)]) for _ in range(2)])
+    d = torch.from_numpy(ct.view(np.int64).copy()).cuda()
+    out = torch.zeros((2, Ql - 1, o.N), dtype=torch.int64, device="cuda")
+    ctx.rescale(d, Ql, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), o.rescale(ct, Ql))
+    ctx.close()

@@ -113,6 +113,14 @@ def _worker(rank, world, port, name, mode, q):
             for j in range(Ql2):
                 full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
         ok &= np.array_equal(full2, o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
+        # rescale: the owner of the last limb broadcasts it (input broadcast)
+        mine3 = list(range(rank, Ql - 1, world)) if not oa else list(range(Ql - 1))
+        dr = local(cts[1])
+        out3 = torch.zeros((2, len(mine3), N), dtype=torch.int64, device="cuda")
+        ctx.rescale(dr, Ql, out3)
+        torch.cuda.synchronize()
+        want3 = o.rescale(cts[1], Ql)[:, mine3]
+        ok &= np.array_equal(out3.cpu().numpy().view(np.uint64), want3)
         ctx.close()
         q.put((rank, bool(ok)))
     except Exception as e:

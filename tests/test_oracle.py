@@ -264,6 +264,25 @@ def test_encode_basis_matches_encode_on_q_limbs():
     assert np.array_equal(ext[:o.L], o.encode(z, 2.0 ** 40, o.L))
 
 
+def test_rescale_decodes_to_product_at_lower_scale():
+    """multiply + relinearise + rescale decodes to the product at scale
+    2^80 / q_last (the reference's rescale_to_next_inplace semantics)."""
+    o = oracle_for("small")
+    s = o.secret(14, 64)
+    Ql = o.L
+    rng = np.random.default_rng(15)
+    z1 = rng.uniform(-1, 1, o.N // 2)
+    z2 = rng.uniform(-1, 1, o.N // 2)
+    c1 = o.encrypt(s, o.encode(z1, 2.0 ** 40, Ql), Ql, 31)
+    c2 = o.encrypt(s, o.encode(z2, 2.0 ** 40, Ql), Ql, 32)
+    rk = o.keygen_relin(s, 33)
+    r = o.relinearize(o.multiply(c1, c2, Ql), Ql, rk)
+    rs = o.rescale(r, Ql)
+    scale = 2.0 ** 80 / float(o.moduli[Ql - 1])
+    dec = o.decode(o.decrypt(s, rs, Ql - 1), Ql - 1, scale)
+    assert np.abs(dec - z1 * z2).mean() < 1e-3
+
+
 def test_secret_hamming_weight_and_gaussian_support():
     o = oracle_for("small")
     s = o.secret(3, 64)
