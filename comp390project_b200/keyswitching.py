@@ -114,6 +114,16 @@ def keyswitching_output_aggregation(ctx: MultiGpuContext, gpu_id: int, encrypted
     keyswitching_input_broadcast(ctx, gpu_id, encrypted, c2, relin_keys, sync=sync)
 
 
+def dist_rescale_to_next(ctx: MultiGpuContext, gpu_id: int, encrypted: Ciphertext, out,
+                         sync: bool = True):
+    """Rescale by the last prime (distributed_eval.cu:265-273, there a gather to
+    GPU 0): ``out`` [2][n_local(Ql-1)][N] receives this rank's limbs of
+    round(encrypted / q_last)."""
+    k = ctx.ctx(gpu_id)
+    k.rescale(encrypted.data, encrypted.coeff_modulus_size, out)
+    _sync(k, sync)
+
+
 def allgather_c2_limbs(ctx: MultiGpuContext, gpu_id: int, local_c2, full_c2, local_limbs: int,
                        total_limbs: int, degree: Optional[int] = None, sync: bool = True):
     """All limbs of c2 on every rank in sequential order (input_broadcast.cu:75-111

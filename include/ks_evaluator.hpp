@@ -142,6 +142,21 @@ class Evaluator {
           mc_.ctx(g_));
     mc_.sync(g_);
   }
+  // Phantom rescale_to_next (reference dist_rescale_to_next_inplace,
+  // distributed_eval.cu:265-273): out receives ct / q_last at one level down
+  // (out.coeff_modulus_size = ct.coeff_modulus_size - 1, separate buffer).
+  void rescale_to_next(const CiphertextView &ct, CiphertextView &out) {
+    check(ks_rescale(mc_.ctx(g_), ct.data, (int)ct.coeff_modulus_size, out.data, mc_.stream(g_)),
+          mc_.ctx(g_));
+    mc_.sync(g_);
+  }
+  // Hoisted rotations: outs[i] = ct rotated by steps[i], one ModUp shared.
+  void rotate_hoisted(const CiphertextView &ct, const int *steps, int n, uint64_t *const *outs) {
+    check(ks_rotate_hoisted(mc_.ctx(g_), ct.data, (int)ct.coeff_modulus_size, steps, n, outs,
+                            mc_.stream(g_)),
+          mc_.ctx(g_));
+    mc_.sync(g_);
+  }
 
  private:
   MultiGpuContext &mc_;

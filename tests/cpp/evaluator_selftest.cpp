@@ -63,6 +63,23 @@ int main() {
     std::printf("relinearisation mismatch\n");
     return 1;
   }
+  // rescale: Evaluator::rescale_to_next vs ks_rescale into separate buffers
+  cudaMemcpy(a, h.data(), words * 8, cudaMemcpyHostToDevice);
+  uint64_t *r1 = nullptr, *r2 = nullptr;
+  cudaMalloc(reinterpret_cast<void **>(&r1), 2 * 2 * (size_t)N * 8);
+  cudaMalloc(reinterpret_cast<void **>(&r2), 2 * 2 * (size_t)N * 8);
+  ks_b200::CiphertextView cin{a, 2, 3, (size_t)N}, cout{r1, 2, 2, (size_t)N};
+  ev.rescale_to_next(cin, cout);
+  ks_b200::check(ks_rescale(ctx, a, 3, r2, nullptr), ctx);
+  cudaDeviceSynchronize();
+  cudaMemcpy(ra.data(), r1, 2 * 2 * (size_t)N * 8, cudaMemcpyDeviceToHost);
+  cudaMemcpy(rb.data(), r2, 2 * 2 * (size_t)N * 8, cudaMemcpyDeviceToHost);
+  if (std::memcmp(ra.data(), rb.data(), 2 * 2 * (size_t)N * 8) != 0) {
+    std::printf("rescale mismatch\n");
+    return 1;
+  }
+  cudaFree(r1);
+  cudaFree(r2);
   // error path: unknown galois element
   bool threw = false;
   try {
