@@ -165,13 +165,21 @@ __device__ __forceinline__ void inv_cols(u64 *sm, int col, int t, int c, int log
 // 16 outputs (canonical) are handed to finish(rr, i, v) for local row rr,
 // index i in the row; the tile is then written by the caller from smem.
 // ---------------------------------------------------------------------------
-template <int LOG_M, bool LAZY>
-__device__ __forceinline__ void fwd_rows_regs(u64 (&x)[kEpt], u64 *sm, const u64 *tile, int t,
-                                              int rr, long long row, int log_n,
-                                              const ulonglong2 *tw, const PrimeDev &P) {
-  using G = RowGeom<LOG_M>;
+// The 16 inputs of thread t of local row rr of a row tile (pattern HI), for
+// callers that load them ahead of the transform.
+template <int LOG_M>
+__device__ __forceinline__ void load_rows_tile(u64 (&x)[kEpt], const u64 *tile, int t, int rr) {
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) x[e] = tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)];
+  for (int e = 0; e < kEpt; ++e)
+    x[e] = tile[rr * RowGeom<LOG_M>::M + lidx<LOG_M, RowGeom<LOG_M>::HI, 4>(t, e)];
+}
+
+// fwd_rows_regs on inputs already in x (load_rows_tile).
+template <int LOG_M, bool LAZY>
+__device__ __forceinline__ void fwd_rows_inregs(u64 (&x)[kEpt], u64 *sm, int t, int rr,
+                                                long long row, int log_n, const ulonglong2 *tw,
+                                                const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
   fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))] = x[e];
@@ -184,6 +192,15 @@ __device__ __forceinline__ void fwd_rows_regs(u64 (&x)[kEpt], u64 *sm, const u64
     x[e] = LAZY ? reduce_full(x[e], P.q, P.mu) : reduce4(x[e], P.q, P.two_q);
   __syncwarp();
 }
+
+template <int LOG_M, bool LAZY>
+__device__ __forceinline__ void fwd_rows_regs(u64 (&x)[kEpt], u64 *sm, const u64 *tile, int t,
+                                              int rr, long long row, int log_n,
+                                              const ulonglong2 *tw, const PrimeDev &P) {
+  load_rows_tile<LOG_M>(x, tile, t, rr);
+  fwd_rows_inregs<LOG_M, LAZY>(x, sm, t, rr, row, log_n, tw, P);
+}
+
 
 // Inverse row pass (the first pass of an inverse transform) over one tile
 // already staged in smem (padx layout); outputs in registers, pattern HI.
@@ -395,14 +412,14 @@ __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int 
 // Forward row pass; the tile holds first-pass bits; canonical outputs in xo
 // (CANON), else the bits of the unreduced doubles (|x| < 12q < 2^47).
 // tw: twiddle getter (TwRowsSmem over a staged block, or TwRowsGlobal).
+// fwd_rows_regs_fp_tw on inputs already in xo (load_rows_tile).
 template <int LOG_M, bool CANON, class Tw>
-__device__ __forceinline__ void fwd_rows_regs_fp_tw(u64 (&xo)[kEpt], u64 *sm, const Tw &tw,
-                                                    const u64 *tile, int t, int rr, long long row,
-                                                    const PrimeDev &P) {
+__device__ __forceinline__ void fwd_rows_fp_inregs(u64 (&xo)[kEpt], u64 *sm, const Tw &tw, int t,
+                                                   int rr, long long row, const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
   double x[kEpt];
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(tile[rr * G::M + lidx<LOG_M, G::HI, 4>(t, e)]);
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(xo[e]);
   fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, tw, P.qd, P.qinv);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, G::HI, 4>(t, e))] = fp_bits(x[e]);
@@ -413,6 +430,14 @@ __device__ __forceinline__ void fwd_rows_regs_fp_tw(u64 (&xo)[kEpt], u64 *sm, co
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) xo[e] = CANON ? fp_to_canon(x[e], P.qd, P.qinv) : fp_bits(x[e]);
   __syncwarp();
+}
+
+template <int LOG_M, bool CANON, class Tw>
+__device__ __forceinline__ void fwd_rows_regs_fp_tw(u64 (&xo)[kEpt], u64 *sm, const Tw &tw,
+                                                    const u64 *tile, int t, int rr, long long row,
+                                                    const PrimeDev &P) {
+  load_rows_tile<LOG_M>(xo, tile, t, rr);
+  fwd_rows_fp_inregs<LOG_M, CANON>(xo, sm, tw, t, rr, row, P);
 }
 
 // smtw: this CTA's twiddle block, staged by stage_row_twiddles (the caller
