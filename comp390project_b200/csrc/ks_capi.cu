@@ -614,8 +614,16 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
 }
 
 void ctx_free(Ctx &c) {
+  if (c.wd_thread.joinable()) {
+    c.wd_stop = true;
+    c.wd_thread.join();
+  }
   cudaSetDevice(c.device);
   cudaDeviceSynchronize();
+  for (auto &w : c.wd_pending) cudaEventDestroy(w.ev);
+  for (cudaEvent_t e : c.wd_free) cudaEventDestroy(e);
+  c.wd_pending.clear();
+  c.wd_free.clear();
   auto f = [](void *p) {
     if (p) cudaFree(p);
   };
@@ -842,8 +850,89 @@ struct StageTimer {
 // ---------------------------------------------------------------------------
 // Collectives
 // ---------------------------------------------------------------------------
-void allgather(ncclComm_t comm, const u64 *send, u64 *recv, size_t words, cudaStream_t s) {
-  KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, comm, s));
+// Collective deadline.  Every collective of the hot path is followed by an
+// event (watch_collective); the context's watchdog thread polls those events
+// and, when one is still pending timeout_ms after it was enqueued (a rank
+// that never joined, a broken link), aborts all of the context's NCCL
+// communicators -- ncclCommAbort makes the waiting NCCL kernels return --
+// and marks the context failed: every later call returns KS_ERR_TIMEOUT and
+// the context can only be destroyed.  Nothing is watched during a graph
+// capture or with timeout_ms <= 0.
+void abort_comms(Ctx &c, const char *why) {
+  std::lock_guard<std::mutex> g(c.nccl_mu);
+  if (c.aborted.exchange(true)) return;
+  for (size_t li = 0; li < c.lanes.size(); ++li) {
+    if (c.lanes[li].comm && c.lanes[li].comm != c.comm) ncclCommAbort(c.lanes[li].comm);
+    c.lanes[li].comm = nullptr;
+  }
+  if (c.comm) ncclCommAbort(c.comm);
+  c.comm = nullptr;
+  c.err = why;
+  set_global_err(why);
+}
+
+void watchdog_loop(Ctx *c) {
+  cudaSetDevice(c->device);
+  while (!c->wd_stop.load()) {
+    std::this_thread::sleep_for(std::chrono::milliseconds(2));
+    bool late = false;
+    {
+      std::lock_guard<std::mutex> g(c->wd_mu);
+      const auto now = std::chrono::steady_clock::now();
+      for (size_t i = 0; i < c->wd_pending.size();) {
+        const cudaError_t q = cudaEventQuery(c->wd_pending[i].ev);
+        if (q == cudaErrorNotReady) {
+          late = late || now > c->wd_pending[i].deadline;
+          ++i;
+        } else {
+          if (q != cudaSuccess) cudaGetLastError();
+          c->wd_free.push_back(c->wd_pending[i].ev);
+          c->wd_pending[i] = c->wd_pending.back();
+          c->wd_pending.pop_back();
+        }
+      }
+    }
+    if (late) {
+      abort_comms(*c, "a collective did not complete within the deadline (ks_set_timeout_ms); "
+                      "communicators aborted, destroy the context");
+      std::lock_guard<std::mutex> g(c->wd_mu);
+      for (auto &w : c->wd_pending) c->wd_free.push_back(w.ev);
+      c->wd_pending.clear();
+    }
+  }
+}
+
+void watch_collective(Ctx &c, cudaStream_t s) {
+  if (c.timeout_ms <= 0 || c.capturing) return;
+  cudaEvent_t e = nullptr;
+  {
+    std::lock_guard<std::mutex> g(c.wd_mu);
+    if (!c.wd_free.empty()) {
+      e = c.wd_free.back();
+      c.wd_free.pop_back();
+    }
+  }
+  if (!e) KS_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  KS_CUDA(cudaEventRecord(e, s));
+  std::lock_guard<std::mutex> g(c.wd_mu);
+  c.wd_pending.push_back(
+      {e, std::chrono::steady_clock::now() + std::chrono::milliseconds(c.timeout_ms)});
+  if (!c.wd_thread.joinable()) c.wd_thread = std::thread(watchdog_loop, &c);
+}
+
+void check_alive(const Ctx &c) {
+  if (c.aborted.load())
+    throw KsError{KS_ERR_TIMEOUT, "context failed: " + c.err};
+}
+
+void allgather(Ctx &c, ncclComm_t comm, const u64 *send, u64 *recv, size_t words,
+               cudaStream_t s) {
+  check_alive(c);
+  {
+    std::lock_guard<std::mutex> g(c.nccl_mu);
+    KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, comm, s));
+  }
+  watch_collective(c, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -865,7 +954,7 @@ void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const u64 *in_ntt, cud
   }
   if (!c.replicated()) {
     StageTimer tm(c, ST_COMM, s);
-    allgather(L.comm, L.s_coef, L.s_coef_all, (size_t)lv.coef_ml * N, s);
+    allgather(c, L.comm, L.s_coef, L.s_coef_all, (size_t)lv.coef_ml * N, s);
   }
   {
     StageTimer tm(c, ST_MODUP_COLS, s);
@@ -881,8 +970,13 @@ void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, cudaStream_t s) {
   if (!c.oa()) return;
   {
     StageTimer tm(c, ST_COMM, s);
-    KS_NCCL(ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum,
-                          L.comm, s));
+    check_alive(c);
+    {
+      std::lock_guard<std::mutex> g(c.nccl_mu);
+      KS_NCCL(ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum,
+                            L.comm, s));
+    }
+    watch_collective(c, s);
   }
   KS_CUDA(mod_reduce(L.s_cx, 2 * lv.n_out, lv.cx_prime.d, c.d_primes, c.log_n, s));
   c.launches += 1;
@@ -917,7 +1011,7 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, u64 *ct0, u64 *ct1, const
       }
     }
     StageTimer tm(c, ST_COMM, s);
-    allgather(L.comm, L.s_ysend, L.s_yall, (size_t)c.max_p_own * 2 * N, s);
+    allgather(c, L.comm, L.s_ysend, L.s_yall, (size_t)c.max_p_own * 2 * N, s);
     y_base = L.s_yall;
   }
   // 6. P -> Q conversion fused into the column pass
@@ -966,7 +1060,9 @@ const Level &level_of(Ctx &c, int Ql) {
 }
 
 void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
-  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  check_alive(c);
+  KS_REQUIRE(aligned16(ct) && (ct != nullptr || n_local(c.rank, c.replicated() ? 1 : c.world, Ql) == 0),
+             "ciphertext pointer null or not 16-byte aligned");
   check_elt(c, elt);
   const Level &lv = level_of(c, Ql);
   const KeyShard &key = key_get(c, KS_KEY_GALOIS, elt);
@@ -1004,7 +1100,9 @@ uint32_t elt_of_step(const Ctx &c, int step) {
 //     ModDown at the end: out = sum_i diags[i] * rot_i(ct).
 void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *const *outs,
                 const u64 *const *diags, u64 *out, cudaStream_t s) {
-  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  check_alive(c);
+  KS_REQUIRE(aligned16(ct) && (ct != nullptr || n_local(c.rank, c.replicated() ? 1 : c.world, Ql) == 0),
+             "ciphertext pointer null or not 16-byte aligned");
   KS_REQUIRE(steps != nullptr && n >= 0, "bad rotation list");
   KS_REQUIRE((outs != nullptr) != (out != nullptr), "give either outs or out");
   const Level &lv = level_of(c, Ql);
@@ -1088,10 +1186,13 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
 // and row kernels, q_{Ql-1} playing the special prime:
 //   out_j = (ct_j - NTT_j([c + h]_{q_last} mod q_j - [h]_{q_j})) * q_last^-1,  h = q_last / 2.
 void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStream_t s) {
-  KS_REQUIRE(ct != nullptr && out != nullptr && aligned16(ct) && aligned16(out),
-             "pointers null or not 16-byte aligned");
-  KS_REQUIRE(ct != out, "out must not alias ct");
+  check_alive(c);
+  KS_REQUIRE(aligned16(ct) && aligned16(out), "pointers not 16-byte aligned");
+  KS_REQUIRE(ct == nullptr || ct != out, "out must not alias ct");
   KS_REQUIRE(Ql >= 2 && Ql <= c.L, "level_limbs must be in [2, L]");
+  KS_REQUIRE((ct != nullptr && out != nullptr) ||
+                 n_local(c.rank, c.replicated() ? 1 : c.world, Ql) == 0,
+             "ciphertext pointers are null");
   const Level &lv = level_of(c, Ql), &lo = level_of(c, Ql - 1);
   const int last = Ql - 1, G = c.replicated() ? 1 : c.world;
   const bool have_last = G == 1 || last % G == c.rank;
@@ -1109,7 +1210,12 @@ void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStrea
   }
   if (G > 1) {
     StageTimer tm(c, ST_COMM, s);
-    KS_NCCL(ncclBroadcast(buf, buf, 2 * N, ncclUint64, last % G, L.comm, s));
+    check_alive(c);
+    {
+      std::lock_guard<std::mutex> g(c.nccl_mu);
+      KS_NCCL(ncclBroadcast(buf, buf, 2 * N, ncclUint64, last % G, L.comm, s));
+    }
+    watch_collective(c, s);
   }
   {
     StageTimer tm(c, ST_MODDOWN_COLS, s);
@@ -1126,7 +1232,9 @@ void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStrea
 }
 
 void do_relin(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, cudaStream_t s) {
-  KS_REQUIRE(ct != nullptr && aligned16(ct), "ciphertext pointer null or not 16-byte aligned");
+  check_alive(c);
+  KS_REQUIRE(aligned16(ct) && (ct != nullptr || n_local(c.rank, c.replicated() ? 1 : c.world, Ql) == 0),
+             "ciphertext pointer null or not 16-byte aligned");
   const Level &lv = level_of(c, Ql);
   const KeyShard &key = key_get(c, KS_KEY_RELIN, 0);
   const size_t nq = lv.n_q, N = c.N;
@@ -1343,9 +1451,12 @@ int ks_keyswitch_add(ks_ctx *ctx, const uint64_t *cin, uint64_t *ct, int level_l
   ctx->c.launches = 0;
   return guarded(ctx, [&] {
     Ctx &c = ctx->c;
-    KS_REQUIRE(cin != nullptr && ct != nullptr && aligned16(cin) && aligned16(ct),
+    KS_REQUIRE(aligned16(cin) && aligned16(ct) &&
+                   ((cin != nullptr && ct != nullptr) ||
+                    n_local(c.rank, c.replicated() ? 1 : c.world, level_limbs) == 0),
                "pointers must be non-null and 16-byte aligned");
     KS_REQUIRE(kind == KS_KEY_RELIN || kind == KS_KEY_GALOIS, "unknown key kind");
+    check_alive(c);
     const Level &lv = level_of(c, level_limbs);
     const KeyShard &key = key_get(c, kind, kind == KS_KEY_RELIN ? 0u : elt);
     const size_t nq = lv.n_q, N = c.N;
@@ -1605,7 +1716,7 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
     const int nl = n_local(c.rank, c.world, total_limbs);
     KS_CUDA(cudaMemsetAsync(send, 0, ml * N * 8, s));
     if (nl > 0) KS_CUDA(cudaMemcpyAsync(send, local_buf, nl * N * 8, cudaMemcpyDeviceToDevice, s));
-    allgather(c.comm, send, recv, ml * N, s);
+    allgather(c, c.comm, send, recv, ml * N, s);
     // rank-grouped [G][ml] -> sequential: limb j at (j % G, j / G)
     for (int j = 0; j < total_limbs; ++j)
       KS_CUDA(cudaMemcpyAsync(full_buf + (size_t)j * N, recv + ((j % G) * ml + j / G) * N, N * 8,

@@ -10,8 +10,12 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <atomic>
+#include <chrono>
 #include <map>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/ks_capi.h"
@@ -137,6 +141,18 @@ struct Ctx {
   ncclComm_t comm = nullptr;
   bool own_comm = false;
   int timeout_ms = 60000;
+  // Collective deadline (see watch_collective): events recorded after the
+  // collectives, polled by a watchdog thread that aborts the communicators
+  // when one is late.  nccl_mu serialises NCCL enqueues with the abort.
+  struct Watch {
+    cudaEvent_t ev;
+    std::chrono::steady_clock::time_point deadline;
+  };
+  std::mutex wd_mu, nccl_mu;
+  std::vector<Watch> wd_pending;
+  std::vector<cudaEvent_t> wd_free;
+  std::thread wd_thread;
+  std::atomic<bool> wd_stop{false}, aborted{false};
   // diagnostics
   std::string err;
   int launches = 0;
