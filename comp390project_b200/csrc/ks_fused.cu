@@ -272,16 +272,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       asm volatile("prefetch.global.L2 [%0];" ::"l"(v + line));
   };
   const int n_dig = lay.n_digits;
-  // the row-pass inputs of the next extended digit are loaded into registers
-  // one digit ahead, so their latency hides behind the current digit's
-  // inner product
-  u64 xn[kEpt];
-  auto load_next = [&](int di) {
-    const int d = __ldg(&lay.digits[di]);
-    if (d != dj) load_rows_tile<LOG_M>(xn, tbase + d * tstride, tt, rr);
-  };
   prefetch(__ldg(&lay.digits[0]));
-  load_next(0);
 #pragma unroll 1
   for (int di = 0; di < n_dig; ++di) {
     const int d = __ldg(&lay.digits[di]);  // digit di of the key shard
@@ -298,15 +289,13 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
     if (di + 1 < n_dig) prefetch(__ldg(&lay.digits[di + 1]));
     if (!own) {
       u64 x[kEpt];
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e) x[e] = xn[e];
-      if (FP) fwd_rows_fp_inregs<LOG_M, false>(x, sm, twf, tt, rr, row, P);
-      else fwd_rows_inregs<LOG_M, LAZY>(x, sm, tt, rr, row, log_n, tw, P);
+      const u64 *tile = tbase + d * tstride;
+      if (FP) fwd_rows_regs_fp_tw<LOG_M, false>(x, sm, twf, tile, tt, rr, row, P);
+      else fwd_rows_regs<LOG_M, LAZY>(x, sm, tile, tt, rr, row, log_n, tw, P);
 #pragma unroll
       for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(tt, e))] = x[e];
       __syncwarp();
     }
-    if (di + 1 < n_dig) load_next(di + 1);
     cp_async_wait_all();  // this lane's own key pairs
     const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll

@@ -146,7 +146,9 @@ def test_multi_gpu_keyswitch_bitexact(name, mode, world, cuda_device):
              for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in range(world))
+    # every worker sets a 60 s collective deadline, so a failed rank ends the
+    # others' collectives with an error instead of a hang
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
     assert all(v is True for v in res.values()), res
