@@ -40,7 +40,7 @@ METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
 # DRAM bytes per launch (read + write) of each key-switch kernel at config 3,
 # one key switch, from `ncu --set full` (profiles/keyswitch_config3_kernels.md).
 PROFILED_TRAFFIC = {
-    "galois": 38.1e6, "intt_input": 55.7e6, "modup_cols": 100.9e6, "modup_rows_ip": 508.8e6,
+    "galois": 38.1e6, "intt_input": 55.7e6, "modup_cols": 98.2e6, "modup_rows_ip": 504.8e6,
     "intt_p": 15.9e6, "moddown_cols": 5.4e6, "moddown_rows": 140.2e6,
 }
 
