@@ -1,5 +1,7 @@
-// ks_kernels.cu -- ModUp base extension, inner product, ModDown finish,
-// automorphism, partition copies and synthetic-key samplers (sm_100a).
+// ks_kernels.cu -- automorphism, the standalone inner products of the
+// hoisted path, the post-all-reduce reduction, partition copies and the
+// synthetic-key samplers (sm_100a).  The fused ModUp / ModDown kernels live
+// in ks_fused.cu.
 //
 // All kernels stream 128-bit words (two coefficients per thread per access)
 // and keep per-limb constants in registers; the limb index of a CTA is
@@ -36,52 +38,6 @@ __global__ void k_galois_ntt(const u64 *__restrict__ in, u64 *__restrict__ out, 
     v.y = t;
   }
   *reinterpret_cast<ulonglong2 *>(out + limb * N + i) = v;
-}
-
-// One thread: two adjacent coefficients of one digit, all output limbs.
-__global__ void __launch_bounds__(kBlk) k_modup_bconv(const u64 *__restrict__ coef,
-                                                     u64 *__restrict__ t, ModUpDev mu,
-                                                     KsLayout lay, const PrimeDev *primes,
-                                                     int log_n) {
-  const int N = 1 << log_n;
-  const int d = blockIdx.y;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
-  const int lo = d * mu.alpha;
-  const int n_src = min(mu.alpha, mu.Ql - lo);
-  u64 v0[KS_MAX_ALPHA], v1[KS_MAX_ALPHA];
-#pragma unroll
-  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-    if (i < n_src) {
-      const int j = lo + i;
-      const long long slot = (long long)(j % lay.coef_G) * lay.coef_ml + j / lay.coef_G;
-      const ulonglong2 x = *reinterpret_cast<const ulonglong2 *>(coef + slot * N + k);
-      const ulonglong2 c = mu.qhatinv[d * mu.alpha + i];
-      const u64 q = primes[mu.prime_of[j]].q;
-      v0[i] = mul_shoup(x.x, c.x, c.y, q);
-      v1[i] = mul_shoup(x.y, c.x, c.y, q);
-    }
-  }
-  u64 *td = t + (long long)d * lay.n_out * N;
-  for (int s = 0; s < lay.n_out; ++s) {
-    const int j = lay.out_j[s];
-    if (j >= lo && j < lo + n_src) continue;
-    const PrimeDev P = primes[mu.prime_of[j]];
-    const u64 *w = mu.w + ((long long)d * mu.QlP + j) * mu.alpha;
-    u128v a0 = {0, 0}, a1 = {0, 0};
-#pragma unroll
-    for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-      if (i < n_src) {
-        const u64 wi = __ldg(&w[i]);
-        mac(a0, v0[i], wi);
-        mac(a1, v1[i], wi);
-      }
-    }
-    ulonglong2 r;
-    r.x = barrett128(a0, P.q, P.br_hi, P.br_lo);
-    r.y = barrett128(a1, P.q, P.br_hi, P.br_lo);
-    *reinterpret_cast<ulonglong2 *>(td + (long long)s * N + k) = r;
-  }
 }
 
 // Inner product of the automorphism X -> X^elt of the extended digits for
@@ -191,90 +147,6 @@ __global__ void __launch_bounds__(kBlk) k_inner_product_acc(
   *reinterpret_cast<ulonglong2 *>(a1) = v1;
 }
 
-// One thread: two coefficients of one poly, all Q output limbs.
-__global__ void __launch_bounds__(kBlk) k_moddown_bconv(const u64 *__restrict__ y_base,
-                                                       const long long *__restrict__ y_off,
-                                                       u64 *__restrict__ z, int n_q,
-                                                       const int *__restrict__ q_index,
-                                                       ModDownDev md, const PrimeDev *primes,
-                                                       int log_n) {
-  const int N = 1 << log_n;
-  const int p = blockIdx.y;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
-  u64 v0[KS_MAX_ALPHA], v1[KS_MAX_ALPHA];
-#pragma unroll
-  for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-    if (i < md.alpha) {
-      const ulonglong2 x =
-          *reinterpret_cast<const ulonglong2 *>(y_base + y_off[p * md.alpha + i] + k);
-      const ulonglong2 c = md.phatinv[i];
-      const u64 q = primes[md.first_p + i].q;
-      v0[i] = mul_shoup(x.x, c.x, c.y, q);
-      v1[i] = mul_shoup(x.y, c.x, c.y, q);
-    }
-  }
-  for (int s = 0; s < n_q; ++s) {
-    const int j = q_index[s];
-    const PrimeDev P = primes[j];
-    const u64 *w = md.w + (long long)j * md.alpha;
-    u128v a0 = {0, 0}, a1 = {0, 0};
-#pragma unroll
-    for (int i = 0; i < KS_MAX_ALPHA; ++i) {
-      if (i < md.alpha) {
-        const u64 wi = __ldg(&w[i]);
-        mac(a0, v0[i], wi);
-        mac(a1, v1[i], wi);
-      }
-    }
-    ulonglong2 r;
-    r.x = barrett128(a0, P.q, P.br_hi, P.br_lo);
-    r.y = barrett128(a1, P.q, P.br_hi, P.br_lo);
-    *reinterpret_cast<ulonglong2 *>(z + ((long long)p * n_q + s) * N + k) = r;
-  }
-}
-
-__global__ void __launch_bounds__(kBlk) k_moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0,
-                                                        const u64 *__restrict__ cx,
-                                                        int cx_stride_poly,
-                                                        const int *__restrict__ cx_slot,
-                                                        const u64 *__restrict__ z, int n_q,
-                                                        const int *__restrict__ q_index,
-                                                        ModDownDev md, const PrimeDev *primes,
-                                                        int log_n, int rotate) {
-  const int N = 1 << log_n;
-  const int s = blockIdx.y;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
-  const int j = q_index[s];
-  const u64 q = primes[j].q;
-  const ulonglong2 pi = md.pinv[j];
-  const long long off = (long long)s * N + k;
-  const long long cxo = (long long)cx_slot[s] * N + k;
-  const ulonglong2 c0 = *reinterpret_cast<const ulonglong2 *>(cx + cxo);
-  const ulonglong2 c1 = *reinterpret_cast<const ulonglong2 *>(cx + cx_stride_poly + cxo);
-  const ulonglong2 z0 = *reinterpret_cast<const ulonglong2 *>(z + off);
-  const ulonglong2 z1 = *reinterpret_cast<const ulonglong2 *>(z + (long long)n_q * N + off);
-  ulonglong2 o0, o1;
-  o0.x = mul_shoup(c0.x + q - z0.x, pi.x, pi.y, q);
-  o0.y = mul_shoup(c0.y + q - z0.y, pi.x, pi.y, q);
-  o1.x = mul_shoup(c1.x + q - z1.x, pi.x, pi.y, q);
-  o1.y = mul_shoup(c1.y + q - z1.y, pi.x, pi.y, q);
-  ulonglong2 base0 = *reinterpret_cast<const ulonglong2 *>((rotate ? g0 : ct0) + off);
-  ulonglong2 r0, r1;
-  r0.x = add_mod(base0.x, o0.x, q);
-  r0.y = add_mod(base0.y, o0.y, q);
-  if (rotate) {
-    r1 = o1;
-  } else {
-    const ulonglong2 b1 = *reinterpret_cast<const ulonglong2 *>(ct1 + off);
-    r1.x = add_mod(b1.x, o1.x, q);
-    r1.y = add_mod(b1.y, o1.y, q);
-  }
-  *reinterpret_cast<ulonglong2 *>(ct0 + off) = r0;
-  *reinterpret_cast<ulonglong2 *>(ct1 + off) = r1;
-}
-
 __global__ void k_mod_reduce(u64 *x, const int *prime_of_slot, const PrimeDev *primes,
                              int log_n) {
   const int N = 1 << log_n;
@@ -382,13 +254,6 @@ cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t
   return cudaGetLastError();
 }
 
-cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLayout &lay,
-                        const PrimeDev *primes, int log_n, cudaStream_t s) {
-  if (mu.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
-  k_modup_bconv<<<grid2(log_n, mu.beta, 2), kBlk, 0, s>>>(coef, t, mu, lay, primes, log_n);
-  return cudaGetLastError();
-}
-
 cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
                               u64 *acc, const u64 *diag, const u64 *c0, const ulonglong2 *pmodq,
                               bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
@@ -408,27 +273,6 @@ cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int ke
   if (!(elt & 1u) || elt >= (2u << log_n)) return cudaErrorInvalidValue;
   k_inner_product<<<grid2(log_n, lay.n_out, 2), kBlk, 0, s>>>(t, c_ntt, key, key_limbs, cx, mu,
                                                               lay, primes, log_n, elt);
-  return cudaGetLastError();
-}
-
-cudaError_t moddown_bconv(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
-                          const int *q_index, const ModDownDev &md, const PrimeDev *primes,
-                          int log_n, cudaStream_t s) {
-  if (md.alpha > KS_MAX_ALPHA) return cudaErrorInvalidValue;
-  if (n_q <= 0) return cudaSuccess;
-  k_moddown_bconv<<<grid2(log_n, 2, 2), kBlk, 0, s>>>(y_base, y_off, z, n_q, q_index, md, primes,
-                                                      log_n);
-  return cudaGetLastError();
-}
-
-cudaError_t moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0, const u64 *cx, int cx_stride_poly,
-                           const int *cx_slot, const u64 *z, int n_q, const int *q_index,
-                           const ModDownDev &md, const PrimeDev *primes, int log_n, bool rotate,
-                           cudaStream_t s) {
-  if (n_q <= 0) return cudaSuccess;
-  k_moddown_finish<<<grid2(log_n, n_q, 2), kBlk, 0, s>>>(ct0, ct1, g0, cx, cx_stride_poly,
-                                                         cx_slot, z, n_q, q_index, md, primes,
-                                                         log_n, rotate ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -48,12 +48,6 @@ struct KsLayout {
 cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
                        cudaStream_t s);
 
-// ModUp base extension for all digits:
-//   t[d][s][k] = sum_i [x_i[k] * qhatinv_{d,i}]_{q_i} * w[d][j][i] mod m_j,  j = out_j[s],
-// for every output slot s with j outside digit d (those slots are left untouched).
-cudaError_t modup_bconv(const u64 *coef, u64 *t, const ModUpDev &mu, const KsLayout &lay,
-                        const PrimeDev *primes, int log_n, cudaStream_t s);
-
 // Inner product of the automorphism X -> X^elt of the extended digits
 // (elt = 1: no automorphism), all in NTT form:
 //   cx[p][s][k] = sum_i src_{d_i}[s][galois_src(k)] * key[i][p][key_slot[s]][k]  mod m_j,
@@ -71,21 +65,6 @@ cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, in
                               u64 *acc, const u64 *diag, const u64 *c0, const ulonglong2 *pmodq,
                               bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
                               const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s);
-
-// z[p][s][k] = sum_i [y_i[k] * phatinv_i]_{p_i} * w[j][i] mod q_j for the Q limbs
-// j = q_index[s], s < n_q; y: pointers to the alpha P-limb coefficient arrays
-// of poly p at y_off[p*alpha + i] (word offsets from y_base).
-cudaError_t moddown_bconv(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
-                          const int *q_index, const ModDownDev &md, const PrimeDev *primes,
-                          int log_n, cudaStream_t s);
-
-// Final ModDown step and the add to the ciphertext, for the Q slots s < n_q:
-//   o_p = (cx[p][cx_slot[s]] - z[p][s]) * P^-1 mod q_j
-//   relin:  ct0 += o_0, ct1 += o_1;   rotate: ct0 = g0 + o_0, ct1 = o_1.
-cudaError_t moddown_finish(u64 *ct0, u64 *ct1, const u64 *g0, const u64 *cx, int cx_stride_poly,
-                           const int *cx_slot, const u64 *z, int n_q, const int *q_index,
-                           const ModDownDev &md, const PrimeDev *primes, int log_n, bool rotate,
-                           cudaStream_t s);
 
 // x %= q for each limb (after an integer all-reduce / reduce-scatter of partial sums).
 cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
