@@ -2,8 +2,10 @@
 
 The product is libks_b200.so (include/ks_capi.h); this package is its Python
 host side: the context wrapper, the reference-style key-switching entry
-points and the cyclic limb partition.
+points, the cyclic limb partition and the wire format of keys and
+ciphertexts.
 """
 from .context import KsContext, KsGraph, gen_primes, nccl_unique_id, secret_generate  # noqa: F401
 from ._capi import (KS_KEY_GALOIS, KS_KEY_RELIN, KS_MODE_INPUT_BROADCAST,  # noqa: F401
                     KS_MODE_OUTPUT_AGGREGATION, KsError)
+from . import wire  # noqa: F401,E402

@@ -24,6 +24,9 @@ KS_KEY_RELIN = 0
 KS_KEY_GALOIS = 1
 KS_MODE_INPUT_BROADCAST = 0
 KS_MODE_OUTPUT_AGGREGATION = 1
+KS_WIRE_RELIN_KEY = 1
+KS_WIRE_GALOIS_KEY = 2
+KS_WIRE_CIPHERTEXT = 3
 KS_NCCL_ID_BYTES = 128
 
 _ERR_NAMES = {
@@ -74,6 +77,12 @@ SIGNATURES = {
     "ks_num_digits": (_I, [_P, _I]),
     "ks_galois_elt": (_I, [_P, _I, C.POINTER(C.c_uint32)]),
     "ks_key_words": (_SZ, [_P]),
+    "ks_wire_size": (_SZ, [C.POINTER(ks_params), _I, _I, _I]),
+    "ks_wire_pack": (_I, [C.POINTER(ks_params), _I, _U32, _I, _I, _u64p, _P, _SZ]),
+    "ks_wire_unpack": (_I, [C.POINTER(ks_params), _P, _SZ, C.POINTER(C.c_int),
+                            C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                            _u64p, _SZ]),
+    "ks_key_upload_wire": (_I, [_P, _P, _SZ]),
     "ks_key_upload": (_I, [_P, _I, _U32, _P, _SZ]),
     "ks_key_upload_device": (_I, [_P, _I, _U32, _P, _SZ, _P]),
     "ks_key_generate": (_I, [_P, _I, _U32, _P, _U64, _P]),

@@ -203,6 +203,12 @@ class KsContext:
         key = np.ascontiguousarray(key, dtype=np.uint64)
         self._check(self.lib.ks_key_upload(self.h, kind, int(elt), key.ctypes.data, key.size))
 
+    def key_upload_wire(self, blob: bytes):
+        """Uploads a key blob of comp390project_b200.wire (validated against
+        this context's parameters; the context keeps its shard)."""
+        raw = C.create_string_buffer(bytes(blob), len(blob))
+        self._check(self.lib.ks_key_upload_wire(self.h, raw, len(blob)))
+
     def key_upload_device(self, kind: int, elt: int, key, stream=None):
         self._check(self.lib.ks_key_upload_device(self.h, kind, int(elt), self._ptr(key),
                                                   key.numel(), _stream_ptr(stream, self.device)))

@@ -1402,6 +1402,25 @@ int ks_key_upload(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *host_key,
   return guarded(ctx, [&] { key_upload(ctx->c, kind, elt, host_key, n, false, 0); });
 }
 
+int ks_key_upload_wire(ks_ctx *ctx, const void *blob, size_t n) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    std::vector<uint64_t> q(c.primes.begin(), c.primes.begin() + c.L),
+        p(c.primes.begin() + c.L, c.primes.end());
+    const ks_params prm{(uint32_t)c.log_n, c.L, q.data(), c.alpha, p.data(), c.mode, 1};
+    int object = 0;
+    uint32_t elt = 0;
+    if (ks_wire_unpack(&prm, blob, n, &object, &elt, nullptr, nullptr, nullptr, 0) != KS_OK)
+      throw KsError{KS_ERR_INVALID, "not a key blob of this context's parameters (or corrupt)"};
+    KS_REQUIRE(object == KS_WIRE_RELIN_KEY || object == KS_WIRE_GALOIS_KEY, "blob is not a key");
+    const int kind = object == KS_WIRE_RELIN_KEY ? KS_KEY_RELIN : KS_KEY_GALOIS;
+    key_upload(c, kind, object == KS_WIRE_RELIN_KEY ? 0u : elt,
+               reinterpret_cast<const u64 *>(static_cast<const unsigned char *>(blob) + 64),
+               full_key_words(c), false, 0);
+  });
+}
+
 int ks_key_upload_device(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *dev_key, size_t n,
                          void *stream) {
   if (!ctx) return KS_ERR_INVALID;

@@ -116,6 +116,28 @@ int ks_key_download(ks_ctx *ctx, int kind, uint32_t galois_elt, uint64_t *host_k
                     size_t n_words);
 int ks_key_drop(ks_ctx *ctx, int kind, uint32_t galois_elt);
 
+/* Wire format (host functions, no device needed): a self-describing
+ * little-endian blob of a full key [digits][2][L+alpha][N] or a ciphertext
+ * [polys][level_limbs][N] -- 64-byte header (magic "KSB2WIRE", version,
+ * object, Galois element, log_n, n_q, n_p, dimensions, FNV-1a digests of the
+ * parameters and of the payload) then the words.  The reference has no
+ * serialised form (its key distribution, distributed_context.cu:112-134,
+ * regenerates keys on every GPU).  Unpack checks parameters, sizes, digests
+ * and that every word is a canonical residue; words may be null to only
+ * validate. */
+#define KS_WIRE_RELIN_KEY 1
+#define KS_WIRE_GALOIS_KEY 2
+#define KS_WIRE_CIPHERTEXT 3
+size_t ks_wire_size(const ks_params *prm, int object, int level_limbs, int n_polys);
+int ks_wire_pack(const ks_params *prm, int object, uint32_t galois_elt, int level_limbs,
+                 int n_polys, const uint64_t *words, void *out, size_t cap);
+int ks_wire_unpack(const ks_params *prm, const void *blob, size_t n, int *object,
+                   uint32_t *galois_elt, int *level_limbs, int *n_polys, uint64_t *words,
+                   size_t cap_words);
+/* Validates a key blob against the context's parameters and uploads it
+ * (the context keeps its shard, as ks_key_upload). */
+int ks_key_upload_wire(ks_ctx *ctx, const void *blob, size_t n);
+
 /* Relinearisation of ct [3][n_local][N] in place: polys 0, 1 receive the
  * result.  Replaces keyswitching_input_broadcast / keyswitching_output_
  * aggregation (input_broadcast.cu:117-176, output_aggregation.cu:197-294). */

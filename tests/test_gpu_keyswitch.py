@@ -231,3 +231,24 @@ def test_rescale_matches_oracle(name, Ql, cuda_device):
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy().view(np.uint64), o.rescale(ct, Ql))
     ctx.close()
+
+
+def test_key_upload_from_wire_blob(cuda_device):
+    """A Galois key shipped as a wire blob rotates like the uploaded array."""
+    from comp390project_b200 import KsContext, wire
+    o = oracle_for("small")
+    log_n, q, p = split(SMALL)
+    ctx = KsContext(log_n, q, p, device=0)
+    s = o.secret(9, 64)
+    elt = o.galois_elt(5)
+    key = o.keygen_galois(s, elt, 55)
+    ctx.key_upload_wire(wire.pack_key(log_n, q, p, key, galois_elt=elt))
+    rng = np.random.default_rng(56)
+    Ql = o.L
+    ct = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                             for j in range(Ql)]) for _ in range(2)])
+    d = torch.from_numpy(ct.view(np.int64).copy()).cuda()
+    ctx.apply_galois(d, Ql, elt)
+    torch.cuda.synchronize()
+    assert np.array_equal(d.cpu().numpy().view(np.uint64), o.apply_galois(ct, Ql, elt, key))
+    ctx.close()
