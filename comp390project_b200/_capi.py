@@ -83,6 +83,7 @@ SIGNATURES = {
                             C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.POINTER(C.c_int),
                             _u64p, _SZ]),
     "ks_key_upload_wire": (_I, [_P, _P, _SZ]),
+    "ks_key_distribute": (_I, [_P, _I, _U32, _P, _I, _P]),
     "ks_key_upload": (_I, [_P, _I, _U32, _P, _SZ]),
     "ks_key_upload_device": (_I, [_P, _I, _U32, _P, _SZ, _P]),
     "ks_key_generate": (_I, [_P, _I, _U32, _P, _U64, _P]),

@@ -203,6 +203,14 @@ class KsContext:
         key = np.ascontiguousarray(key, dtype=np.uint64)
         self._check(self.lib.ks_key_upload(self.h, kind, int(elt), key.ctypes.data, key.size))
 
+    def key_distribute(self, kind: int, elt: int, full_key=None, root: int = 0, stream=None):
+        """Collective: the root passes the full key as a device tensor
+        [digits][2][L+alpha][N], the others None; every rank ends with its
+        shard (NCCL point-to-point from the root)."""
+        ptr = self._ptr(full_key) if full_key is not None else None
+        self._check(self.lib.ks_key_distribute(self.h, kind, int(elt), ptr, int(root),
+                                               _stream_ptr(stream, self.device)))
+
     def key_upload_wire(self, blob: bytes):
         """Uploads a key blob of comp390project_b200.wire (validated against
         this context's parameters; the context keeps its shard)."""

@@ -723,6 +723,39 @@ size_t full_key_words(const Ctx &c) {
   return c.alpha ? (size_t)((c.L + c.alpha - 1) / c.alpha) * 2 * c.K * c.N : 0;
 }
 
+// Words of rank g's shard of a full key (the layout key_alloc gives rank g).
+size_t shard_words(const Ctx &c, int g) {
+  const int beta = (c.L + c.alpha - 1) / c.alpha;
+  if (c.world == 1) return full_key_words(c);
+  if (c.oa()) return (size_t)n_local(g, c.world, beta) * 2 * c.K * c.N;
+  return (size_t)beta * 2 * n_local(g, c.world, c.K) * c.N;
+}
+
+// Copies rank g's shard of the full key src ([beta][2][K][N]) into dst:
+// input broadcast keeps the key-basis limbs kj % G == g of every digit
+// ([beta][2][limbs][N]); output aggregation the digits d % G == g, all limbs.
+void extract_shard(const Ctx &c, int g, const u64 *src, u64 *dst, cudaMemcpyKind dir,
+                   cudaStream_t s) {
+  const size_t N = c.N;
+  const int beta = (c.L + c.alpha - 1) / c.alpha, G = c.world;
+  if (G == 1) {
+    KS_CUDA(cudaMemcpyAsync(dst, src, full_key_words(c) * 8, dir, s));
+  } else if (c.oa()) {
+    int di = 0;
+    for (int d = g; d < beta; d += G, ++di)
+      KS_CUDA(cudaMemcpyAsync(dst + (size_t)2 * di * c.K * N, src + (size_t)2 * d * c.K * N,
+                              (size_t)2 * c.K * N * 8, dir, s));
+  } else {
+    const int limbs = n_local(g, G, c.K);
+    if (limbs == 0) return;
+    for (int d = 0; d < beta; ++d)
+      for (int p = 0; p < 2; ++p)
+        KS_CUDA(cudaMemcpy2DAsync(dst + ((size_t)(2 * d + p) * limbs) * N, N * 8,
+                                  src + (((size_t)(2 * d + p) * c.K) + g) * N,
+                                  (size_t)G * N * 8, N * 8, limbs, dir, s));
+  }
+}
+
 void key_upload(Ctx &c, int kind, uint32_t elt, const u64 *src, size_t n_words, bool from_dev,
                 cudaStream_t s) {
   KS_REQUIRE(src != nullptr, "key pointer is null");
@@ -730,25 +763,63 @@ void key_upload(Ctx &c, int kind, uint32_t elt, const u64 *src, size_t n_words, 
                                                std::to_string(full_key_words(c)) + " words");
   KS_CUDA(cudaSetDevice(c.device));
   KeyShard &k = key_alloc(c, kind, elt);
-  const size_t N = c.N;
-  const cudaMemcpyKind dir = from_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-  if (c.world == 1) {
-    KS_CUDA(cudaMemcpyAsync(k.d, src, n_words * 8, dir, s));
-  } else if (c.oa()) {
-    // digits d % G == g of the full layout [d][p][K], all limbs
-    for (int di = 0; di < k.beta; ++di)
-      KS_CUDA(cudaMemcpyAsync(k.d + (size_t)2 * di * k.limbs * N,
-                              src + (size_t)2 * c.key_digits[di] * c.K * N,
-                              (size_t)2 * c.K * N * 8, dir, s));
-  } else {
-    // rows of the full layout [d][p][K] -> shard [d][p][own]
-    for (int d = 0; d < k.beta; ++d)
-      for (int p = 0; p < 2; ++p)
-        KS_CUDA(cudaMemcpy2DAsync(k.d + ((size_t)(2 * d + p) * k.limbs) * N, N * 8,
-                                  src + (((size_t)(2 * d + p) * c.K) + c.rank) * N,
-                                  (size_t)c.world * N * 8, N * 8, k.limbs, dir, s));
-  }
+  extract_shard(c, c.rank, src, k.d,
+                from_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
   if (!from_dev) KS_CUDA(cudaStreamSynchronize(s));
+}
+
+void check_alive(const Ctx &c);
+void watch_collective(Ctx &c, cudaStream_t s);
+
+// Key distribution: the root holds the full key in its device memory and
+// sends every rank its shard over NCCL point-to-point (the root packs each
+// shard into a staging buffer first); the others receive straight into their
+// key shard.  Collective over the context's ranks; synchronous on return.
+void key_distribute(Ctx &c, int kind, uint32_t elt, const u64 *full_dev, int root,
+                    cudaStream_t s) {
+  KS_REQUIRE(root >= 0 && root < c.world, "root out of range");
+  KS_CUDA(cudaSetDevice(c.device));
+  if (c.world == 1) {
+    KS_REQUIRE(full_dev != nullptr, "key pointer is null");
+    KeyShard &k = key_alloc(c, kind, elt);
+    extract_shard(c, 0, full_dev, k.d, cudaMemcpyDeviceToDevice, s);
+    KS_CUDA(cudaStreamSynchronize(s));
+    return;
+  }
+  check_alive(c);
+  KeyShard &k = key_alloc(c, kind, elt);
+  std::vector<u64 *> staging;
+  if (c.rank == root) {
+    KS_REQUIRE(full_dev != nullptr, "the root needs the full key on its device");
+    for (int g = 0; g < c.world; ++g) {
+      if (g == root) {
+        extract_shard(c, g, full_dev, k.d, cudaMemcpyDeviceToDevice, s);
+        staging.push_back(nullptr);
+      } else {
+        u64 *b = shard_words(c, g) ? dev_alloc<u64>(shard_words(c, g)) : nullptr;
+        if (b) extract_shard(c, g, full_dev, b, cudaMemcpyDeviceToDevice, s);
+        staging.push_back(b);
+      }
+    }
+  }
+  {
+    std::lock_guard<std::mutex> lk(c.nccl_mu);
+    KS_NCCL(ncclGroupStart());
+    if (c.rank == root) {
+      for (int g = 0; g < c.world; ++g)
+        if (g != root && staging[g])
+          KS_NCCL(ncclSend(staging[g], shard_words(c, g), ncclUint64, g, c.comm, s));
+    } else if (shard_words(c, c.rank)) {
+      KS_NCCL(ncclRecv(k.d, shard_words(c, c.rank), ncclUint64, root, c.comm, s));
+    }
+    KS_NCCL(ncclGroupEnd());
+  }
+  watch_collective(c, s);
+  const cudaError_t e = cudaStreamSynchronize(s);
+  for (u64 *b : staging)
+    if (b) cudaFree(b);
+  KS_CUDA(e);
+  check_alive(c);
 }
 
 void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 seed,
@@ -1400,6 +1471,14 @@ size_t ks_key_words(const ks_ctx *ctx) { return ctx ? full_key_words(ctx->c) : 0
 int ks_key_upload(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *host_key, size_t n) {
   if (!ctx) return KS_ERR_INVALID;
   return guarded(ctx, [&] { key_upload(ctx->c, kind, elt, host_key, n, false, 0); });
+}
+
+int ks_key_distribute(ks_ctx *ctx, int kind, uint32_t elt, const uint64_t *full_dev, int root,
+                      void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  return guarded(ctx, [&] {
+    key_distribute(ctx->c, kind, elt, full_dev, root, (cudaStream_t)stream);
+  });
 }
 
 int ks_key_upload_wire(ks_ctx *ctx, const void *blob, size_t n) {

@@ -107,6 +107,14 @@ int ks_key_upload(ks_ctx *ctx, int kind, uint32_t galois_elt, const uint64_t *ho
 /* Same, from a device array of the same full layout. */
 int ks_key_upload_device(ks_ctx *ctx, int kind, uint32_t galois_elt,
                          const uint64_t *dev_key, size_t n_words, void *stream);
+/* Key distribution (collective over the context's ranks; synchronous): the
+ * root passes the full key in ITS device memory, the other ranks pass null;
+ * every rank ends with its shard, sent from the root over NCCL point-to-point
+ * (the reference's distribute_relin_keys / distribute_galois_keys,
+ * distributed_context.cu:112-134, are stubs).  With one rank it is
+ * ks_key_upload_device. */
+int ks_key_distribute(ks_ctx *ctx, int kind, uint32_t galois_elt, const uint64_t *full_dev,
+                      int root, void *stream);
 /* Generates a synthetic key on the device from an int8 ternary secret [N]
  * (host array) and a seed.  The sampler is a counter hash, NOT a secure RNG. */
 int ks_key_generate(ks_ctx *ctx, int kind, uint32_t galois_elt, const int8_t *secret,

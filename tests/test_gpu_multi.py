@@ -113,6 +113,15 @@ def _worker(rank, world, port, name, mode, q):
             for j in range(Ql2):
                 full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
         ok &= np.array_equal(full2, o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
+        # key distribution: rank 0 holds the full key on its device, every
+        # rank receives its shard over NCCL point-to-point
+        ctx.key_drop(KS_KEY_GALOIS, o.galois_elt(1))
+        full = torch.from_numpy(keys[1].view(np.int64).copy()).cuda() if rank == 0 else None
+        ctx.key_distribute(KS_KEY_GALOIS, o.galois_elt(1), full, root=0)
+        dk = local(cts[0])
+        ctx.rotate(dk, Ql, 1)
+        torch.cuda.synchronize()
+        ok &= np.array_equal(gather(dk, 2), o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
         # rescale: the owner of the last limb broadcasts it (input broadcast)
         mine3 = list(range(rank, Ql - 1, world)) if not oa else list(range(Ql - 1))
         dr = local(cts[1])
