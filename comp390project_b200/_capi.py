@@ -100,6 +100,10 @@ SIGNATURES = {
     "ks_rescale": (_I, [_P, _P, _I, _P, _P]),
     "ks_linear_transform_hoisted": (_I, [_P, _P, _I, C.POINTER(C.c_int), _I, C.POINTER(_P),
                                          _P, _P]),
+    "ks_bsgs_workspace_words": (_SZ, [_P, _I, _I, _I]),
+    "ks_bsgs_matmul": (_I, [_P, C.POINTER(_P), C.POINTER(_P), _I, _I, _I, _I, _I, _I, _I,
+                            C.POINTER(_P), C.POINTER(_P), _I, _P, _P]),
+    "ks_reduce_limbs": (_I, [_P, _P, _I, _I, _P]),
     "ks_ntt_forward": (_I, [_P, _P, _I, _I, _I, _P]),
     "ks_ntt_inverse": (_I, [_P, _P, _I, _I, _I, _P]),
     "ks_scatter_limbs": (_I, [_P, _P, _P, _I, _I, _P]),

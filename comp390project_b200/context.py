@@ -325,6 +325,40 @@ class KsContext:
                                                          st, n, dp, self._ptr(out),
                                                          _stream_ptr(stream, self.device)))
 
+    def bsgs_workspace_words(self, level_limbs: int, n_in: int, n_baby: int) -> int:
+        return int(self.lib.ks_bsgs_workspace_words(self.h, int(level_limbs), int(n_in),
+                                                    int(n_baby)))
+
+    def bsgs_matmul(self, xs, level_limbs: int, unit: int, n_baby: int, n_giant: int, pts, ys,
+                    workspace, g_range=None, baby=None, stream=None):
+        """Block BSGS ciphertext x plaintext product (ks_bsgs_matmul):
+        ys[o] = sum_{g in g_range} rot_{g B unit}(sum_i sum_b pts[((o n_in + i) G + g) B + b]
+        * rot_{b unit}(xs[i])).  xs, ys: [2][n_local][N]; pts: [n_local][N] NTT-form
+        diagonals; baby: optional precomputed rotations, baby[i (B-1) + b - 1] =
+        rot_{b unit}(xs[i]); workspace: bsgs_workspace_words(level, n_in, 1 if baby
+        else n_baby) words."""
+        n_in, n_out = len(xs), len(ys)
+        g_lo, g_hi = g_range if g_range is not None else (0, n_giant)
+        if len(pts) != n_out * n_in * n_giant * n_baby:
+            raise ValueError("pts must hold n_out * n_in * n_giant * n_baby diagonals")
+        xp = (C.c_void_p * n_in)(*[self._ptr(t) for t in xs])
+        yp = (C.c_void_p * n_out)(*[self._ptr(t) for t in ys])
+        pp = (C.c_void_p * len(pts))(*[self._ptr(t) for t in pts])
+        bp = None
+        if baby is not None:
+            if len(baby) != n_in * (n_baby - 1):
+                raise ValueError("baby must hold n_in * (n_baby - 1) ciphertexts")
+            bp = (C.c_void_p * max(len(baby), 1))(*[self._ptr(t) for t in baby])
+        self._check(self.lib.ks_bsgs_matmul(
+            self.h, xp, bp, n_in, int(level_limbs), int(unit), int(n_baby), int(n_giant),
+            int(g_lo), int(g_hi), pp, yp, n_out, self._ptr(workspace),
+            _stream_ptr(stream, self.device)))
+
+    def reduce_limbs(self, x, n_polys: int, level_limbs: int, stream=None):
+        """x [n_polys][n_local][N] in place: every word reduced mod its limb's prime."""
+        self._check(self.lib.ks_reduce_limbs(self.h, self._ptr(x), int(n_polys),
+                                             int(level_limbs), _stream_ptr(stream, self.device)))
+
     def ntt_forward(self, data, n_limbs: int, first_prime: int = 0, batch: int = 1, stream=None):
         self._check(self.lib.ks_ntt_forward(self.h, self._ptr(data), int(n_limbs),
                                             int(first_prime), int(batch),

@@ -879,13 +879,15 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
 // ---------------------------------------------------------------------------
 enum Stage {
   ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_COLS, ST_MODUP_ROWS_IP, ST_INTT_P, ST_MODDOWN_COLS,
-  ST_MODDOWN_ROWS, ST_COMM, ST_MODUP_ROWS, ST_INNER_PROD, ST_COUNT
+  ST_MODDOWN_ROWS, ST_COMM, ST_MODUP_ROWS, ST_INNER_PROD, ST_PLAIN_MAC, ST_ADD, ST_COUNT
 };
 // modup_rows and inner_product are the two halves of modup_rows_ip that the
-// hoisted path runs apart (one row pass, one inner product per rotation).
+// hoisted path runs apart (one row pass, one inner product per rotation);
+// plain_mac and add are the plaintext products and sums of the BSGS matmul.
 static const char *kStageNames[ST_COUNT] = {
     "galois",       "intt_input",   "modup_cols",   "modup_rows_ip", "intt_p",
-    "moddown_cols", "moddown_rows", "collective",   "modup_rows",    "inner_product"};
+    "moddown_cols", "moddown_rows", "collective",   "modup_rows",    "inner_product",
+    "plain_mac",    "add"};
 
 cudaEvent_t pool_event(Ctx &c) {
   if (!c.event_pool.empty()) {
@@ -1178,13 +1180,19 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
   KS_REQUIRE((outs != nullptr) != (out != nullptr), "give either outs or out");
   const Level &lv = level_of(c, Ql);
   const size_t nq = lv.n_q, N = c.N;
+  // a rank that owns no limb of this level passes null buffers
+  const bool have_q = nq > 0, have_out = lv.n_out > 0;
   std::vector<uint32_t> elts(n);
   std::vector<const KeyShard *> keys(n);
   for (int i = 0; i < n; ++i) {
     elts[i] = elt_of_step(c, steps[i]);
     keys[i] = &key_get(c, KS_KEY_GALOIS, elts[i]);
-    if (outs) KS_REQUIRE(outs[i] && aligned16(outs[i]), "output pointer null or misaligned");
-    else KS_REQUIRE(diags && diags[i] && aligned16(diags[i]), "diagonal pointer null or misaligned");
+    if (outs)
+      KS_REQUIRE(aligned16(outs[i]) && (outs[i] != nullptr || !have_q),
+                 "output pointer null or misaligned");
+    else
+      KS_REQUIRE(diags && aligned16(diags[i]) && (diags[i] != nullptr || !have_out),
+                 "diagonal pointer null or misaligned");
   }
   KS_CUDA(cudaSetDevice(c.device));
   if (out) KS_CUDA(cudaMemsetAsync(out, 0, 2 * nq * N * 8, s));
@@ -1299,6 +1307,116 @@ void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStrea
                                (long long)lv.n_q * N, out, out + (size_t)lo.n_q * N, nullptr,
                                true, nullptr, lv.rs_md, T, s));
     c.launches += lo.n_q > 0 ? 1 : 0;
+  }
+}
+
+// Words of the BSGS matmul workspace: the baby-step rotations of every input
+// and kMacMaxOut giant-step partial sums, each [2][n_q][N].
+size_t bsgs_workspace_words(Ctx &c, int Ql, int n_in, int n_baby) {
+  const Level &lv = level_of(c, Ql);
+  return ((size_t)n_in * (n_baby - 1) + kMacMaxOut) * 2 * lv.n_q * c.N;
+}
+
+// Block matrix product by the diagonal method with baby and giant steps
+// (Halevi-Shoup diagonals, BSGS split as in Halevi-Shoup 2018):
+//   y[o] = sum_{g in [g_lo, g_hi)} rot_{g B u}( sum_{i < n_in} sum_{b < B}
+//            pts[((o n_in + i) G + g) B + b] (.) rot_{b u}(x[i]) ),
+// B = n_baby, G = n_giant, u = unit.  The baby-step rotations of each input
+// share one ModUp (do_hoisted); the plaintext products of up to kMacMaxOut
+// giant steps are one k_mac_plain pass over the baby-step ciphertexts; each
+// giant-step partial sum g > 0 is rotated by g B u and added to y[o].  The
+// product runs limb-locally in every mode; the key switches do their own
+// communication.  A giant-step range [g_lo, g_hi) smaller than [0, G) gives a
+// partial product (the callers' partition of the giant steps over GPUs).
+void do_bsgs_matmul(Ctx &c, const u64 *const *x, const u64 *const *baby, int n_in, int Ql,
+                    int unit, int n_baby, int n_giant, int g_lo, int g_hi,
+                    const u64 *const *pts, u64 *const *y, int n_out, u64 *work,
+                    cudaStream_t s) {
+  check_alive(c);
+  KS_REQUIRE(x != nullptr && y != nullptr && pts != nullptr, "null pointer list");
+  KS_REQUIRE(n_in >= 1 && n_out >= 1 && n_baby >= 1 && n_giant >= 1, "empty matmul shape");
+  KS_REQUIRE(0 <= g_lo && g_lo < g_hi && g_hi <= n_giant, "giant-step range out of bounds");
+  KS_REQUIRE(unit != 0, "unit rotation step must be nonzero");
+  const Level &lv = level_of(c, Ql);
+  const int nq = lv.n_q;
+  const size_t N = c.N, ct_words = 2 * (size_t)nq * N;
+  const bool have = nq > 0;
+  for (int i = 0; i < n_in; ++i)
+    KS_REQUIRE(aligned16(x[i]) && (x[i] != nullptr || !have), "input pointer null or misaligned");
+  for (int o = 0; o < n_out; ++o) {
+    KS_REQUIRE(aligned16(y[o]) && (y[o] != nullptr || !have), "output pointer null or misaligned");
+    for (int i = 0; i < n_in; ++i) KS_REQUIRE(!have || y[o] != x[i], "an output aliases an input");
+    KS_REQUIRE(!have || y[o] != work, "an output aliases the workspace");
+    for (int i = 0; i < n_in; ++i)
+      for (int g = g_lo; g < g_hi; ++g)
+        for (int b = 0; b < n_baby; ++b) {
+          const u64 *pt = pts[(((size_t)o * n_in + i) * n_giant + g) * n_baby + b];
+          KS_REQUIRE(aligned16(pt) && (pt != nullptr || !have),
+                     "plaintext pointer null or misaligned");
+        }
+  }
+  KS_REQUIRE(aligned16(work) && (work != nullptr || !have), "workspace null or misaligned");
+  if (baby)
+    for (size_t r = 0; r < (size_t)n_in * (n_baby - 1); ++r)
+      KS_REQUIRE(aligned16(baby[r]) && (baby[r] != nullptr || !have),
+                 "baby-step pointer null or misaligned");
+  // every key first, so that a missing one fails before any launch
+  std::vector<int> steps(n_baby > 1 && !baby ? n_baby - 1 : 0);
+  for (size_t b = 0; b < steps.size(); ++b) steps[b] = (int)(b + 1) * unit;
+  for (int st : steps) (void)key_get(c, KS_KEY_GALOIS, elt_of_step(c, st));
+  for (int g = std::max(g_lo, 1); g < g_hi; ++g)
+    (void)key_get(c, KS_KEY_GALOIS, elt_of_step(c, g * n_baby * unit));
+  KS_CUDA(cudaSetDevice(c.device));
+  // rot(i, b) = rot_{b u}(x[i]): the caller's (baby != null) or computed into
+  // the workspace, b = 1 .. B-1; the partial sums follow the rotations
+  u64 *const own = work;
+  auto rot = [&](int i, int b) -> const u64 * {
+    if (b == 0) return x[i];
+    const size_t r = (size_t)i * (n_baby - 1) + (b - 1);
+    return baby ? baby[r] : own + r * ct_words;
+  };
+  u64 *part = work + (baby ? 0 : (size_t)n_in * (n_baby - 1) * ct_words);
+  std::vector<u64 *> outs(steps.size());
+  for (int i = 0; i < n_in && !steps.empty(); ++i) {
+    for (int b = 1; b < n_baby; ++b) outs[b - 1] = const_cast<u64 *>(rot(i, b));
+    do_hoisted(c, x[i], Ql, steps.data(), (int)steps.size(), outs.data(), nullptr, nullptr, s);
+  }
+  const int n_terms = n_in * n_baby;
+  KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
+  Ctx::Lane &L = c.lanes[0];
+  for (int o = 0; o < n_out; ++o) {
+    // g == 0 (if in range) is written straight into y[o] by the first pass;
+    // otherwise y[o] starts from zero
+    if (g_lo > 0 && have) KS_CUDA(cudaMemsetAsync(y[o], 0, ct_words * 8, s));
+    for (int g0 = g_lo; g0 < g_hi; g0 += kMacMaxOut) {
+      const int ng = std::min(kMacMaxOut, g_hi - g0);
+      MacTerms a{};
+      a.n_out = ng;
+      for (int j = 0; j < ng; ++j) a.out[j] = g0 + j == 0 ? y[o] : part + (size_t)j * ct_words;
+      {
+        StageTimer tm(c, ST_PLAIN_MAC, s);
+        for (int m0 = 0; m0 < n_terms; m0 += kMacMaxTerms) {
+          a.n_terms = std::min(kMacMaxTerms, n_terms - m0);
+          a.accumulate = m0 > 0;
+          for (int m = 0; m < a.n_terms; ++m) {
+            const int i = (m0 + m) / n_baby, b = (m0 + m) % n_baby;
+            a.ct[m] = rot(i, b);
+            for (int j = 0; j < ng; ++j)
+              a.pt[j][m] = pts[(((size_t)o * n_in + i) * n_giant + g0 + j) * n_baby + b];
+          }
+          KS_CUDA(mac_plain(a, nq, lv.q_index.d, c.d_primes, c.log_n, s));
+          c.launches += have ? 1 : 0;
+        }
+      }
+      for (int j = 0; j < ng; ++j) {
+        const int g = g0 + j;
+        if (g == 0) continue;
+        do_apply_galois(c, L, a.out[j], Ql, elt_of_step(c, g * n_baby * unit), s);
+        StageTimer tm(c, ST_ADD, s);
+        KS_CUDA(add_ct(y[o], a.out[j], 2, nq, lv.q_index.d, c.d_primes, c.log_n, s));
+        c.launches += have ? 1 : 0;
+      }
+    }
   }
 }
 
@@ -1730,6 +1848,43 @@ int ks_linear_transform_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs
     KS_REQUIRE(out != ct, "out must not alias ct");
     KS_REQUIRE(!ctx->c.lanes.empty(), "context has no special primes (NTT-only context)");
     do_hoisted(ctx->c, ct, level_limbs, steps, n, nullptr, diags, out, (cudaStream_t)stream);
+  });
+}
+
+size_t ks_bsgs_workspace_words(ks_ctx *ctx, int level_limbs, int n_in, int n_baby) {
+  if (!ctx || n_in < 1 || n_baby < 1 || ctx->c.alpha == 0 || level_limbs < 1 ||
+      level_limbs > ctx->c.L)
+    return 0;
+  return bsgs_workspace_words(ctx->c, level_limbs, n_in, n_baby);
+}
+
+int ks_bsgs_matmul(ks_ctx *ctx, const uint64_t *const *x, const uint64_t *const *baby,
+                   int n_in, int level_limbs, int unit, int n_baby, int n_giant, int g_lo,
+                   int g_hi, const uint64_t *const *pts, uint64_t *const *y, int n_out,
+                   uint64_t *workspace, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    KS_REQUIRE(!ctx->c.lanes.empty(), "context has no special primes (NTT-only context)");
+    do_bsgs_matmul(ctx->c, x, baby, n_in, level_limbs, unit, n_baby, n_giant, g_lo, g_hi, pts,
+                   y, n_out, workspace, (cudaStream_t)stream);
+  });
+}
+
+int ks_reduce_limbs(ks_ctx *ctx, uint64_t *x, int n_polys, int level_limbs, void *stream) {
+  if (!ctx) return KS_ERR_INVALID;
+  ctx->c.launches = 0;
+  return guarded(ctx, [&] {
+    Ctx &c = ctx->c;
+    const Level &lv = level_of(c, level_limbs);
+    KS_REQUIRE(n_polys >= 1, "n_polys must be positive");
+    KS_REQUIRE(aligned16(x) && (x != nullptr || lv.n_q == 0), "pointer null or misaligned");
+    KS_CUDA(cudaSetDevice(c.device));
+    for (int p = 0; p < n_polys && lv.n_q > 0; ++p) {
+      KS_CUDA(mod_reduce(x + (size_t)p * lv.n_q * c.N, lv.n_q, lv.q_index.d, c.d_primes,
+                         c.log_n, (cudaStream_t)stream));
+      c.launches += 1;
+    }
   });
 }
 

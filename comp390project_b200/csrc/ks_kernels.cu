@@ -158,6 +158,81 @@ __global__ void k_mod_reduce(u64 *x, const int *prime_of_slot, const PrimeDev *p
   v = reduce_full(v, P.q, P.mu);
 }
 
+// One thread: two adjacent coefficients of one limb slot l, both polys, every
+// output j < NG (the outputs share the ciphertext terms, which are read once):
+//   out_j[p][l] (+)= sum_m pt_j,m[l] * ct_m[p][l]  mod q   (p = 0, 1).
+// 128-bit accumulation, Barrett-reduced every 8 terms: 8 products of words
+// below 2^62 plus one residue stay below 2^128.
+template <int NG>
+__global__ void __launch_bounds__(kBlk, NG >= 3 ? 2 : 3) k_mac_plain(const MacTerms a, int n_limbs,
+                                                   const int *__restrict__ prime_of_slot,
+                                                   const PrimeDev *primes, int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const PrimeDev &P = primes[prime_of_slot[l]];
+  const u64 q = P.q, rh = P.br_hi, rl = P.br_lo;
+  const long long lo = (long long)l * N + k, stride = (long long)n_limbs * N;
+  u128v acc[NG][4];  // [output][poly 0 even, poly 0 odd, poly 1 even, poly 1 odd]
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    if (a.accumulate) {
+      const ulonglong2 y0 = *reinterpret_cast<const ulonglong2 *>(a.out[j] + lo);
+      const ulonglong2 y1 = *reinterpret_cast<const ulonglong2 *>(a.out[j] + stride + lo);
+      acc[j][0] = {y0.x, 0};
+      acc[j][1] = {y0.y, 0};
+      acc[j][2] = {y1.x, 0};
+      acc[j][3] = {y1.y, 0};
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[j][i] = {0, 0};
+    }
+  }
+  for (int m = 0; m < a.n_terms; ++m) {
+    const ulonglong2 x0 = *reinterpret_cast<const ulonglong2 *>(a.ct[m] + lo);
+    const ulonglong2 x1 = *reinterpret_cast<const ulonglong2 *>(a.ct[m] + stride + lo);
+#pragma unroll
+    for (int j = 0; j < NG; ++j) {
+      const ulonglong2 w = *reinterpret_cast<const ulonglong2 *>(a.pt[j][m] + lo);
+      mac(acc[j][0], x0.x, w.x);
+      mac(acc[j][1], x0.y, w.y);
+      mac(acc[j][2], x1.x, w.x);
+      mac(acc[j][3], x1.y, w.y);
+    }
+    if ((m & 7) == 7) {
+#pragma unroll
+      for (int j = 0; j < NG; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = {barrett128(acc[j][i], q, rh, rl), 0};
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    *reinterpret_cast<ulonglong2 *>(a.out[j] + lo) =
+        make_ulonglong2(barrett128(acc[j][0], q, rh, rl), barrett128(acc[j][1], q, rh, rl));
+    *reinterpret_cast<ulonglong2 *>(a.out[j] + stride + lo) =
+        make_ulonglong2(barrett128(acc[j][2], q, rh, rl), barrett128(acc[j][3], q, rh, rl));
+  }
+}
+
+// out[p][l] = out[p][l] + x[p][l] mod q for n_polys polys of n_limbs slots.
+__global__ void k_add_ct(u64 *__restrict__ out, const u64 *__restrict__ x, int n_limbs,
+                         const int *__restrict__ prime_of_slot, const PrimeDev *primes,
+                         int log_n) {
+  const int N = 1 << log_n;
+  const int l = blockIdx.y % n_limbs;
+  const long long off = (long long)blockIdx.y * N;
+  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
+  if (k >= N) return;
+  const u64 q = primes[prime_of_slot[l]].q;
+  ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(out + off + k);
+  const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(x + off + k);
+  a.x = add_mod(a.x, b.x, q);
+  a.y = add_mod(a.y, b.y, q);
+  *reinterpret_cast<ulonglong2 *>(out + off + k) = a;
+}
+
 __global__ void k_scatter(const u64 *__restrict__ gbuf, u64 *__restrict__ lbuf, int total,
                           int n_local, int log_n, int g, int G, int to_local) {
   const int N = 1 << log_n;
@@ -280,6 +355,29 @@ cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const Prim
                        int log_n, cudaStream_t s) {
   if (n_limbs <= 0) return cudaSuccess;
   k_mod_reduce<<<grid2(log_n, n_limbs, 1), kBlk, 0, s>>>(x, prime_of_slot, primes, log_n);
+  return cudaGetLastError();
+}
+
+cudaError_t mac_plain(const MacTerms &a, int n_limbs, const int *prime_of_slot,
+                      const PrimeDev *primes, int log_n, cudaStream_t s) {
+  if (n_limbs <= 0) return cudaSuccess;
+  if (a.n_terms < 1 || a.n_terms > kMacMaxTerms || a.n_out < 1 || a.n_out > kMacMaxOut)
+    return cudaErrorInvalidValue;
+  const dim3 g = grid2(log_n, n_limbs, 2);
+  switch (a.n_out) {
+    case 1: k_mac_plain<1><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
+    case 2: k_mac_plain<2><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
+    case 3: k_mac_plain<3><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
+    default: k_mac_plain<4><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t add_ct(u64 *out, const u64 *x, int n_polys, int n_limbs, const int *prime_of_slot,
+                   const PrimeDev *primes, int log_n, cudaStream_t s) {
+  if (n_limbs <= 0 || n_polys <= 0) return cudaSuccess;
+  k_add_ct<<<grid2(log_n, n_polys * n_limbs, 2), kBlk, 0, s>>>(out, x, n_limbs, prime_of_slot,
+                                                               primes, log_n);
   return cudaGetLastError();
 }
 

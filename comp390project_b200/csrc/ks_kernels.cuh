@@ -66,6 +66,26 @@ cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, in
                               bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
                               const PrimeDev *primes, int log_n, uint32_t elt, cudaStream_t s);
 
+// Plaintext multiply-accumulate over a term list, for up to kMacMaxOut outputs
+// that share the ciphertext terms (passed by value as kernel parameters):
+//   out_j[p][l] (+)= sum_m pt[j][m][l] * ct[m][p][l]  mod q_{prime_of_slot[l]},  p = 0, 1,
+// ct[m] and out_j: [2][n_limbs][N], pt[j][m]: [n_limbs][N], all NTT form with
+// canonical residues; accumulate != 0 adds to out_j's contents.  Every
+// pointer 16-byte aligned.
+constexpr int kMacMaxTerms = 64;
+constexpr int kMacMaxOut = 4;
+struct MacTerms {
+  const u64 *ct[kMacMaxTerms];
+  const u64 *pt[kMacMaxOut][kMacMaxTerms];
+  u64 *out[kMacMaxOut];
+  int n_terms, n_out, accumulate;
+};
+cudaError_t mac_plain(const MacTerms &a, int n_limbs, const int *prime_of_slot,
+                      const PrimeDev *primes, int log_n, cudaStream_t s);
+// out += x  mod q, [n_polys][n_limbs][N].
+cudaError_t add_ct(u64 *out, const u64 *x, int n_polys, int n_limbs, const int *prime_of_slot,
+                   const PrimeDev *primes, int log_n, cudaStream_t s);
+
 // x %= q for each limb (after an integer all-reduce / reduce-scatter of partial sums).
 cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,
                        int log_n, cudaStream_t s);

@@ -216,6 +216,32 @@ int ks_linear_transform_hoisted(ks_ctx *ctx, const uint64_t *ct, int level_limbs
                                 const int *steps, int n, const uint64_t *const *diags,
                                 uint64_t *out, void *stream);
 
+/* Ciphertext x plaintext block matrix product by the diagonal method with
+ * baby and giant steps (B = n_baby, G = n_giant, u = unit):
+ *   y[o] = sum_{g_lo <= g < g_hi} rotate( sum_{i < n_in} sum_{b < B}
+ *            pts[((o n_in + i) G + g) B + b] (.) rotate(x[i], b u),  g B u )
+ * x[i], y[o]: [2][n_local][N] at level_limbs; pts[...]: NTT-form plaintexts
+ * [n_local][N] over the Q limbs (the diagonals, already rotated by -g B u).
+ * baby == NULL: the B - 1 baby-step rotations of each input are computed
+ * here, sharing one ModUp per input; otherwise baby[i (B-1) + b - 1] holds
+ * rotate(x[i], b u) (e.g. computed by several GPUs and all-gathered).  Up to
+ * four giant steps share one pass over the baby-step ciphertexts.  No
+ * rescale.  Galois keys are needed for steps b u (0 < b < B, baby == NULL)
+ * and g B u (g > 0 in range).  [g_lo, g_hi) = [0, G) gives the whole
+ * product; a sub-range gives the partial sum over those giant steps (callers
+ * that split the giant steps over GPUs add the partial sums and call
+ * ks_reduce_limbs).  workspace holds ks_bsgs_workspace_words(ctx,
+ * level_limbs, n_in, baby ? 1 : n_baby) words; y[o] must alias neither an
+ * input nor the workspace. */
+size_t ks_bsgs_workspace_words(ks_ctx *ctx, int level_limbs, int n_in, int n_baby);
+int ks_bsgs_matmul(ks_ctx *ctx, const uint64_t *const *x, const uint64_t *const *baby,
+                   int n_in, int level_limbs, int unit, int n_baby, int n_giant, int g_lo,
+                   int g_hi, const uint64_t *const *pts, uint64_t *const *y, int n_out,
+                   uint64_t *workspace, void *stream);
+/* x [n_polys][n_local][N] in place: every word (any 64-bit value, e.g. a sum
+ * of residues from an integer all-reduce) reduced mod its limb's prime. */
+int ks_reduce_limbs(ks_ctx *ctx, uint64_t *x, int n_polys, int level_limbs, void *stream);
+
 /* Batched negacyclic NTT in place over data [batch][n_limbs][N]; limb i uses
  * prime first_prime + i of the context's basis (Q primes then P primes).
  * Replaces nwt_2d_radix8_forward_inplace / backward_inplace. */

@@ -597,6 +597,58 @@ void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, 
   for (int p = 0; p < 2; ++p) ork_moddown(c, acc.data() + (size_t)p * QlP * N, Ql, out + (size_t)p * QN);
 }
 
+// Ciphertext x plaintext block matrix product by the diagonal method with baby
+// and giant steps (Halevi-Shoup).  The reference has no counterpart: NEXUS's
+// matmul is absent, and the reference describes it as multiply_plain +
+// add_many + rescale per output column (src/benchmarks/bert_matmul_pipeline.cu:7-15).
+//   y[o] = sum_{g in [g_lo, g_hi)} rot_g( sum_{i < n_in} sum_{b < B}
+//            pts[((o n_in + i) G + g) B + b] * rot_b(x[i]) )
+// rot_b (0 < b < B): baby_elts[b - 1] by ork_rotate_hoisted (one ModUp per
+// input); rot_g (g > 0): giant_elts[g] by ork_apply_galois; plaintext products
+// and sums limb by limb mod q_j.
+void ork_bsgs_matmul(const ork_ctx *c, const uint64_t *const *x, int n_in, int Ql, int B,
+                     int G, int g_lo, int g_hi, const uint32_t *baby_elts,
+                     const uint64_t *const *baby_keys, const uint32_t *giant_elts,
+                     const uint64_t *const *giant_keys, const uint64_t *const *pts, int n_out,
+                     uint64_t *const *y) {
+  const size_t N = c->N, QN = (size_t)Ql * N, CT = 2 * QN;
+  std::vector<u64> rots((size_t)n_in * B * CT);
+  for (int i = 0; i < n_in; ++i) {
+    std::memcpy(rots.data() + (size_t)i * B * CT, x[i], CT * 8);
+    if (B > 1)
+      ork_rotate_hoisted(c, x[i], Ql, B - 1, baby_elts, baby_keys,
+                         rots.data() + ((size_t)i * B + 1) * CT);
+  }
+  std::vector<u64> inner(CT), rotated(CT);
+  for (int o = 0; o < n_out; ++o) {
+    std::memset(y[o], 0, CT * 8);
+    for (int g = g_lo; g < g_hi; ++g) {
+      std::fill(inner.begin(), inner.end(), 0);
+      for (int i = 0; i < n_in; ++i)
+        for (int b = 0; b < B; ++b) {
+          const u64 *pt = pts[(((size_t)o * n_in + i) * G + g) * B + b];
+          const u64 *r = rots.data() + ((size_t)i * B + b) * CT;
+#pragma omp parallel for schedule(static)
+          for (int j = 0; j < Ql; ++j) {
+            const u64 q = c->m[j];
+            for (int p = 0; p < 2; ++p)
+              for (size_t k = 0; k < N; ++k) {
+                u64 &a = inner[(size_t)p * QN + (size_t)j * N + k];
+                a = addmod(a, mulmod(pt[(size_t)j * N + k], r[(size_t)p * QN + (size_t)j * N + k], q), q);
+              }
+          }
+        }
+      const u64 *add = inner.data();
+      if (g > 0) {
+        ork_apply_galois(c, inner.data(), Ql, giant_elts[g], giant_keys[g], rotated.data());
+        add = rotated.data();
+      }
+      add_inplace(c, y[o], add, Ql);
+      add_inplace(c, y[o] + QN, add + QN, Ql);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Deterministic sampling (synthetic keys and ciphertexts; NOT a secure RNG)
 // ---------------------------------------------------------------------------

@@ -101,6 +101,14 @@ void ork_rescale(const ork_ctx *c, const uint64_t *ct, int Ql, uint64_t *out);
 void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, int n,
                                   const uint32_t *elts, const uint64_t *const *keys,
                                   const uint64_t *const *diags, uint64_t *out);
+/* Block BSGS matrix product: y[o] [2][Ql][N] =
+ *   sum_{g_lo <= g < g_hi} rot_g( sum_i sum_{b < B} pts[((o n_in + i) G + g) B + b] * rot_b(x[i]) ),
+ * rot_b by baby_elts[b - 1] (hoisted), rot_g by giant_elts[g] (g > 0). */
+void ork_bsgs_matmul(const ork_ctx *c, const uint64_t *const *x, int n_in, int Ql, int B,
+                     int G, int g_lo, int g_hi, const uint32_t *baby_elts,
+                     const uint64_t *const *baby_keys, const uint32_t *giant_elts,
+                     const uint64_t *const *giant_keys, const uint64_t *const *pts, int n_out,
+                     uint64_t *const *y);
 
 /* Deterministic sampling shared with the product's synthetic-key generator. */
 uint64_t ork_prng(uint64_t seed, uint64_t domain, uint64_t idx);

@@ -62,6 +62,10 @@ def lib():
             "ork_linear_transform_hoisted": (V, [P, u64p, I, I, C.POINTER(C.c_uint32),
                                                  C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
                                                  u64p]),
+            "ork_bsgs_matmul": (V, [P, C.POINTER(C.c_void_p), I, I, I, I, I, I,
+                                    C.POINTER(C.c_uint32), C.POINTER(C.c_void_p),
+                                    C.POINTER(C.c_uint32), C.POINTER(C.c_void_p),
+                                    C.POINTER(C.c_void_p), I, C.POINTER(C.c_void_p)]),
             "ork_encode_basis": (V, [P, f64p, f64p, I, D, i32p, I, u64p]),
             "ork_rescale": (V, [P, u64p, I, u64p]),
             "ork_prng": (U64, [U64, U64, U64]),
@@ -228,6 +232,38 @@ class Oracle:
         lib().ork_linear_transform_hoisted(self.h, np.ascontiguousarray(ct).reshape(-1), Ql, n,
                                            e, kp, dp, out.reshape(-1))
         return out
+
+    def bsgs_matmul(self, xs, Ql: int, unit: int, B: int, G: int, pts, keys,
+                    g_range=None, n_out: int | None = None) -> np.ndarray:
+        """Block BSGS matrix product (ork_bsgs_matmul): xs [n_in] ciphertexts
+        [2][Ql][N]; pts[((o n_in + i) G + g) B + b] [Ql][N] NTT-form diagonals;
+        keys: {step: galois key} for steps b*unit (0 < b < B) and g*B*unit
+        (g > 0).  Returns y [n_out][2][Ql][N]."""
+        n_in = len(xs)
+        g_lo, g_hi = g_range if g_range is not None else (0, G)
+        if n_out is None:
+            n_out = len(pts) // (n_in * G * B)
+        assert len(pts) == n_out * n_in * G * B
+        xa = [np.ascontiguousarray(x, dtype=np.uint64) for x in xs]
+        pa = [np.ascontiguousarray(p, dtype=np.uint64) for p in pts]
+        for x in xa:
+            assert x.shape == (2, Ql, self.N)
+        for p in pa:
+            assert p.shape == (Ql, self.N)
+        be = (C.c_uint32 * max(B - 1, 1))(*[self.galois_elt(b * unit) for b in range(1, B)])
+        bk = [np.ascontiguousarray(keys[b * unit]) for b in range(1, B)]
+        bkp = (C.c_void_p * max(B - 1, 1))(*[k.ctypes.data for k in bk])
+        ge = (C.c_uint32 * G)(*[self.galois_elt(g * B * unit) if g else 0 for g in range(G)])
+        gk = [np.ascontiguousarray(keys[g * B * unit]) if g_lo <= g < g_hi and g else None
+              for g in range(G)]
+        gkp = (C.c_void_p * G)(*[k.ctypes.data if k is not None else None for k in gk])
+        y = np.zeros((n_out, 2, Ql, self.N), dtype=np.uint64)
+        xp = (C.c_void_p * n_in)(*[x.ctypes.data for x in xa])
+        pp = (C.c_void_p * len(pa))(*[p.ctypes.data for p in pa])
+        yp = (C.c_void_p * n_out)(*[y[o].ctypes.data for o in range(n_out)])
+        lib().ork_bsgs_matmul(self.h, xp, n_in, Ql, B, G, g_lo, g_hi, be, bkp, ge, gkp, pp,
+                              n_out, yp)
+        return y
 
     def rescale(self, ct: np.ndarray, Ql: int) -> np.ndarray:
         """[2][Ql][N] -> [2][Ql-1][N]: divide by q_{Ql-1} and round."""
