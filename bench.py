@@ -58,9 +58,10 @@ def parse():
     ap.add_argument("--lanes", type=int, default=4,
                     help="execution lanes (streams + scratch) for the batched key switches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["ks", "ntt", "hoisted"], default="ks",
+    ap.add_argument("--workload", choices=["ks", "ntt", "hoisted", "matmul"], default="ks",
                     help="ks: config-3 rotations (default); ntt: config-2 batched NTT; "
-                         "hoisted: config-4 hoisted linear transform")
+                         "hoisted: config-4 hoisted linear transform; matmul: config-5 "
+                         "BSGS matmul layer")
     ap.add_argument("--ntt-polys", type=int, default=128)
     return ap.parse_args()
 
@@ -386,6 +387,211 @@ def run_hoisted(args, rank, world):
     ctx.close()
 
 
+# ---------------------------------------------------------------------------
+# Config 5: BERT-base-shaped BSGS ciphertext x plaintext matmul
+# ---------------------------------------------------------------------------
+MM_TOKENS, MM_D = 128, 768
+
+
+def mac_alg_bytes(lay, g_lo, g_hi, n_limbs, N):
+    """Algorithmic DRAM bytes of the plaintext-product passes of one layer
+    (k_mac_plain): per pass over <= 4 giant steps, every baby-step
+    ciphertext (2 polys) and each giant step's diagonals are read once, and
+    each giant step's partial sum (2 polys) is written; a pass over more than
+    64 terms also re-reads its outputs."""
+    terms = lay.n_in * lay.n_baby
+    total = 0
+    for _o in range(lay.n_out):
+        for g0 in range(g_lo, g_hi, 4):
+            ng = min(4, g_hi - g0)
+            for m0 in range(0, terms, 64):
+                nt = min(64, terms - m0)
+                total += (2 * nt + ng * nt + 2 * ng + (2 * ng if m0 else 0)) * n_limbs * N * 8
+    return total
+
+
+def run_matmul(args, rank, world):
+    """One BERT-base matmul layer per step: Y = X W, X 128 x 768 encrypted
+    (3 ciphertexts, 256 features x 128 tokens each, column-major packing),
+    W 768 x 768 as 2304 NTT-form diagonals (uniform residues: the cost of
+    encoded diagonals), BSGS with B = G = 16 (45 hoisted baby-step and 45
+    giant-step key switches).  Ring and primes of config 3 at Ql = 35.  With
+    N > 1 ranks the giant steps and baby steps are split over the ranks
+    (comp390project_b200.matmul.matmul_giant_parallel): strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from comp390project_b200 import KS_KEY_GALOIS, KsContext, gen_primes, matmul, secret_generate
+
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(dev)
+    pr = gen_primes(LOG_N, QBITS + PBITS)
+    q, p = pr[:len(QBITS)], pr[len(QBITS):]
+    Ql = len(QBITS)
+    N = 1 << LOG_N
+    lay = matmul.layout(N // 2, MM_TOKENS, MM_D, MM_D)
+    ctx = KsContext(LOG_N, q, p, device=dev, max_batch=args.lanes)
+    s = secret_generate(LOG_N, 0, 192)
+    g_lo, g_hi = matmul.giant_ranges(lay.n_giant, world)[rank]
+    mine = matmul.baby_assignment(lay, world, rank)
+    need = sorted({b * lay.unit for _, b in mine} |
+                  {g * lay.n_baby * lay.unit for g in range(max(g_lo, 1), g_hi)})
+    for st in need:
+        ctx.key_generate(KS_KEY_GALOIS, ctx.galois_elt(st), s, 4000 + st)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4 + rank)
+    xs = torch.empty((lay.n_in, 2, Ql, N), dtype=torch.int64, device="cuda")
+    # only this rank's giant steps' diagonals are resident; the others point
+    # at one unread placeholder
+    used = [((o * lay.n_in + i) * lay.n_giant + g) * lay.n_baby + b
+            for o in range(lay.n_out) for i in range(lay.n_in)
+            for g in range(g_lo, g_hi) for b in range(lay.n_baby)]
+    diag = torch.empty((max(len(used), 1), Ql, N), dtype=torch.int64, device="cuda")
+    for j in range(Ql):
+        xs[:, :, j] = torch.randint(0, int(q[j]), (lay.n_in, 2, N), generator=gen, device="cuda",
+                                    dtype=torch.int64)
+        diag[:, j] = torch.randint(0, int(q[j]), (diag.shape[0], N), generator=gen,
+                                   device="cuda", dtype=torch.int64)
+    pts = [diag[0]] * lay.n_diagonals
+    for k, idx in enumerate(used):
+        pts[idx] = diag[k]
+    ys = torch.empty((lay.n_out, 2, Ql, N), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+    if world == 1:
+        work = torch.empty(ctx.bsgs_workspace_words(Ql, lay.n_in, lay.n_baby), dtype=torch.int64,
+                           device="cuda")
+        xl, yl = [xs[i] for i in range(lay.n_in)], [ys[o] for o in range(lay.n_out)]
+
+        def step():
+            ctx.bsgs_matmul(xl, Ql, lay.unit, lay.n_baby, lay.n_giant, pts, yl, work)
+    else:
+        def step():
+            matmul.matmul_giant_parallel(ctx, [xs[i] for i in range(lay.n_in)], Ql, lay, pts, ys)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = ctx.total_launch_count()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    launches = ctx.total_launch_count() - l0
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    n_ks = lay.n_in * (lay.n_baby - 1) + lay.n_out * (lay.n_giant - 1)
+    value = n_ks * args.steps / (ms / 1000.0)
+    # serial per-stage times of one layer (this rank)
+    ctx.profile_enable(True)
+    step()
+    torch.cuda.synchronize()
+    ctx.profile_enable(False)
+    prof = ctx.profile_read()
+    # end to end: the activations up, the product down, every step
+    host_in = torch.empty(xs.shape, dtype=torch.int64).pin_memory()
+    host_in.copy_(xs)
+    host_out = torch.empty(ys.shape, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(max(1, args.e2e_steps)):
+        xs.copy_(host_in, non_blocking=True)
+        step()
+        host_out.copy_(ys, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = {"value": n_ks * max(1, args.e2e_steps) / (ems / 1000.0), "unit": "key-switches/s",
+           "layer_ms": ems / max(1, args.e2e_steps),
+           "h2d_bytes_per_step": host_in.numel() * 8, "d2h_bytes_per_step": host_out.numel() * 8}
+    peak, peak_kind = measured_peaks()
+    mac_ms, n_mac = prof.get("plain_mac", (0.0, 0))
+    alg = mac_alg_bytes(lay, g_lo, g_hi, Ql, N)
+    ach = alg / (mac_ms / 1000.0) / 1e9 if mac_ms > 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = matmul_cpu_baseline(q, p, lay, n_ks)
+    if rank == 0:
+        line = {
+            "metric": "key-switches/s (config 5: BERT-base 128x768x768 BSGS matmul layer)",
+            "value": value, "unit": "key-switches/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+            "config": {"workload": "config5-matmul: X 128x768 (3 ciphertexts) x W 768x768 "
+                                   "(2304 diagonals), BSGS B=G=16, %d key switches" % n_ks,
+                       "N": N, "Ql": Ql, "alpha": len(p),
+                       "parallelism": "giant-step split x%d (all-gather of baby steps, "
+                                      "all-reduce of partial products)" % world,
+                       "l2": "diagonals (%.1f GB on this rank) stream from HBM every step; "
+                             "no flush" % (diag.numel() * 8 / 1e9)},
+            "roofline": {"bound": "hbm", "kernel": "k_mac_plain (plaintext products)",
+                         "achieved": ach, "peak": peak, "unit": "GB/s",
+                         "frac": (ach / peak) if ach else None, "traffic": None,
+                         "alg_bytes_per_layer": alg, "launches_per_layer": n_mac,
+                         "peak_kind": peak_kind},
+            "stages_ms_serial": {k: v[0] for k, v in prof.items()},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
+def matmul_cpu_baseline(q, p, lay, n_ks):
+    """Bounded sample of the config-5 layer on the host cores (oracle/ C++
+    port, OpenMP over limbs): 3 hoisted baby-step rotations of one input, one
+    giant-step rotation and one plaintext-product term, scaled to a layer
+    (n_in (B-1) / 3 hoisted groups, n_out (G-1) giant steps, n_diagonals
+    terms)."""
+    from oracle.oracle import Oracle, set_threads
+    threads = os.cpu_count() or 1
+    set_threads(threads)
+    o = Oracle(LOG_N, q, p)
+    Ql = len(q)
+    N = 1 << LOG_N
+    so = o.secret(0, 192)
+    rng = np.random.default_rng(5)
+    x = np.stack([np.stack([rng.integers(0, int(q[j]), size=N, dtype=np.uint64)
+                            for j in range(Ql)]) for _ in range(2)])
+    pt = np.stack([rng.integers(0, int(q[j]), size=N, dtype=np.uint64) for j in range(Ql)])
+    bs = lay.baby_steps()[:3]
+    keys = {st: o.keygen_galois(so, o.galois_elt(st), 4000 + st) for st in bs}
+    gs = lay.giant_steps()[0]
+    keys[gs] = o.keygen_galois(so, o.galois_elt(gs), 4000 + gs)
+    t0 = time.perf_counter()
+    o.rotate_hoisted(x, Ql, [o.galois_elt(st) for st in bs], [keys[st] for st in bs])
+    t_h = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    o.apply_galois(x, Ql, o.galois_elt(gs), keys[gs])
+    t_g = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    o.bsgs_matmul([x], Ql, lay.unit, 1, 1, [pt], {})
+    t_m = time.perf_counter() - t0
+    layer = (lay.n_in * (lay.n_baby - 1) / 3) * t_h + lay.n_out * (lay.n_giant - 1) * t_g + \
+        lay.n_diagonals * t_m
+    return {"value": n_ks / layer, "unit": "key-switches/s", "cores": threads, "kind": "port",
+            "layer_s": layer,
+            "sample": "3 hoisted rotations (%.2f s), 1 rotation (%.2f s) and 1 plaintext-product "
+                      "term (%.3f s) of the layer on the host, scaled to %d hoisted groups, %d "
+                      "giant steps and %d terms; oracle/ C++ port with OpenMP over limbs"
+                      % (t_h, t_g, t_m, lay.n_in * (lay.n_baby - 1) // 3,
+                         lay.n_out * (lay.n_giant - 1), lay.n_diagonals)}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the oracle port of the reference path on the host cores."""
     if rank != 0:
@@ -640,6 +846,8 @@ def main():
         run_ntt(args, rank, world)
     elif args.workload == "hoisted":
         run_hoisted(args, rank, world)
+    elif args.workload == "matmul":
+        run_matmul(args, rank, world)
     else:
         run_ours(args, rank, world)
     if world > 1:

@@ -110,6 +110,7 @@ SIGNATURES = {
     "ks_gather_limbs": (_I, [_P, _P, _P, _I, _I, _P]),
     "ks_allgather_limbs": (_I, [_P, _P, _P, _I, _P]),
     "ks_last_launch_count": (_I, [_P]),
+    "ks_total_launch_count": (C.c_longlong, [_P]),
     "ks_graph_capture_begin": (_I, [_P, _P]),
     "ks_graph_capture_end": (_I, [_P, _P, C.POINTER(_P)]),
     "ks_graph_launch": (_I, [_P, _P]),

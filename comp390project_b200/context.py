@@ -172,6 +172,10 @@ class KsContext:
     def last_launch_count(self) -> int:
         return int(self.lib.ks_last_launch_count(self.h))
 
+    def total_launch_count(self) -> int:
+        """Kernel launches of every call since the context was created."""
+        return int(self.lib.ks_total_launch_count(self.h))
+
     # -- CUDA graphs -----------------------------------------------------------
     def graph_capture_begin(self, stream):
         """Starts recording the hot-path calls made on ``stream`` (a torch

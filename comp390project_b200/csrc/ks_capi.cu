@@ -1980,7 +1980,10 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
   });
 }
 
-int ks_last_launch_count(const ks_ctx *ctx) { return ctx ? ctx->c.launches : KS_ERR_INVALID; }
+int ks_last_launch_count(const ks_ctx *ctx) { return ctx ? ctx->c.launches.last : KS_ERR_INVALID; }
+long long ks_total_launch_count(const ks_ctx *ctx) {
+  return ctx ? ctx->c.launches.total : KS_ERR_INVALID;
+}
 
 int ks_profile_enable(ks_ctx *ctx, int on) {
   if (!ctx) return KS_ERR_INVALID;

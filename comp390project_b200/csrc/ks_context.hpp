@@ -155,7 +155,22 @@ struct Ctx {
   std::atomic<bool> wd_stop{false}, aborted{false};
   // diagnostics
   std::string err;
-  int launches = 0;
+  // kernel launches of the last API call (reset by each call) and since the
+  // context was created
+  struct LaunchCount {
+    int last = 0;
+    long long total = 0;
+    LaunchCount &operator+=(int n) {
+      last += n;
+      total += n;
+      return *this;
+    }
+    LaunchCount &operator=(int v) {
+      last = v;
+      return *this;
+    }
+    operator int() const { return last; }
+  } launches;
   // optional per-stage timing: event pairs recorded on the launch stream
   bool profile = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;

@@ -263,6 +263,8 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
 
 /* Number of kernels the last hot-path call launched (for bench accounting). */
 int ks_last_launch_count(const ks_ctx *ctx);
+/* Kernel launches of every call since the context was created. */
+long long ks_total_launch_count(const ks_ctx *ctx);
 
 /* CUDA graph capture and replay of hot-path calls (the capture/replay half
  * of the reference's StreamManager, overlap/stream_manager.cu:25-159).
