@@ -1,30 +1,31 @@
-"""A small BERT-shaped matmul case for the BSGS tests: config 1's ring
-(N=2^13, 4096 slots, Q={60,40,40}, P={60}), T=64 tokens, F=64 features per
-ciphertext, d_in = d_out = 128 (two input and two output ciphertexts),
-B = G = 8 by default.  Activations N(0,1) and weights N(0,0.02) from seed 4, as config 5
-draws them; the diagonals are encoded by the oracle at scale 2^40."""
+"""A small BERT-shaped matmul case for the BSGS tests: the SMALL ring
+(N=2^12, 2048 slots, Q = 50 + 6 x 40 bits, P = 3 x 55 bits, three digits),
+T=32 tokens, F=64 features per ciphertext, d_in = d_out = 128 (two input and
+two output ciphertexts), B = G = 8 by default.  Activations N(0,1) and
+weights N(0,0.02) from seed 4, as config 5 draws them; the diagonals are
+encoded by the oracle at scale 2^40."""
 import functools
 
 import numpy as np
 
 from comp390project_b200 import matmul
-from tests.ksparams import CFG1, oracle_for
+from tests.ksparams import SMALL, oracle_for
 
 SCALE = 2.0 ** 40
-TOKENS, D_IN, D_OUT = 64, 128, 128
+TOKENS, D_IN, D_OUT = 32, 128, 128
 
 
 @functools.lru_cache(maxsize=None)
 def case(n_baby=None):
     """n_baby=None: B = G = 8; n_baby=64: G = 1 and 128 plaintext terms per
     output (more than one pass of the product kernel)."""
-    o = oracle_for("cfg1")
+    o = oracle_for("small")
     lay = matmul.layout(o.N // 2, TOKENS, D_IN, D_OUT, n_baby=n_baby)
     rng = np.random.default_rng(4)
     X = rng.normal(0.0, 1.0, (TOKENS, D_IN))
     W = rng.normal(0.0, 0.02, (D_IN, D_OUT))
     s = o.secret(4)
-    Ql = len(CFG1["qbits"])
+    Ql = len(SMALL["qbits"])
     xs = [o.encrypt(s, o.encode(v, SCALE, Ql), Ql, 40 + i)
           for i, v in enumerate(matmul.pack(X, lay))]
     pts = [o.encode(d, SCALE, Ql) for d in matmul.diagonals(W, lay)]

@@ -39,9 +39,9 @@ def _want(g_range=None, n_baby=None):
 
 def _setup(device=0, keys=True, n_baby=None):
     from comp390project_b200 import KS_KEY_GALOIS, KsContext
-    from tests.ksparams import CFG1, split
+    from tests.ksparams import SMALL, split
     c = case(n_baby)
-    log_n, q, p = split(CFG1)
+    log_n, q, p = split(SMALL)
     ctx = KsContext(log_n, q, p, device=device, max_batch=2)
     if keys:
         for st, k in c["keys"].items():
