@@ -214,23 +214,86 @@ def measured_peaks():
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle port running the identical rotation key switch
 # ---------------------------------------------------------------------------
-def cpu_rotation_rate(n_rot: int):
+CONFIG1 = (13, [60, 40, 40], [60])  # N=2^13, Q={60,40,40}, P={60}
+
+
+def cpu_rotation_rate(n_rot: int, threads: int | None = None, cfg=None):
+    """Rotation key switches per second of the oracle port on the host, over
+    n_rot back-to-back rotations (key generation untimed).  threads=None: all
+    host cores (OpenMP over limbs); cfg: (log_n, qbits, pbits), default
+    config 3 (Hamming-weight-192 secret; config 1 uses a uniform ternary one)."""
     from oracle.oracle import Oracle, gen_primes, set_threads
-    threads = os.cpu_count() or 1
+    log_n, qbits, pbits = cfg or (LOG_N, QBITS, PBITS)
+    threads = threads or os.cpu_count() or 1
     set_threads(threads)
-    pr = gen_primes(LOG_N, QBITS + PBITS)
-    o = Oracle(LOG_N, pr[:len(QBITS)], pr[len(QBITS):])
-    s = o.secret(0, 192)
+    pr = gen_primes(log_n, list(qbits) + list(pbits))
+    o = Oracle(log_n, pr[:len(qbits)], pr[len(qbits):])
+    s = o.secret(0, 192 if cfg is None else 0)
     elt = o.galois_elt(1)
     key = o.keygen_galois(s, elt, 1001)
     rng = np.random.default_rng(5)
     z = rng.uniform(-1, 1, o.N // 2)
-    ct = o.encrypt(s, o.encode(z, SCALE, len(QBITS)), len(QBITS), 7)
+    ct = o.encrypt(s, o.encode(z, SCALE, len(qbits)), len(qbits), 7)
     t0 = time.perf_counter()
     for _ in range(n_rot):
-        ct = o.apply_galois(ct, len(QBITS), elt, key)
+        ct = o.apply_galois(ct, len(qbits), elt, key)
     dt = time.perf_counter() - t0
+    set_threads(os.cpu_count() or 1)
     return n_rot / dt, threads, dt
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def cpu_baseline_config3():
+    """The oracle port's rotation key switch on the host (about 15 s): config 3
+    over 3 rotations on all cores (the reported value) and on one core, and
+    config 1 over 20 rotations on all cores."""
+    rate, cores, dt = cpu_rotation_rate(3)
+    rate1, _, dt1 = cpu_rotation_rate(3, threads=1)
+    rc1, _, dtc1 = cpu_rotation_rate(20, cfg=CONFIG1)
+    return {"value": rate, "unit": "key-switches/s", "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": "3 rotation key switches at config 3 on the host (%.1f s), oracle/ C++ "
+                      "port with OpenMP over limbs" % dt,
+            "single_thread": {"value": rate1, "cores": 1,
+                              "sample": "3 rotations at config 3 on one core (%.1f s)" % dt1},
+            "config1": {"value": rc1, "cores": cores,
+                        "sample": "20 rotations at config 1 (N=2^13, Q={60,40,40}, P={60}) "
+                                  "(%.2f s)" % dtc1}}
+
+
+# Per-direction NVLink bandwidth of a peer copy measured on this pool's B200s
+# (900 GB/s nominal per direction per GPU).
+NVLINK_GBS = 770.0
+
+
+def collective_roofline(prof, n_ks, L, alpha, world, N):
+    """NVLink roofline of the input-broadcast collectives from the serial
+    profile: per key switch a rank receives the other ranks' padded shares of
+    the coefficient-form input ((G-1) ceil(L/G) limbs) and of the special-prime
+    limbs of cx ((G-1) 2 max_r |P limbs of r| limbs)."""
+    ms, calls = prof.get("collective", (0.0, 0))
+    if world <= 1 or ms <= 0 or n_ks <= 0:
+        return None
+    coef_ml = -(-L // world)
+    max_p_own = max(sum(1 for i in range(alpha) if (L + i) % world == r) for r in range(world))
+    recv = (world - 1) * (coef_ml + 2 * max_p_own) * N * 8
+    t = ms / n_ks / 1000.0
+    ach = recv / t / 1e9
+    return {"bound": "nvlink", "bytes_received_per_ks": recv, "ms_per_ks": ms / n_ks,
+            "calls_per_ks": calls / n_ks, "achieved": ach, "peak": NVLINK_GBS, "unit": "GB/s",
+            "frac": ach / NVLINK_GBS,
+            "peak_kind": "measured peer copy per direction (serial collectives, latency included)"}
 
 
 # ---------------------------------------------------------------------------
@@ -795,10 +858,8 @@ def run_ours(args, rank, world):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, cores, dt = cpu_rotation_rate(2)
-        cpu = {"value": rate, "unit": "key-switches/s", "cores": cores, "kind": "port",
-               "sample": "2 rotation key switches at config 3 on the host (%.1f s), oracle/ "
-                         "C++ port with OpenMP over limbs" % dt}
+        cpu = cpu_baseline_config3()
+    nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N)
 
     if rank == 0:
         line = {
@@ -816,6 +877,7 @@ def run_ours(args, rank, world):
                          "traffic": traffic, "peak_kind": peak_kind,
                          "alg_bytes": alg.get(dom),
                          "launch_ms": per_launch_ms},
+            "collectives": nvlink,
             "stages_ms_per_ks_serial": {k: v[0] / prof_ks for k, v in stages.items()},
             "cpu_baseline": cpu,
             "e2e": e2e,
