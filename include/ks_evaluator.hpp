@@ -157,6 +157,33 @@ class Evaluator {
           mc_.ctx(g_));
     mc_.sync(g_);
   }
+  // Ciphertext x plaintext matmul by BSGS diagonals (ks_bsgs_matmul), the
+  // product NEXUS's BERT layers run (reference bert_matmul_pipeline.cu:7-15):
+  // y[o] = sum_g rot_{g B unit}(sum_i sum_b pts[((o n_in + i) G + g) B + b] * rot_{b unit}(x[i]))
+  // with B = n_baby, G = n_giant; pts are NTT-form diagonals [n_local][N].
+  // The workspace is allocated and freed around the call.
+  void matmul_bsgs(const std::vector<CiphertextView> &x, int unit, int n_baby, int n_giant,
+                   const std::vector<const uint64_t *> &pts, std::vector<CiphertextView> &y) {
+    if (x.empty() || y.empty()) throw std::runtime_error("ks_b200: empty matmul operand list");
+    std::vector<const uint64_t *> xp;
+    for (const CiphertextView &v : x) xp.push_back(v.data);
+    std::vector<uint64_t *> yp;
+    for (CiphertextView &v : y) yp.push_back(v.data);
+    const int Ql = (int)x[0].coeff_modulus_size;
+    ks_ctx *ctx = mc_.ctx(g_);
+    const size_t words = ks_bsgs_workspace_words(ctx, Ql, (int)x.size(), n_baby);
+    uint64_t *work = nullptr;
+    if (words > 0 && cudaMalloc(reinterpret_cast<void **>(&work), words * sizeof(uint64_t)) !=
+                         cudaSuccess)
+      throw std::runtime_error("ks_b200: cannot allocate the matmul workspace");
+    const int rc = ks_bsgs_matmul(ctx, xp.data(), nullptr, (int)x.size(), Ql, unit, n_baby,
+                                  n_giant, 0, n_giant, pts.data(), yp.data(), (int)y.size(),
+                                  work, mc_.stream(g_));
+    const cudaError_t se = cudaStreamSynchronize(mc_.stream(g_));
+    cudaFree(work);
+    check(rc, ctx);
+    if (se != cudaSuccess) throw std::runtime_error("ks_b200: stream synchronisation failed");
+  }
 
  private:
   MultiGpuContext &mc_;
