@@ -107,6 +107,28 @@ def test_rotate_bitexact(name, cfg, Ql, step, cuda_device):
     assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
 
 
+def test_conjugate_bitexact(cuda_device):
+    """Complex conjugation: Galois element 2N - 1 (Phantom's conjugate), on
+    complex slots."""
+    o = oracle_for("small")
+    ctx = _ctx(SMALL)
+    s = o.secret(0)
+    elt = 2 * o.N - 1
+    key = o.keygen_galois(s, elt, 13)
+    ctx.key_upload(1, elt, key)
+    rng = np.random.default_rng(8)
+    Ql = o.L
+    z = rng.uniform(-1, 1, o.N // 2) + 1j * rng.uniform(-1, 1, o.N // 2)
+    ct = o.encrypt(s, o.encode(z, 2.0 ** 40, Ql), Ql, 108)
+    ref = o.apply_galois(ct, Ql, elt, key)
+    d = _to_dev(ct)
+    ctx.apply_galois(d, Ql, elt)
+    out = _to_host(d).reshape(2, Ql, o.N)
+    assert np.array_equal(out, ref)
+    dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 40)
+    assert np.abs(dec - np.conj(z)).mean() < 1e-3
+
+
 @pytest.mark.parametrize("name,cfg,Ql", [("cfg1", CFG1, 3), ("small", SMALL, 7), ("small", SMALL, 4)])
 def test_relinearize_bitexact(name, cfg, Ql, cuda_device):
     o = oracle_for(name)

@@ -192,6 +192,19 @@ def test_rotation_decodes_to_rolled_slots(step):
     assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
 
 
+def test_conjugation_decodes_to_conjugate_slots():
+    """Galois element 2N - 1 (X -> X^-1) conjugates every slot."""
+    o = oracle_for("cfg1")
+    s = o.secret(0)
+    elt = 2 * o.N - 1
+    key = o.keygen_galois(s, elt, 12)
+    rng = np.random.default_rng(9)
+    z = rng.uniform(-1, 1, o.N // 2) + 1j * rng.uniform(-1, 1, o.N // 2)
+    ct = o.encrypt(s, o.encode(z, 2.0 ** 40, 3), 3, 6)
+    dec = o.decode(o.decrypt(s, o.apply_galois(ct, 3, elt, key), 3), 3, 2.0 ** 40)
+    assert np.abs(dec - np.conj(z)).mean() < 1e-3
+
+
 def test_relinearisation_decodes_to_product():
     o = oracle_for("cfg1")
     s = o.secret(1)
