@@ -78,6 +78,13 @@ def test_null_context_calls_fail_cleanly():
     assert lib.ks_ntt_forward(None, None, 1, 0, 1, None) == KS_ERR_INVALID
     assert lib.ks_ctx_destroy(None) == KS_ERR_INVALID
     assert lib.ks_key_words(None) == 0
+    assert lib.ks_bsgs_workspace_words(None, 3, 1, 4) == 0
+    assert lib.ks_bsgs_matmul(None, None, None, 1, 3, 1, 2, 2, 0, 2, None, None, 1, None,
+                              None) == KS_ERR_INVALID
+    assert lib.ks_reduce_limbs(None, None, 2, 3, None) == KS_ERR_INVALID
+    assert lib.ks_rescale(None, None, 3, None, None) == KS_ERR_INVALID
+    assert lib.ks_total_launch_count(None) == KS_ERR_INVALID
+    assert lib.ks_last_launch_count(None) == KS_ERR_INVALID
     buf = C.create_string_buffer(8)
     assert lib.ks_last_error(None, buf, 0) == KS_ERR_INVALID
 
