@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <string>
 #include <thread>
 #include <vector>
@@ -94,9 +95,19 @@ int guarded(ks_ctx *ctx, F &&f) {
     set_global_err(e.msg);
     abort_capture(ctx);
     return e.code;
+  } catch (const std::bad_alloc &) {
+    if (ctx) ctx->c.err = "host allocation failed";
+    set_global_err("host allocation failed");
+    abort_capture(ctx);
+    return KS_ERR_ALLOC;
   } catch (const std::exception &e) {
     if (ctx) ctx->c.err = e.what();
     set_global_err(e.what());
+    abort_capture(ctx);
+    return KS_ERR_INVALID;
+  } catch (...) {
+    if (ctx) ctx->c.err = "unknown exception";
+    set_global_err("unknown exception");
     abort_capture(ctx);
     return KS_ERR_INVALID;
   }
@@ -1494,7 +1505,11 @@ int ks_ctx_create(const ks_params *prm, int device, int rank, int world, const v
     return KS_ERR_INVALID;
   }
   *out = nullptr;
-  ks_ctx *ctx = new ks_ctx();
+  ks_ctx *ctx = new (std::nothrow) ks_ctx();
+  if (!ctx) {
+    set_global_err("host allocation failed");
+    return KS_ERR_ALLOC;
+  }
   int rc = guarded(ctx, [&] { ctx_init(ctx->c, prm, device, rank, world, nullptr, nccl_id); });
   if (rc != KS_OK) {
     set_global_err(ctx->c.err);
@@ -1519,17 +1534,26 @@ int ks_ctx_create_all(const ks_params *prm, const int *devices, int n, ks_ctx **
       return KS_ERR_NCCL;
     }
   }
+  for (int i = 0; i < n; ++i) outs[i] = nullptr;
   for (int i = 0; i < n; ++i) {
-    outs[i] = new ks_ctx();
-    int rc = guarded(outs[i], [&] { ctx_init(outs[i]->c, prm, devices[i], i, n, comms[i], nullptr); });
+    outs[i] = new (std::nothrow) ks_ctx();
+    int rc = KS_ERR_ALLOC;
+    if (outs[i])
+      rc = guarded(outs[i],
+                   [&] { ctx_init(outs[i]->c, prm, devices[i], i, n, comms[i], nullptr); });
+    else
+      set_global_err("host allocation failed");
     if (rc != KS_OK) {
-      set_global_err(outs[i]->c.err);
+      if (outs[i]) set_global_err(outs[i]->c.err);
+      // communicators a failed context did not adopt are destroyed here
+      const bool adopted = outs[i] && outs[i]->c.comm == comms[i];
       for (int k = 0; k <= i; ++k) {
+        if (!outs[k]) continue;
         ctx_free(outs[k]->c);
         delete outs[k];
         outs[k] = nullptr;
       }
-      for (int k = i + 1; k < n; ++k)
+      for (int k = adopted ? i + 1 : i; k < n; ++k)
         if (comms[k]) ncclCommDestroy(comms[k]);
       return rc;
     }
