@@ -8,7 +8,6 @@ all-gather that cannot complete: the context's collective deadline
 every later call must fail with KS_ERR_TIMEOUT instead of hanging.  Skipped
 when fewer than two GPUs are visible."""
 import os
-import socket
 import sys
 import time
 
@@ -19,14 +18,6 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-
-
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _worker(rank, world, port, q, left):
@@ -82,17 +73,7 @@ def _worker(rank, world, port, q, left):
 def test_rank_that_never_joins_times_out(cuda_device):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
-    world = 2
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    left = ctx.Event()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, left)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=300) for _ in range(world))
-    for p in procs:
-        p.join(timeout=60)
-    assert res[1] is True, res
-    assert isinstance(res[0], tuple) and res[0][0], res
+    from tests.procs import run_ranks
+    res = run_ranks(_worker, 2, extra_objs=lambda ctx: [ctx.Event()])
+    assert res.get(1) is True, res
+    assert isinstance(res.get(0), tuple) and res[0][0], res

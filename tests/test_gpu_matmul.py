@@ -7,7 +7,6 @@ giant-step split over two GPUs (all-gather of the baby steps, integer
 all-reduce of the partial products); the product decodes to X W."""
 import functools
 import os
-import socket
 import sys
 
 import numpy as np
@@ -129,14 +128,6 @@ def test_bsgs_matmul_rejects_missing_key_and_alias(cuda_device):
     ctx.close()
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
-
-
 def _worker(rank, world, port, q):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -166,14 +157,6 @@ def test_giant_parallel_two_gpus(cuda_device):
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip("needs %d GPUs" % world)
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    res = dict(q.get(timeout=300) for _ in range(world))
-    for p in procs:
-        p.join(timeout=120)
-    assert all(v is True for v in res.values()), res
+    from tests.procs import run_ranks
+    res = run_ranks(_worker, world)
+    assert len(res) == world and all(v is True for v in res.values()), res

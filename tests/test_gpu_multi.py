@@ -6,7 +6,6 @@ for bit.  Output aggregation: every rank holds the whole ciphertext and its
 digits of the key, and every rank's result must equal the oracle.  Skipped
 when fewer than two GPUs are visible."""
 import os
-import socket
 import sys
 
 import numpy as np
@@ -18,15 +17,7 @@ torch = pytest.importorskip("torch")
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
-
-
-def _worker(rank, world, port, name, mode, q):
+def _worker(rank, world, port, q, name, mode):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import torch
@@ -147,17 +138,8 @@ def test_multi_gpu_keyswitch_bitexact(name, mode, world, cuda_device):
     contributes a zero partial sum."""
     if torch.cuda.device_count() < world:
         pytest.skip("needs %d GPUs" % world)
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, name, mode, q))
-             for r in range(world)]
-    for p in procs:
-        p.start()
+    from tests.procs import run_ranks
     # every worker sets a 60 s collective deadline, so a failed rank ends the
     # others' collectives with an error instead of a hang
-    res = dict(q.get(timeout=300) for _ in range(world))
-    for p in procs:
-        p.join(timeout=120)
-    assert all(v is True for v in res.values()), res
+    res = run_ranks(_worker, world, extra_args=(name, mode))
+    assert len(res) == world and all(v is True for v in res.values()), res
