@@ -51,7 +51,8 @@ extern "C" {
 #define KS_KEY_GALOIS 1
 
 #define KS_MODE_INPUT_BROADCAST 0   /* all-gather c2 limbs, limb-local extension */
-#define KS_MODE_OUTPUT_AGGREGATION 1 /* digit-split inner product + reduce-scatter */
+#define KS_MODE_OUTPUT_AGGREGATION 1 /* whole ciphertext per rank, digit-split inner product,
+                                        all-reduce of the partial sums */
 
 typedef struct ks_ctx ks_ctx;
 

@@ -8,10 +8,15 @@ data with real torch.distributed collectives:
                        to ceil(Ql/G) slots, rank-grouped), limb-local ModUp and
                        inner product, all-gather of the special-prime limbs,
                        limb-local ModDown;
-  output aggregation:  digit-split inner product over all extended limbs,
-                       uint64 reduce-scatter of the partial sums + mod reduce.
-The gathered result must equal the single-process oracle key switch bit for
-bit.  The arithmetic is the CPU oracle's; what is under test is the
+  output aggregation:  every rank holds the whole input and the digits
+                       d % G == g; it converts and extends only its digits'
+                       limbs, forms the partial inner product over all
+                       extended limbs, and a uint64 all-reduce + mod reduce
+                       gives every rank the whole cx; ModDown on every rank
+                       (the library's plan, after the reference's
+                       keyswitching_output_aggregation).
+The result (gathered, for input broadcast) must equal the single-process
+oracle key switch bit for bit.  The arithmetic is the CPU oracle's; what is under test is the
 partition, padding, slot order and collective plan."""
 import os
 import socket
@@ -62,6 +67,34 @@ def _worker(rank, world, port, mode, result_q):
         ref = o.keyswitch(c, Ql, key)
         idx = list(range(Ql)) + [L + i for i in range(a)]  # key-basis index of QlP limb j
         G, g = world, rank
+        digits = P.digits(Ql, a)
+        beta = len(digits)
+        if mode == "oa":
+            # 1. the limbs of this rank's digits to coefficient form (whole input here)
+            mine_d = list(range(g, beta, G))
+            dl = [j for d in mine_d for j in digits[d]]
+            coef = np.zeros((Ql, N), dtype=np.uint64)
+            if dl:
+                coef[dl] = o.ntt(c[dl], dl, inverse=True)
+            t = np.zeros((beta, QlP, N), dtype=np.uint64)
+            for d in mine_d:
+                D = digits[d]
+                for j in range(QlP):
+                    if j in D:
+                        t[d, j] = c[j]
+                    else:
+                        t[d, j] = o.ntt(o.bconv(coef[D], D, [idx[j]]), [idx[j]])[0]
+            part = o.inner_product(t, Ql, key)  # [2][QlP][N], partial over my digits
+            # 2. uint64 all-reduce (G q < 2^64: the integer sum is exact) + mod q
+            tt = torch.from_numpy(np.ascontiguousarray(part).view(np.int64))
+            dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+            q_of = np.array([int(o.moduli[idx[j]]) for j in range(QlP)],
+                            dtype=np.uint64)[None, :, None]
+            cx = tt.numpy().view(np.uint64) % q_of
+            # 3. ModDown of both polys on every rank: the whole result everywhere
+            full = np.stack([o.moddown(cx[p], Ql) for p in range(2)])
+            result_q.put((rank, bool(np.array_equal(full, ref))))
+            return
         my_q = P.limbs_for_gpu(g, G, Ql)
         # 1. own limbs to coefficient form, padded rank-grouped all-gather
         ml = P.max_local(Ql, G)
@@ -72,8 +105,6 @@ def _worker(rank, world, port, mode, result_q):
         coef = np.stack([gathered[P.owner_of_limb(j, G)][P.local_index_of_limb(j, G)]
                          for j in range(Ql)])
         assert np.array_equal(coef, o.ntt(c, list(range(Ql)), inverse=True))
-        digits = P.digits(Ql, a)
-        beta = len(digits)
 
         def extend(d, j):
             """t[d][j] in NTT form from the all-gathered coefficients."""
@@ -83,35 +114,13 @@ def _worker(rank, world, port, mode, result_q):
             y = o.bconv(coef[D], D, [idx[j]])
             return o.ntt(y, [idx[j]])[0]
 
-        if mode == "ib":
-            outs = P.owned_output_limbs(g, G, Ql, L, a)
-            t = np.zeros((beta, QlP, N), dtype=np.uint64)
-            for d in range(beta):
-                for j in outs:
-                    t[d, j] = extend(d, j)
-            cx_full = o.inner_product(t, Ql, key)  # limb-wise: only owned rows are used
-            mine = {j: cx_full[:, j] for j in outs}
-        else:  # output aggregation: digits d % G == g over every extended limb
-            t = np.zeros((beta, QlP, N), dtype=np.uint64)
-            for d in range(g, beta, G):
-                for j in range(QlP):
-                    t[d, j] = extend(d, j)
-            part = o.inner_product(t, Ql, key)  # partial sum over my digits
-            # uint64 reduce-scatter: rank r receives the limbs it owns (padded slots)
-            owners = [P.owned_output_limbs(r, G, Ql, L, a) for r in range(G)]
-            mo = max(len(x) for x in owners)
-            send = np.zeros((G, mo, 2, N), dtype=np.uint64)
-            for r in range(G):
-                for sl, j in enumerate(owners[r]):
-                    send[r, sl] = part[:, j]
-            st = torch.from_numpy(send.view(np.int64))
-            recv = torch.empty((mo, 2, N), dtype=torch.int64)
-            dist.reduce_scatter_tensor(recv, st.reshape(G * mo, 2, N), op=dist.ReduceOp.SUM)
-            rv = recv.numpy().view(np.uint64)
-            mine = {}
-            for sl, j in enumerate(owners[g]):
-                m = np.uint64(int(o.moduli[idx[j]]))
-                mine[j] = rv[sl] % m  # G * q < 2^64: the integer sum is exact
+        outs = P.owned_output_limbs(g, G, Ql, L, a)
+        t = np.zeros((beta, QlP, N), dtype=np.uint64)
+        for d in range(beta):
+            for j in outs:
+                t[d, j] = extend(d, j)
+        cx_full = o.inner_product(t, Ql, key)  # limb-wise: only owned rows are used
+        mine = {j: cx_full[:, j] for j in outs}
         # 2. special-prime limbs of cx to every rank
         own_p = [j for j in mine if j >= Ql]
         maxp = max(len([i for i in range(a) if (L + i) % G == r]) for r in range(G))
