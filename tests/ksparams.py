@@ -17,6 +17,9 @@ CFG1 = dict(log_n=13, qbits=(60, 40, 40), pbits=(60,))
 CFG3 = dict(log_n=16, qbits=(58,) + (42,) * 34, pbits=(60,) * 5)
 # small multi-digit case: N=2^12, 7 Q primes, alpha=3 (3 digits, the last short)
 SMALL = dict(log_n=12, qbits=(50,) + (40,) * 6, pbits=(55,) * 3)
+# the reference's own correctness test: N=8192, bit sizes {60,40,40,40,60}, the
+# last prime special (src/benchmarks/multi_gpu_keyswitch_test.cu:186-195)
+REFTEST = dict(log_n=13, qbits=(60, 40, 40, 40), pbits=(60,))
 
 
 def split(cfg):
@@ -27,7 +30,7 @@ def split(cfg):
 
 @functools.lru_cache(maxsize=None)
 def oracle_for(name):
-    cfg = {"cfg1": CFG1, "cfg3": CFG3, "small": SMALL}[name]
+    cfg = {"cfg1": CFG1, "cfg3": CFG3, "small": SMALL, "reftest": REFTEST}[name]
     log_n, q, p = split(cfg)
     return Oracle(log_n, q, p)
 
@@ -38,3 +41,10 @@ def random_limbs(moduli, n_limbs_each, N, seed):
     for i, q in enumerate(moduli):
         out[i] = rng.integers(0, int(q), size=N, dtype=np.uint64)
     return out
+
+
+def reference_test_values(n, seed):
+    """The reference test's input distribution, (rand() % 1000) / 100 - 5
+    (multi_gpu_keyswitch_test.cu:211-215), drawn from a seeded generator."""
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 1000, size=n) / 100.0 - 5.0

@@ -149,6 +149,31 @@ def test_relinearize_bitexact(name, cfg, Ql, cuda_device):
         assert np.abs(dec - z1 * z2).mean() < 1e-3
 
 
+def test_relinearize_on_the_reference_test_parameters(cuda_device):
+    """The reference's own correctness test (multi_gpu_keyswitch_test.cu:186-332):
+    N=8192, {60,40,40,40,60}, inputs (rand() % 1000) / 100 - 5; the GPU result
+    must equal the oracle bit for bit and decode to the product (MAE < 1e-3)."""
+    from tests.ksparams import REFTEST, reference_test_values
+    o = oracle_for("reftest")
+    ctx = _ctx(REFTEST)
+    Ql = o.L
+    s = o.secret(42)
+    key = o.keygen_relin(s, 42)
+    ctx.key_upload(0, 0, key)
+    z1 = reference_test_values(o.N // 2, 42)
+    z2 = reference_test_values(o.N // 2, 43)
+    c1 = o.encrypt(s, o.encode(z1, 2.0 ** 40, Ql), Ql, 1)
+    c2 = o.encrypt(s, o.encode(z2, 2.0 ** 40, Ql), Ql, 2)
+    m = o.multiply(c1, c2, Ql)
+    ref = o.relinearize(m, Ql, key)
+    d = _to_dev(m)
+    ctx.relinearize(d, Ql)
+    out = _to_host(d).reshape(3, Ql, o.N)[:2]
+    assert np.array_equal(out, ref)
+    dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 80)
+    assert np.abs(dec - z1 * z2).mean() < 1e-3
+
+
 @pytest.mark.parametrize("name,cfg,kind", [("cfg1", CFG1, 1), ("small", SMALL, 1), ("small", SMALL, 0)])
 def test_gpu_keygen_matches_oracle(name, cfg, kind, cuda_device):
     o = oracle_for(name)

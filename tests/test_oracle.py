@@ -218,6 +218,24 @@ def test_relinearisation_decodes_to_product():
     assert np.abs(dec - z1 * z2).mean() < 1e-3
 
 
+def test_relinearisation_on_the_reference_test_parameters():
+    """The reference's multi_gpu_keyswitch_test (src/benchmarks/
+    multi_gpu_keyswitch_test.cu:186-332): N=8192, {60,40,40,40,60}, inputs
+    (rand() % 1000) / 100 - 5, multiply + relinearise, decode MAE < 1e-3."""
+    from tests.ksparams import reference_test_values
+    o = oracle_for("reftest")
+    Ql = o.L
+    s = o.secret(42)
+    key = o.keygen_relin(s, 42)
+    z1 = reference_test_values(o.N // 2, 42)
+    z2 = reference_test_values(o.N // 2, 43)
+    c1 = o.encrypt(s, o.encode(z1, 2.0 ** 40, Ql), Ql, 1)
+    c2 = o.encrypt(s, o.encode(z2, 2.0 ** 40, Ql), Ql, 2)
+    r = o.relinearize(o.multiply(c1, c2, Ql), Ql, key)
+    dec = o.decode(o.decrypt(s, r, Ql), Ql, 2.0 ** 80)
+    assert np.abs(dec - z1 * z2).mean() < 1e-3
+
+
 def test_keyswitch_noise_is_small():
     o = oracle_for("small")
     s = o.secret(2)
