@@ -20,6 +20,10 @@ SMALL = dict(log_n=12, qbits=(50,) + (40,) * 6, pbits=(55,) * 3)
 # the reference's own correctness test: N=8192, bit sizes {60,40,40,40,60}, the
 # last prime special (src/benchmarks/multi_gpu_keyswitch_test.cu:186-195)
 REFTEST = dict(log_n=13, qbits=(60, 40, 40, 40), pbits=(60,))
+# the other ring sizes of the reference's published correctness table
+# (N = 16384; and 32768): column pass of 2^7 points
+N14 = dict(log_n=14, qbits=(50, 40, 40, 40), pbits=(55, 55))
+N15 = dict(log_n=15, qbits=(55,) + (40,) * 4, pbits=(58, 58, 58))
 
 
 def split(cfg):
@@ -30,7 +34,8 @@ def split(cfg):
 
 @functools.lru_cache(maxsize=None)
 def oracle_for(name):
-    cfg = {"cfg1": CFG1, "cfg3": CFG3, "small": SMALL, "reftest": REFTEST}[name]
+    cfg = {"cfg1": CFG1, "cfg3": CFG3, "small": SMALL, "reftest": REFTEST, "n14": N14,
+           "n15": N15}[name]
     log_n, q, p = split(cfg)
     return Oracle(log_n, q, p)
 

@@ -39,6 +39,38 @@ def test_ntt_roundtrip_bitexact(name, cfg, cuda_device):
     assert np.array_equal(_to_host(d), x)
 
 
+@pytest.mark.parametrize("name", ["n14", "n15"])
+def test_other_ring_sizes_bitexact(name, cuda_device):
+    """N = 2^14 and 2^15 (2^7-point column pass): NTT round trip and a
+    rotation key switch against the oracle, and the rotation decodes."""
+    from tests.ksparams import N14, N15
+    cfg = {"n14": N14, "n15": N15}[name]
+    o = oracle_for(name)
+    ctx = _ctx(cfg)
+    K = o.L + o.alpha
+    rng = np.random.default_rng(3)
+    x = np.stack([rng.integers(0, int(m), size=o.N, dtype=np.uint64) for m in o.moduli])
+    d = _to_dev(x)
+    ctx.ntt_forward(d, K, 0, 1)
+    assert np.array_equal(_to_host(d), o.ntt(x, list(range(K))))
+    ctx.ntt_inverse(d, K, 0, 1)
+    assert np.array_equal(_to_host(d), x)
+    s = o.secret(5)
+    step = 7
+    elt = o.galois_elt(step)
+    key = o.keygen_galois(s, elt, 17)
+    ctx.key_upload(1, elt, key)
+    Ql = o.L
+    z, ct = _encrypted(o, Ql, 9, s)
+    ref = o.apply_galois(ct, Ql, elt, key)
+    d = _to_dev(ct)
+    ctx.rotate(d, Ql, step)
+    out = _to_host(d).reshape(2, Ql, o.N)
+    assert np.array_equal(out, ref)
+    dec = o.decode(o.decrypt(s, out, Ql), Ql, 2.0 ** 40)
+    assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
+
+
 @pytest.mark.parametrize("pattern", ["max", "zero", "alt", "one", "ramp"])
 def test_ntt_extreme_inputs(pattern, cuda_device):
     """Inputs at the ends of [0, q) stress the lazy-reduction bounds of every
