@@ -101,3 +101,41 @@ def test_linear_transform_hoisted_decodes(cuda_device):
     want = sum(x * np.roll(z, -st) for x, st in zip(dz, STEPS))
     assert np.abs(dec - want).mean() < 1e-3
     ctx.close()
+
+
+def test_config4_hoisted_bitexact(cuda_device):
+    """Config 4's ring (N = 2^16, alpha = 5) at level 24 (Ql = 25, five full
+    digits): hoisted rotations and the hoisted linear transform over baby and
+    giant steps, word for word against the oracle."""
+    from comp390project_b200 import KS_KEY_GALOIS, KsContext
+    from tests.ksparams import CFG3
+    o = oracle_for("cfg3")
+    log_n, q, p = split(CFG3)
+    ctx = KsContext(log_n, q, p, device=0, max_batch=2)
+    s = o.secret(7, 192)
+    steps = [1, 5, 32, 64]
+    keys = {}
+    for st in steps:
+        e = o.galois_elt(st)
+        keys[st] = o.keygen_galois(s, e, 300 + st)
+        ctx.key_upload(KS_KEY_GALOIS, e, keys[st])
+    Ql = 25
+    rng = np.random.default_rng(21)
+    ct = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                             for j in range(Ql)]) for _ in range(2)])
+    elts = [o.galois_elt(st) for st in steps]
+    d = _dev(ct)
+    outs = [torch.zeros_like(d) for _ in steps]
+    ctx.rotate_hoisted(d, Ql, steps, outs)
+    torch.cuda.synchronize()
+    want = o.rotate_hoisted(ct, Ql, elts, [keys[st] for st in steps])
+    for i, out in enumerate(outs):
+        assert np.array_equal(_host(out), want[i]), "rotation %d differs" % steps[i]
+    diags = [np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                       for j in _ext_basis(o, Ql)]) for _ in steps]
+    out = torch.zeros_like(d)
+    ctx.linear_transform_hoisted(d, Ql, steps, [_dev(x) for x in diags], out)
+    torch.cuda.synchronize()
+    want = o.linear_transform_hoisted(ct, Ql, elts, [keys[st] for st in steps], diags)
+    assert np.array_equal(_host(out), want)
+    ctx.close()
