@@ -161,7 +161,8 @@ def test_conjugate_bitexact(cuda_device):
     assert np.abs(dec - np.conj(z)).mean() < 1e-3
 
 
-@pytest.mark.parametrize("name,cfg,Ql", [("cfg1", CFG1, 3), ("small", SMALL, 7), ("small", SMALL, 4)])
+@pytest.mark.parametrize("name,cfg,Ql", [("cfg1", CFG1, 3), ("small", SMALL, 7), ("small", SMALL, 4),
+                                         ("cfg3", CFG3, 35)])
 def test_relinearize_bitexact(name, cfg, Ql, cuda_device):
     o = oracle_for(name)
     ctx = _ctx(cfg)
