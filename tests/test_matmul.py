@@ -107,3 +107,34 @@ def test_oracle_partial_products_add_up():
     for p in parts:
         acc = (acc + p) % q
     assert np.array_equal(acc, full)
+
+
+def test_bsgs_identity_for_random_shapes():
+    """Property: for any power-of-two packing the pre-rotated diagonals and the
+    BSGS formula reproduce X W in the clear (slots 64..1024, any B dividing F)."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=40, deadline=None)
+    @given(log_s=st.integers(6, 10), log_t=st.integers(0, 4), n_in=st.integers(1, 3),
+           n_out=st.integers(1, 3), log_b=st.integers(0, 6), seed=st.integers(0, 2 ** 31))
+    def check(log_s, log_t, n_in, n_out, log_b, seed):
+        slots, T = 1 << log_s, 1 << log_t
+        F = slots // T
+        B = 1 << min(log_b, F.bit_length() - 1)
+        lay = matmul.layout(slots, T, n_in * F, n_out * F, n_baby=B)
+        rng = np.random.default_rng(seed)
+        X = rng.normal(size=(T, n_in * F))
+        W = rng.normal(size=(n_in * F, n_out * F))
+        xs = matmul.pack(X, lay)
+        d = matmul.diagonals(W, lay).reshape(n_out, n_in, lay.n_giant, B, slots)
+        ys = []
+        for o in range(n_out):
+            acc = np.zeros(slots)
+            for g in range(lay.n_giant):
+                inner = sum(d[o, i, g, b] * _rot(xs[i], b * lay.unit)
+                            for i in range(n_in) for b in range(B))
+                acc = acc + _rot(inner, g * B * lay.unit)
+            ys.append(acc)
+        assert np.allclose(matmul.unpack(np.array(ys), lay), X @ W, atol=1e-8)
+
+    check()
