@@ -7,23 +7,24 @@
 //
 //   offset size
 //     0     8   magic "KSB2WIRE"
-//     8     4   format version (1)
+//     8     4   format version (2)
 //    12     4   object: KS_WIRE_RELIN_KEY, KS_WIRE_GALOIS_KEY, KS_WIRE_CIPHERTEXT
-//    16     4   Galois element (Galois keys), else 0
+//    16     4   Galois element (Galois keys: odd, < 2N), else 0
 //    20     4   log_n
 //    24     4   n_q (L)
 //    28     4   n_p (alpha)
 //    32     4   dim0: key digits ceil(L / alpha) | ciphertext polys
 //    36     4   dim1: 2 | ciphertext level_limbs
 //    40     4   dim2: L + alpha | 0
-//    44     4   0
+//    44     4   0 (reserved)
 //    48     8   parameter digest: FNV-1a 64 of (log_n, q_0..q_{L-1}, p_0..p_{alpha-1})
-//    56     8   payload digest: FNV-1a 64 of the payload bytes
+//    56     8   blob digest: FNV-1a 64 of header bytes 0..55, then the payload bytes
 //    64     -   payload: uint64 words in the in-memory layout
 //                ([digits][2][L+alpha][N] keys, [polys][level_limbs][N] ciphertexts)
 //
-// Unpacking checks the magic, version, parameters, sizes, both digests and
-// that every word is a canonical residue of its limb's prime.
+// Unpacking checks the magic, version, parameters, sizes, the Galois element,
+// both digests (so a change to any header or payload byte is caught) and that
+// every word is a canonical residue of its limb's prime.
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -34,7 +35,7 @@
 namespace {
 
 constexpr char kMagic[8] = {'K', 'S', 'B', '2', 'W', 'I', 'R', 'E'};
-constexpr uint32_t kVersion = 1;
+constexpr uint32_t kVersion = 2;
 constexpr size_t kHeader = 64;
 
 uint64_t fnv1a(uint64_t h, const void *data, size_t n) {
@@ -122,6 +123,9 @@ int ks_wire_pack(const ks_params *prm, int object, uint32_t galois_elt, int leve
   if (!params_ok(prm) || !words || !out) return KS_ERR_INVALID;
   const Shape sh = shape_of(prm, object, level_limbs, n_polys);
   if (!sh.words || cap < kHeader + sh.words * 8) return KS_ERR_INVALID;
+  if (object == KS_WIRE_GALOIS_KEY &&
+      (!(galois_elt & 1u) || galois_elt >= (2ull << prm->log_n)))
+    return KS_ERR_INVALID;
   unsigned char *b = static_cast<unsigned char *>(out);
   std::memset(b, 0, kHeader);
   std::memcpy(b, kMagic, 8);
@@ -136,7 +140,7 @@ int ks_wire_pack(const ks_params *prm, int object, uint32_t galois_elt, int leve
   put<uint32_t>(b, 40, sh.d2);
   put<uint64_t>(b, 48, params_digest(prm));
   std::memcpy(b + kHeader, words, sh.words * 8);
-  put<uint64_t>(b, 56, fnv1a(kFnvBasis, words, sh.words * 8));
+  put<uint64_t>(b, 56, fnv1a(fnv1a(kFnvBasis, b, 56), words, sh.words * 8));
   return KS_OK;
 }
 
@@ -156,11 +160,17 @@ int ks_wire_unpack(const ks_params *prm, const void *blob, size_t n, int *object
   if (!sh.words || get<uint32_t>(b, 32) != sh.d0 || get<uint32_t>(b, 36) != sh.d1 ||
       get<uint32_t>(b, 40) != sh.d2 || n != kHeader + sh.words * 8)
     return KS_ERR_INVALID;
-  if (fnv1a(kFnvBasis, b + kHeader, sh.words * 8) != get<uint64_t>(b, 56)) return KS_ERR_INVALID;
+  const uint32_t elt = get<uint32_t>(b, 16);
+  const uint64_t two_n = 2ull << prm->log_n;
+  if (obj == KS_WIRE_GALOIS_KEY ? (!(elt & 1u) || elt >= two_n) : elt != 0)
+    return KS_ERR_INVALID;
+  if (get<uint32_t>(b, 44) != 0) return KS_ERR_INVALID;
+  if (fnv1a(fnv1a(kFnvBasis, b, 56), b + kHeader, sh.words * 8) != get<uint64_t>(b, 56))
+    return KS_ERR_INVALID;
   for (size_t w = 0; w < sh.words; ++w)
     if (get<uint64_t>(b, kHeader + w * 8) >= prime_of_word(prm, obj, sh, w)) return KS_ERR_INVALID;
   if (object) *object = obj;
-  if (galois_elt) *galois_elt = get<uint32_t>(b, 16);
+  if (galois_elt) *galois_elt = elt;
   if (level_limbs) *level_limbs = ql;
   if (n_polys) *n_polys = np;
   if (words) {

@@ -1,10 +1,11 @@
 """Wire format of evaluation keys and ciphertexts (ks_wire_* of the C ABI).
 
 A blob is a 64-byte header (magic, version, object, Galois element, ring and
-basis sizes, FNV-1a digests of the parameters and of the payload) followed by
+basis sizes, FNV-1a digests of the parameters and of the header + payload) followed by
 the uint64 words in the in-memory layout: a full key [digits][2][L+alpha][N]
 or a ciphertext [polys][level_limbs][N].  Unpacking rejects another parameter
-set, a wrong size, a digest mismatch or a non-canonical residue.  The
+set, a wrong size, a bad Galois element, a digest mismatch (any changed byte)
+or a non-canonical residue.  The
 reference has no serialised form: its key distribution
 (src/multi_gpu/distributed_context.cu:112-134) regenerates keys per GPU.
 Host functions only; no device is needed."""

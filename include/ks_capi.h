@@ -129,7 +129,7 @@ int ks_key_drop(ks_ctx *ctx, int kind, uint32_t galois_elt);
  * little-endian blob of a full key [digits][2][L+alpha][N] or a ciphertext
  * [polys][level_limbs][N] -- 64-byte header (magic "KSB2WIRE", version,
  * object, Galois element, log_n, n_q, n_p, dimensions, FNV-1a digests of the
- * parameters and of the payload) then the words.  The reference has no
+ * parameters and of the header + payload) then the words.  The reference has no
  * serialised form (its key distribution, distributed_context.cu:112-134,
  * regenerates keys on every GPU).  Unpack checks parameters, sizes, digests
  * and that every word is a canonical residue; words may be null to only
