@@ -320,8 +320,11 @@ class KsContext:
 
     def linear_transform_hoisted(self, ct, level_limbs: int, steps: Sequence[int], diags, out,
                                  stream=None):
-        """out = sum_i diags[i] * rotate(ct, steps[i]) with one shared ModUp
-        (diags: NTT-form plaintexts [n_local][N])."""
+        """out = sum_i diags[i] * rotate(ct, steps[i]) with one shared ModUp and
+        one ModDown.  diags[i]: NTT-form plaintext in the extended basis, one
+        word row per output limb of this rank: [Ql + alpha][N] (Q limbs, then
+        P limbs) on one GPU or in output aggregation, the owned Q limbs then the
+        owned P limbs in input broadcast."""
         n = len(steps)
         dp = (C.c_void_p * n)(*[self._ptr(t) for t in diags])
         st = (C.c_int * n)(*[int(s) for s in steps])
