@@ -168,6 +168,28 @@ class Evaluator:
     def apply_galois_inplace(self, ct: Ciphertext, galois_elt: int):
         self.ctx.apply_galois(ct.data, ct.coeff_modulus_size, galois_elt)
 
+    def rescale_to_next(self, ct: Ciphertext) -> Ciphertext:
+        """Phantom rescale_to_next (the reference's dist_rescale_to_next_inplace,
+        distributed_eval.cu:265-273): a new ciphertext one level down, scale
+        divided by the dropped prime."""
+        import torch
+        Ql = ct.coeff_modulus_size
+        n_out = self.ctx.n_local_limbs(Ql - 1) if self.ctx.world > 1 and \
+            self.ctx.mode == KS_MODE_INPUT_BROADCAST else Ql - 1
+        out = torch.empty((2, n_out, ct.poly_modulus_degree), dtype=torch.int64,
+                          device=ct.data.device)
+        self.ctx.rescale(ct.data[:2].contiguous(), Ql, out)
+        q_last = float(self.ctx.q[Ql - 1])
+        return Ciphertext(out, Ql - 1, ct.poly_modulus_degree, ct.scale / q_last)
+
+    def rotate_hoisted(self, ct: Ciphertext, steps: Sequence[int]) -> List[Ciphertext]:
+        """Rotations of one ciphertext by every step with one shared ModUp."""
+        import torch
+        outs = [torch.empty_like(ct.data[:2]) for _ in steps]
+        self.ctx.rotate_hoisted(ct.data[:2].contiguous(), ct.coeff_modulus_size, steps, outs)
+        return [Ciphertext(o, ct.coeff_modulus_size, ct.poly_modulus_degree, ct.scale)
+                for o in outs]
+
     def rotate_batch_inplace(self, cts: Sequence[Ciphertext], steps: Sequence[int]):
         if not cts:
             return

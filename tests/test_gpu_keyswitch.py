@@ -332,3 +332,30 @@ def test_key_upload_from_wire_blob(cuda_device):
     torch.cuda.synchronize()
     assert np.array_equal(d.cpu().numpy().view(np.uint64), o.apply_galois(ct, Ql, elt, key))
     ctx.close()
+
+
+def test_python_evaluator_rescale_and_hoisted(cuda_device):
+    """keyswitching.Evaluator (the reference-named Python API): rescale_to_next
+    and rotate_hoisted return the oracle's words and the right metadata."""
+    from comp390project_b200.keyswitching import Ciphertext, Evaluator
+    o = oracle_for("small")
+    ctx = _ctx(SMALL, max_batch=2)
+    s = o.secret(3, 64)
+    steps = [1, 4]
+    keys = {}
+    for st in steps:
+        e = o.galois_elt(st)
+        keys[st] = o.keygen_galois(s, e, 40 + st)
+        ctx.key_upload(1, e, keys[st])
+    Ql = o.L
+    z, ct = _encrypted(o, Ql, 12, s)
+    ev = Evaluator(ctx)
+    c = Ciphertext(_to_dev(ct), Ql, o.N, 2.0 ** 40)
+    r = ev.rescale_to_next(c)
+    assert r.coeff_modulus_size == Ql - 1 and r.scale == 2.0 ** 40 / float(o.moduli[Ql - 1])
+    assert np.array_equal(_to_host(r.data).reshape(2, Ql - 1, o.N), o.rescale(ct, Ql))
+    rots = ev.rotate_hoisted(c, steps)
+    want = o.rotate_hoisted(ct, Ql, [o.galois_elt(st) for st in steps], [keys[st] for st in steps])
+    for i, rc in enumerate(rots):
+        assert np.array_equal(_to_host(rc.data).reshape(2, Ql, o.N), want[i])
+    ctx.close()
