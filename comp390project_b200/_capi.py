@@ -109,6 +109,8 @@ SIGNATURES = {
     "ks_scatter_limbs": (_I, [_P, _P, _P, _I, _I, _P]),
     "ks_gather_limbs": (_I, [_P, _P, _P, _I, _I, _P]),
     "ks_allgather_limbs": (_I, [_P, _P, _P, _I, _P]),
+    "ks_scatter_ciphertext_to_gpu": (_I, [_P, _P, _SZ, _SZ, _SZ, _I, _I, _P]),
+    "ks_gather_ciphertext_from_gpu": (_I, [_P, _P, _SZ, _SZ, _SZ, _I, _I, _P]),
     "ks_last_launch_count": (_I, [_P]),
     "ks_total_launch_count": (C.c_longlong, [_P]),
     "ks_graph_capture_begin": (_I, [_P, _P]),

@@ -19,6 +19,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <new>
 #include <string>
@@ -133,6 +134,18 @@ T *upload(const std::vector<T> &v) {
 
 void up_ints(DevInts &t) { t.d = upload(t.h); }
 void up_i64(DevI64 &t) { t.d = upload(t.h); }
+
+// Temporary device buffer of a set-up call, freed on every exit path.
+template <class T>
+struct DevBuf {
+  T *p = nullptr;
+  explicit DevBuf(size_t n) : p(dev_alloc<T>(n)) {}
+  DevBuf(const DevBuf &) = delete;
+  DevBuf &operator=(const DevBuf &) = delete;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
 
 inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
@@ -721,6 +734,25 @@ KeyShard &key_alloc(Ctx &c, int kind, uint32_t elt) {
   return c.keys[id] = k;
 }
 
+// Unregisters and frees key (kind, elt) when the call that fills it fails
+// part-way (upload, generation or distribution), so no later key switch runs
+// on a half-written key.  dismiss() on success.
+struct KeyFillGuard {
+  Ctx &c;
+  unsigned long long id;
+  bool ok = false;
+  KeyFillGuard(Ctx &c_, int kind, uint32_t elt) : c(c_), id(key_id(kind, elt)) {}
+  void dismiss() { ok = true; }
+  ~KeyFillGuard() {
+    if (ok) return;
+    auto it = c.keys.find(id);
+    if (it == c.keys.end()) return;
+    cudaSetDevice(c.device);
+    cudaFree(it->second.d);  // cudaFree synchronises with the device before releasing
+    c.keys.erase(it);
+  }
+};
+
 const KeyShard &key_get(Ctx &c, int kind, uint32_t elt) {
   auto it = c.keys.find(key_id(kind, elt));
   if (it == c.keys.end())
@@ -773,14 +805,18 @@ void key_upload(Ctx &c, int kind, uint32_t elt, const u64 *src, size_t n_words, 
   KS_REQUIRE(n_words == full_key_words(c), "key size mismatch: expected " +
                                                std::to_string(full_key_words(c)) + " words");
   KS_CUDA(cudaSetDevice(c.device));
+  KeyFillGuard guard(c, kind, elt);
   KeyShard &k = key_alloc(c, kind, elt);
   extract_shard(c, c.rank, src, k.d,
                 from_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
   if (!from_dev) KS_CUDA(cudaStreamSynchronize(s));
+  guard.dismiss();
 }
 
 void check_alive(const Ctx &c);
 void watch_collective(Ctx &c, cudaStream_t s);
+template <class F>
+void enqueue_nccl(Ctx &c, ncclComm_t const &comm, cudaStream_t s, F &&call);
 
 // Key distribution: the root holds the full key in its device memory and
 // sends every rank its shard over NCCL point-to-point (the root packs each
@@ -790,57 +826,56 @@ void key_distribute(Ctx &c, int kind, uint32_t elt, const u64 *full_dev, int roo
                     cudaStream_t s) {
   KS_REQUIRE(root >= 0 && root < c.world, "root out of range");
   KS_CUDA(cudaSetDevice(c.device));
+  KeyFillGuard guard(c, kind, elt);
   if (c.world == 1) {
     KS_REQUIRE(full_dev != nullptr, "key pointer is null");
     KeyShard &k = key_alloc(c, kind, elt);
     extract_shard(c, 0, full_dev, k.d, cudaMemcpyDeviceToDevice, s);
     KS_CUDA(cudaStreamSynchronize(s));
+    guard.dismiss();
     return;
   }
   check_alive(c);
   KeyShard &k = key_alloc(c, kind, elt);
-  std::vector<u64 *> staging;
+  std::vector<std::unique_ptr<DevBuf<u64>>> staging(c.world);
   if (c.rank == root) {
     KS_REQUIRE(full_dev != nullptr, "the root needs the full key on its device");
     for (int g = 0; g < c.world; ++g) {
       if (g == root) {
         extract_shard(c, g, full_dev, k.d, cudaMemcpyDeviceToDevice, s);
-        staging.push_back(nullptr);
-      } else {
-        u64 *b = shard_words(c, g) ? dev_alloc<u64>(shard_words(c, g)) : nullptr;
-        if (b) extract_shard(c, g, full_dev, b, cudaMemcpyDeviceToDevice, s);
-        staging.push_back(b);
+      } else if (shard_words(c, g)) {
+        staging[g].reset(new DevBuf<u64>(shard_words(c, g)));
+        extract_shard(c, g, full_dev, staging[g]->p, cudaMemcpyDeviceToDevice, s);
       }
     }
   }
-  {
-    std::lock_guard<std::mutex> lk(c.nccl_mu);
-    KS_NCCL(ncclGroupStart());
+  enqueue_nccl(c, c.comm, s, [&](ncclComm_t cm) {
+    ncclResult_t r = ncclGroupStart();
+    if (r != ncclSuccess) return r;
     if (c.rank == root) {
-      for (int g = 0; g < c.world; ++g)
-        if (g != root && staging[g])
-          KS_NCCL(ncclSend(staging[g], shard_words(c, g), ncclUint64, g, c.comm, s));
+      for (int g = 0; g < c.world && r == ncclSuccess; ++g)
+        if (g != root && staging[g]) r = ncclSend(staging[g]->p, shard_words(c, g), ncclUint64, g, cm, s);
     } else if (shard_words(c, c.rank)) {
-      KS_NCCL(ncclRecv(k.d, shard_words(c, c.rank), ncclUint64, root, c.comm, s));
+      r = ncclRecv(k.d, shard_words(c, c.rank), ncclUint64, root, cm, s);
     }
-    KS_NCCL(ncclGroupEnd());
-  }
-  watch_collective(c, s);
-  const cudaError_t e = cudaStreamSynchronize(s);
-  for (u64 *b : staging)
-    if (b) cudaFree(b);
-  KS_CUDA(e);
+    const ncclResult_t r2 = ncclGroupEnd();
+    return r != ncclSuccess ? r : r2;
+  });
+  KS_CUDA(cudaStreamSynchronize(s));  // the staging buffers are freed after this
   check_alive(c);
+  guard.dismiss();
 }
 
 void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 seed,
                   cudaStream_t s) {
   KS_REQUIRE(sk_host != nullptr, "secret is null");
   KS_CUDA(cudaSetDevice(c.device));
+  KeyFillGuard guard(c, kind, elt);
   KeyShard &k = key_alloc(c, kind, elt);
   const int n = k.limbs, N = c.N;
   const NttTables T = c.tables();
-  int8_t *d_sk = dev_alloc<int8_t>(N);
+  DevBuf<int8_t> sk_buf(N);
+  int8_t *d_sk = sk_buf.p;
   KS_CUDA(cudaMemcpyAsync(d_sk, sk_host, N, cudaMemcpyHostToDevice, s));
   u64 *st = c.lanes[0].s_t;
   u64 *s_ntt = st, *snew = st + (size_t)n * N, *e = st + 2 * (size_t)n * N;
@@ -853,8 +888,10 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
   // per-slot constants
   std::vector<int> in_digit(n);
   std::vector<u64> pmodq(n);
-  u64 *d_pmq = dev_alloc<u64>(n);
-  int *d_in = dev_alloc<int>(n);
+  DevBuf<u64> pmq_buf(n);
+  DevBuf<int> in_buf(n);
+  u64 *d_pmq = pmq_buf.p;
+  int *d_in = in_buf.p;
   for (int sl = 0; sl < n; ++sl) {
     const int kj = c.own_key[sl];
     const u64 q = c.primes[kj];
@@ -880,9 +917,7 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
                          c.d_primes, c.log_n, s));
     KS_CUDA(cudaStreamSynchronize(s));  // flags buffer is reused per digit
   }
-  cudaFree(d_sk);
-  cudaFree(d_pmq);
-  cudaFree(d_in);
+  guard.dismiss();
 }
 
 // ---------------------------------------------------------------------------
@@ -944,14 +979,17 @@ struct StageTimer {
 // capture or with timeout_ms <= 0.
 void abort_comms(Ctx &c, const char *why) {
   std::lock_guard<std::mutex> g(c.nccl_mu);
-  if (c.aborted.exchange(true)) return;
+  if (c.aborted.load()) return;
+  // the message is written before the flag, and only here: check_alive reads
+  // it once the flag is set, never racing the calling thread's c.err
+  c.abort_msg = why;
+  c.aborted.store(true);
   for (size_t li = 0; li < c.lanes.size(); ++li) {
     if (c.lanes[li].comm && c.lanes[li].comm != c.comm) ncclCommAbort(c.lanes[li].comm);
     c.lanes[li].comm = nullptr;
   }
   if (c.comm) ncclCommAbort(c.comm);
   c.comm = nullptr;
-  c.err = why;
   set_global_err(why);
 }
 
@@ -1006,17 +1044,29 @@ void watch_collective(Ctx &c, cudaStream_t s) {
 
 void check_alive(const Ctx &c) {
   if (c.aborted.load())
-    throw KsError{KS_ERR_TIMEOUT, "context failed: " + c.err};
+    throw KsError{KS_ERR_TIMEOUT, "context failed: " + c.abort_msg};
 }
 
-void allgather(Ctx &c, ncclComm_t comm, const u64 *send, u64 *recv, size_t words,
-               cudaStream_t s) {
-  check_alive(c);
+// Enqueues one NCCL call on the communicator held in `comm` (a lane's or the
+// context's field).  The field is read under nccl_mu, the lock the watchdog
+// holds while it aborts and clears the communicators, after re-checking the
+// aborted flag: a communicator that ncclCommAbort has freed is never used.
+template <class F>
+void enqueue_nccl(Ctx &c, ncclComm_t const &comm, cudaStream_t s, F &&call) {
   {
     std::lock_guard<std::mutex> g(c.nccl_mu);
-    KS_NCCL(ncclAllGather(send, recv, words, ncclUint64, comm, s));
+    check_alive(c);
+    if (comm == nullptr) throw KsError{KS_ERR_TIMEOUT, "context failed: no communicator"};
+    KS_NCCL(call(comm));
   }
   watch_collective(c, s);
+}
+
+void allgather(Ctx &c, ncclComm_t const &comm, const u64 *send, u64 *recv, size_t words,
+               cudaStream_t s) {
+  enqueue_nccl(c, comm, s, [&](ncclComm_t cm) {
+    return ncclAllGather(send, recv, words, ncclUint64, cm, s);
+  });
 }
 
 // ---------------------------------------------------------------------------
@@ -1054,13 +1104,9 @@ void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, cudaStream_t s) {
   if (!c.oa()) return;
   {
     StageTimer tm(c, ST_COMM, s);
-    check_alive(c);
-    {
-      std::lock_guard<std::mutex> g(c.nccl_mu);
-      KS_NCCL(ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum,
-                            L.comm, s));
-    }
-    watch_collective(c, s);
+    enqueue_nccl(c, L.comm, s, [&](ncclComm_t cm) {
+      return ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum, cm, s);
+    });
   }
   KS_CUDA(mod_reduce(L.s_cx, 2 * lv.n_out, lv.cx_prime.d, c.d_primes, c.log_n, s));
   c.launches += 1;
@@ -1300,12 +1346,9 @@ void do_rescale(Ctx &c, Ctx::Lane &L, const u64 *ct, int Ql, u64 *out, cudaStrea
   }
   if (G > 1) {
     StageTimer tm(c, ST_COMM, s);
-    check_alive(c);
-    {
-      std::lock_guard<std::mutex> g(c.nccl_mu);
-      KS_NCCL(ncclBroadcast(buf, buf, 2 * N, ncclUint64, last % G, L.comm, s));
-    }
-    watch_collective(c, s);
+    enqueue_nccl(c, L.comm, s, [&](ncclComm_t cm) {
+      return ncclBroadcast(buf, buf, 2 * N, ncclUint64, last % G, cm, s);
+    });
   }
   {
     StageTimer tm(c, ST_MODDOWN_COLS, s);
@@ -1973,6 +2016,37 @@ int ks_gather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *global_buf
   });
 }
 
+int ks_scatter_ciphertext_to_gpu(const uint64_t *global_buf, uint64_t *local_buf, size_t n_polys,
+                                 size_t total_limbs, size_t degree, int gpu_id, int n_gpus,
+                                 void *stream) {
+  return guarded(nullptr, [&] {
+    KS_REQUIRE(n_gpus >= 1 && gpu_id >= 0 && gpu_id < n_gpus, "gpu_id out of range");
+    KS_REQUIRE(degree >= 1 && n_polys <= 65535 && total_limbs <= ((size_t)1 << 40),
+               "bad sizes");
+    if (n_local(gpu_id, n_gpus, (int)std::min<size_t>(total_limbs, 1u << 30)) == 0 || n_polys == 0)
+      return;
+    KS_REQUIRE(global_buf != nullptr && local_buf != nullptr, "null buffer");
+    KS_CUDA(partition_copy(global_buf, local_buf, (long long)n_polys, (long long)total_limbs,
+                           (long long)degree, gpu_id, n_gpus, true, (cudaStream_t)stream));
+  });
+}
+
+int ks_gather_ciphertext_from_gpu(const uint64_t *local_buf, uint64_t *global_buf, size_t n_polys,
+                                  size_t total_limbs, size_t degree, int gpu_id, int n_gpus,
+                                  void *stream) {
+  return guarded(nullptr, [&] {
+    KS_REQUIRE(n_gpus >= 1 && gpu_id >= 0 && gpu_id < n_gpus, "gpu_id out of range");
+    KS_REQUIRE(degree >= 1 && n_polys <= 65535 && total_limbs <= ((size_t)1 << 40),
+               "bad sizes");
+    if (n_local(gpu_id, n_gpus, (int)std::min<size_t>(total_limbs, 1u << 30)) == 0 || n_polys == 0)
+      return;
+    KS_REQUIRE(global_buf != nullptr && local_buf != nullptr, "null buffer");
+    KS_CUDA(partition_copy(global_buf, const_cast<uint64_t *>(local_buf), (long long)n_polys,
+                           (long long)total_limbs, (long long)degree, gpu_id, n_gpus, false,
+                           (cudaStream_t)stream));
+  });
+}
+
 int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_buf,
                        int total_limbs, void *stream) {
   if (!ctx) return KS_ERR_INVALID;
@@ -1989,7 +2063,8 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
       return;
     }
     // pad to ml limbs, gather rank-grouped, then reorder to limb order
-    u64 *send = dev_alloc<u64>(ml * N), *recv = dev_alloc<u64>(G * ml * N);
+    DevBuf<u64> send_buf(ml * N), recv_buf(G * ml * N);
+    u64 *send = send_buf.p, *recv = recv_buf.p;
     const int nl = n_local(c.rank, c.world, total_limbs);
     KS_CUDA(cudaMemsetAsync(send, 0, ml * N * 8, s));
     if (nl > 0) KS_CUDA(cudaMemcpyAsync(send, local_buf, nl * N * 8, cudaMemcpyDeviceToDevice, s));
@@ -1998,9 +2073,7 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
     for (int j = 0; j < total_limbs; ++j)
       KS_CUDA(cudaMemcpyAsync(full_buf + (size_t)j * N, recv + ((j % G) * ml + j / G) * N, N * 8,
                               cudaMemcpyDeviceToDevice, s));
-    KS_CUDA(cudaStreamSynchronize(s));
-    cudaFree(send);
-    cudaFree(recv);
+    KS_CUDA(cudaStreamSynchronize(s));  // before the staging buffers are freed
   });
 }
 
@@ -2086,22 +2159,25 @@ extern "C" int ks_apply_galois_noalloc(ks_ctx *ctx, uint64_t *ct, int level_limb
     KS_REQUIRE(c.alpha > 0, "context has no special primes (NTT-only context)");
     KS_REQUIRE(c.world == 1, "the allocation-free rotation serves single-GPU contexts only");
     KS_REQUIRE(!c.profile, "disable per-stage profiling before the allocation-free rotation");
-    if (c.arena_words > kNoAllocWords)
+    // the lane layout of the context's own arena, laid over the static array:
+    // automorphism output, coefficient input, extended digits, cx, z
+    const size_t N = c.N, nq = n_local(0, 1, c.L), ml = c.L;
+    const Level &top = c.levels[c.L];
+    const size_t w_t = std::max((size_t)top.beta * top.n_out * N, 3 * c.own_key.size() * N);
+    const size_t need = 2 * nq * N + ml * N + w_t + 2 * (size_t)top.n_out * N + 2 * nq * N;
+    if (need > kNoAllocWords)
       throw KsError{KS_ERR_UNSUPPORTED,
-                    "parameter set needs " + std::to_string(c.arena_words * 8) +
+                    "parameter set needs " + std::to_string(need * 8) +
                         " bytes of scratch; the allocation-free rotation holds at most " +
                         std::to_string(kNoAllocWords * 8)};
     KS_CUDA(cudaSetDevice(c.device));
     u64 *p = noalloc_base(c.device);
-    // the lane layout of the context's own arena, laid over the static array
-    const size_t N = c.N, nq = n_local(0, 1, c.L), ml = c.L;
-    const Level &top = c.levels[c.L];
     Ctx::Lane ln;
     ln.comm = nullptr;
     ln.s_g = p; p += 2 * nq * N;
     ln.s_coef = p; p += ml * N;
     ln.s_coef_all = ln.s_coef;
-    ln.s_t = p; p += std::max((size_t)top.beta * top.n_out * N, 3 * c.own_key.size() * N);
+    ln.s_t = p; p += w_t;
     ln.s_cx = p; p += 2 * (size_t)top.n_out * N;
     ln.s_ysend = ln.s_yall = p;
     ln.s_z = p;

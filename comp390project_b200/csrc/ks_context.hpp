@@ -153,6 +153,8 @@ struct Ctx {
   std::vector<cudaEvent_t> wd_free;
   std::thread wd_thread;
   std::atomic<bool> wd_stop{false}, aborted{false};
+  // written once by the watchdog, before `aborted` is set
+  std::string abort_msg;
   // diagnostics
   std::string err;
   // kernel launches of the last API call (reset by each call) and since the

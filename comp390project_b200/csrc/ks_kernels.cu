@@ -233,19 +233,28 @@ __global__ void k_add_ct(u64 *__restrict__ out, const u64 *__restrict__ x, int n
   *reinterpret_cast<ulonglong2 *>(out + off + k) = a;
 }
 
-__global__ void k_scatter(const u64 *__restrict__ gbuf, u64 *__restrict__ lbuf, int total,
-                          int n_local, int log_n, int g, int G, int to_local) {
-  const int N = 1 << log_n;
-  const int poly = blockIdx.z, loc = blockIdx.y;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
-  const long long glimb = (long long)loc * G + g;
-  if (glimb >= total) return;
-  ulonglong2 *gp = reinterpret_cast<ulonglong2 *>(const_cast<u64 *>(gbuf) +
-                                                  ((long long)poly * total + glimb) * N + k);
-  ulonglong2 *lp = reinterpret_cast<ulonglong2 *>(lbuf + ((long long)poly * n_local + loc) * N + k);
-  if (to_local) *lp = *gp;
-  else *gp = *lp;
+// Cyclic-partition copy between the global layout [poly][total][degree]
+// and rank g's local layout [poly][n_local][degree] (global limb loc*G + g at
+// local slot loc, loc < n_local); to_local picks the direction.  VEC: the
+// degree is even and both bases are 16-byte aligned, so every limb starts on
+// a 16-byte boundary and each thread moves one ulonglong2.
+template <bool VEC>
+__global__ void k_scatter(const u64 *__restrict__ gbuf, u64 *__restrict__ lbuf, long long total,
+                          long long n_local, long long degree, int g, int G, int to_local) {
+  const long long poly = blockIdx.z, loc = blockIdx.y;
+  const long long k = ((long long)blockIdx.x * kBlk + threadIdx.x) * (VEC ? 2 : 1);
+  if (k >= degree) return;
+  const long long glimb = loc * G + g;
+  u64 *gp = const_cast<u64 *>(gbuf) + (poly * total + glimb) * degree + k;
+  u64 *lp = lbuf + (poly * n_local + loc) * degree + k;
+  if (VEC) {
+    ulonglong2 *a = reinterpret_cast<ulonglong2 *>(gp), *b = reinterpret_cast<ulonglong2 *>(lp);
+    if (to_local) *b = *a;
+    else *a = *b;
+  } else {
+    if (to_local) *lp = *gp;
+    else *gp = *lp;
+  }
 }
 
 __global__ void k_keygen(u64 *key_b, u64 *key_a, const u64 *__restrict__ s_ntt,
@@ -381,23 +390,38 @@ cudaError_t add_ct(u64 *out, const u64 *x, int n_polys, int n_limbs, const int *
   return cudaGetLastError();
 }
 
+cudaError_t partition_copy(const u64 *global_buf, u64 *local_buf, long long n_polys,
+                           long long total_limbs, long long degree, int g, int G, bool to_local,
+                           cudaStream_t s) {
+  if (G < 1 || g < 0 || g >= G || n_polys < 0 || total_limbs < 0 || degree < 1)
+    return cudaErrorInvalidValue;
+  const long long n_local = g < total_limbs ? (total_limbs - g - 1) / G + 1 : 0;
+  if (n_local == 0 || n_polys == 0) return cudaSuccess;
+  if (n_local > 65535 || n_polys > 65535) return cudaErrorInvalidValue;
+  const bool vec = degree % 2 == 0 && ((uintptr_t)global_buf & 15) == 0 &&
+                   ((uintptr_t)local_buf & 15) == 0;
+  const long long per_thread = vec ? 2 : 1;
+  const long long bx = (degree / per_thread + kBlk - 1) / kBlk;
+  if (bx > 0x7fffffffLL) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)bx, (unsigned)n_local, (unsigned)n_polys);
+  if (vec)
+    k_scatter<true><<<grid, kBlk, 0, s>>>(global_buf, local_buf, total_limbs, n_local, degree, g,
+                                          G, to_local ? 1 : 0);
+  else
+    k_scatter<false><<<grid, kBlk, 0, s>>>(global_buf, local_buf, total_limbs, n_local, degree, g,
+                                           G, to_local ? 1 : 0);
+  return cudaGetLastError();
+}
+
 cudaError_t scatter_limbs(const u64 *global_buf, u64 *local_buf, int n_polys, int total_limbs,
                           int log_n, int g, int G, cudaStream_t s) {
-  const int n_local = g < total_limbs ? (total_limbs - g - 1) / G + 1 : 0;
-  if (n_local == 0 || n_polys == 0) return cudaSuccess;
-  dim3 grid(((1 << log_n) / 2 + kBlk - 1) / kBlk, n_local, n_polys);
-  k_scatter<<<grid, kBlk, 0, s>>>(global_buf, local_buf, total_limbs, n_local, log_n, g, G, 1);
-  return cudaGetLastError();
+  return partition_copy(global_buf, local_buf, n_polys, total_limbs, 1ll << log_n, g, G, true, s);
 }
 
 cudaError_t gather_limbs(const u64 *local_buf, u64 *global_buf, int n_polys, int total_limbs,
                          int log_n, int g, int G, cudaStream_t s) {
-  const int n_local = g < total_limbs ? (total_limbs - g - 1) / G + 1 : 0;
-  if (n_local == 0 || n_polys == 0) return cudaSuccess;
-  dim3 grid(((1 << log_n) / 2 + kBlk - 1) / kBlk, n_local, n_polys);
-  k_scatter<<<grid, kBlk, 0, s>>>(global_buf, const_cast<u64 *>(local_buf), total_limbs, n_local,
-                                  log_n, g, G, 0);
-  return cudaGetLastError();
+  return partition_copy(global_buf, const_cast<u64 *>(local_buf), n_polys, total_limbs,
+                        1ll << log_n, g, G, false, s);
 }
 
 cudaError_t keygen_digit(u64 *key_b, u64 *key_a, const u64 *s_ntt, const u64 *snew_ntt,

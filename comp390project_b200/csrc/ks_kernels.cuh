@@ -92,6 +92,11 @@ cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const Prim
 
 // Cyclic partition copies: global [poly][total][N] <-> local [poly][n_local][N]
 // for the limbs j = local*G + g (reference rns_partition.cu:26-80).
+// Cyclic-partition copy for rank g of G with an arbitrary degree (words per
+// limb): global [n_polys][total][degree] <-> local [n_polys][n_local][degree].
+cudaError_t partition_copy(const u64 *global_buf, u64 *local_buf, long long n_polys,
+                           long long total_limbs, long long degree, int g, int G, bool to_local,
+                           cudaStream_t s);
 cudaError_t scatter_limbs(const u64 *global_buf, u64 *local_buf, int n_polys, int total_limbs,
                           int log_n, int g, int G, cudaStream_t s);
 cudaError_t gather_limbs(const u64 *local_buf, u64 *global_buf, int n_polys, int total_limbs,

@@ -26,6 +26,11 @@
  *  - Streams are passed as `void *` holding a cudaStream_t (NULL = legacy
  *    default stream).  Calls are asynchronous on that stream.
  *  - One host thread drives one context; contexts are independent.
+ *  - Calls on one context must be stream-ordered: every call shares the
+ *    context's scratch (lane 0's arena is used by every call, and batched
+ *    calls fork their lanes from, and join them back into, the caller's
+ *    stream only).  Use one stream per context, or order calls made on
+ *    different streams with events; calls that overlap on the GPU race.
  *  - All device pointers must be 16-byte aligned.
  */
 #ifndef KS_CAPI_H
@@ -257,6 +262,17 @@ int ks_scatter_limbs(ks_ctx *ctx, const uint64_t *global_buf, uint64_t *local_bu
                      int n_polys, int total_limbs, void *stream);
 int ks_gather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *global_buf,
                     int n_polys, int total_limbs, void *stream);
+/* The same copies without a context, with the reference's own signature
+ * (scatter_ciphertext_to_gpu / gather_ciphertext_from_gpu,
+ * rns_partition.cuh:165-190): rank gpu_id of n_gpus, any degree (words per
+ * limb), both buffers on the current device.  A rank that owns no limb copies
+ * nothing (the reference returns early too). */
+int ks_scatter_ciphertext_to_gpu(const uint64_t *global_buf, uint64_t *local_buf, size_t n_polys,
+                                 size_t total_limbs, size_t degree, int gpu_id, int n_gpus,
+                                 void *stream);
+int ks_gather_ciphertext_from_gpu(const uint64_t *local_buf, uint64_t *global_buf, size_t n_polys,
+                                  size_t total_limbs, size_t degree, int gpu_id, int n_gpus,
+                                  void *stream);
 /* All-gather of local limbs [n_local][N] into sequential order [total][N]
  * on every rank (allgather_c2_limbs + reorder, input_broadcast.cu:45-111). */
 int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_buf,

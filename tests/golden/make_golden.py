@@ -81,7 +81,7 @@ def partition_ref():
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT", "/root/reference")
     with open(os.path.join(HERE, "prime_kat.json"), "w") as f:
         json.dump(prime_kat(ref), f, indent=1)
     with open(os.path.join(HERE, "partition_ref.json"), "w") as f:

@@ -96,3 +96,15 @@ def test_nccl_unique_id_needs_no_device():
     except _capi.KsError as e:  # NCCL bootstrap may be unavailable in a sandbox
         pytest.skip("NCCL bootstrap unavailable here: %s" % e)
     assert len(a) == _capi.KS_NCCL_ID_BYTES
+
+
+def test_partition_copy_argument_checks_without_a_gpu():
+    """The context-free partition copies reject a rank outside [0, n_gpus)
+    and return without any CUDA call for a rank that owns no limb."""
+    lib = _capi.load()
+    assert lib.ks_scatter_ciphertext_to_gpu(None, None, 1, 4, 8, 4, 4, None) == KS_ERR_INVALID
+    assert lib.ks_gather_ciphertext_from_gpu(None, None, 1, 4, 8, -1, 4, None) == KS_ERR_INVALID
+    assert lib.ks_scatter_ciphertext_to_gpu(None, None, 1, 4, 0, 0, 4, None) == KS_ERR_INVALID
+    # rank 3 of 8 owns no limb of a 3-limb ciphertext: nothing to copy
+    assert lib.ks_scatter_ciphertext_to_gpu(None, None, 2, 3, 8, 3, 8, None) == KS_OK
+    assert lib.ks_gather_ciphertext_from_gpu(None, None, 2, 3, 8, 3, 8, None) == KS_OK

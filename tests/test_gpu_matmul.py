@@ -160,3 +160,40 @@ def test_giant_parallel_two_gpus(cuda_device):
     from tests.procs import run_ranks
     res = run_ranks(_worker, world)
     assert len(res) == world and all(v is True for v in res.values()), res
+
+
+def test_bsgs_matmul_config3_ring_reduced_layer(cuda_device):
+    """The BSGS product on config 5's own ring (config 3: N = 2^16, Ql = 35,
+    alpha = 5, dnum = 7) with a reduced layer: 8192 tokens give F = 4
+    features per ciphertext, so d_in = d_out = 4 is one input and one output
+    ciphertext with B = G = 2 (one hoisted baby step, one giant step, four
+    diagonals).  Ciphertexts and diagonals are uniform residues; every output
+    word must equal the oracle's ork_bsgs_matmul."""
+    from comp390project_b200 import KS_KEY_GALOIS, KsContext, matmul
+    from tests.ksparams import CFG3, oracle_for, split
+    o = oracle_for("cfg3")
+    log_n, q, p = split(CFG3)
+    Ql, N = 35, o.N
+    lay = matmul.layout(N // 2, 8192, 4, 4, n_baby=2)
+    assert (lay.n_in, lay.n_out, lay.n_baby, lay.n_giant) == (1, 1, 2, 2)
+    s = o.secret(4, 192)
+    steps = lay.baby_steps() + lay.giant_steps()
+    keys = {st: o.keygen_galois(s, o.galois_elt(st), 700 + k) for k, st in enumerate(steps)}
+    rng = np.random.default_rng(44)
+    x = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
+                            for j in range(Ql)]) for _ in range(2)])
+    pts = [np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
+                     for j in range(Ql)]) for _ in range(lay.n_diagonals)]
+    want = o.bsgs_matmul([x], Ql, lay.unit, lay.n_baby, lay.n_giant, pts, keys)
+    ctx = KsContext(log_n, q, p, device=0, max_batch=2)
+    for st, k in keys.items():
+        ctx.key_upload(KS_KEY_GALOIS, ctx.galois_elt(st), k)
+    xd = _dev(x)
+    pd = [_dev(pt) for pt in pts]
+    ys = torch.zeros((1, 2, Ql, N), dtype=torch.int64, device="cuda")
+    work = torch.empty(ctx.bsgs_workspace_words(Ql, 1, lay.n_baby), dtype=torch.int64,
+                       device="cuda")
+    ctx.bsgs_matmul([xd], Ql, lay.unit, lay.n_baby, lay.n_giant, pd, [ys[0]], work)
+    torch.cuda.synchronize()
+    assert np.array_equal(_host(ys), want), "config-3 ring BSGS product differs from the oracle"
+    ctx.close()

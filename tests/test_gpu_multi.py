@@ -121,6 +121,17 @@ def _worker(rank, world, port, q, name, mode):
         torch.cuda.synchronize()
         want3 = o.rescale(cts[1], Ql)[:, mine3]
         ok &= np.array_equal(out3.cpu().numpy().view(np.uint64), want3)
+        # ks_allgather_limbs: every rank ends with the limbs in sequential
+        # order, as allgather_c2_limbs + reorder_gathered_to_sequential give
+        # (input_broadcast.cu:45-111); a rank without limbs still joins
+        seq = cts[0][1]
+        mine_ag = list(range(rank, Ql, world))
+        loc = (torch.from_numpy(np.ascontiguousarray(seq[mine_ag]).view(np.int64)).cuda()
+               if mine_ag else torch.zeros(2, dtype=torch.int64, device="cuda"))
+        full_ag = torch.zeros((Ql, N), dtype=torch.int64, device="cuda")
+        ctx.allgather_limbs(loc, full_ag, Ql)
+        torch.cuda.synchronize()
+        ok &= np.array_equal(full_ag.cpu().numpy().view(np.uint64), seq)
         ctx.close()
         q.put((rank, bool(ok)))
     except Exception as e:

@@ -40,9 +40,14 @@ def test_noalloc_rotation_matches_apply_galois_twice(name, cfg, Ql, cuda_device)
         a = torch.from_numpy(ct.view(np.int64).copy()).cuda()
         b = a.clone()
         stream = torch.cuda.current_stream().cuda_stream
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
         rc = lib.ks_apply_galois_noalloc(ctx.h, C.c_void_p(a.data_ptr()), Ql, elt,
                                          C.c_void_p(stream))
         assert rc == 0, _capi.last_error(ctx.h)
+        torch.cuda.synchronize()
+        if call > 0:  # after the first call has set up the device address
+            assert torch.cuda.mem_get_info()[0] == free0, "the call allocated device memory"
         rc = lib.ks_apply_galois(ctx.h, C.c_void_p(b.data_ptr()), Ql, elt, C.c_void_p(stream))
         assert rc == 0, _capi.last_error(ctx.h)
         torch.cuda.synchronize()
