@@ -39,6 +39,8 @@ SCALE = 2.0 ** 40
 METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
 # DRAM bytes per launch (read + write) of each key-switch kernel at config 3,
 # one key switch, from `ncu --set full` (profiles/keyswitch_config3_kernels.md).
+PROFILED_TRAFFIC_SOURCE = ("constant from one ncu capture (profiles/keyswitch_config3_kernels.md), "
+                           "not measured in this run")
 PROFILED_TRAFFIC = {
     "galois": 38.1e6, "intt_input": 55.7e6, "modup_cols": 98.2e6, "modup_rows_ip": 504.8e6,
     "intt_p": 15.9e6, "moddown_cols": 5.4e6, "moddown_rows": 140.2e6,
@@ -63,28 +65,37 @@ def parse():
                          "hoisted: config-4 hoisted linear transform; matmul: config-5 "
                          "BSGS matmul layer")
     ap.add_argument("--ntt-polys", type=int, default=128)
+    ap.add_argument("--no-ntt", action="store_true",
+                    help="leave the config-2 NTT record out of the default line")
     return ap.parse_args()
 
 
 # ---------------------------------------------------------------------------
 # Config 2: standalone batched forward + inverse NTT
 # ---------------------------------------------------------------------------
-def run_ntt(args, rank, world):
-    """128 polynomials x 36 limbs (one 58-bit + 35 x 42-bit primes, all 1 mod
-    2^17), N = 2^16, forward then inverse.  Limbs are sharded cyclically over
-    ranks (weak in nothing: total work fixed, strong scaling)."""
+NTT_QBITS = [58] + [42] * 35  # config 2: one 58-bit + 35 x 42-bit primes, all 1 mod 2^17
+NTT_METRIC = "NTT-coefficients/s (config 2, forward+inverse)"
+
+
+def ntt_measure(polys, steps, warmup, rank, world, clocks=None):
+    """Config 2 on this rank: 128 polynomials x 36 limbs (one 58-bit + 35 x
+    42-bit primes, all 1 mod 2^17), N = 2^16, coefficients uniform in
+    [0, q_i) from seed 1, batched forward then inverse transform, limbs
+    sharded cyclically over the ranks (strong scaling).  Returns the timing
+    record (max over ranks): NTT-coefficients/s of both directions over all
+    ranks, and the forward transform's HBM roofline (each limb read and
+    written once per direction: 16 N bytes)."""
     import torch
     import torch.distributed as dist
     from comp390project_b200 import KsContext, gen_primes
 
-    dev = int(os.environ.get("LOCAL_RANK", 0))
-    torch.cuda.set_device(dev)
-    q = gen_primes(LOG_N, [58] + [42] * 35)
+    dev = torch.cuda.current_device()
+    q = gen_primes(LOG_N, NTT_QBITS)
     nl = len(range(rank, len(q), world))
     own = [q[j] for j in range(rank, len(q), world)]
     ctx = KsContext(LOG_N, own, [], device=dev)
     N = 1 << LOG_N
-    P = args.ntt_polys
+    P = polys
     g = torch.Generator(device="cuda")
     g.manual_seed(1 + rank)
     data = torch.empty((P, nl, N), dtype=torch.int64, device="cuda")
@@ -92,19 +103,19 @@ def run_ntt(args, rank, world):
         data[:, sl, :] = torch.randint(0, int(own[sl]), (P, N), generator=g, device="cuda",
                                        dtype=torch.int64)
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ctx.ntt_forward(data, nl, 0, P)
         ctx.ntt_inverse(data, nl, 0, P)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(dev)
-    clocks.start()
-    time.sleep(0.3)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+    if clocks is not None:
+        clocks.start()
+        time.sleep(0.3)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps + 1)]
     evs[0].record(stream)
     launches = 0
-    for i in range(args.steps):
+    for i in range(steps):
         ctx.ntt_forward(data, nl, 0, P)
         launches += ctx.last_launch_count()
         evs[2 * i + 1].record(stream)
@@ -112,36 +123,61 @@ def run_ntt(args, rank, world):
         launches += ctx.last_launch_count()
         evs[2 * i + 2].record(stream)
     torch.cuda.synchronize()
-    clocks.stop()
-    fwd = sum(evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(args.steps))
-    inv = sum(evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(args.steps))
+    if clocks is not None:
+        clocks.stop()
+    fwd = sum(evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(steps))
+    inv = sum(evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(steps))
     ms = fwd + inv
     if world > 1:
-        t = torch.tensor([ms], device="cuda")
+        t = torch.tensor([ms, fwd, inv], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    coeffs = 2 * P * len(q) * N * args.steps  # both directions, all ranks
+        ms, fwd, inv = (float(x) for x in t.tolist())
+    coeffs = 2 * P * len(q) * N * steps  # both directions, all ranks
     peak, peak_kind = measured_peaks()
     alg_per_launch = P * nl * 16 * N  # one direction on this rank
-    f_ms = fwd / args.steps
+    f_ms, i_ms = fwd / steps, inv / steps
     achieved = alg_per_launch / (f_ms / 1000.0) / 1e9
+    achieved_inv = alg_per_launch / (i_ms / 1000.0) / 1e9
+    # pipe bound of the FP64 path: 8 FP64 instructions per butterfly, 64 FP64
+    # lanes per SM (N/2 log N butterflies per limb transform)
+    bfly = P * nl * (N // 2) * LOG_N
+    ctx.close()
+    del data
+    return {
+        "metric": NTT_METRIC, "value": coeffs / (ms / 1000), "unit": "coefficients/s",
+        "ms_per_step": ms / steps, "steps": steps, "warmup": warmup, "launches": launches,
+        "config": {"workload": "config2-ntt: %d polys x 36 limbs x 2^16" % P,
+                   "parallelism": "limb-sharded x%d" % world,
+                   "l2": "%.2f GB resident per rank, exceeds L2; no flush"
+                         % (P * nl * N * 8 / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "ntt_forward (column + row pass)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                     "launch_ms": f_ms, "inverse_ms": i_ms,
+                     "inverse_achieved": achieved_inv, "inverse_frac": achieved_inv / peak,
+                     "butterflies_per_launch": bfly,
+                     "two_pass_cap": 0.5,
+                     "note": "two HBM passes per direction: the algorithmic bytes count each "
+                             "limb once, so a two-pass transform is capped at frac 0.5"},
+    }
+
+
+def run_ntt(args, rank, world):
+    """--workload ntt: config 2 as its own bench line."""
+    import torch
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(dev)
+    clocks = ClockSampler(dev)
+    rec = ntt_measure(args.ntt_polys, args.steps, args.warmup, rank, world, clocks)
     if rank == 0:
         line = {
-            "metric": "NTT-coefficients/s (config 2, forward+inverse)", "value": coeffs / (ms / 1000),
-            "unit": "coefficients/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-            "config": {"workload": "config2-ntt: %d polys x 36 limbs x 2^16" % P,
-                       "parallelism": "limb-sharded x%d" % world,
-                       "l2": "%.2f GB resident, exceeds L2; no flush" % (data.numel() * 8 / 1e9)},
-            "roofline": {"bound": "hbm", "kernel": "ntt_forward (column + row pass)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                         "launch_ms": f_ms, "inverse_ms": inv / args.steps},
-            "gpu_launches": launches, "clocks": clocks.summary(),
+            "metric": rec["metric"], "value": rec["value"], "unit": rec["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic", "config": rec["config"], "roofline": rec["roofline"],
+            "gpu_launches": rec["launches"], "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    ctx.close()
 
 
 # ---------------------------------------------------------------------------
@@ -211,6 +247,46 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def host_copy_probe(host_buf, dev_buf, rank, world, reps=2):
+    """Host-side copy limit of this rank while every rank copies at once: the
+    whole pinned host buffer to the device on one stream and the device
+    buffer back to (the same) host memory on another, concurrently, as the
+    end-to-end path's lanes do; GB/s per direction, max time over ranks."""
+    import torch
+    import torch.distributed as dist
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    nbytes = host_buf.numel() * host_buf.element_size()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e_in, e_out = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
+    scratch = torch.empty_like(dev_buf)
+    for _ in range(reps):
+        with torch.cuda.stream(s_in):
+            scratch.copy_(host_buf, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            host_buf.copy_(dev_buf, non_blocking=True)
+    e_in.record(s_in)
+    e_out.record(s_out)
+    torch.cuda.synchronize()
+    t_in, t_out = e0.elapsed_time(e_in), e0.elapsed_time(e_out)
+    if world > 1:
+        t = torch.tensor([t_in, t_out], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_in, t_out = (float(x) for x in t.tolist())
+    del scratch
+    return {"h2d_gbs": reps * nbytes / (t_in / 1000) / 1e9,
+            "d2h_gbs": reps * nbytes / (t_out / 1000) / 1e9,
+            "bytes_per_direction": reps * nbytes,
+            "note": "pure pinned-memory copies, both directions at once on every rank, no "
+                    "compute: the host-side limit of this rank's end-to-end path"}
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle port running the identical rotation key switch
 # ---------------------------------------------------------------------------
@@ -275,6 +351,7 @@ def cpu_baseline_config3():
 # Per-direction NVLink bandwidth of a peer copy measured on this pool's B200s
 # (900 GB/s nominal per direction per GPU).
 NVLINK_GBS = 770.0
+NVLINK_NOMINAL_GBS = 900.0  # NVLink 5, per direction per GPU
 
 
 def collective_roofline(prof, n_ks, L, alpha, world, N):
@@ -293,7 +370,9 @@ def collective_roofline(prof, n_ks, L, alpha, world, N):
     return {"bound": "nvlink", "bytes_received_per_ks": recv, "ms_per_ks": ms / n_ks,
             "calls_per_ks": calls / n_ks, "achieved": ach, "peak": NVLINK_GBS, "unit": "GB/s",
             "frac": ach / NVLINK_GBS,
-            "peak_kind": "measured peer copy per direction (serial collectives, latency included)"}
+            "peak_kind": "this pool's measured peer copy per direction (serial collectives, "
+                         "latency included)",
+            "peak_nominal": NVLINK_NOMINAL_GBS, "frac_nominal": ach / NVLINK_NOMINAL_GBS}
 
 
 # ---------------------------------------------------------------------------
@@ -798,10 +877,11 @@ def run_ours(args, rank, world):
     total_ks = B * args.steps
     value = total_ks / (ms / 1000.0)
 
-    # dominant stage and its roofline (two-pass NTT counted as one transform)
+    # dominant compute stage and its roofline (two-pass NTT counted as one
+    # transform); the collectives have their own NVLink roofline below
     stages = {k: v for k, v in prof.items() if v[1] > 0}
     prof_ks = n_prof
-    dom = max(stages, key=lambda k: stages[k][0])
+    dom = max((k for k in stages if k != "collective"), key=lambda k: stages[k][0])
     per_launch_ms = stages[dom][0] / stages[dom][1]
     QlP = L + len(p)
     beta = 7
@@ -825,8 +905,10 @@ def run_ours(args, rank, world):
     }
     peak, peak_kind = measured_peaks()
     achieved = alg[dom] / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
-    # DRAM traffic per launch of the dominant kernel from one ncu capture
-    # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/keyswitch_config3_kernels.md)
+    # DRAM traffic per launch of the dominant kernel: not measurable without a
+    # profiler, so it is the constant of one ncu capture of the same kernel at
+    # the same workload (dram__bytes_read.sum + dram__bytes_write.sum), named
+    # in traffic_source; one GPU only (the capture is of the one-GPU launch)
     traffic = PROFILED_TRAFFIC.get(dom) if world == 1 else None
 
     # end to end through the C ABI with host buffers: ks_rotate_batch_host on
@@ -854,12 +936,18 @@ def run_ours(args, rank, world):
             ems = float(t.item())
         nbytes = host_in.numel() * 8
         e2e = {"value": B * args.e2e_steps / (ems / 1000.0), "unit": "key-switches/s",
-               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes}
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+               "host_copy": host_copy_probe(host_in, cts, rank, world)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_config3()
     nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N)
+    # the second half of the headline metric: config 2's NTT on the same GPUs
+    # (every rank, after the key-switch measurements)
+    ntt = None
+    if not args.no_ntt:
+        ntt = ntt_measure(args.ntt_polys, max(3, args.steps // 2), 3, rank, world)
 
     if rank == 0:
         line = {
@@ -875,9 +963,11 @@ def run_ours(args, rank, world):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                          "traffic": traffic, "peak_kind": peak_kind,
+                         "traffic_source": (PROFILED_TRAFFIC_SOURCE if traffic else None),
                          "alg_bytes": alg.get(dom),
-                         "launch_ms": per_launch_ms},
+                         "launch_ms": per_launch_ms, "per_rank": world > 1},
             "collectives": nvlink,
+            "ntt": ntt,
             "stages_ms_per_ks_serial": {k: v[0] / prof_ks for k, v in stages.items()},
             "cpu_baseline": cpu,
             "e2e": e2e,
