@@ -16,8 +16,8 @@
 // epilogue is coalesced.
 #include "ks_fused.cuh"
 #include "ks_galois.cuh"
+#include "ks_launch.cuh"
 #include "ks_ntt_impl.cuh"
-#include "ks_tmem.cuh"
 
 namespace ksb {
 namespace {
@@ -190,47 +190,134 @@ __device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool r
 // ---------------------------------------------------------------------------
 // ModUp row pass fused with the evaluation-key inner product
 // ---------------------------------------------------------------------------
-// One CTA: one 4096-word tile of one output limb s (prime m_j), all digits.
-// For each digit d the tile of t[d][s] gets its row pass in registers (the
-// digit that contains q_j instead reads the NTT-form input limb), goes
-// through shared memory into a warp-coalesced order (warp w owns tile words
-// [512w, 512w + 512), lane l the pairs 2l + 64i, i < 8), and is multiplied
-// into the two accumulators against the key limbs of digit d:
+// One CTA: one kBipTile-word tile of one output limb s (prime m_j), all
+// digits of the key shard.  Per digit the CTA's inputs are three contiguous
+// 16 KB blocks -- the tile of t[d][s] (column pass done; for the digit that
+// holds q_j, the aligned source tile of the NTT-form input instead), and the
+// tiles of the two key polys -- which one thread moves into shared memory
+// with cp.async.bulk (the bulk-copy engine, completion counted in bytes on an
+// mbarrier).  Two stages alternate: the copies of digit d + 1 run while digit
+// d computes, so the HBM latency is hidden by the copy engine rather than by
+// resident warps.  Per digit the tile gets its row pass (the second pass of
+// the forward NTT) in registers with the exchange done in place in the stage
+// buffer, swizzled so that both access patterns are free of bank conflicts,
+// and is multiplied into the two accumulators:
 //   cx[0][s] = sum_d t[d][s] * key[d][0][j],   cx[1][s] = sum_d t[d][s] * key[d][1][j].
-// The key pairs of a lane are copied into shared memory with cp.async when
-// the digit starts, so they arrive while the butterflies run; the next
-// digit's value tile is prefetched into L2.  The 32 accumulators of a
-// thread live in TMEM (64 columns: poly 0 in [0, 32), poly 1 in [32, 64),
-// one u64 as two columns), not in registers.  The extended limbs never
-// return to HBM.
+// The 32 accumulators of a thread (two polys x 16 words) stay in registers:
+// shared memory limits the SM to two CTAs, so registers are plentiful.
 struct RowsIpArgs {
   const u64 *t, *c_ntt, *key;
   u64 *cx;
   int key_limbs;
   uint32_t elt;  // c_ntt is read through X -> X^elt (1: as it is)
+  int *status;   // device status word: kDevTimeout when a copy never completed
 };
 
-// A CTA is kRipWarps warps; warp w owns the 512 tile words [512w, 512w + 512)
-// (32 / TT rows of M words).  Smaller CTAs than the NTT kernels' 8 warps
-// shorten the wave tail of this long-running kernel.
-constexpr int kRipWarps = 4;
-constexpr int kRipThreads = kRipWarps * 32;
-constexpr int kRipTile = kRipWarps * 512;
+constexpr int kBipWarps = 4;
+constexpr int kBipThreads = kBipWarps * 32;
+constexpr int kBipTile = kBipWarps * 512;       // words of one CTA tile
+constexpr int kBipBlockBytes = kBipTile * 8;    // one 16 KB block
+constexpr int kBipStageWords = 3 * kBipTile;    // t, key poly 0, key poly 1
+constexpr size_t kBipSmemBytes = 2 * (size_t)kBipStageWords * 8;  // two stages: 96 KB
 
-template <int LOG_M>
-__host__ __device__ constexpr int rows_ip_rows() {  // rows of M words per CTA
-  return kRipTile >> LOG_M;
+// Physical position of row-local word i of a row in the exchange: i with its
+// 16-word group index XORed into its low four bits.  Thread t's 16 words
+// {16e + t} (first round) and {16t + e} (second round) then fall in 16
+// different bank groups, and the warp's pair reads cover whole segments.
+__device__ __forceinline__ int bip_swz(int i) { return i ^ ((i >> 4) & 15); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
 }
-template <int LOG_M>
-__host__ __device__ constexpr size_t rows_ip_smem_bytes() {
-  // padded exchange rows + per-warp key stage [warps][2 polys][8 pairs][32 lanes] x 16 B
-  return (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16) * 8 +
-         (size_t)kRipWarps * 2 * 8 * 32 * 16;
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits for the phase of the given parity, at most limit_ns; false on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > limit_ns) return false;
+  return true;
+}
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// this GPU's global memory into this CTA's shared memory, counted on bar.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+// Row pass of the tile in the stage buffer tb (rows of M words, row-major as
+// the bulk copy left them), thread (rr, t); the result stays in tb at the
+// swizzled positions (rr M + bip_swz(i)).  FP: the values are the bits of
+// doubles, |x| < 12q; integer: canonical.
+template <int LOG_M, bool FP, bool LAZY>
+__device__ __forceinline__ void bip_row_pass(u64 *tb, int t, int rr, long long row,
+                                             const NttTables &T, int prime, const PrimeDev &P) {
+  using G = RowGeom<LOG_M>;
+  u64 *rb = tb + (rr << LOG_M);
+  const int log_n = T.log_n, N = 1 << log_n;
+  if (FP) {
+    const TwRowsGlobal<LOG_M> tw{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
+    double x[kEpt];
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) x[e] = as_fp(rb[lidx<LOG_M, G::HI, 4>(t, e)]);
+    fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, tw, P.qd, P.qinv);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, G::HI, 4>(t, e))] = fp_bits(x[e]);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) x[e] = as_fp(rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))]);
+    fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, tw, P.qd, P.qinv);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))] = fp_bits(x[e]);
+  } else {
+    const ulonglong2 *tw = T.fwd + (long long)prime * N;
+    u64 x[kEpt];
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) x[e] = rb[lidx<LOG_M, G::HI, 4>(t, e)];
+    fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, G::HI, 4>(t, e))] = x[e];
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) x[e] = rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))];
+    fwd_round<LOG_M, 0, G::NLO, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e) {
+      const u64 v = LAZY ? reduce_full(x[e], P.q, P.mu) : reduce4(x[e], P.q, P.two_q);
+      rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))] = v;
+    }
+  }
+  __syncwarp();
 }
 
 // FP: prime below kFpBound (FP64 butterflies); else LAZY selects the
@@ -238,177 +325,139 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 template <int LOG_M, bool FP, bool LAZY>
 __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
                                              const KsLayout &lay, const NttTables &T, int s,
-                                             int prime, u64 *sm, ulonglong2 *kst, uint32_t tacc) {
+                                             int prime, u64 *stages, uint64_t *bars) {
   using G = RowGeom<LOG_M>;
+  constexpr int M = 1 << LOG_M;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
   const int j = lay.out_j[s];
   const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long tile0 = (long long)blockIdx.x * kRipTile;
-  const long long row = (long long)blockIdx.x * rows_ip_rows<LOG_M>() + rr;
-  const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's pairs in the tile
+  const long long tile0 = (long long)blockIdx.x * kBipTile;
+  const long long row = (tile0 >> LOG_M) + rr;
+  const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's word pairs in the tile
   const int dj = j < mu.Ql ? j / mu.alpha : -1;
   const long long kstride = (long long)A.key_limbs * N;
-  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0 + wofs;
+  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0;
   const u64 *tbase = A.t + (long long)s * N + tile0;
   const long long tstride = (long long)lay.n_out * N;
-  // own-digit limb, read through the automorphism: the CTA's tile gathers
-  // from the aligned source tile cown, pair (k, k+1) from (src & ~1) (swapped
-  // when src is odd)
-  const u64 *climb = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N : nullptr;
-  const u64 *cown =
-      climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
-            : nullptr;
-  const ulonglong2 *tw = T.fwd + (long long)prime * N;
-  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
-  kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
-  // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
-  // over the CTA's threads.
-  auto prefetch = [&](int d) {
-    const u64 *v = d == dj ? cown : tbase + d * tstride;
-#pragma unroll
-    for (int line = threadIdx.x * 16; line < kRipTile; line += kRipThreads * 16)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(v + line));
-  };
+  // own-digit limb, read through the automorphism: the tile gathers from one
+  // aligned source tile of the same size
+  const u64 *cown = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N +
+                                  (galois_src((uint32_t)tile0, A.elt, log_n) &
+                                   ~(uint32_t)(kBipTile - 1))
+                            : nullptr;
   const int n_dig = lay.n_digits;
-  prefetch(__ldg(&lay.digits[0]));
+  auto issue = [&](int di) {  // thread 0: the three blocks of digit di -> stage di & 1
+    const int d = __ldg(&lay.digits[di]);
+    u64 *st = stages + (di & 1) * kBipStageWords;
+    uint64_t *bar = bars + (di & 1);
+    const u64 *kb = kbase + (long long)(2 * di) * kstride;
+    mbar_expect_tx(bar, 3 * kBipBlockBytes);
+    bulk_g2s(st, d == dj ? cown : tbase + d * tstride, kBipBlockBytes, bar);
+    bulk_g2s(st + kBipTile, kb, kBipBlockBytes, bar);
+    bulk_g2s(st + 2 * kBipTile, kb + kstride, kBipBlockBytes, bar);
+  };
+  if (threadIdx.x == 0) {
+    issue(0);
+    if (n_dig > 1) issue(1);
+  }
+  u64 acc0[kEpt], acc1[kEpt];
+  bool failed = false;
+  int stalled = 0;
 #pragma unroll 1
   for (int di = 0; di < n_dig; ++di) {
-    const int d = __ldg(&lay.digits[di]);  // digit di of the key shard
+    u64 *st = stages + (di & 1) * kBipStageWords;
+    const bool ok = mbar_wait_bounded(bars + (di & 1), (di >> 1) & 1, 1000000000ull);
+    if (__syncthreads_or(!ok)) {  // a copy never completed: give up uniformly
+      failed = true;
+      stalled = di;
+      break;
+    }
+    const int d = __ldg(&lay.digits[di]);
     const bool own = d == dj;
-    {
-      const u64 *kb = kbase + (long long)(2 * di) * kstride;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        cp_async16(kst + i * 32, kb + 64 * i);
-        cp_async16(kst + (8 + i) * 32, kb + kstride + 64 * i);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    if (di + 1 < n_dig) prefetch(__ldg(&lay.digits[di + 1]));
-    if (!own) {
-      u64 x[kEpt];
-      const u64 *tile = tbase + d * tstride;
-      if (FP) fwd_rows_regs_fp_tw<LOG_M, false>(x, sm, twf, tile, tt, rr, row, P);
-      else fwd_rows_regs<LOG_M, LAZY>(x, sm, tile, tt, rr, row, log_n, tw, P);
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(tt, e))] = x[e];
-      __syncwarp();
-    }
-    cp_async_wait_all();  // this lane's own key pairs
+    if (!own) bip_row_pass<LOG_M, FP, LAZY>(st, tt, rr, row, T, prime, P);
+    const u64 *k0b = st + kBipTile, *k1b = st + 2 * kBipTile;
     const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      u64 y[4];
-      ulonglong2 k0[2], k1[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int i = 2 * h + q;
-        k0[q] = kst[i * 32];
-        k1[q] = kst[(8 + i) * 32];
-        if (own) {
-          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), A.elt, log_n);
-          ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
-          if (src & 1u) {
-            const u64 tmp = v.x;
-            v.x = v.y;
-            v.y = tmp;
-          }
-          y[2 * q] = FP ? fp_bits(u64_to_fp(v.x)) : v.x;
-          y[2 * q + 1] = FP ? fp_bits(u64_to_fp(v.y)) : v.y;
-        } else {
-          const int w = wofs + 64 * i;
-          const int a = padx<LOG_M>(w >> LOG_M, w & (G::M - 1));  // pair's second word: a + 1
-          y[2 * q] = sm[a];
-          y[2 * q + 1] = sm[a + 1];
+    for (int i = 0; i < 8; ++i) {
+      const int w = wofs + 64 * i;  // even tile word
+      u64 y0, y1;
+      if (own) {
+        const uint32_t src =
+            galois_src((uint32_t)(tile0 + w), A.elt, log_n) & (uint32_t)(kBipTile - 1);
+        const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(st + (src & ~1u));
+        y0 = (src & 1u) ? v.y : v.x;
+        y1 = (src & 1u) ? v.x : v.y;
+        if (FP) {
+          y0 = fp_bits(u64_to_fp(y0));
+          y1 = fp_bits(u64_to_fp(y1));
         }
+      } else {
+        const int c = w & (M - 1), x = (c >> 4) & 15;
+        const ulonglong2 v =
+            *reinterpret_cast<const ulonglong2 *>(st + (w - c) + ((c ^ x) & ~1));
+        y0 = (x & 1) ? v.y : v.x;
+        y1 = (x & 1) ? v.x : v.y;
       }
-      uint32_t r0[8], r1[8];
-      if (!first) {
-        tmem::ld8(tacc + 8 * h, r0);
-        tmem::ld8(tacc + 32 + 8 * h, r1);
-        tmem::wait_ld(r0, r1);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const u64 b = (u & 1) ? k0[u >> 1].y : k0[u >> 1].x;
-        const u64 a = (u & 1) ? k1[u >> 1].y : k1[u >> 1].x;
-        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], b, first, recentre, P);
-        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], a, first, recentre, P);
-        r0[2 * u] = (uint32_t)v0;
-        r0[2 * u + 1] = (uint32_t)(v0 >> 32);
-        r1[2 * u] = (uint32_t)v1;
-        r1[2 * u + 1] = (uint32_t)(v1 >> 32);
-      }
-      tmem::st8(tacc + 8 * h, r0);
-      tmem::st8(tacc + 32 + 8 * h, r1);
+      const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(k0b + w);
+      const ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(k1b + w);
+      acc0[2 * i] = ip_term<FP>(acc0[2 * i], y0, b.x, first, recentre, P);
+      acc0[2 * i + 1] = ip_term<FP>(acc0[2 * i + 1], y1, b.y, first, recentre, P);
+      acc1[2 * i] = ip_term<FP>(acc1[2 * i], y0, a.x, first, recentre, P);
+      acc1[2 * i + 1] = ip_term<FP>(acc1[2 * i + 1], y1, a.y, first, recentre, P);
     }
-    tmem::wait_st();
-    __syncwarp();  // exchange buffer and key stage are reused by the next digit
+    // every thread's generic accesses to this stage precede the next bulk
+    // copy into it (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0 && di + 2 < n_dig) issue(di + 2);
+  }
+  if (failed) {
+    if (threadIdx.x == 0) {
+      atomicExch(A.status, kDevTimeout);
+      // wait (bounded) for the copies still in flight before the CTA exits:
+      // those of the digit that timed out and of the one after it
+      const int di = stalled;
+      mbar_wait_bounded(bars + (di & 1), (di >> 1) & 1, 1000000000ull);
+      if (di + 1 < n_dig) mbar_wait_bounded(bars + ((di + 1) & 1), ((di + 1) >> 1) & 1, 1000000000ull);
+    }
+    __syncthreads();
+    return;
   }
   u64 *o0 = A.cx + (long long)s * N + tile0 + wofs;
   u64 *o1 = o0 + (long long)lay.n_out * N;
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    uint32_t r0[8], r1[8];
-    tmem::ld8(tacc + 8 * h, r0);
-    tmem::ld8(tacc + 32 + 8 * h, r1);
-    tmem::wait_ld(r0, r1);
-    u64 v0[4], v1[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      v0[u] = tmem::pack(r0[2 * u], r0[2 * u + 1]);
-      v1[u] = tmem::pack(r1[2 * u], r1[2 * u + 1]);
-      if (FP) {
-        v0[u] = fp_to_canon(as_fp(v0[u]), P.qd, P.qinv);
-        v1[u] = fp_to_canon(as_fp(v1[u]), P.qd, P.qinv);
-      }
+  for (int i = 0; i < 8; ++i) {
+    u64 v0 = acc0[2 * i], v1 = acc0[2 * i + 1], u0 = acc1[2 * i], u1 = acc1[2 * i + 1];
+    if (FP) {
+      v0 = fp_to_canon(as_fp(v0), P.qd, P.qinv);
+      v1 = fp_to_canon(as_fp(v1), P.qd, P.qinv);
+      u0 = fp_to_canon(as_fp(u0), P.qd, P.qinv);
+      u1 = fp_to_canon(as_fp(u1), P.qd, P.qinv);
     }
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int i = 2 * h + q;
-      *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0[2 * q], v0[2 * q + 1]);
-      *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
-    }
+    *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0, v1);
+    *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(u0, u1);
   }
 }
 
 template <int LOG_M>
-__global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
+__global__ void __launch_bounds__(kBipThreads, 2)
     k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
-  // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
-  // needs 64 columns per group of four warps.  Shared memory caps how many
-  // CTAs share an SM so that their columns never exceed the 512 of an SM,
-  // hence tmem::alloc never waits.
-  constexpr uint32_t kCols = kRipWarps > 4 ? 128 : 64;
-  static_assert(kRipWarps == 4 || kRipWarps == 8, "CTA of 4 or 8 warps");
-  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / (512 / kCols + 1),
-                "TMEM columns could be oversubscribed");
-  extern __shared__ __align__(16) u64 dsm[];
-  __shared__ uint32_t tmem_slot;
-  u64 *sm = dsm;
-  ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
-      dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
+  extern __shared__ __align__(128) u64 dsm[];
+  __shared__ __align__(8) uint64_t bars[2];
   const int s = blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
-  const int warp = threadIdx.x >> 5;
-  if (warp == 0) tmem::alloc(&tmem_slot, kCols);
-  tmem::fence_before_sync();
-  __syncthreads();
-  tmem::fence_after_sync();
-  // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
-  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
-  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
-  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, tacc);
-  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
-  tmem::fence_before_sync();
-  __syncthreads();
-  if (warp == 0) {
-    tmem::fence_after_sync();
-    tmem::dealloc(tmem_slot, kCols);
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  __syncthreads();
+  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, dsm, bars);
+  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, dsm, bars);
+  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, dsm, bars);
 }
 
 // ---------------------------------------------------------------------------
@@ -558,13 +607,9 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
                                int rot, const u64 *diag, const ModDownDev &md,
                                const NttTables &T) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_moddown_rows<LOG_M>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<unsigned> attr_done{0};
+  cudaError_t e = ensure_dynamic_smem(k_moddown_rows<LOG_M>, smem, attr_done);
+  if (e != cudaSuccess) return e;
   k_moddown_rows<LOG_M><<<grid, kThreads, smem, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly,
                                                      ct0, ct1, g0, rot, diag, md, T);
   return cudaGetLastError();
@@ -573,18 +618,13 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
 template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt, const u64 *key,
                                  int key_limbs, u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                 const NttTables &T, uint32_t elt) {
-  constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_modup_rows_ip<LOG_M>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out);
-  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt};
-  k_modup_rows_ip<LOG_M><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
+                                 const NttTables &T, uint32_t elt, int *status) {
+  static std::atomic<unsigned> attr_done{0};
+  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M>, kBipSmemBytes, attr_done);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((1 << T.log_n) / kBipTile, lay.n_out);
+  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt, status};
+  k_modup_rows_ip<LOG_M><<<grid, kBipThreads, kBipSmemBytes, s>>>(A, mu, lay, T);
   return cudaGetLastError();
 }
 
@@ -634,16 +674,16 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s,
-                                     uint32_t elt) {
+                                     uint32_t elt, int *status) {
   if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
   if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
     return cudaErrorInvalidValue;
   if (lay.n_out == 0) return cudaSuccess;
   const int s2 = T.log_n - T.log_n / 2;
   switch (s2) {
-    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
-    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
-    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
+    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
+    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
+    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -5,6 +5,8 @@
 // choice between the lazy butterflies (small primes) and Harvey's reduced
 // butterflies (60-bit primes) are CTA-uniform.
 #include "ks_ntt.cuh"
+#include "ks_launch.cuh"
+#include "ks_launch.cuh"
 #include "ks_ntt_impl.cuh"
 #include "ks_galois.cuh"
 
@@ -137,13 +139,9 @@ template <int LOG_M, bool FWD>
 cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
                         cudaStream_t s, uint32_t elt = 1) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
-  static bool attr_set = false;  // idempotent; one call per instantiation suffices
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(ntt_rows<LOG_M, FWD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<unsigned> attr_done{0};
+  cudaError_t e = ensure_dynamic_smem(ntt_rows<LOG_M, FWD>, smem, attr_done);
+  if (e != cudaSuccess) return e;
   dim3 grid((1 << T.log_n) / kTile, n_limbs);
   ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T, elt);
   return cudaGetLastError();
