@@ -17,6 +17,7 @@
 #include "ks_fused.cuh"
 #include "ks_galois.cuh"
 #include "ks_launch.cuh"
+#include "ks_tmem.cuh"
 #include "ks_ntt_impl.cuh"
 
 namespace ksb {
@@ -191,20 +192,23 @@ __device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool r
 // ModUp row pass fused with the evaluation-key inner product
 // ---------------------------------------------------------------------------
 // One CTA: one kBipTile-word tile of one output limb s (prime m_j), all
-// digits of the key shard.  Per digit the CTA's inputs are three contiguous
-// 16 KB blocks -- the tile of t[d][s] (column pass done; for the digit that
-// holds q_j, the aligned source tile of the NTT-form input instead), and the
-// tiles of the two key polys -- which one thread moves into shared memory
-// with cp.async.bulk (the bulk-copy engine, completion counted in bytes on an
-// mbarrier).  Two stages alternate: the copies of digit d + 1 run while digit
-// d computes, so the HBM latency is hidden by the copy engine rather than by
-// resident warps.  Per digit the tile gets its row pass (the second pass of
-// the forward NTT) in registers with the exchange done in place in the stage
-// buffer, swizzled so that both access patterns are free of bank conflicts,
-// and is multiplied into the two accumulators:
+// digits of the key shard; each warp owns the 512 words [512 w, 512 w + 512)
+// of the tile (whole rows) and runs on its own, with no CTA-wide barrier
+// after set-up.  Per digit a warp's inputs are three contiguous 4 KB blocks
+// -- its slice of t[d][s] (column pass done; for the digit that holds q_j,
+// the aligned source slice of the NTT-form input instead) and its slices of
+// the two key polys -- which lane 0 moves into the warp's shared-memory
+// stage with cp.async.bulk (the bulk-copy engine; completion counted in
+// bytes on the warp's mbarrier), and whose next-digit blocks it prefetches
+// into L2 with cp.async.bulk.prefetch, so the refill of the stage is an L2
+// hit.  The slice gets its row pass (the second pass of the forward NTT) in
+// registers with the exchange done in place in the stage, swizzled so that
+// both access patterns are free of bank conflicts, and is multiplied into
+// the two accumulators:
 //   cx[0][s] = sum_d t[d][s] * key[d][0][j],   cx[1][s] = sum_d t[d][s] * key[d][1][j].
-// The 32 accumulators of a thread (two polys x 16 words) stay in registers:
-// shared memory limits the SM to two CTAs, so registers are plentiful.
+// The 32 accumulators of a thread (two polys x 16 words) live in Tensor
+// Memory (tcgen05.ld / st), which keeps the kernel at 128 registers and four
+// CTAs (16 warps) per SM.
 struct RowsIpArgs {
   const u64 *t, *c_ntt, *key;
   u64 *cx;
@@ -215,10 +219,11 @@ struct RowsIpArgs {
 
 constexpr int kBipWarps = 4;
 constexpr int kBipThreads = kBipWarps * 32;
-constexpr int kBipTile = kBipWarps * 512;       // words of one CTA tile
-constexpr int kBipBlockBytes = kBipTile * 8;    // one 16 KB block
-constexpr int kBipStageWords = 3 * kBipTile;    // t, key poly 0, key poly 1
-constexpr size_t kBipSmemBytes = 2 * (size_t)kBipStageWords * 8;  // two stages: 96 KB
+constexpr int kBipTile = kBipWarps * 512;      // words of one CTA tile
+constexpr int kBipSlice = 512;                 // words of one warp's slice
+constexpr int kBipSliceBytes = kBipSlice * 8;  // one 4 KB block
+constexpr int kBipWarpWords = 3 * kBipSlice;   // t, key poly 0, key poly 1
+constexpr size_t kBipSmemBytes = (size_t)kBipWarps * kBipWarpWords * 8;  // 48 KB
 
 // Physical position of row-local word i of a row in the exchange: i with its
 // 16-word group index XORed into its low four bits.  Thread t's 16 words
@@ -272,16 +277,21 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) of this GPU's
+// global memory into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
-// Row pass of the tile in the stage buffer tb (rows of M words, row-major as
-// the bulk copy left them), thread (rr, t); the result stays in tb at the
-// swizzled positions (rr M + bip_swz(i)).  FP: the values are the bits of
-// doubles, |x| < 12q; integer: canonical.
+// Row pass of the warp's slice in its stage buffer sb (rows of M words,
+// row-major as the bulk copy left them), thread (row rw of the slice, t);
+// the result stays in sb at the swizzled positions (rw M + bip_swz(i)).
+// FP: the bits of doubles, |x| < 12q; integer: canonical.
 template <int LOG_M, bool FP, bool LAZY>
-__device__ __forceinline__ void bip_row_pass(u64 *tb, int t, int rr, long long row,
+__device__ __forceinline__ void bip_row_pass(u64 *sb, int t, int rw, long long row,
                                              const NttTables &T, int prime, const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
-  u64 *rb = tb + (rr << LOG_M);
+  u64 *rb = sb + (rw << LOG_M);
   const int log_n = T.log_n, N = 1 << log_n;
   if (FP) {
     const TwRowsGlobal<LOG_M> tw{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
@@ -321,143 +331,205 @@ __device__ __forceinline__ void bip_row_pass(u64 *tb, int t, int rr, long long r
 }
 
 // FP: prime below kFpBound (FP64 butterflies); else LAZY selects the
-// integer butterflies without reductions.
+// integer butterflies without reductions.  Returns false when a copy did not
+// complete within the bound (the caller records it).
 template <int LOG_M, bool FP, bool LAZY>
-__device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
+__device__ __forceinline__ bool rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
                                              const KsLayout &lay, const NttTables &T, int s,
-                                             int prime, u64 *stages, uint64_t *bars) {
+                                             int prime, u64 *sb, uint64_t *bar, uint32_t tacc) {
   using G = RowGeom<LOG_M>;
   constexpr int M = 1 << LOG_M;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
   const int j = lay.out_j[s];
-  const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long tile0 = (long long)blockIdx.x * kBipTile;
-  const long long row = (tile0 >> LOG_M) + rr;
-  const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's word pairs in the tile
+  const int tt = lane % G::TT, rw = lane / G::TT;  // thread of a row, row of the slice
+  const long long slice0 = (long long)blockIdx.x * kBipTile + warp * kBipSlice;
+  const long long row = (slice0 >> LOG_M) + rw;
   const int dj = j < mu.Ql ? j / mu.alpha : -1;
   const long long kstride = (long long)A.key_limbs * N;
-  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0;
-  const u64 *tbase = A.t + (long long)s * N + tile0;
+  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + slice0;
+  const u64 *tbase = A.t + (long long)s * N + slice0;
   const long long tstride = (long long)lay.n_out * N;
-  // own-digit limb, read through the automorphism: the tile gathers from one
-  // aligned source tile of the same size
+  // own-digit limb, read through the automorphism: the slice gathers from
+  // one aligned source slice of the same size
   const u64 *cown = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N +
-                                  (galois_src((uint32_t)tile0, A.elt, log_n) &
-                                   ~(uint32_t)(kBipTile - 1))
+                                  (galois_src((uint32_t)slice0, A.elt, log_n) &
+                                   ~(uint32_t)(kBipSlice - 1))
                             : nullptr;
   const int n_dig = lay.n_digits;
-  auto issue = [&](int di) {  // thread 0: the three blocks of digit di -> stage di & 1
+  auto src_t = [&](int di) {
     const int d = __ldg(&lay.digits[di]);
-    u64 *st = stages + (di & 1) * kBipStageWords;
-    uint64_t *bar = bars + (di & 1);
-    const u64 *kb = kbase + (long long)(2 * di) * kstride;
-    mbar_expect_tx(bar, 3 * kBipBlockBytes);
-    bulk_g2s(st, d == dj ? cown : tbase + d * tstride, kBipBlockBytes, bar);
-    bulk_g2s(st + kBipTile, kb, kBipBlockBytes, bar);
-    bulk_g2s(st + 2 * kBipTile, kb + kstride, kBipBlockBytes, bar);
+    return d == dj ? cown : tbase + d * tstride;
   };
-  if (threadIdx.x == 0) {
+  auto issue = [&](int di) {  // lane 0: digit di's three blocks -> the stage
+    const u64 *kb = kbase + (long long)(2 * di) * kstride;
+    mbar_expect_tx(bar, 3 * kBipSliceBytes);
+    bulk_g2s(sb, src_t(di), kBipSliceBytes, bar);
+    bulk_g2s(sb + kBipSlice, kb, kBipSliceBytes, bar);
+    bulk_g2s(sb + 2 * kBipSlice, kb + kstride, kBipSliceBytes, bar);
+  };
+  auto prefetch = [&](int di) {  // lane 0: digit di's three blocks -> L2
+    const u64 *kb = kbase + (long long)(2 * di) * kstride;
+    bulk_prefetch_l2(src_t(di), kBipSliceBytes);
+    bulk_prefetch_l2(kb, kBipSliceBytes);
+    bulk_prefetch_l2(kb + kstride, kBipSliceBytes);
+  };
+  if (lane == 0) {
     issue(0);
-    if (n_dig > 1) issue(1);
+    if (n_dig > 1) prefetch(1);
   }
-  u64 acc0[kEpt], acc1[kEpt];
-  bool failed = false;
-  int stalled = 0;
 #pragma unroll 1
   for (int di = 0; di < n_dig; ++di) {
-    u64 *st = stages + (di & 1) * kBipStageWords;
-    const bool ok = mbar_wait_bounded(bars + (di & 1), (di >> 1) & 1, 1000000000ull);
-    if (__syncthreads_or(!ok)) {  // a copy never completed: give up uniformly
-      failed = true;
-      stalled = di;
-      break;
+    const bool ok = mbar_wait_bounded(bar, di & 1, 1000000000ull);
+    if (__any_sync(0xffffffffu, !ok)) {
+      // a copy never completed: wait (bounded) for it before the CTA exits
+      if (lane == 0) mbar_wait_bounded(bar, di & 1, 1000000000ull);
+      __syncwarp();
+      return false;
     }
+    if (lane == 0 && di + 2 < n_dig) prefetch(di + 2);
     const int d = __ldg(&lay.digits[di]);
     const bool own = d == dj;
-    if (!own) bip_row_pass<LOG_M, FP, LAZY>(st, tt, rr, row, T, prime, P);
-    const u64 *k0b = st + kBipTile, *k1b = st + 2 * kBipTile;
+    if (!own) bip_row_pass<LOG_M, FP, LAZY>(sb, tt, rw, row, T, prime, P);
+    const u64 *k0b = sb + kBipSlice, *k1b = sb + 2 * kBipSlice;
     const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int w = wofs + 64 * i;  // even tile word
-      u64 y0, y1;
-      if (own) {
-        const uint32_t src =
-            galois_src((uint32_t)(tile0 + w), A.elt, log_n) & (uint32_t)(kBipTile - 1);
-        const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(st + (src & ~1u));
-        y0 = (src & 1u) ? v.y : v.x;
-        y1 = (src & 1u) ? v.x : v.y;
-        if (FP) {
-          y0 = fp_bits(u64_to_fp(y0));
-          y1 = fp_bits(u64_to_fp(y1));
+    for (int h = 0; h < 4; ++h) {
+      u64 y[4], kb0[4], kb1[4];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int w = 2 * lane + 64 * (2 * h + q);  // even slice word
+        u64 y0, y1;
+        if (own) {
+          const uint32_t src =
+              galois_src((uint32_t)(slice0 + w), A.elt, log_n) & (uint32_t)(kBipSlice - 1);
+          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(sb + (src & ~1u));
+          y0 = (src & 1u) ? v.y : v.x;
+          y1 = (src & 1u) ? v.x : v.y;
+          if (FP) {
+            y0 = fp_bits(u64_to_fp(y0));
+            y1 = fp_bits(u64_to_fp(y1));
+          }
+        } else {
+          const int c = w & (M - 1), x = (c >> 4) & 15;
+          const ulonglong2 v =
+              *reinterpret_cast<const ulonglong2 *>(sb + (w - c) + ((c ^ x) & ~1));
+          y0 = (x & 1) ? v.y : v.x;
+          y1 = (x & 1) ? v.x : v.y;
         }
-      } else {
-        const int c = w & (M - 1), x = (c >> 4) & 15;
-        const ulonglong2 v =
-            *reinterpret_cast<const ulonglong2 *>(st + (w - c) + ((c ^ x) & ~1));
-        y0 = (x & 1) ? v.y : v.x;
-        y1 = (x & 1) ? v.x : v.y;
+        const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(k0b + w);
+        const ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(k1b + w);
+        y[2 * q] = y0;
+        y[2 * q + 1] = y1;
+        kb0[2 * q] = b.x;
+        kb0[2 * q + 1] = b.y;
+        kb1[2 * q] = a.x;
+        kb1[2 * q + 1] = a.y;
       }
-      const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(k0b + w);
-      const ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(k1b + w);
-      acc0[2 * i] = ip_term<FP>(acc0[2 * i], y0, b.x, first, recentre, P);
-      acc0[2 * i + 1] = ip_term<FP>(acc0[2 * i + 1], y1, b.y, first, recentre, P);
-      acc1[2 * i] = ip_term<FP>(acc1[2 * i], y0, a.x, first, recentre, P);
-      acc1[2 * i + 1] = ip_term<FP>(acc1[2 * i + 1], y1, a.y, first, recentre, P);
+      uint32_t r0[8], r1[8];
+      if (!first) {
+        tmem::ld8(tacc + 8 * h, r0);
+        tmem::ld8(tacc + 32 + 8 * h, r1);
+        tmem::wait_ld(r0, r1);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], kb0[u], first,
+                                   recentre, P);
+        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], kb1[u], first,
+                                   recentre, P);
+        r0[2 * u] = (uint32_t)v0;
+        r0[2 * u + 1] = (uint32_t)(v0 >> 32);
+        r1[2 * u] = (uint32_t)v1;
+        r1[2 * u + 1] = (uint32_t)(v1 >> 32);
+      }
+      tmem::st8(tacc + 8 * h, r0);
+      tmem::st8(tacc + 32 + 8 * h, r1);
     }
-    // every thread's generic accesses to this stage precede the next bulk
-    // copy into it (async proxy)
+    tmem::wait_st();
+    // the warp's generic accesses to the stage precede the next bulk copy
+    // into it (async proxy)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (threadIdx.x == 0 && di + 2 < n_dig) issue(di + 2);
+    __syncwarp();
+    if (lane == 0 && di + 1 < n_dig) issue(di + 1);
   }
-  if (failed) {
-    if (threadIdx.x == 0) {
-      atomicExch(A.status, kDevTimeout);
-      // wait (bounded) for the copies still in flight before the CTA exits:
-      // those of the digit that timed out and of the one after it
-      const int di = stalled;
-      mbar_wait_bounded(bars + (di & 1), (di >> 1) & 1, 1000000000ull);
-      if (di + 1 < n_dig) mbar_wait_bounded(bars + ((di + 1) & 1), ((di + 1) >> 1) & 1, 1000000000ull);
-    }
-    __syncthreads();
-    return;
-  }
-  u64 *o0 = A.cx + (long long)s * N + tile0 + wofs;
+  u64 *o0 = A.cx + (long long)s * N + slice0 + 2 * lane;
   u64 *o1 = o0 + (long long)lay.n_out * N;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    u64 v0 = acc0[2 * i], v1 = acc0[2 * i + 1], u0 = acc1[2 * i], u1 = acc1[2 * i + 1];
-    if (FP) {
-      v0 = fp_to_canon(as_fp(v0), P.qd, P.qinv);
-      v1 = fp_to_canon(as_fp(v1), P.qd, P.qinv);
-      u0 = fp_to_canon(as_fp(u0), P.qd, P.qinv);
-      u1 = fp_to_canon(as_fp(u1), P.qd, P.qinv);
+  for (int h = 0; h < 4; ++h) {
+    uint32_t r0[8], r1[8];
+    tmem::ld8(tacc + 8 * h, r0);
+    tmem::ld8(tacc + 32 + 8 * h, r1);
+    tmem::wait_ld(r0, r1);
+    u64 v0[4], v1[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v0[u] = tmem::pack(r0[2 * u], r0[2 * u + 1]);
+      v1[u] = tmem::pack(r1[2 * u], r1[2 * u + 1]);
+      if (FP) {
+        v0[u] = fp_to_canon(as_fp(v0[u]), P.qd, P.qinv);
+        v1[u] = fp_to_canon(as_fp(v1[u]), P.qd, P.qinv);
+      }
     }
-    *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0, v1);
-    *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(u0, u1);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = 2 * h + q;
+      *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0[2 * q], v0[2 * q + 1]);
+      *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
+    }
   }
+  return true;
+}
+
+// The integer bodies (q_0 and the special primes) stay out of line: inlined
+// they would push the FP64 body, which most output limbs run, into spills.
+template <int LOG_M, bool LAZY>
+__device__ __noinline__ bool rows_ip_body_int(const RowsIpArgs &A, const ModUpDev &mu,
+                                              const KsLayout &lay, const NttTables &T, int s,
+                                              int prime, u64 *sb, uint64_t *bar, uint32_t tacc) {
+  return rows_ip_body<LOG_M, false, LAZY>(A, mu, lay, T, s, prime, sb, bar, tacc);
 }
 
 template <int LOG_M>
-__global__ void __launch_bounds__(kBipThreads, 2)
+__global__ void __launch_bounds__(kBipThreads, 4)
     k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
+  // TMEM: warp w uses lane quarter w (32x32b shape) and 64 columns (two polys
+  // x 16 words x 2 columns per word).  Shared memory (48 KB per CTA) caps
+  // residency at four CTAs per SM, 256 columns of the 512, so the
+  // allocation never waits.
+  constexpr uint32_t kCols = 64;
+  static_assert(kBipWarps == 4, "one TMEM lane quarter per warp");
+  static_assert(kBipSmemBytes > 232448 / (512 / kCols + 1),
+                "TMEM columns could be oversubscribed");
   extern __shared__ __align__(128) u64 dsm[];
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[kBipWarps];
+  __shared__ uint32_t tmem_slot;
   const int s = blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
-  if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) tmem::alloc(&tmem_slot, kCols);
+  if (lane == 0) {
+    mbar_init(&bars[warp], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  tmem::fence_before_sync();
   __syncthreads();
-  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, dsm, bars);
-  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, dsm, bars);
-  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, dsm, bars);
+  tmem::fence_after_sync();
+  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * warp) << 16);
+  u64 *sb = dsm + warp * kBipWarpWords;
+  bool ok;
+  if (q < kFpBound) ok = rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
+  else if (q < kFwdLazyBound) ok = rows_ip_body_int<LOG_M, true>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
+  else ok = rows_ip_body_int<LOG_M, false>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
+  if (!ok && lane == 0) atomicExch(A.status, kDevTimeout);
+  tmem::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tmem::fence_after_sync();
+    tmem::dealloc(tmem_slot, kCols);
+  }
 }
 
 // ---------------------------------------------------------------------------
