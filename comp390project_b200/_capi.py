@@ -28,7 +28,6 @@ KS_WIRE_RELIN_KEY = 1
 KS_WIRE_GALOIS_KEY = 2
 KS_WIRE_CIPHERTEXT = 3
 KS_NCCL_ID_BYTES = 128
-KS_DEV_TIMEOUT = 1
 
 _ERR_NAMES = {
     KS_ERR_INVALID: "KS_ERR_INVALID", KS_ERR_CUDA: "KS_ERR_CUDA", KS_ERR_NCCL: "KS_ERR_NCCL",
@@ -112,7 +111,6 @@ SIGNATURES = {
     "ks_allgather_limbs": (_I, [_P, _P, _P, _I, _P]),
     "ks_scatter_ciphertext_to_gpu": (_I, [_P, _P, _SZ, _SZ, _SZ, _I, _I, _P]),
     "ks_gather_ciphertext_from_gpu": (_I, [_P, _P, _SZ, _SZ, _SZ, _I, _I, _P]),
-    "ks_device_status": (_I, [_P, C.POINTER(C.c_int)]),
     "ks_last_launch_count": (_I, [_P]),
     "ks_total_launch_count": (C.c_longlong, [_P]),
     "ks_graph_capture_begin": (_I, [_P, _P]),

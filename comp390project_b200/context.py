@@ -169,14 +169,6 @@ class KsContext:
     def key_words(self) -> int:
         return int(self.lib.ks_key_words(self.h))
 
-    def device_status(self) -> int:
-        """Waits for the device; returns and clears the code a kernel stored
-        since the last query (0: none; KS_DEV_TIMEOUT: a bounded wait on an
-        asynchronous copy gave up and that call's output is invalid)."""
-        v = C.c_int(0)
-        self._check(self.lib.ks_device_status(self.h, C.byref(v)))
-        return int(v.value)
-
     def last_launch_count(self) -> int:
         return int(self.lib.ks_last_launch_count(self.h))
 

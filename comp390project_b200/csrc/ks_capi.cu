@@ -33,8 +33,6 @@
 
 using namespace ksb;
 
-static_assert(kDevTimeout == KS_DEV_TIMEOUT, "device status codes of the ABI");
-
 struct ks_ctx {
   Ctx c;
 };
@@ -561,8 +559,6 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     for (int k2 = 0; k2 < k; ++k2) KS_REQUIRE(c.primes[k2] != q, "primes must be distinct");
   }
   KS_CUDA(cudaSetDevice(device));
-  c.d_status = dev_alloc<int>(1);
-  KS_CUDA(cudaMemset(c.d_status, 0, sizeof(int)));
   build_tables(c);
   // key shard: cyclic key-basis limbs of all digits (input broadcast), or
   // all limbs of the digits d % world == rank (output aggregation)
@@ -688,7 +684,6 @@ void ctx_free(Ctx &c) {
   f(c.d_tw_fwd_col);
   f(c.d_tw_inv_col);
   f(c.d_gauss);
-  f(c.d_status);
   f(c.d_phatinv);
   f(c.d_pinv);
   f(c.d_pmodq);
@@ -1178,7 +1173,7 @@ void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, 
     StageTimer tm(c, ST_MODUP_ROWS_IP, s);
     if (lv.lay.n_digits > 0) {
       KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay,
-                                       T, s, elt, c.d_status));
+                                       T, s, elt));
       c.launches += lv.lay.n_out > 0 ? 1 : 0;
     } else {  // output aggregation with more ranks than digits: a zero partial sum
       KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));
@@ -2079,19 +2074,6 @@ int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_bu
       KS_CUDA(cudaMemcpyAsync(full_buf + (size_t)j * N, recv + ((j % G) * ml + j / G) * N, N * 8,
                               cudaMemcpyDeviceToDevice, s));
     KS_CUDA(cudaStreamSynchronize(s));  // before the staging buffers are freed
-  });
-}
-
-int ks_device_status(ks_ctx *ctx, int *status) {
-  if (!ctx || !status) return KS_ERR_INVALID;
-  return guarded(ctx, [&] {
-    Ctx &c = ctx->c;
-    KS_CUDA(cudaSetDevice(c.device));
-    KS_CUDA(cudaDeviceSynchronize());
-    int v = 0;
-    KS_CUDA(cudaMemcpy(&v, c.d_status, sizeof(int), cudaMemcpyDeviceToHost));
-    KS_CUDA(cudaMemset(c.d_status, 0, sizeof(int)));
-    *status = v;
   });
 }
 

@@ -102,7 +102,6 @@ struct Ctx {
   double *d_tw_fwd_fp = nullptr, *d_tw_inv_fp = nullptr;
   double2 *d_tw_fwd_col = nullptr, *d_tw_inv_col = nullptr;
   u64 *d_gauss = nullptr;
-  int *d_status = nullptr;  // device status word (kDevTimeout, ...), 0 when no fault was seen
   ModDownDev md{};
   ulonglong2 *d_phatinv = nullptr, *d_pinv = nullptr;
   ulonglong2 *d_pmodq = nullptr;  // [L] {[P]_{q_j}, Shoup}

