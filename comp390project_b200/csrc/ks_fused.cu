@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
   const ulonglong2 *tw = T.inv + (long long)prime * N;
-  const int c = threadIdx.x % G::C, t = threadIdx.x / G::C;
+  const int c = threadIdx.x % G::C, t = (threadIdx.x / G::C) & (G::TT - 1);  // known range t < TT
   const int col = blockIdx.x * G::C + c;
   const ulonglong2 s0 = scale[2 * li], s1 = scale[2 * li + 1];
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int prime = mu.prime_of[j];
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
-  const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
+  const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
   const long long wo = ((long long)d * mu.QlP + j) * mu.alpha;
@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
-  const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
+  const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const long long wo = (long long)j * md.alpha;
   auto src = [&](int i) { return y_base + y_off[p * md.alpha + i]; };
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
-  const int c = threadIdx.x % G::C, tt = threadIdx.x / G::C;
+  const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const u64 h = q_last >> 1, hj = reduce_full(h, P.q, P.mu);
   const u64 *src = last + (long long)p * N;

@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
   const ulonglong2 *tw = (FWD ? T.fwd : T.inv) + (long long)prime * N;
-  const int c = threadIdx.x % G::C, t = threadIdx.x / G::C;
+  const int c = threadIdx.x % G::C, t = (threadIdx.x / G::C) & (G::TT - 1);  // known range t < TT
   const int col = blockIdx.x * G::C + c;
   auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
   auto fill = [&](u64 (&x)[kEpt]) { fill_cols<LOG_M>(x, t, col, load); };

@@ -26,20 +26,21 @@ constexpr int kTile = kThreads * kEpt;  // 4096 words per CTA
 
 // Register e = (g << NB) | v holds the local index
 //   ((u >> LO) << (LO + NB)) | (v << LO) | (u & ((1 << LO) - 1)),  u = (g << LOG_T) | t.
+// The three fields occupy disjoint bits, so the index is written as a sum:
+// the part that depends on e is then a compile-time constant the compiler
+// folds into the immediate offset of the load or store, and only the t part
+// is computed at run time (once per thread).
 template <int LOG_M, int LO, int NB>
 __device__ __forceinline__ int lidx(int t, int e) {
   constexpr int LOG_T = LOG_M - 4;
   const int g = e >> NB, v = e & ((1 << NB) - 1);
-  const int u = (g << LOG_T) | t;
-  return ((u >> LO) << (LO + NB)) | (v << LO) | (u & ((1 << LO) - 1));
+  // t < 2^LOG_T; split u = (g << LOG_T) + t into its parts above and below LO
+  const int t_hi = (t >> LO) << (LO + NB), t_lo = t & ((1 << LO) - 1);
+  const int g_hi = LO <= LOG_T ? (g << (LOG_T - LO)) << (LO + NB) : 0;
+  const int g_lo = LO <= LOG_T ? 0 : ((g << LOG_T) & ((1 << LO) - 1));
+  const int g_mid = LO <= LOG_T ? 0 : (((g << LOG_T) >> LO) << (LO + NB));
+  return t_hi + g_hi + g_mid + (v << LO) + t_lo + g_lo;
 }
-
-// Twiddle sharing inside a round.  The twiddle of the pair (e, e | 2^k) at
-// local bit b = LO + k only sees H >> (b + 1), i.e. e >> (k + 1) (the group
-// bits g = e >> NB included, since k < NB): the 2^k pairs e = r .. r + 2^k - 1
-// of a representative r (bits 0..k of r clear) share one twiddle.  The
-// rounds below load it once per representative, just before its pairs, so a
-// radix-16 round issues 8 + 4 + 2 + 1 = 15 twiddle loads instead of 32.
 
 // Forward stages on local bits [LO, LO+NB), high bit first.  Global bit of
 // local bit b is b + gofs; the twiddle of the pair whose lower element has
@@ -53,14 +54,12 @@ __device__ __forceinline__ void fwd_round(u64 (&x)[kEpt], int t, long long prefi
     const int b = LO + k;
     const int base = 1 << (log_n - 1 - b - gofs);
 #pragma unroll
-    for (int r = 0; r < kEpt; r += 2 << k) {
-      const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, r);
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
       const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
-#pragma unroll
-      for (int e = r; e < r + (1 << k); ++e) {
-        if (LAZY) ct_bfly_lazy(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
-        else ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
-      }
+      if (LAZY) ct_bfly_lazy(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
+      else ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
     }
   }
 }
@@ -79,25 +78,19 @@ __device__ __forceinline__ void inv_round(u64 (&x)[kEpt], int t, long long prefi
     const int base = 1 << (log_n - 1 - gb);
     const u64 K = P.q << gb;  // >= bound of the operands entering this stage (lazy path)
 #pragma unroll
-    for (int r = 0; r < kEpt; r += 2 << k) {
-      ulonglong2 w = make_ulonglong2(0, 0);
-      if (!(LAST && k == NB - 1)) {
-        const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, r);
-        w = __ldg(&tw[base + (int)(H >> (b + 1))]);
-      }
-#pragma unroll
-      for (int e = r; e < r + (1 << k); ++e) {
-        u64 &X = x[e], &Y = x[e | (1 << k)];
-        if (LAST && k == NB - 1) {
-          const u64 s = LAZY ? X + Y : X + Y;  // < 2^64 on both paths
-          const u64 d = LAZY ? X + K - Y : X - Y + P.two_q;
-          X = mul_shoup_lazy(s, s0.x, s0.y, P.q);
-          Y = mul_shoup_lazy(d, s1.x, s1.y, P.q);
-        } else if (LAZY) {
-          gs_bfly_lazy(X, Y, w.x, w.y, P.q, K);
-        } else {
-          gs_bfly(X, Y, w.x, w.y, P.q, P.two_q);
-        }
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      u64 &X = x[e], &Y = x[e | (1 << k)];
+      if (LAST && k == NB - 1) {
+        const u64 s = LAZY ? X + Y : X + Y;  // < 2^64 on both paths
+        const u64 d = LAZY ? X + K - Y : X - Y + P.two_q;
+        X = mul_shoup_lazy(s, s0.x, s0.y, P.q);
+        Y = mul_shoup_lazy(d, s1.x, s1.y, P.q);
+      } else {
+        const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
+        const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+        if (LAZY) gs_bfly_lazy(X, Y, w.x, w.y, P.q, K);
+        else gs_bfly(X, Y, w.x, w.y, P.q, P.two_q);
       }
     }
   }
@@ -319,7 +312,6 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // Bound: operands < B on entry -> < B + 4 * 0.57q on exit (additive growth).
-// One twiddle load per representative pair group (see fwd_round).
 template <int LOG_M, int LO, int NB, class Tw>
 __device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long prefix,
                                              const Tw &tw, double q, double qinv) {
@@ -327,11 +319,11 @@ __device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long
   for (int k = NB - 1; k >= 0; --k) {
     const int b = LO + k;
 #pragma unroll
-    for (int r = 0; r < kEpt; r += 2 << k) {
-      const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, r);
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
       const double2 w = tw(b, H);
-#pragma unroll
-      for (int e = r; e < r + (1 << k); ++e) fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
+      fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
     }
   }
 }
@@ -348,22 +340,17 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
   for (int k = 0; k < NB; ++k) {
     const int b = LO + k;
 #pragma unroll
-    for (int r = 0; r < kEpt; r += 2 << k) {
-      double2 w = make_double2(0, 0);
-      if (!(LAST && k == NB - 1)) {
-        const long long H = (prefix << LOG_M) | lidx<LOG_M, LO, NB>(t, r);
-        w = tw(b, H);
-      }
-#pragma unroll
-      for (int e = r; e < r + (1 << k); ++e) {
-        double &X = x[e], &Y = x[e | (1 << k)];
-        if (LAST && k == NB - 1) {
-          const double s = __dadd_rn(X, Y), d = __dsub_rn(X, Y);
-          X = fp_mulmod(s, s0.x, s0.y, P.qd);
-          Y = fp_mulmod(d, s1.x, s1.y, P.qd);
-        } else {
-          fp_gs_bfly(X, Y, w.x, w.y, P.qd);
-        }
+    for (int e = 0; e < kEpt; ++e) {
+      if (e & (1 << k)) continue;
+      double &X = x[e], &Y = x[e | (1 << k)];
+      if (LAST && k == NB - 1) {
+        const double s = __dadd_rn(X, Y), d = __dsub_rn(X, Y);
+        X = fp_mulmod(s, s0.x, s0.y, P.qd);
+        Y = fp_mulmod(d, s1.x, s1.y, P.qd);
+      } else {
+        const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
+        const double2 w = tw(b, H);
+        fp_gs_bfly(X, Y, w.x, w.y, P.qd);
       }
     }
   }
