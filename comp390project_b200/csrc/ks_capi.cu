@@ -151,6 +151,23 @@ inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 int n_local(int g, int G, int total) { return g < total ? (total - g - 1) / G + 1 : 0; }
 
+// Merges two job lists with the `rare` jobs at evenly spaced positions, the
+// first of them at the front (the rare jobs are the long-running ones).
+template <class T>
+std::vector<T> interleave_jobs(const std::vector<T> &common, const std::vector<T> &rare) {
+  std::vector<T> out;
+  const size_t n = common.size() + rare.size();
+  out.reserve(n);
+  size_t ic = 0, ir = 0;
+  for (size_t k = 0; k < n; ++k) {
+    // rare job ir belongs at position floor(ir * n / rare.size())
+    if (ir < rare.size() && k >= ir * n / rare.size()) out.push_back(rare[ir++]);
+    else if (ic < common.size()) out.push_back(common[ic++]);
+    else out.push_back(rare[ir++]);
+  }
+  return out;
+}
+
 u64 mix64h(u64 z) {
   z ^= z >> 30;
   z *= 0xBF58476D1CE4E5B9ull;
@@ -430,26 +447,40 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       const int j = d * a + i;
       lv.src_slot.h.push_back(j < Ql ? (j % G) * lv.coef_ml + j / G : 0);
     }
-  // jobs whose target prime takes the FP64 path first, then the integer ones
-  for (int pass = 0; pass < 2; ++pass)
-    for (int d = 0; d < lv.beta; ++d)
-      for (int s = 0; s < lv.n_out; ++s) {
-        const int pj = lv.t_jobs.h[(size_t)d * lv.n_out + s];
-        if (pj < 0 || (c.primes[pj] < kFpBound) != (pass == 0)) continue;
-        lv.job_d.h.push_back(d);
-        lv.job_s.h.push_back(s);
-        lv.job_prime.h.push_back(pj);
-        lv.job_off.h.push_back(((long long)d * lv.n_out + s) * N);
-        if (pass == 0) ++lv.n_jobs_fp;
-      }
+  // Job order of the fused column passes: jobs whose target prime takes the
+  // integer path (q_0 and the 60-bit special primes) run 2-3x longer than
+  // the FP64 ones and use the integer pipes, so they are spread evenly over
+  // the list (the first at the front): co-resident CTAs then keep the FP64
+  // and integer pipes busy at the same time, and no wave at the end runs
+  // integer work alone.
+  std::vector<std::pair<int, int>> fp_jobs, int_jobs;  // (d, s)
+  for (int d = 0; d < lv.beta; ++d)
+    for (int s = 0; s < lv.n_out; ++s) {
+      const int pj = lv.t_jobs.h[(size_t)d * lv.n_out + s];
+      if (pj < 0) continue;
+      (c.primes[pj] < kFpBound ? fp_jobs : int_jobs).push_back({d, s});
+    }
+  for (const auto &ds : interleave_jobs(fp_jobs, int_jobs)) {
+    const int d = ds.first, s = ds.second, pj = lv.t_jobs.h[(size_t)d * lv.n_out + s];
+    lv.job_d.h.push_back(d);
+    lv.job_s.h.push_back(s);
+    lv.job_prime.h.push_back(pj);
+    lv.job_off.h.push_back(((long long)d * lv.n_out + s) * N);
+    if (c.primes[pj] < kFpBound) ++lv.n_jobs_fp;
+  }
   lv.n_jobs = (int)lv.job_d.h.size();
-  for (int pass = 0; pass < 2; ++pass)
-    for (int p = 0; p < 2; ++p)
-      for (int s = 0; s < lv.n_q; ++s) {
-        if ((c.primes[lv.out_j.h[s]] < kFpBound) != (pass == 0)) continue;
-        lv.md_job_ps.h.push_back(p * lv.n_q + s);
-        if (pass == 0) ++lv.n_md_fp;
-      }
+  std::vector<int> md_fp, md_int;
+  for (int p = 0; p < 2; ++p)
+    for (int s = 0; s < lv.n_q; ++s)
+      (c.primes[lv.out_j.h[s]] < kFpBound ? md_fp : md_int).push_back(p * lv.n_q + s);
+  lv.md_job_ps.h = interleave_jobs(md_fp, md_int);
+  lv.n_md_fp = (int)md_fp.size();
+  // the fused row pass + inner product walks the output slots in the same
+  // spirit: integer slots spread among the FP64 ones
+  std::vector<int> rip_fp, rip_int;
+  for (int s = 0; s < lv.n_out; ++s)
+    (c.primes[lv.prime_of.h[lv.out_j.h[s]]] < kFpBound ? rip_fp : rip_int).push_back(s);
+  lv.rip_order.h = interleave_jobs(rip_fp, rip_int);
   std::vector<ulonglong2> sin, sp;
   for (int i = 0; i < lv.n_intt; ++i) {
     const int j = lv.intt_prime.h[i], d = j / a;
@@ -487,6 +518,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
     lv.rs_md = ModDownDev{1, last, nullptr, nullptr, lv.rs_pinv, nullptr, nullptr};
   }
   up_ints(lv.src_slot);
+  up_ints(lv.rip_order);
   up_ints(lv.digits);
   up_ints(lv.cx_prime);
   up_ints(lv.intt_prime);
@@ -524,8 +556,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   lv.wsh = upload(wsh);
   lv.wq = upload(wq);
   lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh, lv.wq};
-  lv.lay = KsLayout{lv.n_out,  lv.out_j.d,    lv.key_slot.d,          lv.c_slot.d, G,
-                    lv.coef_ml, lv.digits.d, (int)lv.digits.h.size()};
+  lv.lay = KsLayout{lv.n_out,  lv.out_j.d,  lv.key_slot.d,           lv.c_slot.d, G,
+                    lv.coef_ml, lv.digits.d, (int)lv.digits.h.size(), lv.rip_order.d};
 }
 
 void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncclComm_t comm,
@@ -661,7 +693,7 @@ void ctx_free(Ctx &c) {
     f(lv.y_off.d);
     f(lv.qhatinv);
     for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
-                       &lv.digits, &lv.cx_prime, &lv.intt_prime})
+                       &lv.digits, &lv.cx_prime, &lv.intt_prime, &lv.rip_order})
       f(t->d);
     f(lv.job_off.d);
     f(lv.intt_off.d);

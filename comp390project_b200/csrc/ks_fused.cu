@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   u64 *sm = dsm;
   ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
       dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
-  const int s = blockIdx.y;
+  const int s = lay.slot_order ? lay.slot_order[blockIdx.y] : (int)blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
   const int warp = threadIdx.x >> 5;

@@ -22,8 +22,9 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
 // where v_i are the digit's scaled coefficient limbs (v_all at limb slot
 // src_slot[d*alpha + i]).  Result (column pass done) -> t[d][s].
-// The first n_fp jobs have targets below kFpBound (FP64 kernel), the rest
-// run the integer kernel.
+// n_fp of the jobs have targets below kFpBound (FP64 path); the path is
+// chosen per CTA from the target prime, so the job order is free (the
+// context spreads the integer jobs evenly over the list).
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
                              int n_fp, const NttTables &T, cudaStream_t s);
@@ -32,7 +33,8 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 // out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner
 // product against the key shard ([n_digits][2][key_limbs][N], limb key_slot[s]):
 //   cx[p][s] = sum_i NTT_rows(t[d_i][s]) * key[i][p][key_slot[s]]  (p = 0, 1,
-// d_i = lay.digits[i], lay.n_digits >= 1).
+// d_i = lay.digits[i], lay.n_digits >= 1).  Launch row y serves output slot
+// lay.slot_order[y] (all slots, any order; null: slot y).
 // elt != 1: the NTT-form input c_ntt is read through X -> X^elt.
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
@@ -42,7 +44,8 @@ cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
 // scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].
-// job_ps[2*n_q] lists p*n_q + s, the first n_fp with q_j below kFpBound.
+// job_ps[2*n_q] lists p*n_q + s in launch order; n_fp of them have q_j
+// below kFpBound.
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
                                const int *q_index, const ModDownDev &md, const int *job_ps,
                                int n_fp, const NttTables &T, cudaStream_t s);

@@ -42,6 +42,7 @@ struct KsLayout {
   int coef_G, coef_ml;        // coefficient-form Q limb j at slot (j % G) * ml + j / G
   const int *digits;          // [n_digits] digits summed by the inner product, ascending;
   int n_digits;               // digit digits[i] is digit i of the key shard
+  const int *slot_order;      // [n_out] output slot of launch row y (a permutation), or null
 };
 
 // out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
