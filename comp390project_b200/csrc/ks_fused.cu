@@ -25,9 +25,10 @@ namespace {
 
 using namespace ntt;
 
-template <int LOG_M>
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTables T,
                                                              const ulonglong2 *scale) {
+  constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   const int li = blockIdx.y;
@@ -35,7 +36,7 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   const int prime = m.prime_tab ? m.prime_tab[li] : m.first_prime + (li % m.period);
   if (prime < 0) return;
   const PrimeDev P = T.primes[prime];
-  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
   const ulonglong2 *tw = T.inv + (long long)prime * N;
   const int c = threadIdx.x % G::C, t = (threadIdx.x / G::C) & (G::TT - 1);  // known range t < TT
   const int col = blockIdx.x * G::C + c;
@@ -132,18 +133,19 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
 // ---------------------------------------------------------------------------
 // The arithmetic path is chosen per CTA from the target prime (FP64 below
 // kFpBound, integer above); jobs are ordered FP64 first.
-template <int LOG_M>
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 3)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
                  const int *__restrict__ job_s, int job0, NttTables T) {
+  constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   const int d = job_d[job0 + blockIdx.y], s = job_s[job0 + blockIdx.y];
   const int j = lay.out_j[s];
   const int prime = mu.prime_of[j];
   const PrimeDev P = T.primes[prime];
-  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
   const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
@@ -415,18 +417,19 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
 // ---------------------------------------------------------------------------
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
-template <int LOG_M>
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 2)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
                    int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
                    const int *__restrict__ job_ps, int job0) {
+  constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   const int ps = job_ps[job0 + blockIdx.y];
   const int p = ps / n_q, s = ps % n_q;
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
-  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
   const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const long long wo = (long long)j * md.alpha;
@@ -519,16 +522,17 @@ __global__ void __launch_bounds__(kThreads)
 // Job (p, s), j = q_index[s]: y = ([c_p + h]_{q_last} mod q_j) - [h]_{q_j},
 // h = floor(q_last / 2), c_p the last limb of poly p (last[p * N + k];
 // stored as the bits of a double when q_last < kFpBound).
-template <int LOG_M>
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 3)
     k_rescale_cols(const u64 *__restrict__ last, u64 q_last, int last_fp, u64 *z, int n_q,
                    const int *__restrict__ q_index, NttTables T) {
+  constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   const int p = blockIdx.y / n_q, s = blockIdx.y % n_q;
   const int j = q_index[s];
   const PrimeDev P = T.primes[j];
-  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
   const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const u64 h = q_last >> 1, hj = reduce_full(h, P.q, P.mu);
@@ -598,10 +602,12 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
   if (e != cudaSuccess) return e;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_limbs);
-  switch (s1) {
-    case 6: k_inv_cols_scaled<6><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
-    case 7: k_inv_cols_scaled<7><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
-    case 8: k_inv_cols_scaled<8><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+  switch (T.log_n) {
+    case 12: k_inv_cols_scaled<12><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 13: k_inv_cols_scaled<13><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 14: k_inv_cols_scaled<14><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 15: k_inv_cols_scaled<15><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
+    case 16: k_inv_cols_scaled<16><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -615,10 +621,12 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
   if (n_jobs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_jobs);
-  switch (s1) {
-    case 6: k_modup_cols<6><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 7: k_modup_cols<7><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 8: k_modup_cols<8><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+  switch (T.log_n) {
+    case 12: k_modup_cols<12><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 13: k_modup_cols<13><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 14: k_modup_cols<14><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 15: k_modup_cols<15><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 16: k_modup_cols<16><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -649,10 +657,12 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
   if (n_q == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
-  switch (s1) {
-    case 6: k_moddown_cols<6><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 7: k_moddown_cols<7><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 8: k_moddown_cols<8><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+  switch (T.log_n) {
+    case 12: k_moddown_cols<12><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 13: k_moddown_cols<13><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 14: k_moddown_cols<14><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 15: k_moddown_cols<15><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 16: k_moddown_cols<16><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -665,10 +675,12 @@ cudaError_t rescale_fused_cols(const u64 *last, u64 q_last, bool last_fp, u64 *z
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
   const int fp = last_fp ? 1 : 0;
-  switch (s1) {
-    case 6: k_rescale_cols<6><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
-    case 7: k_rescale_cols<7><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
-    case 8: k_rescale_cols<8><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+  switch (T.log_n) {
+    case 12: k_rescale_cols<12><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 13: k_rescale_cols<13><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 14: k_rescale_cols<14><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 15: k_rescale_cols<15><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
+    case 16: k_rescale_cols<16><<<grid, kThreads, 0, s>>>(last, q_last, fp, z, n_q, q_index, T); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

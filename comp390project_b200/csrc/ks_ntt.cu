@@ -20,8 +20,9 @@ __device__ __forceinline__ void limb_of(const LimbMap &m, int i, u64 *&ptr, int 
   prime = m.prime_tab ? m.prime_tab[i] : m.first_prime + (i % m.period);
 }
 
-template <int LOG_M, bool FWD>
+template <int LOG_N, bool FWD>
 __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
+  constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points; stride M2 is a constant
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   u64 *a;
@@ -29,7 +30,7 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
   limb_of(m, blockIdx.y, a, prime);
   if (prime < 0) return;
   const PrimeDev P = T.primes[prime];
-  const int log_n = T.log_n, N = 1 << log_n, M2 = N >> LOG_M;
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
   const ulonglong2 *tw = (FWD ? T.fwd : T.inv) + (long long)prime * N;
   const int c = threadIdx.x % G::C, t = (threadIdx.x / G::C) & (G::TT - 1);  // known range t < TT
   const int col = blockIdx.x * G::C + c;
@@ -128,11 +129,11 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
   }
 }
 
-template <int LOG_M, bool FWD>
+template <int LOG_N, bool FWD>
 cudaError_t launch_cols(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s) {
-  const int M2 = (1 << T.log_n) >> LOG_M;
+  constexpr int LOG_M = LOG_N / 2, M2 = (1 << LOG_N) >> LOG_M;
   dim3 grid(M2 / ColGeom<LOG_M>::C, n_limbs);
-  ntt_cols<LOG_M, FWD><<<grid, kThreads, 0, s>>>(m, T);
+  ntt_cols<LOG_N, FWD><<<grid, kThreads, 0, s>>>(m, T);
   return cudaGetLastError();
 }
 template <int LOG_M, bool FWD>
@@ -151,10 +152,20 @@ template <bool FWD>
 cudaError_t launch_pass(bool cols, int log_m, const LimbMap &m, int n, const NttTables &T,
                         cudaStream_t s, const LimbMap *mo = nullptr, uint32_t elt = 1) {
   const LimbMap &o = mo ? *mo : m;
+  if (cols) {
+    switch (T.log_n) {
+      case 12: return launch_cols<12, FWD>(m, n, T, s);
+      case 13: return launch_cols<13, FWD>(m, n, T, s);
+      case 14: return launch_cols<14, FWD>(m, n, T, s);
+      case 15: return launch_cols<15, FWD>(m, n, T, s);
+      case 16: return launch_cols<16, FWD>(m, n, T, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (log_m) {
-    case 6: return cols ? launch_cols<6, FWD>(m, n, T, s) : launch_rows<6, FWD>(m, o, n, T, s, elt);
-    case 7: return cols ? launch_cols<7, FWD>(m, n, T, s) : launch_rows<7, FWD>(m, o, n, T, s, elt);
-    case 8: return cols ? launch_cols<8, FWD>(m, n, T, s) : launch_rows<8, FWD>(m, o, n, T, s, elt);
+    case 6: return launch_rows<6, FWD>(m, o, n, T, s, elt);
+    case 7: return launch_rows<7, FWD>(m, o, n, T, s, elt);
+    case 8: return launch_rows<8, FWD>(m, o, n, T, s, elt);
     default: return cudaErrorInvalidValue;
   }
 }
