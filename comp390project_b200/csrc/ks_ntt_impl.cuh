@@ -26,38 +26,51 @@ constexpr int kTile = kThreads * kEpt;  // 4096 words per CTA
 
 // Register e = (g << NB) | v holds the local index
 //   ((u >> LO) << (LO + NB)) | (v << LO) | (u & ((1 << LO) - 1)),  u = (g << LOG_T) | t.
-// The three fields occupy disjoint bits, so the index is written as a sum:
-// the part that depends on e is then a compile-time constant the compiler
-// folds into the immediate offset of the load or store, and only the t part
-// is computed at run time (once per thread).
+// The fields of t and of e occupy disjoint bits, so the index is the sum
+// lidx_t(t) + lidx_e(e): the e part is a compile-time constant that folds
+// into immediate offsets, and only the t part is computed at run time.  Every
+// round has LO <= LOG_T.
+template <int LOG_M, int LO, int NB>
+__device__ __forceinline__ int lidx_t(int t) {
+  static_assert(LO <= LOG_M - 4, "round below the thread bits");
+  return ((t >> LO) << (LO + NB)) + (t & ((1 << LO) - 1));
+}
+template <int LOG_M, int LO, int NB>
+__host__ __device__ constexpr int lidx_e(int e) {
+  return (((e >> NB) << (LOG_M - 4 - LO)) << (LO + NB)) + ((e & ((1 << NB) - 1)) << LO);
+}
 template <int LOG_M, int LO, int NB>
 __device__ __forceinline__ int lidx(int t, int e) {
-  constexpr int LOG_T = LOG_M - 4;
-  const int g = e >> NB, v = e & ((1 << NB) - 1);
-  // t < 2^LOG_T; split u = (g << LOG_T) + t into its parts above and below LO
-  const int t_hi = (t >> LO) << (LO + NB), t_lo = t & ((1 << LO) - 1);
-  const int g_hi = LO <= LOG_T ? (g << (LOG_T - LO)) << (LO + NB) : 0;
-  const int g_lo = LO <= LOG_T ? 0 : ((g << LOG_T) & ((1 << LO) - 1));
-  const int g_mid = LO <= LOG_T ? 0 : (((g << LOG_T) >> LO) << (LO + NB));
-  return t_hi + g_hi + g_mid + (v << LO) + t_lo + g_lo;
+  return lidx_t<LOG_M, LO, NB>(t) + lidx_e<LOG_M, LO, NB>(e);
 }
 
-// Forward stages on local bits [LO, LO+NB), high bit first.  Global bit of
-// local bit b is b + gofs; the twiddle of the pair whose lower element has
-// local index i is tw[(1 << (logN-1-b-gofs)) + (((prefix << LOG_M) | i) >> (b+1))].
+// Twiddle addressing.  The pair whose lower element has local index
+// i = lidx(t, e) at local bit b of a pass over rows of 2^LOG_M words uses
+// the twiddle at index (1 << (logN-1-b-gofs)) + (((prefix << LOG_M) + i) >> (b+1)).
+// Because the t and e fields are disjoint, i >> (b + 1) =
+// (lidx_t >> (b + 1)) + (lidx_e >> (b + 1)): the first part (with the prefix)
+// gives one per-thread base per stage, the second a compile-time offset, so a
+// butterfly's twiddle is one load at a constant offset from the stage base.
+// The FP64 getters below keep that split (their tables may permute the
+// within-row index by row_tw_pos, a bit permutation, which distributes over
+// the two disjoint parts).
+
+// Forward stages on local bits [LO, LO+NB), high bit first; integer tables
+// {w, w_shoup} in natural order.
 template <int LOG_M, int LO, int NB, bool LAZY>
 __device__ __forceinline__ void fwd_round(u64 (&x)[kEpt], int t, long long prefix, int gofs,
                                           int log_n, const ulonglong2 *__restrict__ tw, u64 q,
                                           u64 two_q) {
+  const int lt = lidx_t<LOG_M, LO, NB>(t);
 #pragma unroll
   for (int k = NB - 1; k >= 0; --k) {
     const int b = LO + k;
-    const int base = 1 << (log_n - 1 - b - gofs);
+    const int twk =  // stage base (an index below N)
+        (1 << (log_n - 1 - b - gofs)) + (int)(prefix << (LOG_M - b - 1)) + (lt >> (b + 1));
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
-      const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
-      const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+      const ulonglong2 w = __ldg(&tw[twk + (lidx_e<LOG_M, LO, NB>(e) >> (b + 1))]);
       if (LAZY) ct_bfly_lazy(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
       else ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q, two_q);
     }
@@ -71,11 +84,13 @@ template <int LOG_M, int LO, int NB, bool LAZY, bool LAST>
 __device__ __forceinline__ void inv_round(u64 (&x)[kEpt], int t, long long prefix, int gofs,
                                           int log_n, const ulonglong2 *__restrict__ tw,
                                           const PrimeDev &P, ulonglong2 s0, ulonglong2 s1) {
+  const int lt = lidx_t<LOG_M, LO, NB>(t);
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
     const int b = LO + k;
     const int gb = b + gofs;
-    const int base = 1 << (log_n - 1 - gb);
+    const int twk =  // stage base (an index below N)
+        (1 << (log_n - 1 - gb)) + (int)(prefix << (LOG_M - b - 1)) + (lt >> (b + 1));
     const u64 K = P.q << gb;  // >= bound of the operands entering this stage (lazy path)
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
@@ -87,8 +102,7 @@ __device__ __forceinline__ void inv_round(u64 (&x)[kEpt], int t, long long prefi
         X = mul_shoup_lazy(s, s0.x, s0.y, P.q);
         Y = mul_shoup_lazy(d, s1.x, s1.y, P.q);
       } else {
-        const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
-        const ulonglong2 w = __ldg(&tw[base + (int)(H >> (b + 1))]);
+        const ulonglong2 w = __ldg(&tw[twk + (lidx_e<LOG_M, LO, NB>(e) >> (b + 1))]);
         if (LAZY) gs_bfly_lazy(X, Y, w.x, w.y, P.q, K);
         else gs_bfly(X, Y, w.x, w.y, P.q, P.two_q);
       }
@@ -232,9 +246,9 @@ __device__ __forceinline__ void inv_rows_regs(u64 (&x)[kEpt], u64 *sm, int t, in
 // ===========================================================================
 // FP64 variants (primes below kFpBound).  Values travel between the passes as
 // the bits of signed integer-valued doubles; the pass inputs and the final
-// outputs are canonical uint64.  A twiddle getter tw(b, H) returns {w, wq}
-// for the pair at local bit b whose lower element has extended index
-// H = (prefix << LOG_M) | local: w = psi^(+-brev) and wq the quotient factor,
+// outputs are canonical uint64.  A twiddle getter (stage / get, see the
+// twiddle addressing note above) returns {w, wq} for the pair at local bit b:
+// w = psi^(+-brev) and wq the quotient factor,
 // either fl(w/q) from the column tables (2^(logN/2) pairs per prime) or
 // w * fl(1/q) formed next to its use from the row tables (w only, to keep the
 // staged row blocks small); both keep the estimate error below
@@ -245,28 +259,35 @@ __device__ __forceinline__ double as_fp(u64 b) { return __longlong_as_double((lo
 __device__ __forceinline__ u64 fp_bits(double d) { return (u64)__double_as_longlong(d); }
 
 // Column-pass getter: the prime's {w, fl(w/q)} column table (index
-// 2^(LOG_M-1-b) + (H >> (b+1)) < 2^LOG_M; every column of a CTA shares them).
+// 2^(LOG_M-1-b) + (i >> (b+1)) < 2^LOG_M; every column of a CTA shares them;
+// the prefix is 0).  stage(b, prefix, ts) is the per-thread base of local bit
+// b (ts = lidx_t >> (b + 1)), get(base, b, es) the twiddle at the constant
+// offset es = lidx_e >> (b + 1).
 template <int LOG_M>
 struct TwCols {
   const double2 *tw;
-  __device__ __forceinline__ double2 operator()(int b, long long H) const {
-    return __ldg(&tw[(1 << (LOG_M - 1 - b)) + (int)(H >> (b + 1))]);
+  __device__ __forceinline__ int stage(int b, long long, int ts) const {
+    return (1 << (LOG_M - 1 - b)) + ts;
+  }
+  __device__ __forceinline__ double2 get(int base, int, int es) const {
+    return __ldg(tw + base + es);
   }
 };
 
 // Shared-memory getter for a row pass over rows [row0, row0 + R): the block
 // of local bit b holds R * 2^u twiddles, u = LOG_M - 1 - b, at offset
-// R (2^u - 1).
+// R (2^u - 1); the within-row index is permuted by row_tw_pos.
 template <int LOG_M, int R>
 struct TwRowsSmem {
   const double *sm;
   long long row0;
   double qinv;
-  __device__ __forceinline__ double2 operator()(int b, long long H) const {
+  __device__ __forceinline__ int stage(int b, long long prefix, int ts) const {
     const int u = LOG_M - 1 - b;
-    const long long hk = H >> (b + 1);
-    const int k = (int)hk & ((1 << u) - 1);
-    const double w = sm[R * ((1 << u) - 1) + (int)(((hk >> u) - row0) << u) + row_tw_pos(LOG_M, b, k)];
+    return R * ((1 << u) - 1) + (int)((prefix - row0) << u) + row_tw_pos(LOG_M, b, ts);
+  }
+  __device__ __forceinline__ double2 get(int base, int b, int es) const {
+    const double w = sm[base + row_tw_pos(LOG_M, b, es)];
     return make_double2(w, __dmul_rn(w, qinv));
   }
 };
@@ -278,12 +299,12 @@ struct TwRowsGlobal {
   const double *tw;
   int log_n;
   double qinv;
-  __device__ __forceinline__ double2 operator()(int b, long long H) const {
-    const int u = LOG_M - 1 - b;
-    const long long hk = H >> (b + 1);
-    const int k = (int)hk & ((1 << u) - 1);
-    const double w =
-        __ldg(&tw[(1ll << (log_n - 1 - b)) + ((hk >> u) << u) + row_tw_pos(LOG_M, b, k)]);
+  __device__ __forceinline__ int stage(int b, long long prefix, int ts) const {
+    const int u = LOG_M - 1 - b;  // an index below N
+    return (1 << (log_n - 1 - b)) + (int)(prefix << u) + row_tw_pos(LOG_M, b, ts);
+  }
+  __device__ __forceinline__ double2 get(int base, int b, int es) const {
+    const double w = __ldg(tw + base + row_tw_pos(LOG_M, b, es));
     return make_double2(w, __dmul_rn(w, qinv));
   }
 };
@@ -315,14 +336,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <int LOG_M, int LO, int NB, class Tw>
 __device__ __forceinline__ void fwd_round_fp(double (&x)[kEpt], int t, long long prefix,
                                              const Tw &tw, double q, double qinv) {
+  const int lt = lidx_t<LOG_M, LO, NB>(t);
 #pragma unroll
   for (int k = NB - 1; k >= 0; --k) {
     const int b = LO + k;
+    const int base = tw.stage(b, prefix, lt >> (b + 1));
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
-      const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
-      const double2 w = tw(b, H);
+      const double2 w = tw.get(base, b, lidx_e<LOG_M, LO, NB>(e) >> (b + 1));
       fp_ct_bfly(x[e], x[e | (1 << k)], w.x, w.y, q);
     }
   }
@@ -334,11 +356,13 @@ template <int LOG_M, int LO, int NB, bool LAST, class Tw>
 __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long prefix,
                                              const Tw &tw, const PrimeDev &P, double2 s0,
                                              double2 s1) {
+  const int lt = lidx_t<LOG_M, LO, NB>(t);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = fp_reduce_sym(x[e], P.qd, P.qinv);
 #pragma unroll
   for (int k = 0; k < NB; ++k) {
     const int b = LO + k;
+    const int base = tw.stage(b, prefix, lt >> (b + 1));
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) {
       if (e & (1 << k)) continue;
@@ -348,8 +372,7 @@ __device__ __forceinline__ void inv_round_fp(double (&x)[kEpt], int t, long long
         X = fp_mulmod(s, s0.x, s0.y, P.qd);
         Y = fp_mulmod(d, s1.x, s1.y, P.qd);
       } else {
-        const long long H = (prefix << LOG_M) + lidx<LOG_M, LO, NB>(t, e);
-        const double2 w = tw(b, H);
+        const double2 w = tw.get(base, b, lidx_e<LOG_M, LO, NB>(e) >> (b + 1));
         fp_gs_bfly(X, Y, w.x, w.y, P.qd);
       }
     }
