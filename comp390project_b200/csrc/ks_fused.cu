@@ -275,15 +275,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       asm volatile("prefetch.global.L2 [%0];" ::"l"(v + line));
   };
   const int n_dig = lay.n_digits;
-  // The value tile of the next digit is loaded into registers one digit
-  // ahead (xn), so its latency hides behind a whole digit of work; the one
-  // after that is prefetched into L2.
-  u64 xn[kEpt];
-  {
-    const int d0 = __ldg(&lay.digits[0]);
-    if (d0 != dj) load_rows_tile<LOG_M>(xn, tbase + d0 * tstride, tt, rr);
-    if (n_dig > 1) prefetch(__ldg(&lay.digits[1]));
-  }
+  prefetch(__ldg(&lay.digits[0]));
 #pragma unroll 1
   for (int di = 0; di < n_dig; ++di) {
     const int d = __ldg(&lay.digits[di]);  // digit di of the key shard
@@ -297,17 +289,12 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    u64 x[kEpt];
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e) x[e] = xn[e];
-    if (di + 1 < n_dig) {
-      const int dn = __ldg(&lay.digits[di + 1]);
-      if (dn != dj) load_rows_tile<LOG_M>(xn, tbase + dn * tstride, tt, rr);
-      if (di + 2 < n_dig) prefetch(__ldg(&lay.digits[di + 2]));
-    }
+    if (di + 1 < n_dig) prefetch(__ldg(&lay.digits[di + 1]));
     if (!own) {
-      if (FP) fwd_rows_fp_inregs<LOG_M, false>(x, sm, twf, tt, rr, row, P);
-      else fwd_rows_inregs<LOG_M, LAZY>(x, sm, tt, rr, row, log_n, tw, P);
+      u64 x[kEpt];
+      const u64 *tile = tbase + d * tstride;
+      if (FP) fwd_rows_regs_fp_tw<LOG_M, false>(x, sm, twf, tile, tt, rr, row, P);
+      else fwd_rows_regs<LOG_M, LAZY>(x, sm, tile, tt, rr, row, log_n, tw, P);
 #pragma unroll
       for (int e = 0; e < kEpt; ++e) sm[padx<LOG_M>(rr, lidx<LOG_M, 0, G::NLO>(tt, e))] = x[e];
       __syncwarp();
@@ -391,7 +378,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
 }
 
 template <int LOG_M>
-__global__ void __launch_bounds__(kRipThreads, 3)
+__global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
   // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
   // needs 64 columns per group of four warps.  Shared memory caps how many
