@@ -227,8 +227,10 @@ __host__ __device__ constexpr int rows_ip_rows() {  // rows of M words per CTA
 template <int LOG_M>
 __host__ __device__ constexpr size_t rows_ip_smem_bytes() {
   // padded exchange rows + per-warp key stage [warps][2 polys][8 pairs][32 lanes] x 16 B
+  // + the row-pass twiddles of the CTA's rows (FP64 primes; the same for every digit)
   return (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16) * 8 +
-         (size_t)kRipWarps * 2 * 8 * 32 * 16;
+         (size_t)kRipWarps * 2 * 8 * 32 * 16 +
+         (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) - 1) * 8;
 }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -241,7 +243,8 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 template <int LOG_M, bool FP, bool LAZY>
 __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev &mu,
                                              const KsLayout &lay, const NttTables &T, int s,
-                                             int prime, u64 *sm, ulonglong2 *kst, uint32_t tacc) {
+                                             int prime, u64 *sm, ulonglong2 *kst,
+                                             const double *smtw, uint32_t tacc) {
   using G = RowGeom<LOG_M>;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
@@ -264,7 +267,9 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
             : nullptr;
   const ulonglong2 *tw = T.fwd + (long long)prime * N;
-  const TwRowsGlobal<LOG_M> twf{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
+  // FP64 primes: the CTA's row twiddles, staged once in shared memory
+  const TwRowsSmem<LOG_M, rows_ip_rows<LOG_M>()> twf{
+      smtw, (long long)blockIdx.x * rows_ip_rows<LOG_M>(), P.qinv};
   kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
   // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
   // over the CTA's threads.
@@ -393,6 +398,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   u64 *sm = dsm;
   ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
       dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
+  double *smtw = reinterpret_cast<double *>(kst + kRipWarps * 2 * 8 * 32);
   const int s = lay.slot_order ? lay.slot_order[blockIdx.y] : (int)blockIdx.y;
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
@@ -403,9 +409,18 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   tmem::fence_after_sync();
   // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
   const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
-  if (q < kFpBound) rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
-  else if (q < kFwdLazyBound) rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, tacc);
-  else rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, tacc);
+  if (q < kFpBound) {
+    constexpr int R = rows_ip_rows<LOG_M>();
+    stage_row_twiddles<LOG_M, R, kRipThreads>(smtw, T.fwd_fp + (long long)prime * (1 << T.log_n),
+                                             T.log_n, (long long)blockIdx.x * R);
+    cp_async_wait_all();
+    __syncthreads();
+    rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
+  } else if (q < kFwdLazyBound) {
+    rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
+  } else {
+    rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
+  }
   tmem::fence_before_sync();
   __syncthreads();
   if (warp == 0) {

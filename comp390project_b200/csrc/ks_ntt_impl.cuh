@@ -309,16 +309,16 @@ struct TwRowsGlobal {
   }
 };
 
-// Issues cp.async copies of the row-pass twiddle block (R (M - 1) doubles)
-// of rows [row0, row0 + R) into sm; the caller waits with cp_async_wait_all.
+// Issues cp.async copies (by the NTHR threads of the CTA) of the row-pass
+// twiddle block (R (M - 1) doubles) of rows [row0, row0 + R) into sm; the caller waits with cp_async_wait_all.
 // Block u (u = 0..LOG_M-1) is tw[2^(logN-LOG_M+u) + row0 2^u, +R 2^u); with R
 // even every block starts and ends on a 16-byte boundary.
-template <int LOG_M, int R>
+template <int LOG_M, int R, int NTHR = kThreads>
 __device__ __forceinline__ void stage_row_twiddles(double *sm, const double *tw, int log_n,
                                                    long long row0) {
   constexpr int M = 1 << LOG_M, TOTAL = R * (M - 1);
   static_assert(R % 2 == 0, "row blocks must be 16-byte multiples");
-  for (int ch = threadIdx.x; ch < TOTAL / 2; ch += kThreads) {
+  for (int ch = threadIdx.x; ch < TOTAL / 2; ch += NTHR) {
     const int e = 2 * ch;
     const int u = 31 - __clz(e / R + 1);
     const int o = e - R * ((1 << u) - 1);
