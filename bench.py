@@ -59,6 +59,8 @@ def parse():
                     help="launch the batch directly instead of replaying its CUDA graph")
     ap.add_argument("--lanes", type=int, default=4,
                     help="execution lanes (streams + scratch) for the batched key switches")
+    ap.add_argument("--group", type=int, default=1,
+                    help="key switches each lane pushes through every launch together (1..8)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["ks", "ntt", "hoisted", "matmul"], default="ks",
                     help="ks: config-3 rotations (default); ntt: config-2 batched NTT; "
@@ -792,9 +794,10 @@ def run_ours(args, rank, world):
     q, p = pr[:len(QBITS)], pr[len(QBITS):]
     L = len(q)
     if world > 1:
-        ctx = KsContext.from_process_group(LOG_N, q, p, device=dev, max_batch=args.lanes)
+        ctx = KsContext.from_process_group(LOG_N, q, p, device=dev, max_batch=args.lanes,
+                                           batch_group=args.group)
     else:
-        ctx = KsContext(LOG_N, q, p, device=dev, max_batch=args.lanes)
+        ctx = KsContext(LOG_N, q, p, device=dev, max_batch=args.lanes, batch_group=args.group)
     N = 1 << LOG_N
     nloc = ctx.n_local_limbs(L)
     B = args.batch
@@ -957,7 +960,8 @@ def run_ours(args, rank, world):
             "data": "synthetic",
             "config": {"workload": "config3-rotation: 64 ciphertexts, steps 1..64, 64 Galois keys",
                        "N": N, "L": L, "alpha": len(p), "dnum": beta, "batch": B,
-                       "parallelism": "limb-sharded x%d (input broadcast), %d lanes" % (world, args.lanes),
+                       "parallelism": "limb-sharded x%d (input broadcast), %d lanes x groups "
+                                      "of %d" % (world, args.lanes, args.group),
                        "cuda_graph": graph is not None,
                        "l2": "inputs (2.3 GB cts + 18.8 GB keys) exceed L2; no flush"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,

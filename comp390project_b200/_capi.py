@@ -53,6 +53,7 @@ class ks_params(C.Structure):
         ("p", C.POINTER(C.c_uint64)),
         ("mode", C.c_int),
         ("max_batch", C.c_int),
+        ("group", C.c_int),
     ]
 
 

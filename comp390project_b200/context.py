@@ -79,7 +79,8 @@ class KsContext:
 
     def __init__(self, log_n: int, q: Sequence[int], p: Sequence[int], device: int = 0,
                  rank: int = 0, world: int = 1, nccl_id: Optional[bytes] = None,
-                 mode: int = KS_MODE_INPUT_BROADCAST, max_batch: int = 1, _handle=None):
+                 mode: int = KS_MODE_INPUT_BROADCAST, max_batch: int = 1,
+                 batch_group: int = 1, _handle=None):
         self.lib = _capi.load()
         self.log_n = int(log_n)
         self.N = 1 << self.log_n
@@ -91,7 +92,7 @@ class KsContext:
         if _handle is not None:
             self.h = _handle
             return
-        prm = self._params(max_batch)
+        prm = self._params(max_batch, batch_group)
         h = C.c_void_p()
         idb = None
         if world > 1:
@@ -102,11 +103,11 @@ class KsContext:
                                      C.byref(h)))
         self.h = h
 
-    def _params(self, max_batch=1):
+    def _params(self, max_batch=1, batch_group=1):
         self._qbuf = (C.c_uint64 * self.L)(*[int(x) for x in self.q])
         self._pbuf = (C.c_uint64 * max(1, self.alpha))(*[int(x) for x in self.p] or [0])
         return ks_params(self.log_n, self.L, self._qbuf, self.alpha, self._pbuf, int(self.mode),
-                         int(max_batch))
+                         int(max_batch), int(batch_group))
 
     @classmethod
     def create_all(cls, log_n, q, p, devices: Sequence[int], mode=KS_MODE_INPUT_BROADCAST):
@@ -126,7 +127,7 @@ class KsContext:
 
     @classmethod
     def from_process_group(cls, log_n, q, p, device: Optional[int] = None, group=None,
-                           mode=KS_MODE_INPUT_BROADCAST, max_batch=1):
+                           mode=KS_MODE_INPUT_BROADCAST, max_batch=1, batch_group=1):
         """One context per torch.distributed rank; rank 0's NCCL id is broadcast."""
         import torch.distributed as dist
         torch = _torch()
@@ -137,7 +138,8 @@ class KsContext:
         if world > 1:
             dist.broadcast_object_list(obj, src=0, group=group)
         return cls(log_n, q, p, device=device, rank=rank, world=world,
-                   nccl_id=obj[0] if world > 1 else None, mode=mode, max_batch=max_batch)
+                   nccl_id=obj[0] if world > 1 else None, mode=mode, max_batch=max_batch,
+                   batch_group=batch_group)
 
     # -- lifecycle -----------------------------------------------------------
     def close(self):

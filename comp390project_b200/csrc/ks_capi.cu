@@ -576,6 +576,8 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
   KS_REQUIRE(c.mode == KS_MODE_INPUT_BROADCAST || c.mode == KS_MODE_OUTPUT_AGGREGATION,
              "unknown mode");
   c.max_batch = std::max(1, prm->max_batch);
+  c.group = std::max(1, prm->group);
+  KS_REQUIRE(c.group <= kMaxGroup, "group must be in [1, 8]");
   c.log_n = (int)prm->log_n;
   c.N = 1 << c.log_n;
   c.L = prm->n_q;
@@ -619,15 +621,29 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     const size_t nq = ib ? n_local(rank, world, c.L) : c.L;
     const size_t ml = ib ? (c.L + world - 1) / world : c.L;
     const size_t n_key_own = c.own_key.size();
-    size_t w_g = 2 * nq * N, w_coef = ml * N, w_coef_all = ib ? world * ml * N : 0;
-    size_t w_t = std::max((size_t)top.beta * top.n_out * N, 3 * n_key_own * N);
-    size_t w_cx = 2 * (size_t)top.n_out * N;
-    size_t w_ys = ib ? (size_t)c.max_p_own * 2 * N : 0;
-    size_t w_ya = ib ? (size_t)world * c.max_p_own * 2 * N : 0;
-    size_t w_z = 2 * nq * N;
-    size_t w_ct = 2 * nq * N;  // device copy of a host ciphertext (ks_rotate_batch_host)
+    // per member of a group (member strides of the group layout): automorphism
+    // output g0, coefficient input (send buffer of the all-gather) and its
+    // gathered form [G][ml][N], extended digits t, cx, the P limbs sent and
+    // gathered before ModDown, z, and the staging of a host ciphertext
+    const size_t g = c.group;
+    c.st_g = 2 * nq * N;
+    c.st_coef = ml * N;
+    c.st_coef_all = ib ? world * ml * N : ml * N;
+    c.st_t = (size_t)top.beta * top.n_out * N;
+    c.st_cx = 2 * (size_t)top.n_out * N;
+    c.st_ys = ib ? (size_t)c.max_p_own * 2 * N : 0;
+    c.st_ya = ib ? (size_t)world * c.st_ys : 0;
+    c.st_z = 2 * nq * N;
+    c.st_ct = 2 * nq * N;
+    size_t w_g = g * c.st_g, w_coef = g * c.st_coef, w_coef_all = ib ? g * c.st_coef_all : 0;
+    size_t w_t = std::max<size_t>(g * c.st_t, 3 * n_key_own * N);  // key generation borrows lane 0's t
+    size_t w_cx = g * c.st_cx;
+    size_t w_ys = g * c.st_ys;
+    size_t w_ya = g * c.st_ya;
+    size_t w_z = g * c.st_z;
+    size_t w_ct = g * c.st_ct;  // device copies of host ciphertexts (ks_rotate_batch_host)
     c.arena_words = w_g + w_coef + w_coef_all + w_t + w_cx + w_ys + w_ya + w_z + w_ct;
-    // one scratch arena per lane; lanes = max_batch (1..8)
+    // one scratch arena per lane; lanes = max_batch (1..8), each for `group` key switches
     // (contexts made by ks_ctx_create_all are set up one after another on one
     // thread, where splitting communicators would block, so they keep one lane)
     c.lanes.resize(comm ? 1 : std::min(8, c.max_batch));
@@ -1104,115 +1120,187 @@ void allgather(Ctx &c, ncclComm_t const &comm, const u64 *send, u64 *recv, size_
 // ---------------------------------------------------------------------------
 // The key switch
 // ---------------------------------------------------------------------------
-// Steps 2-3: scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j} of the
-// input limbs this rank extends (input broadcast all-gathers them), then the
-// base extension fused into the column pass -> L.s_t.
-void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const u64 *in_ntt, cudaStream_t s,
-                   uint32_t elt = 1) {
+// One member of a group of key switches that share every launch (grid z =
+// member; at most kMaxGroup).  The switched polynomial `in` (this rank's Q
+// limbs, NTT form) is read through X -> X^elt; the result goes to ct0, ct1:
+// with rotate, ct0 = g0 + ks0 (g0 null: ct0 = ks0) and ct1 = ks1; otherwise
+// ct0 += ks0, ct1 += ks1.
+struct KsMember {
+  const u64 *in = nullptr;
+  uint32_t elt = 1;
+  const KeyShard *key = nullptr;
+  u64 *ct0 = nullptr, *ct1 = nullptr;
+  const u64 *g0 = nullptr;
+};
+
+// g all-gathers of `words` words per rank, member b from send + b sst into
+// recv + b rst, as one NCCL group (one launch).
+void allgather_group(Ctx &c, ncclComm_t const &comm, const u64 *send, long long sst, u64 *recv,
+                     long long rst, size_t words, int g, cudaStream_t s) {
+  enqueue_nccl(c, comm, s, [&](ncclComm_t cm) {
+    ncclResult_t r = ncclGroupStart();
+    for (int b = 0; b < g && r == ncclSuccess; ++b)
+      r = ncclAllGather(send + b * sst, recv + b * rst, words, ncclUint64, cm, s);
+    const ncclResult_t r2 = ncclGroupEnd();
+    return r != ncclSuccess ? r : r2;
+  });
+}
+
+// Steps 2-3 for a group: scaled coefficient form v_j = [x_j (Q_d/q_j)^-1]_{q_j}
+// of the input limbs this rank extends (input broadcast all-gathers them),
+// then the base extension fused into the column pass -> the lane's t.
+void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
+                   cudaStream_t s) {
   const size_t N = c.N;
   const NttTables T = c.tables();
   {
     StageTimer tm(c, ST_INTT_IN, s);
-    LimbMap min{const_cast<u64 *>(in_ntt), 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
-    LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s, elt));
+    MemberIn mi{};
+    for (int b = 0; b < g; ++b) {
+      mi.in[b] = m[b].in;
+      mi.elt[b] = m[b].elt;
+    }
+    LimbMap min{const_cast<u64 *>(m[0].in), 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, 0};
+    LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, c.st_coef};
+    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s, 1, &mi, g));
     c.launches += lv.n_intt > 0 ? 2 : 0;
   }
   if (!c.replicated()) {
     StageTimer tm(c, ST_COMM, s);
-    allgather(c, L.comm, L.s_coef, L.s_coef_all, (size_t)lv.coef_ml * N, s);
+    allgather_group(c, L.comm, L.s_coef, c.st_coef, L.s_coef_all, c.st_coef_all,
+                    (size_t)lv.coef_ml * N, g, s);
   }
   {
     StageTimer tm(c, ST_MODUP_COLS, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
-                             lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s));
+                             lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s, g, c.st_coef_all, c.st_t));
     c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
 }
 
 // Output aggregation: sum the partial inner products of all ranks (every
 // rank then holds all of cx; G q < 2^64) and reduce mod the limb primes.
-void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, cudaStream_t s) {
+void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, int g, cudaStream_t s) {
   if (!c.oa()) return;
   {
     StageTimer tm(c, ST_COMM, s);
+    const size_t words = (size_t)(g - 1) * c.st_cx + (size_t)2 * lv.n_out * c.N;
     enqueue_nccl(c, L.comm, s, [&](ncclComm_t cm) {
-      return ncclAllReduce(L.s_cx, L.s_cx, (size_t)2 * lv.n_out * c.N, ncclUint64, ncclSum, cm, s);
+      return ncclAllReduce(L.s_cx, L.s_cx, words, ncclUint64, ncclSum, cm, s);
     });
   }
-  KS_CUDA(mod_reduce(L.s_cx, 2 * lv.n_out, lv.cx_prime.d, c.d_primes, c.log_n, s));
-  c.launches += 1;
+  for (int b = 0; b < g; ++b) {
+    KS_CUDA(mod_reduce(L.s_cx + b * c.st_cx, 2 * lv.n_out, lv.cx_prime.d, c.d_primes, c.log_n, s));
+    c.launches += 1;
+  }
 }
 
-// Steps 5-7: ModDown of L.s_cx into the ciphertext (see moddown_fused_rows
-// for rotate / diag).
-void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, u64 *ct0, u64 *ct1, const u64 *g0,
-                bool rotate, const u64 *diag, cudaStream_t s) {
+// Steps 5-7 for a group: ModDown of each member's cx into its ciphertext
+// (see moddown_fused_rows for rotate).
+void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g, bool rotate,
+                cudaStream_t s) {
   const size_t N = c.N;
   const NttTables T = c.tables();
   // 5. P part to scaled coefficient form [y_i (P/p_i)^-1]_{p_i}
   const u64 *y_base;
+  long long y_bstride;
   if (c.replicated()) {
     StageTimer tm(c, ST_INTT_P, s);
-    LimbMap mp{L.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-    KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
+    LimbMap mp{L.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_cx};
+    KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
     c.launches += 2;
     y_base = L.s_cx;
+    y_bstride = c.st_cx;
   } else {
     {
       StageTimer tm(c, ST_INTT_P, s);
-      for (int p = 0; p < 2; ++p)
-        for (int k = 0; k < lv.n_p; ++k)
-          KS_CUDA(cudaMemcpyAsync(L.s_ysend + ((size_t)k * 2 + p) * N,
-                                  L.s_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N, N * 8,
-                                  cudaMemcpyDeviceToDevice, s));
+      for (int b = 0; b < g; ++b)
+        for (int p = 0; p < 2; ++p)
+          for (int k = 0; k < lv.n_p; ++k)
+            KS_CUDA(cudaMemcpyAsync(L.s_ysend + b * c.st_ys + ((size_t)k * 2 + p) * N,
+                                    L.s_cx + b * c.st_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N,
+                                    N * 8, cudaMemcpyDeviceToDevice, s));
       if (lv.n_p > 0) {
-        LimbMap mp{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1};
-        KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s));
+        LimbMap mp{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_ys};
+        KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
         c.launches += 2;
       }
     }
     StageTimer tm(c, ST_COMM, s);
-    allgather(c, L.comm, L.s_ysend, L.s_yall, (size_t)c.max_p_own * 2 * N, s);
+    allgather_group(c, L.comm, L.s_ysend, c.st_ys, L.s_yall, c.st_ya,
+                    (size_t)c.max_p_own * 2 * N, g, s);
     y_base = L.s_yall;
+    y_bstride = c.st_ya;
   }
   // 6. P -> Q conversion fused into the column pass
   {
     StageTimer tm(c, ST_MODDOWN_COLS, s);
     KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md,
-                               lv.md_job_ps.d, lv.n_md_fp, T, s));
+                               lv.md_job_ps.d, lv.n_md_fp, T, s, g, y_bstride, c.st_z));
     c.launches += lv.n_q > 0 ? 1 : 0;
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {
     StageTimer tm(c, ST_MODDOWN_ROWS, s);
-    KS_CUDA(moddown_fused_rows(L.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, L.s_cx,
-                               (long long)lv.n_out * N, ct0, ct1, g0, rotate, diag, c.md, T, s));
-    c.launches += 1;
+    GroupArgs G{};
+    G.n = g;
+    G.z = c.st_z;
+    G.cx = c.st_cx;
+    for (int b = 0; b < g; ++b) {
+      G.ct0[b] = m[b].ct0;
+      G.ct1[b] = m[b].ct1;
+      G.g0p[b] = m[b].g0;
+    }
+    KS_CUDA(moddown_fused_rows_group(G, L.s_z, lv.n_q, lv.q_index.d, lv.cx_slot_q.d, L.s_cx,
+                                     (long long)lv.n_out * N, rotate, c.md, T, s));
+    c.launches += lv.n_q > 0 ? 1 : 0;
   }
 }
 
-// in_ntt: the polynomial to switch (NTT form, owned Q limbs [n_q][N]), read
-// through X -> X^elt (elt = 1: as it is).
-// rotate: ct0 = g0 + ks0, ct1 = ks1; else ct0 += ks0, ct1 += ks1.
-void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt,
-                    u64 *ct0, u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s,
-                    uint32_t elt = 1) {
+// The key switch of a group of g members on lane L (steps 2-7; the caller has
+// done step 1, the automorphism of c0, where it rotates).
+void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
+                     bool rotate, cudaStream_t s) {
+  KS_REQUIRE(g >= 1 && g <= c.group, "group larger than the context's scratch");
   const NttTables T = c.tables();
-  ks_modup_cols(c, L, lv, in_ntt, s, elt);
+  ks_modup_cols(c, L, lv, m, g, s);
   // 4. row pass of every extended limb fused with the inner product
   {
     StageTimer tm(c, ST_MODUP_ROWS_IP, s);
     if (lv.lay.n_digits > 0) {
-      KS_CUDA(modup_rows_inner_product(L.s_t, in_ntt, key.d, key.limbs, L.s_cx, lv.mu, lv.lay,
-                                       T, s, elt));
+      GroupArgs G{};
+      G.n = g;
+      G.t = c.st_t;
+      G.cx = c.st_cx;
+      for (int b = 0; b < g; ++b) {
+        G.in.in[b] = m[b].in;
+        G.in.elt[b] = m[b].elt;
+        G.key[b] = m[b].key->d;
+      }
+      KS_CUDA(modup_rows_inner_product_group(G, L.s_t, m[0].key->limbs, L.s_cx, lv.mu, lv.lay,
+                                             T, s));
       c.launches += lv.lay.n_out > 0 ? 1 : 0;
     } else {  // output aggregation with more ranks than digits: a zero partial sum
-      KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));
+      for (int b = 0; b < g; ++b)
+        KS_CUDA(cudaMemsetAsync(L.s_cx + b * c.st_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));
     }
   }
-  ks_aggregate(c, L, lv, s);
-  ks_moddown(c, L, lv, ct0, ct1, g0, rotate, nullptr, s);
+  ks_aggregate(c, L, lv, g, s);
+  ks_moddown(c, L, lv, m, g, rotate, s);
+}
+
+// One key switch (a group of one).
+void keyswitch_core(Ctx &c, Ctx::Lane &L, const Level &lv, const KeyShard &key, const u64 *in_ntt,
+                    u64 *ct0, u64 *ct1, const u64 *g0, bool rotate, cudaStream_t s,
+                    uint32_t elt = 1) {
+  KsMember m;
+  m.in = in_ntt;
+  m.elt = elt;
+  m.key = &key;
+  m.ct0 = ct0;
+  m.ct1 = ct1;
+  m.g0 = g0;
+  keyswitch_group(c, L, lv, &m, 1, rotate, s);
 }
 
 const Level &level_of(Ctx &c, int Ql) {
@@ -1221,23 +1309,43 @@ const Level &level_of(Ctx &c, int Ql) {
   return c.levels[Ql];
 }
 
-void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
+// Rotations of a group of g ciphertexts cts[b] ([2][n_q][N], in place) by
+// their Galois elements elts[b], pushed through every launch together.
+void do_apply_galois_group(Ctx &c, Ctx::Lane &L, u64 *const *cts, const uint32_t *elts, int g,
+                           int Ql, cudaStream_t s) {
   check_alive(c);
-  KS_REQUIRE(aligned16(ct) && (ct != nullptr || n_local(c.rank, c.replicated() ? 1 : c.world, Ql) == 0),
-             "ciphertext pointer null or not 16-byte aligned");
-  check_elt(c, elt);
+  KS_REQUIRE(g >= 1 && g <= c.group, "group larger than the context's scratch");
   const Level &lv = level_of(c, Ql);
-  const KeyShard &key = key_get(c, KS_KEY_GALOIS, elt);
   const size_t nq = lv.n_q, N = c.N;
+  KsMember m[kMaxGroup];
+  MemberIn mi{};
+  for (int b = 0; b < g; ++b) {
+    u64 *ct = cts[b];
+    KS_REQUIRE(aligned16(ct) && (ct != nullptr || nq == 0),
+               "ciphertext pointer null or not 16-byte aligned");
+    check_elt(c, elts[b]);
+    m[b].in = nq ? ct + nq * N : nullptr;
+    m[b].elt = elts[b];
+    m[b].key = &key_get(c, KS_KEY_GALOIS, elts[b]);
+    m[b].ct0 = ct;
+    m[b].ct1 = nq ? ct + nq * N : nullptr;
+    m[b].g0 = L.s_g + b * c.st_g;
+    mi.in[b] = ct;
+    mi.elt[b] = elts[b];
+  }
   KS_CUDA(cudaSetDevice(c.device));
-  // 1. automorphism of c0 -> g0 (c1 is read through the automorphism by the
-  //    input INTT and the inner product; it is overwritten only at the end)
-  {
+  // 1. automorphism of every c0 -> g0 (c1 is read through the automorphism by
+  //    the input INTT and the inner product; it is overwritten only at the end)
+  if (nq > 0) {
     StageTimer tm(c, ST_GALOIS, s);
-    KS_CUDA(galois_ntt(ct, L.s_g, (int)nq, c.log_n, elt, s));
+    KS_CUDA(galois_ntt_group(mi, g, L.s_g, c.st_g, (int)nq, c.log_n, s));
     c.launches += 1;
   }
-  keyswitch_core(c, L, lv, key, ct + nq * N, ct, ct + nq * N, L.s_g, true, s, elt);
+  keyswitch_group(c, L, lv, m, g, true, s);
+}
+
+void do_apply_galois(Ctx &c, Ctx::Lane &L, u64 *ct, int Ql, uint32_t elt, cudaStream_t s) {
+  do_apply_galois_group(c, L, &ct, &elt, 1, Ql, s);
 }
 
 uint32_t elt_of_step(const Ctx &c, int step) {
@@ -1289,7 +1397,9 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
   const NttTables T = c.tables();
   Ctx::Lane &L0 = c.lanes[0];
   const u64 *c1 = ct + nq * N;
-  ks_modup_cols(c, L0, lv, c1, s);
+  KsMember m0;
+  m0.in = c1;
+  ks_modup_cols(c, L0, lv, &m0, 1, s);
   {
     StageTimer tm(c, ST_MODUP_ROWS, s);
     LimbMap mt{L0.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
@@ -1309,8 +1419,11 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
         KS_CUDA(cudaMemsetAsync(L0.s_cx, 0, (size_t)2 * lv.n_out * N * 8, s));
       }
     }
-    ks_aggregate(c, L0, lv, s);
-    ks_moddown(c, L0, lv, out, out + nq * N, nullptr, true, nullptr, s);
+    ks_aggregate(c, L0, lv, 1, s);
+    KsMember mo;
+    mo.ct0 = out;
+    mo.ct1 = out + nq * N;
+    ks_moddown(c, L0, lv, &mo, 1, true, s);  // rotate without g0: out = ModDown(acc)
     return;
   }
   const int nl = std::min<int>((int)c.lanes.size(), n);
@@ -1337,8 +1450,12 @@ void do_hoisted(Ctx &c, const u64 *ct, int Ql, const int *steps, int n, u64 *con
         KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * N * 8, ls));
       }
     }
-    ks_aggregate(c, L, lv, ls);
-    ks_moddown(c, L, lv, outs[i], outs[i] + nq * N, L.s_g, true, nullptr, ls);
+    ks_aggregate(c, L, lv, 1, ls);
+    KsMember mo;
+    mo.ct0 = outs[i];
+    mo.ct1 = outs[i] + nq * N;
+    mo.g0 = L.s_g;
+    ks_moddown(c, L, lv, &mo, 1, true, ls);
   }
   for (int li = 1; li < nl; ++li) {
     KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));
@@ -1807,23 +1924,26 @@ int ks_rotate_batch(ks_ctx *ctx, uint64_t *const *cts, const int *steps, int n, 
     Ctx &c = ctx->c;
     KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
     const cudaStream_t s = (cudaStream_t)stream;
-    const int nl = std::min<int>((int)c.lanes.size(), n);
+    // groups of up to c.group consecutive rotations, spread over the lanes
+    const int g = c.group, n_groups = (n + g - 1) / g;
+    const int nl = std::min<int>((int)c.lanes.size(), n_groups);
+    std::vector<uint32_t> elts(n);
+    for (int i = 0; i < n; ++i) elts[i] = elt_of_step(c, steps[i]);
     if (nl <= 1) {
-      for (int i = 0; i < n; ++i)
-        do_apply_galois(c, c.lanes[0], cts[i], level_limbs, elt_of_step(c, steps[i]), s);
+      for (int i0 = 0; i0 < n; i0 += g)
+        do_apply_galois_group(c, c.lanes[0], cts + i0, elts.data() + i0, std::min(g, n - i0),
+                              level_limbs, s);
       return;
     }
     // fork: every lane waits for the work already queued on the caller's stream
     KS_CUDA(cudaSetDevice(c.device));
     KS_CUDA(cudaEventRecord(c.ev_fork, s));
-    for (int li = 0; li < nl; ++li) {
+    for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
+    for (int gi = 0; gi < n_groups; ++gi) {
+      const int li = gi % nl, i0 = gi * g;
       cudaStream_t ls = li == 0 ? s : c.lanes[li].stream;
-      if (li > 0) KS_CUDA(cudaStreamWaitEvent(ls, c.ev_fork, 0));
-    }
-    for (int i = 0; i < n; ++i) {
-      const int li = i % nl;
-      cudaStream_t ls = li == 0 ? s : c.lanes[li].stream;
-      do_apply_galois(c, c.lanes[li], cts[i], level_limbs, elt_of_step(c, steps[i]), ls);
+      do_apply_galois_group(c, c.lanes[li], cts + i0, elts.data() + i0, std::min(g, n - i0),
+                            level_limbs, ls);
     }
     // join: the caller's stream waits for every lane
     for (int li = 1; li < nl; ++li) {
@@ -1852,21 +1972,30 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     const Level &lv = level_of(c, level_limbs);
     const size_t bytes = 2 * (size_t)lv.n_q * c.N * 8;
     const cudaStream_t s = (cudaStream_t)stream;
-    const int nl = std::min<int>((int)c.lanes.size(), std::max(n, 1));
+    const int g = c.group, n_groups = (n + g - 1) / g;
+    const int nl = std::min<int>((int)c.lanes.size(), std::max(n_groups, 1));
+    for (int i = 0; i < n; ++i) KS_REQUIRE(host_cts[i] != nullptr, "host ciphertext pointer is null");
     KS_CUDA(cudaSetDevice(c.device));
-    // fork the lanes from the caller's stream; on each lane: copy in, rotate
-    // in the lane's staging buffer, copy out -- the copies of one lane run on
-    // the copy engines while the other lanes compute
+    // fork the lanes from the caller's stream; on each lane, per group: copy
+    // the members in, rotate them in the lane's staging buffers, copy them
+    // out -- the copies of one lane run on the copy engines while the other
+    // lanes compute
     KS_CUDA(cudaEventRecord(c.ev_fork, s));
     for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
-    for (int i = 0; i < n; ++i) {
-      KS_REQUIRE(host_cts[i] != nullptr, "host ciphertext pointer is null");
-      const int li = i % nl;
+    for (int gi = 0; gi < n_groups; ++gi) {
+      const int li = gi % nl, i0 = gi * g, gs = std::min(g, n - i0);
       Ctx::Lane &L = c.lanes[li];
       const cudaStream_t ls = li == 0 ? s : L.stream;
-      KS_CUDA(cudaMemcpyAsync(L.s_ct, host_cts[i], bytes, cudaMemcpyHostToDevice, ls));
-      do_apply_galois(c, L, L.s_ct, level_limbs, elt_of_step(c, steps[i]), ls);
-      KS_CUDA(cudaMemcpyAsync(host_cts[i], L.s_ct, bytes, cudaMemcpyDeviceToHost, ls));
+      u64 *dev[kMaxGroup];
+      uint32_t elts[kMaxGroup];
+      for (int b = 0; b < gs; ++b) {
+        dev[b] = L.s_ct + b * c.st_ct;
+        elts[b] = elt_of_step(c, steps[i0 + b]);
+        KS_CUDA(cudaMemcpyAsync(dev[b], host_cts[i0 + b], bytes, cudaMemcpyHostToDevice, ls));
+      }
+      do_apply_galois_group(c, L, dev, elts, gs, level_limbs, ls);
+      for (int b = 0; b < gs; ++b)
+        KS_CUDA(cudaMemcpyAsync(host_cts[i0 + b], dev[b], bytes, cudaMemcpyDeviceToHost, ls));
     }
     for (int li = 1; li < nl; ++li) {
       KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));

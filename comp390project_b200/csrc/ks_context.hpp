@@ -137,6 +137,11 @@ struct Ctx {
   std::vector<Lane> lanes;
   cudaEvent_t ev_fork = nullptr;
   size_t arena_words = 0;
+  // Groups: a lane pushes up to `group` key switches through every launch
+  // together; member b of a lane's scratch buffer X sits b * st_X words on.
+  int group = 1;
+  long long st_g = 0, st_coef = 0, st_coef_all = 0, st_t = 0, st_cx = 0, st_ys = 0, st_ya = 0,
+            st_z = 0, st_ct = 0;
   int max_p_own = 0;
   // comm (lane 0's communicator)
   ncclComm_t comm = nullptr;

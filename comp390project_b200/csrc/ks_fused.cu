@@ -32,7 +32,8 @@ __global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTabl
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
   const int li = blockIdx.y;
-  u64 *a = m.base + (m.offsets ? m.offsets[li] : (long long)li * m.stride);
+  u64 *a = m.base + (m.offsets ? m.offsets[li] : (long long)li * m.stride) +
+           (long long)blockIdx.z * m.bstride;
   const int prime = m.prime_tab ? m.prime_tab[li] : m.first_prime + (li % m.period);
   if (prime < 0) return;
   const PrimeDev P = T.primes[prime];
@@ -137,7 +138,8 @@ template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 3)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
-                 const int *__restrict__ job_s, int job0, NttTables T) {
+                 const int *__restrict__ job_s, int job0, NttTables T, long long v_bstride,
+                 long long t_bstride) {
   constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
@@ -150,8 +152,9 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int col = blockIdx.x * G::C + c;
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
   const long long wo = ((long long)d * mu.QlP + j) * mu.alpha;
+  v_all += blockIdx.z * v_bstride;  // member of the group
   auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
-  u64 *out = t + ((long long)d * lay.n_out + s) * N;
+  u64 *out = t + blockIdx.z * t_bstride + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
     const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
@@ -207,10 +210,13 @@ __device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool r
 // one u64 as two columns), not in registers.  The extended limbs never
 // return to HBM.
 struct RowsIpArgs {
-  const u64 *t, *c_ntt, *key;
-  u64 *cx;
+  const u64 *t;                  // member b: t + b t_bstride
+  u64 *cx;                       // member b: cx + b cx_bstride
+  long long t_bstride, cx_bstride;
   int key_limbs;
-  uint32_t elt;  // c_ntt is read through X -> X^elt (1: as it is)
+  const u64 *c_ntt[kMaxGroup];   // NTT-form input of member b ...
+  uint32_t elt[kMaxGroup];       // ... read through X -> X^elt[b] (1: as it is)
+  const u64 *key[kMaxGroup];     // key shard of member b
 };
 
 // A CTA is kRipWarps warps; warp w owns the 512 tile words [512w, 512w + 512)
@@ -247,6 +253,11 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
                                              const double *smtw, uint32_t tacc) {
   using G = RowGeom<LOG_M>;
   const PrimeDev P = T.primes[prime];
+  const int mb = blockIdx.z;  // member of the group
+  const u64 *const a_key = A.key[mb], *const a_t = A.t + mb * A.t_bstride;
+  const u64 *const a_c = A.c_ntt[mb];
+  u64 *const a_cx = A.cx + mb * A.cx_bstride;
+  const uint32_t elt = A.elt[mb];
   const int log_n = T.log_n, N = 1 << log_n;
   const int j = lay.out_j[s];
   const int tt = threadIdx.x % G::TT, rr = threadIdx.x / G::TT;
@@ -256,15 +267,15 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
   const int wofs = warp * 512 + 2 * lane;  // + 64 i: this lane's pairs in the tile
   const int dj = j < mu.Ql ? j / mu.alpha : -1;
   const long long kstride = (long long)A.key_limbs * N;
-  const u64 *kbase = A.key + (long long)lay.key_slot[s] * N + tile0 + wofs;
-  const u64 *tbase = A.t + (long long)s * N + tile0;
+  const u64 *kbase = a_key + (long long)lay.key_slot[s] * N + tile0 + wofs;
+  const u64 *tbase = a_t + (long long)s * N + tile0;
   const long long tstride = (long long)lay.n_out * N;
   // own-digit limb, read through the automorphism: the CTA's tile gathers
   // from the aligned source tile cown, pair (k, k+1) from (src & ~1) (swapped
   // when src is odd)
-  const u64 *climb = dj >= 0 ? A.c_ntt + (long long)lay.c_slot[s] * N : nullptr;
+  const u64 *climb = dj >= 0 ? a_c + (long long)lay.c_slot[s] * N : nullptr;
   const u64 *cown =
-      climb ? climb + (galois_src((uint32_t)tile0, A.elt, log_n) & ~(uint32_t)(kRipTile - 1))
+      climb ? climb + (galois_src((uint32_t)tile0, elt, log_n) & ~(uint32_t)(kRipTile - 1))
             : nullptr;
   const ulonglong2 *tw = T.fwd + (long long)prime * N;
   // FP64 primes: the CTA's row twiddles, staged once in shared memory
@@ -316,7 +327,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
         k0[q] = kst[i * 32];
         k1[q] = kst[(8 + i) * 32];
         if (own) {
-          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), A.elt, log_n);
+          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), elt, log_n);
           ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
           if (src & 1u) {
             const u64 tmp = v.x;
@@ -355,7 +366,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
     tmem::wait_st();
     __syncwarp();  // exchange buffer and key stage are reused by the next digit
   }
-  u64 *o0 = A.cx + (long long)s * N + tile0 + wofs;
+  u64 *o0 = a_cx + (long long)s * N + tile0 + wofs;
   u64 *o1 = o0 + (long long)lay.n_out * N;
 #pragma unroll
   for (int h = 0; h < 4; ++h) {
@@ -436,7 +447,8 @@ template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 2)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
                    int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
-                   const int *__restrict__ job_ps, int job0) {
+                   const int *__restrict__ job_ps, int job0, long long y_bstride,
+                   long long z_bstride) {
   constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];
@@ -448,6 +460,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int c = threadIdx.x % G::C, tt = (threadIdx.x / G::C) & (G::TT - 1);  // tt < TT (known range)
   const int col = blockIdx.x * G::C + c;
   const long long wo = (long long)j * md.alpha;
+  y_base += blockIdx.z * y_bstride;  // member of the group
+  z += blockIdx.z * z_bstride;
   auto src = [&](int i) { return y_base + y_off[p * md.alpha + i]; };
   auto fp_src = [&](int i) { return T.primes[md.first_p + i].q < kFpBound; };
   auto fill = [&](u64 (&x)[kEpt]) {
@@ -472,14 +486,26 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// Per-member buffers of a group for the ModDown row pass (by value).
+struct MdGroup {
+  long long z_bstride, cx_bstride;
+  u64 *ct0[kMaxGroup], *ct1[kMaxGroup];
+  const u64 *g0[kMaxGroup];
+};
+
 // Row pass of z with the ModDown finish fused into the epilogue.
 template <int LOG_M>
 __global__ void __launch_bounds__(kThreads)
     k_moddown_rows(const u64 *__restrict__ z, int n_q, const int *__restrict__ q_index,
                    const int *__restrict__ cx_slot, const u64 *__restrict__ cx,
-                   long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0, int rotate,
+                   long long cx_stride_poly, MdGroup grp, int rotate,
                    const u64 *__restrict__ diag, ModDownDev md, NttTables T) {
   using G = RowGeom<LOG_M>;
+  const int mb = blockIdx.z;  // member of the group
+  z += mb * grp.z_bstride;
+  cx += mb * grp.cx_bstride;
+  u64 *const ct0 = grp.ct0[mb], *const ct1 = grp.ct1[mb];
+  const u64 *const g0 = grp.g0[mb];
   extern __shared__ __align__(16) u64 dsm[];
   u64 *sm = dsm;
   double *smtw = reinterpret_cast<double *>(dsm + G::SMEM);
@@ -574,28 +600,25 @@ __global__ void __launch_bounds__(kThreads, 3)
 template <int LOG_M>
 cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q,
                                const int *q_index, const int *cx_slot, const u64 *cx,
-                               long long cx_stride_poly, u64 *ct0, u64 *ct1, const u64 *g0,
-                               int rot, const u64 *diag, const ModDownDev &md,
-                               const NttTables &T) {
+                               long long cx_stride_poly, const MdGroup &grp, int rot,
+                               const u64 *diag, const ModDownDev &md, const NttTables &T) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
   static std::atomic<unsigned> attr_done{0};
   cudaError_t e = ensure_dynamic_smem(k_moddown_rows<LOG_M>, smem, attr_done);
   if (e != cudaSuccess) return e;
   k_moddown_rows<LOG_M><<<grid, kThreads, smem, s>>>(z, n_q, q_index, cx_slot, cx, cx_stride_poly,
-                                                     ct0, ct1, g0, rot, diag, md, T);
+                                                     grp, rot, diag, md, T);
   return cudaGetLastError();
 }
 
 template <int LOG_M>
-cudaError_t launch_modup_rows_ip(cudaStream_t s, const u64 *t, const u64 *c_ntt, const u64 *key,
-                                 int key_limbs, u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                 const NttTables &T, uint32_t elt) {
+cudaError_t launch_modup_rows_ip(cudaStream_t s, const RowsIpArgs &A, int group,
+                                 const ModUpDev &mu, const KsLayout &lay, const NttTables &T) {
   constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
   static std::atomic<unsigned> attr_done{0};
   cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M>, smem, attr_done);
   if (e != cudaSuccess) return e;
-  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out);
-  const RowsIpArgs A{t, c_ntt, key, cx, key_limbs, elt};
+  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out, group);
   k_modup_rows_ip<LOG_M><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
   return cudaGetLastError();
 }
@@ -609,14 +632,15 @@ inline int col_tiles(int log_n, int log_m) {
 
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
                                const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
-                               uint32_t elt) {
+                               uint32_t elt, const MemberIn *mi, int group) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
   if (n_limbs == 0) return cudaSuccess;
   // first pass: the ordinary inverse row pass, src (through elt) -> dst
-  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst, elt);
+  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst, elt, mi, group);
   if (e != cudaSuccess) return e;
   const int s1 = T.log_n / 2;
-  dim3 grid(col_tiles(T.log_n, s1), n_limbs);
+  dim3 grid(col_tiles(T.log_n, s1), n_limbs, group);
   switch (T.log_n) {
     case 12: k_inv_cols_scaled<12><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
     case 13: k_inv_cols_scaled<13><<<grid, kThreads, 0, s>>>(dst, T, scale); break;
@@ -630,54 +654,82 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
 
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
-                             int n_fp, const NttTables &T, cudaStream_t s) {
+                             int n_fp, const NttTables &T, cudaStream_t s, int group,
+                             long long v_bstride, long long t_bstride) {
   if (!ntt_supported_log_n(T.log_n) || n_jobs < 0 || n_jobs > 65535) return cudaErrorInvalidValue;
   if (mu.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > n_jobs) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
   if (n_jobs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  dim3 grid(col_tiles(T.log_n, s1), n_jobs);
+  dim3 grid(col_tiles(T.log_n, s1), n_jobs, group);
   switch (T.log_n) {
-    case 12: k_modup_cols<12><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 13: k_modup_cols<13><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 14: k_modup_cols<14><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 15: k_modup_cols<15><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
-    case 16: k_modup_cols<16><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T); break;
+    case 12: k_modup_cols<12><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 13: k_modup_cols<13><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 14: k_modup_cols<14><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 15: k_modup_cols<15><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 16: k_modup_cols<16><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int key_limbs,
+                                           u64 *cx, const ModUpDev &mu, const KsLayout &lay,
+                                           const NttTables &T, cudaStream_t s) {
+  if (G.n < 1 || G.n > kMaxGroup) return cudaErrorInvalidValue;
+  for (int b = 0; b < G.n; ++b)
+    if (!(G.in.elt[b] & 1u) || G.in.elt[b] >= (2u << T.log_n)) return cudaErrorInvalidValue;
+  if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
+    return cudaErrorInvalidValue;
+  if (lay.n_out == 0) return cudaSuccess;
+  RowsIpArgs A{};
+  A.t = t;
+  A.cx = cx;
+  A.t_bstride = G.t;
+  A.cx_bstride = G.cx;
+  A.key_limbs = key_limbs;
+  for (int b = 0; b < G.n; ++b) {
+    A.c_ntt[b] = G.in.in[b];
+    A.elt[b] = G.in.elt[b];
+    A.key[b] = G.key[b];
+  }
+  const int s2 = T.log_n - T.log_n / 2;
+  switch (s2) {
+    case 6: return launch_modup_rows_ip<6>(s, A, G.n, mu, lay, T);
+    case 7: return launch_modup_rows_ip<7>(s, A, G.n, mu, lay, T);
+    case 8: return launch_modup_rows_ip<8>(s, A, G.n, mu, lay, T);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s,
                                      uint32_t elt) {
-  if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
-  if (!ntt_supported_log_n(T.log_n) || lay.n_out < 0 || lay.n_out > 65535)
-    return cudaErrorInvalidValue;
-  if (lay.n_out == 0) return cudaSuccess;
-  const int s2 = T.log_n - T.log_n / 2;
-  switch (s2) {
-    case 6: return launch_modup_rows_ip<6>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
-    case 7: return launch_modup_rows_ip<7>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
-    case 8: return launch_modup_rows_ip<8>(s, t, c_ntt, key, key_limbs, cx, mu, lay, T, elt);
-    default: return cudaErrorInvalidValue;
-  }
+  GroupArgs G{};
+  G.n = 1;
+  G.in.in[0] = c_ntt;
+  G.in.elt[0] = elt;
+  G.key[0] = key;
+  return modup_rows_inner_product_group(G, t, key_limbs, cx, mu, lay, T, s);
 }
 
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
                                const int *q_index, const ModDownDev &md, const int *job_ps,
-                               int n_fp, const NttTables &T, cudaStream_t s) {
+                               int n_fp, const NttTables &T, cudaStream_t s, int group,
+                               long long y_bstride, long long z_bstride) {
   if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
   if (md.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > 2 * n_q) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
   if (n_q == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q);
+  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q, group);
   switch (T.log_n) {
-    case 12: k_moddown_cols<12><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 13: k_moddown_cols<13><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 14: k_moddown_cols<14><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 15: k_moddown_cols<15><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
-    case 16: k_moddown_cols<16><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0); break;
+    case 12: k_moddown_cols<12><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 13: k_moddown_cols<13><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 14: k_moddown_cols<14><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 15: k_moddown_cols<15><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 16: k_moddown_cols<16><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -701,21 +753,52 @@ cudaError_t rescale_fused_cols(const u64 *last, u64 q_last, bool last_fp, u64 *z
   return cudaGetLastError();
 }
 
+static cudaError_t moddown_rows_dispatch(const u64 *z, int n_q, const int *q_index,
+                                         const int *cx_slot, const u64 *cx,
+                                         long long cx_stride_poly, const MdGroup &grp, int group,
+                                         bool rotate, const u64 *diag, const ModDownDev &md,
+                                         const NttTables &T, cudaStream_t s) {
+  if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (n_q == 0) return cudaSuccess;
+  const int s2 = T.log_n - T.log_n / 2;
+  dim3 grid((1 << T.log_n) / kTile, 2 * n_q, group);
+  const int rot = rotate ? 1 : 0;
+  switch (s2) {
+    case 6: return launch_moddown_rows<6>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, grp, rot, diag, md, T);
+    case 7: return launch_moddown_rows<7>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, grp, rot, diag, md, T);
+    case 8: return launch_moddown_rows<8>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, grp, rot, diag, md, T);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const int *cx_slot,
                                const u64 *cx, long long cx_stride_poly, u64 *ct0, u64 *ct1,
                                const u64 *g0, bool rotate, const u64 *diag,
                                const ModDownDev &md, const NttTables &T, cudaStream_t s) {
-  if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
-  if (n_q == 0) return cudaSuccess;
-  const int s2 = T.log_n - T.log_n / 2;
-  dim3 grid((1 << T.log_n) / kTile, 2 * n_q);
-  const int rot = rotate ? 1 : 0;
-  switch (s2) {
-    case 6: return launch_moddown_rows<6>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
-    case 7: return launch_moddown_rows<7>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
-    case 8: return launch_moddown_rows<8>(grid, s, z, n_q, q_index, cx_slot, cx, cx_stride_poly, ct0, ct1, g0, rot, diag, md, T);
-    default: return cudaErrorInvalidValue;
+  MdGroup grp{};
+  grp.ct0[0] = ct0;
+  grp.ct1[0] = ct1;
+  grp.g0[0] = g0;
+  return moddown_rows_dispatch(z, n_q, q_index, cx_slot, cx, cx_stride_poly, grp, 1, rotate,
+                               diag, md, T, s);
+}
+
+cudaError_t moddown_fused_rows_group(const GroupArgs &G, const u64 *z, int n_q,
+                                     const int *q_index, const int *cx_slot, const u64 *cx,
+                                     long long cx_stride_poly, bool rotate, const ModDownDev &md,
+                                     const NttTables &T, cudaStream_t s) {
+  if (G.n < 1 || G.n > kMaxGroup) return cudaErrorInvalidValue;
+  MdGroup grp{};
+  grp.z_bstride = G.z;
+  grp.cx_bstride = G.cx;
+  for (int b = 0; b < G.n; ++b) {
+    grp.ct0[b] = G.ct0[b];
+    grp.ct1[b] = G.ct1[b];
+    grp.g0[b] = G.g0p[b];
   }
+  return moddown_rows_dispatch(z, n_q, q_index, cx_slot, cx, cx_stride_poly, grp, G.n, rotate,
+                               nullptr, md, T, s);
 }
 
 }  // namespace ksb

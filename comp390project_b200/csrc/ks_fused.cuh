@@ -16,7 +16,19 @@ namespace ksb {
 // double, the others canonical uint64 (the form the base conversions read).
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
                                const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
-                               uint32_t elt = 1);
+                               uint32_t elt = 1, const MemberIn *mi = nullptr, int group = 1);
+
+// A group of key switches pushed through each launch together (grid z =
+// member): the member strides (words) of the scratch buffers, and the
+// buffers of each member that the caller owns.
+struct GroupArgs {
+  int n;                                 // members, 1..kMaxGroup
+  long long t, cx, z, g0;                // member strides of t, cx, z, g0
+  MemberIn in;                           // NTT-form input (read through elt) of each member
+  const u64 *key[kMaxGroup];             // key shard of each member
+  u64 *ct0[kMaxGroup], *ct1[kMaxGroup];  // output polys of each member
+  const u64 *g0p[kMaxGroup];             // rotated c0 of each member (null: none)
+};
 
 // ModUp: for each job (digit d, output slot s) the column pass of the
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
@@ -25,9 +37,11 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
 // n_fp of the jobs have targets below kFpBound (FP64 path); the path is
 // chosen per CTA from the target prime, so the job order is free (the
 // context spreads the integer jobs evenly over the list).
+// group > 1: member b reads v_all + b v_bstride and writes t + b t_bstride.
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
-                             int n_fp, const NttTables &T, cudaStream_t s);
+                             int n_fp, const NttTables &T, cudaStream_t s, int group = 1,
+                             long long v_bstride = 0, long long t_bstride = 0);
 
 // ModUp row pass (t[d][s] from modup_fused_cols, d outside the digit of
 // out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner
@@ -40,15 +54,22 @@ cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *
                                      int key_limbs, u64 *cx, const ModUpDev &mu,
                                      const KsLayout &lay, const NttTables &T, cudaStream_t s,
                                      uint32_t elt = 1);
+// The same for a group: member b uses t + b G.t, G.in.in[b] read through
+// G.in.elt[b], G.key[b], and writes cx + b G.cx.
+cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int key_limbs,
+                                           u64 *cx, const ModUpDev &mu, const KsLayout &lay,
+                                           const NttTables &T, cudaStream_t s);
 
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
 // scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].
 // job_ps[2*n_q] lists p*n_q + s in launch order; n_fp of them have q_j
 // below kFpBound.
+// group > 1: member b reads y_base + b y_bstride and writes z + b z_bstride.
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
                                const int *q_index, const ModDownDev &md, const int *job_ps,
-                               int n_fp, const NttTables &T, cudaStream_t s);
+                               int n_fp, const NttTables &T, cudaStream_t s, int group = 1,
+                               long long y_bstride = 0, long long z_bstride = 0);
 
 // Rescale, first part: for every job (poly p, Q slot s), j = q_index[s], the
 // column pass of the forward NTT of ([c_p + h]_{q_last} mod q_j) - [h]_{q_j},
@@ -68,5 +89,11 @@ cudaError_t moddown_fused_rows(const u64 *z, int n_q, const int *q_index, const 
                                const u64 *cx, long long cx_stride_poly, u64 *ct0, u64 *ct1,
                                const u64 *g0, bool rotate, const u64 *diag,
                                const ModDownDev &md, const NttTables &T, cudaStream_t s);
+// The same for a group (no diag): member b reads z + b G.z, cx + b G.cx,
+// G.g0p[b] and writes G.ct0[b], G.ct1[b].
+cudaError_t moddown_fused_rows_group(const GroupArgs &G, const u64 *z, int n_q,
+                                     const int *q_index, const int *cx_slot, const u64 *cx,
+                                     long long cx_stride_poly, bool rotate, const ModDownDev &md,
+                                     const NttTables &T, cudaStream_t s);
 
 }  // namespace ksb

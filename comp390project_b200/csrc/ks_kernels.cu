@@ -24,10 +24,17 @@ __device__ __forceinline__ u64 mix64(u64 z) {
 }
 
 // One thread: the output pair (2m, 2m + 1) from the aligned source pair.
+// Member b of a group (grid z) reads mi.in[b] through mi.elt[b] and writes
+// out + b out_bstride (mi.in[0] null: in, elt).
 __global__ void k_galois_ntt(const u64 *__restrict__ in, u64 *__restrict__ out, int log_n,
-                             uint32_t elt) {
+                             uint32_t elt, MemberIn mi, long long out_bstride) {
   const int N = 1 << log_n;
   const long long limb = blockIdx.y;
+  if (mi.in[0]) {
+    in = mi.in[blockIdx.z];
+    elt = mi.elt[blockIdx.z];
+  }
+  out += blockIdx.z * out_bstride;
   const uint32_t i = (blockIdx.x * kBlk + threadIdx.x) * 2;
   if (i >= (uint32_t)N) return;
   const uint32_t src = galois_src(i, elt, log_n);
@@ -334,7 +341,20 @@ inline dim3 grid2(int log_n, int y, int per_thread) {
 cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
                        cudaStream_t s) {
   if (n_limbs <= 0) return cudaSuccess;
-  k_galois_ntt<<<grid2(log_n, n_limbs, 2), kBlk, 0, s>>>(in, out, log_n, elt);
+  const MemberIn none{};
+  k_galois_ntt<<<grid2(log_n, n_limbs, 2), kBlk, 0, s>>>(in, out, log_n, elt, none, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t galois_ntt_group(const MemberIn &mi, int group, u64 *out, long long out_bstride,
+                             int n_limbs, int log_n, cudaStream_t s) {
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  for (int b = 0; b < group; ++b)
+    if (!mi.in[b] || !(mi.elt[b] & 1u) || mi.elt[b] >= (2u << log_n)) return cudaErrorInvalidValue;
+  if (n_limbs <= 0) return cudaSuccess;
+  dim3 g = grid2(log_n, n_limbs, 2);
+  g.z = group;
+  k_galois_ntt<<<g, kBlk, 0, s>>>(nullptr, out, log_n, 1, mi, out_bstride);
   return cudaGetLastError();
 }
 

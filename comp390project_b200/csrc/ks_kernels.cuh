@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "ks_arith.cuh"
+#include "ks_ntt.cuh"
 
 namespace ksb {
 
@@ -48,6 +49,10 @@ struct KsLayout {
 // out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
 cudaError_t galois_ntt(const u64 *in, u64 *out, int n_limbs, int log_n, uint32_t elt,
                        cudaStream_t s);
+// The same for a group: member b permutes mi.in[b] by mi.elt[b] into
+// out + b out_bstride.
+cudaError_t galois_ntt_group(const MemberIn &mi, int group, u64 *out, long long out_bstride,
+                             int n_limbs, int log_n, cudaStream_t s);
 
 // Inner product of the automorphism X -> X^elt of the extended digits
 // (elt = 1: no automorphism), all in NTT form:

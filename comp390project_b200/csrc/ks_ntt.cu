@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
 // one aligned source tile); elt = 1 reads it as it is.
 template <int LOG_M, bool FWD>
 __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T,
-                                                     uint32_t elt) {
+                                                     uint32_t elt, MemberIn mi) {
   using G = RowGeom<LOG_M>;
   extern __shared__ __align__(16) u64 dsm[];
   u64 *sm = dsm;
@@ -71,6 +71,14 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
   limb_of(m, blockIdx.y, a, prime);
   limb_of(mo, blockIdx.y, o, prime_o);  // output limb (== input limb when in place)
   if (prime < 0) return;
+  const int mb = blockIdx.z;  // member of the group
+  if (mi.in[0]) {
+    a = const_cast<u64 *>(mi.in[mb]) + (a - m.base);
+    elt = mi.elt[mb];
+  } else {
+    a += mb * m.bstride;
+  }
+  o += mb * mo.bstride;
   const PrimeDev P = T.primes[prime];
   const int log_n = T.log_n, N = 1 << log_n;
   const ulonglong2 *tw = (FWD ? T.fwd : T.inv) + (long long)prime * N;
@@ -138,19 +146,22 @@ cudaError_t launch_cols(const LimbMap &m, int n_limbs, const NttTables &T, cudaS
 }
 template <int LOG_M, bool FWD>
 cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
-                        cudaStream_t s, uint32_t elt = 1) {
+                        cudaStream_t s, uint32_t elt = 1, const MemberIn *mi = nullptr,
+                        int group = 1) {
   constexpr size_t smem = row_smem_bytes<LOG_M>();
   static std::atomic<unsigned> attr_done{0};
   cudaError_t e = ensure_dynamic_smem(ntt_rows<LOG_M, FWD>, smem, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid((1 << T.log_n) / kTile, n_limbs);
-  ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T, elt);
+  dim3 grid((1 << T.log_n) / kTile, n_limbs, group);
+  const MemberIn none{};
+  ntt_rows<LOG_M, FWD><<<grid, kThreads, smem, s>>>(m, mo, T, elt, mi ? *mi : none);
   return cudaGetLastError();
 }
 
 template <bool FWD>
 cudaError_t launch_pass(bool cols, int log_m, const LimbMap &m, int n, const NttTables &T,
-                        cudaStream_t s, const LimbMap *mo = nullptr, uint32_t elt = 1) {
+                        cudaStream_t s, const LimbMap *mo = nullptr, uint32_t elt = 1,
+                        const MemberIn *mi = nullptr, int group = 1) {
   const LimbMap &o = mo ? *mo : m;
   if (cols) {
     switch (T.log_n) {
@@ -163,9 +174,9 @@ cudaError_t launch_pass(bool cols, int log_m, const LimbMap &m, int n, const Ntt
     }
   }
   switch (log_m) {
-    case 6: return launch_rows<6, FWD>(m, o, n, T, s, elt);
-    case 7: return launch_rows<7, FWD>(m, o, n, T, s, elt);
-    case 8: return launch_rows<8, FWD>(m, o, n, T, s, elt);
+    case 6: return launch_rows<6, FWD>(m, o, n, T, s, elt, mi, group);
+    case 7: return launch_rows<7, FWD>(m, o, n, T, s, elt, mi, group);
+    case 8: return launch_rows<8, FWD>(m, o, n, T, s, elt, mi, group);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -191,12 +202,21 @@ cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables
 }
 
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
-                                  cudaStream_t s, const LimbMap *out, uint32_t elt) {
+                                  cudaStream_t s, const LimbMap *out, uint32_t elt,
+                                  const MemberIn *mi, int group) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
-  if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
-  if (elt != 1u && (!out || out->base == m.base)) return cudaErrorInvalidValue;  // gather needs a separate output
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (mi && mi->in[0]) {  // per-member inputs: every member's element checked, output separate
+    for (int b = 0; b < group; ++b)
+      if (!mi->in[b] || !(mi->elt[b] & 1u) || mi->elt[b] >= (2u << T.log_n))
+        return cudaErrorInvalidValue;
+    if (!out) return cudaErrorInvalidValue;
+  } else {
+    if (!(elt & 1u) || elt >= (2u << T.log_n)) return cudaErrorInvalidValue;
+    if (elt != 1u && (!out || out->base == m.base)) return cudaErrorInvalidValue;  // gather needs a separate output
+  }
   if (n_limbs == 0) return cudaSuccess;
-  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s, out, elt);
+  return launch_pass<false>(false, T.log_n - T.log_n / 2, m, n_limbs, T, s, out, elt, mi, group);
 }
 
 cudaError_t ntt_inverse(const LimbMap &m, int n_limbs, const NttTables &T, cudaStream_t s) {

@@ -12,13 +12,25 @@
 
 namespace ksb {
 
-// Where limb i of a batch lives and which prime it uses.
+// Where limb i of a batch lives and which prime it uses.  Launches over a
+// group of key switches add a third grid dimension: member b of the group
+// finds its limbs bstride words further on.
 struct LimbMap {
   u64 *base;
   long long stride;          // words between consecutive limbs (normally N)
   const long long *offsets;  // device array; if set, limb i is at base + offsets[i]
   const int *prime_tab;      // device array; if null: first_prime + (i % period)
   int first_prime, period;
+  long long bstride;         // words between the limbs of consecutive group members
+};
+
+// A group of independent key switches run through each launch together (the
+// third grid dimension is the member).  Buffers the caller owns differ per
+// member and are passed by value; scratch buffers sit at uniform strides.
+constexpr int kMaxGroup = 8;
+struct MemberIn {             // per-member input limbs read through an automorphism
+  const u64 *in[kMaxGroup];   // null in[0]: use the LimbMap's own base
+  uint32_t elt[kMaxGroup];
 };
 
 // The FP64 tables hold w as a double at the same index as the integer
@@ -59,8 +71,12 @@ cudaError_t ntt_forward_rows_only(const LimbMap &m, int n_limbs, const NttTables
                                   cudaStream_t s);
 // out: optional separate destination (same limb order and primes as m).
 // elt != 1: the input is read through X -> X^elt (needs a separate out).
+// mi (with group > 1 or a per-member input): member b reads its limbs at
+// mi->in[b] + (the limb's offset from m.base) through mi->elt[b]; the output
+// of member b is out->base + b * out->bstride.
 cudaError_t ntt_inverse_rows_only(const LimbMap &m, int n_limbs, const NttTables &T,
                                   cudaStream_t s, const LimbMap *out = nullptr,
-                                  uint32_t elt = 1);
+                                  uint32_t elt = 1, const MemberIn *mi = nullptr,
+                                  int group = 1);
 
 }  // namespace ksb

@@ -68,7 +68,10 @@ typedef struct ks_params {
   int n_p;              /* alpha: number of special (P) primes = digit size (0..8) */
   const uint64_t *p;    /* P primes */
   int mode;             /* KS_MODE_* (ignored when world == 1) */
-  int max_batch;        /* ciphertexts per batched call the scratch is sized for (>=1) */
+  int max_batch;        /* execution lanes (streams with their own scratch) of batched calls, 1..8 */
+  int group;            /* key switches each lane pushes through every launch together
+                           (0 or 1: one; up to 8); scratch holds max_batch x group key
+                           switches.  Zero-initialised callers get one. */
 } ks_params;
 
 /* Phantom/SEAL CoeffModulus::Create: the largest primes below 2^bits that are

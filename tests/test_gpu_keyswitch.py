@@ -264,13 +264,50 @@ def test_rotate_batch_lanes(lanes, cuda_device):
         assert np.array_equal(_to_host(d).reshape(2, 7, o.N), ref)
 
 
+@pytest.mark.parametrize("name,lanes,group,n", [("small", 1, 2, 5), ("small", 2, 3, 7),
+                                                 ("small", 3, 8, 8), ("cfg3", 2, 2, 3)])
+def test_rotate_batch_groups(name, lanes, group, n, cuda_device):
+    """Groups of rotations pushed through every launch together (grid z =
+    member), over one or more lanes, a short last group included: every
+    member equals the oracle word for word."""
+    cfg = {"small": SMALL, "cfg3": CFG3}[name]
+    o = oracle_for(name)
+    ctx = _ctx(cfg, max_batch=lanes, batch_group=group)
+    s = o.secret(6, 192 if name == "cfg3" else 0)
+    steps = [1, 2, 3, -1, 5, 1, 2, 4][:n] if name == "small" else [1, 2, 1]
+    keys = {}
+    for st in sorted(set(steps)):
+        elt = o.galois_elt(st)
+        keys[st] = o.keygen_galois(s, elt, 60 + st)
+        ctx.key_upload(1, elt, keys[st])
+    Ql = o.L
+    rng = np.random.default_rng(31)
+    cts = [np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=o.N, dtype=np.uint64)
+                               for j in range(Ql)]) for _ in range(2)]) for _ in steps]
+    devs = [_to_dev(ct) for ct in cts]
+    ctx.rotate_batch(devs, steps, Ql)
+    torch.cuda.synchronize()
+    for ct, d, st in zip(cts, devs, steps):
+        ref = o.apply_galois(ct, Ql, o.galois_elt(st), keys[st])
+        assert np.array_equal(_to_host(d).reshape(2, Ql, o.N), ref)
+    # a lower level through the same group scratch
+    Ql2 = Ql - 2
+    devs2 = [_to_dev(ct[:, :Ql2]) for ct in cts]
+    ctx.rotate_batch(devs2, steps, Ql2)
+    torch.cuda.synchronize()
+    for ct, d, st in zip(cts, devs2, steps):
+        ref = o.apply_galois(np.ascontiguousarray(ct[:, :Ql2]), Ql2, o.galois_elt(st), keys[st])
+        assert np.array_equal(_to_host(d).reshape(2, Ql2, o.N), ref)
+    ctx.close()
+
+
 def test_rotate_batch_host_matches_device_batch(cuda_device):
     """ks_rotate_batch_host (host ciphertexts, copies pipelined over lanes)
     returns the words of ks_rotate_batch on device copies."""
     from comp390project_b200 import KS_KEY_GALOIS, KsContext
     o = oracle_for("small")
     log_n, q, p = split(SMALL)
-    ctx = KsContext(log_n, q, p, device=0, max_batch=3)
+    ctx = KsContext(log_n, q, p, device=0, max_batch=2, batch_group=2)
     s = o.secret(8, 64)
     steps = [1, 2, 3, 1, 2]
     for st in sorted(set(steps)):

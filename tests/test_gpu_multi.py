@@ -34,7 +34,7 @@ def _worker(rank, world, port, q, name, mode):
         N, L = o.N, o.L
         Ql = L
         oa = mode == "oa"
-        ctx = KsContext.from_process_group(log_n, qs, ps, device=rank, max_batch=2,
+        ctx = KsContext.from_process_group(log_n, qs, ps, device=rank, max_batch=2, batch_group=2,
                                            mode=KS_MODE_OUTPUT_AGGREGATION if oa else 0)
         ctx.set_timeout_ms(60000)
         s = o.secret(11, 64 if name == "small" else 192)
@@ -49,7 +49,7 @@ def _worker(rank, world, port, q, name, mode):
         ctx.key_upload(KS_KEY_RELIN, 0, rk)
         rng = np.random.default_rng(77)
         cts = [np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
-                                   for j in range(Ql)]) for _ in range(2)]) for _ in steps]
+                                   for j in range(Ql)]) for _ in range(2)]) for _ in steps + [1]]
         c3 = np.stack([np.stack([rng.integers(0, int(o.moduli[j]), size=N, dtype=np.uint64)
                                  for j in range(Ql)]) for _ in range(3)])
         mine = list(range(rank, Ql, world)) if not oa else list(range(Ql))
@@ -75,11 +75,13 @@ def _worker(rank, world, port, q, name, mode):
         ctx.rotate(d, Ql, steps[0])
         torch.cuda.synchronize()
         ok &= np.array_equal(gather(d, 2), o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
-        # batch over two lanes (each with its own split communicator)
+        # batch of three: a group of two on lane 0 (grouped all-gathers /
+        # all-reduce) and a group of one on lane 1 (its own split communicator)
+        bsteps = steps + [1]
         ds = [local(c) for c in cts]
-        ctx.rotate_batch(ds, steps, Ql)
+        ctx.rotate_batch(ds, bsteps, Ql)
         torch.cuda.synchronize()
-        for c, dd, st in zip(cts, ds, steps):
+        for c, dd, st in zip(cts, ds, bsteps):
             ok &= np.array_equal(gather(dd, 2), o.apply_galois(c, Ql, o.galois_elt(st), keys[st]))
         # relinearisation
         d3 = local(c3)
