@@ -59,7 +59,7 @@ def parse():
                     help="launch the batch directly instead of replaying its CUDA graph")
     ap.add_argument("--lanes", type=int, default=4,
                     help="execution lanes (streams + scratch) for the batched key switches")
-    ap.add_argument("--group", type=int, default=1,
+    ap.add_argument("--group", type=int, default=4,
                     help="key switches each lane pushes through every launch together (1..8)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["ks", "ntt", "hoisted", "matmul"], default="ks",

@@ -385,6 +385,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   for (int p = 0; p < 2; ++p)
     for (int k = 0; k < lv.n_p; ++k) {
       lv.p_jobs.h.push_back(L + own_p[k]);
+      lv.p_cx_offsets.h.push_back(((long long)p * lv.n_out + lv.n_q + k) * N);
       if (G == 1) lv.p_offsets.h.push_back(((long long)p * lv.n_out + lv.n_q + k) * N);
       else lv.p_offsets.h.push_back(((long long)k * 2 + p) * N);  // ysend [max_p][2][N]
     }
@@ -540,6 +541,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   up_ints(lv.cx_slot_q);
   up_ints(lv.p_jobs);
   up_i64(lv.p_offsets);
+  up_i64(lv.p_cx_offsets);
   up_i64(lv.y_off);
   lv.qhatinv = upload(qhi);
   std::vector<u64> wsh(w.size());
@@ -706,6 +708,7 @@ void ctx_free(Ctx &c) {
                        &lv.q_index, &lv.z_jobs, &lv.cx_slot_q, &lv.p_jobs})
       f(t->d);
     f(lv.p_offsets.d);
+    f(lv.p_cx_offsets.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
     for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
@@ -1212,19 +1215,12 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
     y_base = L.s_cx;
     y_bstride = c.st_cx;
   } else {
-    {
+    if (lv.n_p > 0) {  // the owned P limbs of cx, inverse-transformed into the send buffer
       StageTimer tm(c, ST_INTT_P, s);
-      for (int b = 0; b < g; ++b)
-        for (int p = 0; p < 2; ++p)
-          for (int k = 0; k < lv.n_p; ++k)
-            KS_CUDA(cudaMemcpyAsync(L.s_ysend + b * c.st_ys + ((size_t)k * 2 + p) * N,
-                                    L.s_cx + b * c.st_cx + ((size_t)p * lv.n_out + lv.n_q + k) * N,
-                                    N * 8, cudaMemcpyDeviceToDevice, s));
-      if (lv.n_p > 0) {
-        LimbMap mp{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_ys};
-        KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
-        c.launches += 2;
-      }
+      LimbMap src{L.s_cx, 0, lv.p_cx_offsets.d, lv.p_jobs.d, 0, 1, c.st_cx};
+      LimbMap dst{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_ys};
+      KS_CUDA(ntt_inverse_scaled(src, dst, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
+      c.launches += 2;
     }
     StageTimer tm(c, ST_COMM, s);
     allgather_group(c, L.comm, L.s_ysend, c.st_ys, L.s_yall, c.st_ya,

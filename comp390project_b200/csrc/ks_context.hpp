@@ -49,6 +49,7 @@ struct Level {
   DevInts cx_slot_q;  // [n_q]
   DevInts p_jobs;     // [2 * n_p] primes of the owned P slots being inverse-transformed
   DevI64 p_offsets;   // [2 * n_p] word offsets of those slots (in cx for G=1, in ysend otherwise)
+  DevI64 p_cx_offsets;  // [2 * n_p] word offsets of the same slots in cx
   DevI64 y_off;       // [2 * alpha] offsets of P limb i of poly p in the y buffer
   ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
   u64 *w = nullptr;               // [beta][QlP][alpha]
