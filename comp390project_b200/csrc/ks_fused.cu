@@ -395,7 +395,7 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
 
 template <int LOG_M>
 __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
-    k_modup_rows_ip(RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
+    k_modup_rows_ip(const __grid_constant__ RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
   // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
   // needs 64 columns per group of four warps.  Shared memory caps how many
   // CTAs share an SM so that their columns never exceed the 512 of an SM,
@@ -498,7 +498,7 @@ template <int LOG_M>
 __global__ void __launch_bounds__(kThreads)
     k_moddown_rows(const u64 *__restrict__ z, int n_q, const int *__restrict__ q_index,
                    const int *__restrict__ cx_slot, const u64 *__restrict__ cx,
-                   long long cx_stride_poly, MdGroup grp, int rotate,
+                   long long cx_stride_poly, const __grid_constant__ MdGroup grp, int rotate,
                    const u64 *__restrict__ diag, ModDownDev md, NttTables T) {
   using G = RowGeom<LOG_M>;
   const int mb = blockIdx.z;  // member of the group

@@ -27,7 +27,8 @@ __device__ __forceinline__ u64 mix64(u64 z) {
 // Member b of a group (grid z) reads mi.in[b] through mi.elt[b] and writes
 // out + b out_bstride (mi.in[0] null: in, elt).
 __global__ void k_galois_ntt(const u64 *__restrict__ in, u64 *__restrict__ out, int log_n,
-                             uint32_t elt, MemberIn mi, long long out_bstride) {
+                             uint32_t elt, const __grid_constant__ MemberIn mi,
+                             long long out_bstride) {
   const int N = 1 << log_n;
   const long long limb = blockIdx.y;
   if (mi.in[0]) {

@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
 // one aligned source tile); elt = 1 reads it as it is.
 template <int LOG_M, bool FWD>
 __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T,
-                                                     uint32_t elt, MemberIn mi) {
+                                                     uint32_t elt,
+                                                     const __grid_constant__ MemberIn mi) {
   using G = RowGeom<LOG_M>;
   extern __shared__ __align__(16) u64 dsm[];
   u64 *sm = dsm;
