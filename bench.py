@@ -859,15 +859,17 @@ def run_ours(args, rank, world):
     clocks.stop()
     ms = ev0.elapsed_time(ev1)
     # Per-kernel times come from a serial pass right after the timed region
-    # (one key switch at a time on one stream, CUDA events around every stage),
-    # because in the timed region key switches of different lanes overlap.
-    n_prof = min(B, 8)
+    # (one group of key switches at a time on one stream, CUDA events around
+    # every stage), because in the timed region the lanes overlap.  A batch
+    # of exactly one group runs on lane 0 alone.
+    gsz = max(1, args.group)
+    n_prof = max(1, min(B, 8) // gsz) * gsz
     ctx.profile_enable(True)
     # NVTX range "ks_serial" lets a profiler select exactly these launches
     # (ncu --nvtx --nvtx-include "ks_serial/").
     torch.cuda.nvtx.range_push("ks_serial")
-    for i in range(n_prof):
-        ctx.rotate(views[i], L, steps_of[i], stream=stream)
+    for i0 in range(0, n_prof, gsz):
+        ctx.rotate_batch(views[i0:i0 + gsz], steps_of[i0:i0 + gsz], L, stream=stream)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     ctx.profile_enable(False)
@@ -907,12 +909,15 @@ def run_ours(args, rank, world):
         "moddown_rows": 7 * n_q * U,
     }
     peak, peak_kind = measured_peaks()
-    achieved = alg[dom] / (per_launch_ms / 1000.0) / 1e9 if dom in alg else None
+    # one launch of a stage serves a whole group of gsz key switches
+    alg_launch = alg[dom] * gsz if dom in alg else None
+    achieved = alg_launch / (per_launch_ms / 1000.0) / 1e9 if alg_launch else None
     # DRAM traffic per launch of the dominant kernel: not measurable without a
     # profiler, so it is the constant of one ncu capture of the same kernel at
-    # the same workload (dram__bytes_read.sum + dram__bytes_write.sum), named
-    # in traffic_source; one GPU only (the capture is of the one-GPU launch)
-    traffic = PROFILED_TRAFFIC.get(dom) if world == 1 else None
+    # the same workload (dram__bytes_read.sum + dram__bytes_write.sum, one key
+    # switch) scaled to the group, named in traffic_source; one GPU only (the
+    # capture is of the one-GPU launch)
+    traffic = PROFILED_TRAFFIC.get(dom) * gsz if world == 1 and dom in PROFILED_TRAFFIC else None
 
     # end to end through the C ABI with host buffers: ks_rotate_batch_host on
     # pinned host ciphertexts (copy in, rotate, copy out, pipelined over the
@@ -968,7 +973,7 @@ def run_ours(args, rank, world):
                          "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                          "traffic": traffic, "peak_kind": peak_kind,
                          "traffic_source": (PROFILED_TRAFFIC_SOURCE if traffic else None),
-                         "alg_bytes": alg.get(dom),
+                         "alg_bytes": alg_launch, "ks_per_launch": gsz,
                          "launch_ms": per_launch_ms, "per_rank": world > 1},
             "collectives": nvlink,
             "ntt": ntt,
