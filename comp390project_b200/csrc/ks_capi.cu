@@ -476,12 +476,10 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       (c.primes[lv.out_j.h[s]] < kFpBound ? md_fp : md_int).push_back(p * lv.n_q + s);
   lv.md_job_ps.h = interleave_jobs(md_fp, md_int);
   lv.n_md_fp = (int)md_fp.size();
-  // the fused row pass + inner product walks the output slots in the same
-  // spirit: integer slots spread among the FP64 ones
-  std::vector<int> rip_fp, rip_int;
+  // the fused row pass + inner product runs one launch over the FP64 output
+  // slots and one over the integer ones
   for (int s = 0; s < lv.n_out; ++s)
-    (c.primes[lv.prime_of.h[lv.out_j.h[s]]] < kFpBound ? rip_fp : rip_int).push_back(s);
-  lv.rip_order.h = interleave_jobs(rip_fp, rip_int);
+    (c.primes[lv.prime_of.h[lv.out_j.h[s]]] < kFpBound ? lv.rip_fp : lv.rip_int).h.push_back(s);
   std::vector<ulonglong2> sin, sp;
   for (int i = 0; i < lv.n_intt; ++i) {
     const int j = lv.intt_prime.h[i], d = j / a;
@@ -519,7 +517,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
     lv.rs_md = ModDownDev{1, last, nullptr, nullptr, lv.rs_pinv, nullptr, nullptr};
   }
   up_ints(lv.src_slot);
-  up_ints(lv.rip_order);
+  up_ints(lv.rip_fp);
+  up_ints(lv.rip_int);
   up_ints(lv.digits);
   up_ints(lv.cx_prime);
   up_ints(lv.intt_prime);
@@ -559,7 +558,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   lv.wq = upload(wq);
   lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh, lv.wq};
   lv.lay = KsLayout{lv.n_out,  lv.out_j.d,  lv.key_slot.d,           lv.c_slot.d, G,
-                    lv.coef_ml, lv.digits.d, (int)lv.digits.h.size(), lv.rip_order.d};
+                    lv.coef_ml, lv.digits.d, (int)lv.digits.h.size(), lv.rip_fp.d,
+                    lv.rip_int.d, (int)lv.rip_fp.h.size(), (int)lv.rip_int.h.size()};
 }
 
 void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncclComm_t comm,
@@ -712,7 +712,7 @@ void ctx_free(Ctx &c) {
     f(lv.y_off.d);
     f(lv.qhatinv);
     for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
-                       &lv.digits, &lv.cx_prime, &lv.intt_prime, &lv.rip_order})
+                       &lv.digits, &lv.cx_prime, &lv.intt_prime, &lv.rip_fp, &lv.rip_int})
       f(t->d);
     f(lv.job_off.d);
     f(lv.intt_off.d);
@@ -1275,7 +1275,7 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
       }
       KS_CUDA(modup_rows_inner_product_group(G, L.s_t, m[0].key->limbs, L.s_cx, lv.mu, lv.lay,
                                              T, s));
-      c.launches += lv.lay.n_out > 0 ? 1 : 0;
+      c.launches += (lv.lay.n_slots_fp > 0 ? 1 : 0) + (lv.lay.n_slots_int > 0 ? 1 : 0);
     } else {  // output aggregation with more ranks than digits: a zero partial sum
       for (int b = 0; b < g; ++b)
         KS_CUDA(cudaMemsetAsync(L.s_cx + b * c.st_cx, 0, (size_t)2 * lv.n_out * c.N * 8, s));

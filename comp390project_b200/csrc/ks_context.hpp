@@ -69,7 +69,7 @@ struct Level {
   DevI64 intt_off;
   DevInts intt_prime;
   DevInts digits;                 // digits of the inner product (all, or this rank's)
-  DevInts rip_order;              // [n_out] output slots in the launch order of the row pass
+  DevInts rip_fp, rip_int;        // output slots of the FP64 / integer row-pass launches
   DevInts cx_prime;               // [2 * n_out] prime of cx slot (post-all-reduce reduction)
   ulonglong2 *scale_in = nullptr; // [2 * n_intt] last-stage INTT scales with (Q_d/q_j)^-1 folded in
   ulonglong2 *scale_p = nullptr;  // [2 * 2 * n_p] same with (P/p_i)^-1 for the owned P limbs

@@ -393,7 +393,10 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
   }
 }
 
-template <int LOG_M>
+// FP_SLOTS: the launch over lay.slots_fp (FP64 bodies only); otherwise the
+// launch over lay.slots_int (the two integer bodies).  One arithmetic kind
+// per kernel keeps its code small enough for the instruction cache.
+template <int LOG_M, bool FP_SLOTS>
 __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(const __grid_constant__ RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
   // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   ulonglong2 *kst = reinterpret_cast<ulonglong2 *>(
       dsm + (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16));
   double *smtw = reinterpret_cast<double *>(kst + kRipWarps * 2 * 8 * 32);
-  const int s = lay.slot_order ? lay.slot_order[blockIdx.y] : (int)blockIdx.y;
+  const int s = FP_SLOTS ? lay.slots_fp[blockIdx.y] : lay.slots_int[blockIdx.y];
   const int prime = mu.prime_of[lay.out_j[s]];
   const u64 q = T.primes[prime].q;
   const int warp = threadIdx.x >> 5;
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   tmem::fence_after_sync();
   // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
   const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
-  if (q < kFpBound) {
+  if (FP_SLOTS) {
     constexpr int R = rows_ip_rows<LOG_M>();
     stage_row_twiddles<LOG_M, R, kRipThreads>(smtw, T.fwd_fp + (long long)prime * (1 << T.log_n),
                                              T.log_n, (long long)blockIdx.x * R);
@@ -615,12 +618,23 @@ template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const RowsIpArgs &A, int group,
                                  const ModUpDev &mu, const KsLayout &lay, const NttTables &T) {
   constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
-  static std::atomic<unsigned> attr_done{0};
-  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M>, smem, attr_done);
+  static std::atomic<unsigned> attr_fp{0}, attr_int{0};
+  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, true>, smem, attr_fp);
+  if (e == cudaSuccess) e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, false>, smem, attr_int);
   if (e != cudaSuccess) return e;
-  const dim3 grid((1 << T.log_n) / kRipTile, lay.n_out, group);
-  k_modup_rows_ip<LOG_M><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
-  return cudaGetLastError();
+  // the integer slots (longer per tile) first, then the FP64 ones
+  if (lay.n_slots_int > 0) {
+    const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_int, group);
+    k_modup_rows_ip<LOG_M, false><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (lay.n_slots_fp > 0) {
+    const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_fp, group);
+    k_modup_rows_ip<LOG_M, true><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
+    e = cudaGetLastError();
+  }
+  return e;
 }
 
 inline int col_tiles(int log_n, int log_m) {

@@ -47,8 +47,8 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 // out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner
 // product against the key shard ([n_digits][2][key_limbs][N], limb key_slot[s]):
 //   cx[p][s] = sum_i NTT_rows(t[d_i][s]) * key[i][p][key_slot[s]]  (p = 0, 1,
-// d_i = lay.digits[i], lay.n_digits >= 1).  Launch row y serves output slot
-// lay.slot_order[y] (all slots, any order; null: slot y).
+// d_i = lay.digits[i], lay.n_digits >= 1).  Two launches: one over the
+// integer output slots lay.slots_int, one over the FP64 slots lay.slots_fp.
 // elt != 1: the NTT-form input c_ntt is read through X -> X^elt.
 cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *key,
                                      int key_limbs, u64 *cx, const ModUpDev &mu,

@@ -43,7 +43,11 @@ struct KsLayout {
   int coef_G, coef_ml;        // coefficient-form Q limb j at slot (j % G) * ml + j / G
   const int *digits;          // [n_digits] digits summed by the inner product, ascending;
   int n_digits;               // digit digits[i] is digit i of the key shard
-  const int *slot_order;      // [n_out] output slot of launch row y (a permutation), or null
+  // the output slots whose prime takes the FP64 path and the others, each
+  // served by its own launch of the fused row pass (kernels of one arithmetic
+  // kind keep the instruction cache warm)
+  const int *slots_fp, *slots_int;
+  int n_slots_fp, n_slots_int;
 };
 
 // out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
