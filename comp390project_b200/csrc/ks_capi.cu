@@ -151,6 +151,23 @@ inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 int n_local(int g, int G, int total) { return g < total ? (total - g - 1) / G + 1 : 0; }
 
+// Merges two job lists with the `rare` jobs at evenly spaced positions, the
+// first of them at the front (the rare jobs are the long-running ones).
+template <class T>
+std::vector<T> interleave_jobs(const std::vector<T> &common, const std::vector<T> &rare) {
+  std::vector<T> out;
+  const size_t n = common.size() + rare.size();
+  out.reserve(n);
+  size_t ic = 0, ir = 0;
+  for (size_t k = 0; k < n; ++k) {
+    // rare job ir belongs at position floor(ir * n / rare.size())
+    if (ir < rare.size() && k >= ir * n / rare.size()) out.push_back(rare[ir++]);
+    else if (ic < common.size()) out.push_back(common[ic++]);
+    else out.push_back(rare[ir++]);
+  }
+  return out;
+}
+
 u64 mix64h(u64 z) {
   z ^= z >> 30;
   z *= 0xBF58476D1CE4E5B9ull;
@@ -431,9 +448,12 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       const int j = d * a + i;
       lv.src_slot.h.push_back(j < Ql ? (j % G) * lv.coef_ml + j / G : 0);
     }
-  // Job lists of the fused column passes: the jobs whose target prime takes
-  // the FP64 path first, then those on the integer path (q_0 and the 60-bit
-  // special primes); each kind gets its own launch.
+  // Job order of the fused column passes: jobs whose target prime takes the
+  // integer path (q_0 and the 60-bit special primes) run 2-3x longer than
+  // the FP64 ones and use the integer pipes, so they are spread evenly over
+  // the list (the first at the front): co-resident CTAs then keep the FP64
+  // and integer pipes busy at the same time, and no wave at the end runs
+  // integer work alone.
   std::vector<std::pair<int, int>> fp_jobs, int_jobs;  // (d, s)
   for (int d = 0; d < lv.beta; ++d)
     for (int s = 0; s < lv.n_out; ++s) {
@@ -441,8 +461,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       if (pj < 0) continue;
       (c.primes[pj] < kFpBound ? fp_jobs : int_jobs).push_back({d, s});
     }
-  fp_jobs.insert(fp_jobs.end(), int_jobs.begin(), int_jobs.end());
-  for (const auto &ds : fp_jobs) {
+  for (const auto &ds : interleave_jobs(fp_jobs, int_jobs)) {
     const int d = ds.first, s = ds.second, pj = lv.t_jobs.h[(size_t)d * lv.n_out + s];
     lv.job_d.h.push_back(d);
     lv.job_s.h.push_back(s);
@@ -455,8 +474,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   for (int p = 0; p < 2; ++p)
     for (int s = 0; s < lv.n_q; ++s)
       (c.primes[lv.out_j.h[s]] < kFpBound ? md_fp : md_int).push_back(p * lv.n_q + s);
-  lv.md_job_ps.h = md_fp;
-  lv.md_job_ps.h.insert(lv.md_job_ps.h.end(), md_int.begin(), md_int.end());
+  lv.md_job_ps.h = interleave_jobs(md_fp, md_int);
   lv.n_md_fp = (int)md_fp.size();
   // the fused row pass + inner product runs one launch over the FP64 output
   // slots and one over the integer ones
@@ -1159,7 +1177,7 @@ void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int
     StageTimer tm(c, ST_MODUP_COLS, s);
     KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
                              lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s, g, c.st_coef_all, c.st_t));
-    c.launches += (lv.n_jobs_fp > 0 ? 1 : 0) + (lv.n_jobs > lv.n_jobs_fp ? 1 : 0);
+    c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
 }
 
@@ -1215,7 +1233,7 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
     StageTimer tm(c, ST_MODDOWN_COLS, s);
     KS_CUDA(moddown_fused_cols(y_base, lv.y_off.d, L.s_z, lv.n_q, lv.q_index.d, c.md,
                                lv.md_job_ps.d, lv.n_md_fp, T, s, g, y_bstride, c.st_z));
-    c.launches += (lv.n_md_fp > 0 ? 1 : 0) + (2 * lv.n_q > lv.n_md_fp ? 1 : 0);
+    c.launches += lv.n_q > 0 ? 1 : 0;
   }
   // 7. row pass with (cx - z) * P^-1 and the add to the ciphertext in the epilogue
   {

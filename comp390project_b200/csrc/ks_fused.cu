@@ -133,9 +133,8 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
 // ModUp: base conversion + forward column pass
 // ---------------------------------------------------------------------------
 // The arithmetic path is chosen per CTA from the target prime (FP64 below
-// kFpBound, integer above); jobs are ordered FP64 first, and each kind has its
-// own launch (FP: the FP64 jobs), so a kernel holds one arithmetic kind's code.
-template <int LOG_N, bool FP>
+// kFpBound, integer above); jobs are ordered FP64 first.
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 3)
     k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
@@ -157,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
   u64 *out = t + blockIdx.z * t_bstride + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (FP) {
+  if (P.q < kFpBound) {
     const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
     auto filld = [&](double (&x)[kEpt]) {
       bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src,
@@ -447,7 +446,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
 // ---------------------------------------------------------------------------
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
-template <int LOG_N, bool FP>
+template <int LOG_N>
 __global__ void __launch_bounds__(kThreads, 2)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
                    int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
@@ -473,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
-  if (FP) {
+  if (P.q < kFpBound) {
     // FP64 conversion (sources reduced mod q_j first when they do not fit):
     // spreads the work over the FP64 and integer pipes
     auto filld = [&](double (&x)[kEpt]) {
@@ -674,31 +673,18 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
   if (!ntt_supported_log_n(T.log_n) || n_jobs < 0 || n_jobs > 65535) return cudaErrorInvalidValue;
   if (mu.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > n_jobs) return cudaErrorInvalidValue;
   if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (n_jobs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  // integer jobs [n_fp, n_jobs) first (longer per job), then the FP64 jobs [0, n_fp)
-  for (int kind = 0; kind < 2; ++kind) {
-    const bool fp = kind == 1;
-    const int n = fp ? n_fp : n_jobs - n_fp, job0 = fp ? 0 : n_fp;
-    if (n == 0) continue;
-    dim3 grid(col_tiles(T.log_n, s1), n, group);
-#define KS_MODUP_COLS(LN)                                                                     \
-  (fp ? k_modup_cols<LN, true><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, \
-                                                         job0, T, v_bstride, t_bstride)      \
-      : k_modup_cols<LN, false><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d,     \
-                                                          job_s, job0, T, v_bstride, t_bstride))
-    switch (T.log_n) {
-      case 12: KS_MODUP_COLS(12); break;
-      case 13: KS_MODUP_COLS(13); break;
-      case 14: KS_MODUP_COLS(14); break;
-      case 15: KS_MODUP_COLS(15); break;
-      case 16: KS_MODUP_COLS(16); break;
-      default: return cudaErrorInvalidValue;
-    }
-#undef KS_MODUP_COLS
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  dim3 grid(col_tiles(T.log_n, s1), n_jobs, group);
+  switch (T.log_n) {
+    case 12: k_modup_cols<12><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 13: k_modup_cols<13><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 14: k_modup_cols<14><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 15: k_modup_cols<15><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 16: k_modup_cols<16><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    default: return cudaErrorInvalidValue;
   }
-  return cudaSuccess;
+  return cudaGetLastError();
 }
 
 cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int key_limbs,
@@ -749,31 +735,18 @@ cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z
   if (!ntt_supported_log_n(T.log_n) || n_q < 0 || 2 * n_q > 65535) return cudaErrorInvalidValue;
   if (md.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > 2 * n_q) return cudaErrorInvalidValue;
   if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (n_q == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
-  // integer jobs [n_fp, 2 n_q) first, then the FP64 jobs [0, n_fp)
-  for (int kind = 0; kind < 2; ++kind) {
-    const bool fp = kind == 1;
-    const int n = fp ? n_fp : 2 * n_q - n_fp, job0 = fp ? 0 : n_fp;
-    if (n == 0) continue;
-    dim3 grid(col_tiles(T.log_n, s1), n, group);
-#define KS_MODDOWN_COLS(LN)                                                                   \
-  (fp ? k_moddown_cols<LN, true><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, \
-                                                           job_ps, job0, y_bstride, z_bstride) \
-      : k_moddown_cols<LN, false><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T,  \
-                                                            job_ps, job0, y_bstride, z_bstride))
-    switch (T.log_n) {
-      case 12: KS_MODDOWN_COLS(12); break;
-      case 13: KS_MODDOWN_COLS(13); break;
-      case 14: KS_MODDOWN_COLS(14); break;
-      case 15: KS_MODDOWN_COLS(15); break;
-      case 16: KS_MODDOWN_COLS(16); break;
-      default: return cudaErrorInvalidValue;
-    }
-#undef KS_MODDOWN_COLS
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  dim3 grid(col_tiles(T.log_n, s1), 2 * n_q, group);
+  switch (T.log_n) {
+    case 12: k_moddown_cols<12><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 13: k_moddown_cols<13><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 14: k_moddown_cols<14><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 15: k_moddown_cols<15><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    case 16: k_moddown_cols<16><<<grid, kThreads, 0, s>>>(y_base, y_off, z, n_q, q_index, md, T, job_ps, 0, y_bstride, z_bstride); break;
+    default: return cudaErrorInvalidValue;
   }
-  return cudaSuccess;
+  return cudaGetLastError();
 }
 
 cudaError_t rescale_fused_cols(const u64 *last, u64 q_last, bool last_fp, u64 *z, int n_q,

@@ -34,8 +34,9 @@ struct GroupArgs {
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
 // where v_i are the digit's scaled coefficient limbs (v_all at limb slot
 // src_slot[d*alpha + i]).  Result (column pass done) -> t[d][s].
-// The first n_fp jobs have targets below kFpBound (FP64 path), the rest take
-// the integer path; each kind runs as its own launch.
+// n_fp of the jobs have targets below kFpBound (FP64 path); the path is
+// chosen per CTA from the target prime, so the job order is free (the
+// context spreads the integer jobs evenly over the list).
 // group > 1: member b reads v_all + b v_bstride and writes t + b t_bstride.
 cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
@@ -62,8 +63,8 @@ cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
 // scaled P limbs of poly p at y_base + y_off[p*alpha + i].  -> z[p][s].
-// job_ps[2*n_q] lists p*n_q + s, the first n_fp with q_j below kFpBound
-// (FP64 launch), the others on the integer path (their own launch).
+// job_ps[2*n_q] lists p*n_q + s in launch order; n_fp of them have q_j
+// below kFpBound.
 // group > 1: member b reads y_base + b y_bstride and writes z + b z_bstride.
 cudaError_t moddown_fused_cols(const u64 *y_base, const long long *y_off, u64 *z, int n_q,
                                const int *q_index, const ModDownDev &md, const int *job_ps,
