@@ -664,6 +664,9 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       ln.s_ct = p; p += w_ct;
       if (li > 0) KS_CUDA(cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking));
       KS_CUDA(cudaEventCreateWithFlags(&ln.done, cudaEventDisableTiming));
+      KS_CUDA(cudaStreamCreateWithFlags(&ln.side, cudaStreamNonBlocking));
+      KS_CUDA(cudaEventCreateWithFlags(&ln.ev_fork, cudaEventDisableTiming));
+      KS_CUDA(cudaEventCreateWithFlags(&ln.ev_join, cudaEventDisableTiming));
     }
     KS_CUDA(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
   }
@@ -746,6 +749,9 @@ void ctx_free(Ctx &c) {
     f(ln.arena);
     if (ln.stream) cudaStreamDestroy(ln.stream);
     if (ln.done) cudaEventDestroy(ln.done);
+    if (ln.side) cudaStreamDestroy(ln.side);
+    if (ln.ev_fork) cudaEventDestroy(ln.ev_fork);
+    if (ln.ev_join) cudaEventDestroy(ln.ev_join);
     if (li > 0 && ln.comm) ncclCommDestroy(ln.comm);
   }
   c.lanes.clear();
@@ -1273,8 +1279,11 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
         G.in.elt[b] = m[b].elt;
         G.key[b] = m[b].key->d;
       }
+      // (profiling times the stage on s alone, so it keeps both launches there)
+      const bool fork = !c.profile;
       KS_CUDA(modup_rows_inner_product_group(G, L.s_t, m[0].key->limbs, L.s_cx, lv.mu, lv.lay,
-                                             T, s));
+                                             T, s, fork ? L.side : nullptr, L.ev_fork,
+                                             L.ev_join));
       c.launches += (lv.lay.n_slots_fp > 0 ? 1 : 0) + (lv.lay.n_slots_int > 0 ? 1 : 0);
     } else {  // output aggregation with more ranks than digits: a zero partial sum
       for (int b = 0; b < g; ++b)

@@ -129,6 +129,10 @@ struct Ctx {
   struct Lane {
     cudaStream_t stream = nullptr;  // null for lane 0 (uses the caller's stream)
     cudaEvent_t done = nullptr;
+    // side stream of the lane with its fork / join events: the integer launch
+    // of the fused row pass overlaps the FP64 launch on it
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     u64 *arena = nullptr;
     u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr,
         *s_cx = nullptr, *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr,

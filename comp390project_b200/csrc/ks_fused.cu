@@ -616,25 +616,37 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
 
 template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const RowsIpArgs &A, int group,
-                                 const ModUpDev &mu, const KsLayout &lay, const NttTables &T) {
+                                 const ModUpDev &mu, const KsLayout &lay, const NttTables &T,
+                                 cudaStream_t side, cudaEvent_t ev_fork, cudaEvent_t ev_join) {
   constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
   static std::atomic<unsigned> attr_fp{0}, attr_int{0};
   cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, true>, smem, attr_fp);
   if (e == cudaSuccess) e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, false>, smem, attr_int);
   if (e != cudaSuccess) return e;
-  // the integer slots (longer per tile) first, then the FP64 ones
+  // the integer slots (longer per tile, few tiles) on the side stream when
+  // there is one, overlapping the FP64 launch on s
+  const bool fork = side && ev_fork && ev_join && lay.n_slots_int > 0 && lay.n_slots_fp > 0;
   if (lay.n_slots_int > 0) {
+    cudaStream_t si = s;
+    if (fork) {
+      if ((e = cudaEventRecord(ev_fork, s)) != cudaSuccess) return e;
+      if ((e = cudaStreamWaitEvent(side, ev_fork, 0)) != cudaSuccess) return e;
+      si = side;
+    }
     const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_int, group);
-    k_modup_rows_ip<LOG_M, false><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    k_modup_rows_ip<LOG_M, false><<<grid, kRipThreads, smem, si>>>(A, mu, lay, T);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (lay.n_slots_fp > 0) {
     const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_fp, group);
     k_modup_rows_ip<LOG_M, true><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
-    e = cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  return e;
+  if (fork) {
+    if ((e = cudaEventRecord(ev_join, side)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(s, ev_join, 0)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 inline int col_tiles(int log_n, int log_m) {
@@ -689,7 +701,8 @@ cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, cons
 
 cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int key_limbs,
                                            u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                           const NttTables &T, cudaStream_t s) {
+                                           const NttTables &T, cudaStream_t s, cudaStream_t side,
+                                           cudaEvent_t ev_fork, cudaEvent_t ev_join) {
   if (G.n < 1 || G.n > kMaxGroup) return cudaErrorInvalidValue;
   for (int b = 0; b < G.n; ++b)
     if (!(G.in.elt[b] & 1u) || G.in.elt[b] >= (2u << T.log_n)) return cudaErrorInvalidValue;
@@ -709,9 +722,9 @@ cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int
   }
   const int s2 = T.log_n - T.log_n / 2;
   switch (s2) {
-    case 6: return launch_modup_rows_ip<6>(s, A, G.n, mu, lay, T);
-    case 7: return launch_modup_rows_ip<7>(s, A, G.n, mu, lay, T);
-    case 8: return launch_modup_rows_ip<8>(s, A, G.n, mu, lay, T);
+    case 6: return launch_modup_rows_ip<6>(s, A, G.n, mu, lay, T, side, ev_fork, ev_join);
+    case 7: return launch_modup_rows_ip<7>(s, A, G.n, mu, lay, T, side, ev_fork, ev_join);
+    case 8: return launch_modup_rows_ip<8>(s, A, G.n, mu, lay, T, side, ev_fork, ev_join);
     default: return cudaErrorInvalidValue;
   }
 }

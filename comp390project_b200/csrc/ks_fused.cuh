@@ -56,9 +56,14 @@ cudaError_t modup_rows_inner_product(const u64 *t, const u64 *c_ntt, const u64 *
                                      uint32_t elt = 1);
 // The same for a group: member b uses t + b G.t, G.in.in[b] read through
 // G.in.elt[b], G.key[b], and writes cx + b G.cx.
+// side (optional, with two events): the integer launch runs on it, forked
+// from and joined back into s, so that it overlaps the FP64 launch.
 cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int key_limbs,
                                            u64 *cx, const ModUpDev &mu, const KsLayout &lay,
-                                           const NttTables &T, cudaStream_t s);
+                                           const NttTables &T, cudaStream_t s,
+                                           cudaStream_t side = nullptr,
+                                           cudaEvent_t ev_fork = nullptr,
+                                           cudaEvent_t ev_join = nullptr);
 
 // ModDown: for each job (poly p, Q slot s) the column pass of the forward
 // NTT of  z[k] = sum_i v_i[k] * w[j][i] mod q_j  (j = q_index[s]), v_i the
