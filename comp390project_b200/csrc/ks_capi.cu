@@ -389,6 +389,16 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       if (G == 1) lv.p_offsets.h.push_back(((long long)p * lv.n_out + lv.n_q + k) * N);
       else lv.p_offsets.h.push_back(((long long)k * 2 + p) * N);  // ysend [max_p][2][N]
     }
+  // The integer launch of the fused row pass also runs the inverse row pass
+  // of the owned P slots (the first half of step 5) when every P prime takes
+  // the non-lazy integer inverse path; output aggregation sums cx over the
+  // ranks first, so it keeps the separate pass.
+  bool fold = !oa && lv.n_p > 0;
+  for (int k = 0; k < lv.n_p; ++k) fold = fold && c.primes[L + own_p[k]] >= kInvLazyBound;
+  if (fold)
+    for (int s = 0; s < lv.n_out; ++s)
+      for (int p = 0; p < 2; ++p)
+        lv.fold_off.h.push_back(s < lv.n_q ? -1 : lv.p_offsets.h[p * lv.n_p + (s - lv.n_q)]);
   // where P limb i of poly p lives after the (optional) all-gather
   for (int p = 0; p < 2; ++p)
     for (int i = 0; i < a; ++i) {
@@ -541,6 +551,7 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   up_ints(lv.p_jobs);
   up_i64(lv.p_offsets);
   up_i64(lv.p_cx_offsets);
+  up_i64(lv.fold_off);
   up_i64(lv.y_off);
   lv.qhatinv = upload(qhi);
   std::vector<u64> wsh(w.size());
@@ -559,7 +570,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
   lv.mu = ModUpDev{Ql, lv.QlP, lv.beta, a, lv.prime_of.d, lv.qhatinv, lv.w, lv.wsh, lv.wq};
   lv.lay = KsLayout{lv.n_out,  lv.out_j.d,  lv.key_slot.d,           lv.c_slot.d, G,
                     lv.coef_ml, lv.digits.d, (int)lv.digits.h.size(), lv.rip_fp.d,
-                    lv.rip_int.d, (int)lv.rip_fp.h.size(), (int)lv.rip_int.h.size()};
+                    lv.rip_int.d, (int)lv.rip_fp.h.size(), (int)lv.rip_int.h.size(),
+                    lv.fold_off.h.empty() ? nullptr : lv.fold_off.d};
 }
 
 void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncclComm_t comm,
@@ -712,6 +724,7 @@ void ctx_free(Ctx &c) {
       f(t->d);
     f(lv.p_offsets.d);
     f(lv.p_cx_offsets.d);
+    f(lv.fold_off.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
     for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
@@ -1207,7 +1220,7 @@ void ks_aggregate(Ctx &c, Ctx::Lane &L, const Level &lv, int g, cudaStream_t s) 
 // Steps 5-7 for a group: ModDown of each member's cx into its ciphertext
 // (see moddown_fused_rows for rotate).
 void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g, bool rotate,
-                cudaStream_t s) {
+                cudaStream_t s, bool p_rows_done = false) {
   const size_t N = c.N;
   const NttTables T = c.tables();
   // 5. P part to scaled coefficient form [y_i (P/p_i)^-1]_{p_i}
@@ -1216,8 +1229,13 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
   if (c.replicated()) {
     StageTimer tm(c, ST_INTT_P, s);
     LimbMap mp{L.s_cx, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_cx};
-    KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
-    c.launches += 2;
+    if (p_rows_done) {  // the fused row pass has run the inverse row pass in place
+      KS_CUDA(ntt_inverse_cols_scaled(mp, 2 * lv.n_p, lv.scale_p, T, s, g));
+      c.launches += lv.n_p > 0 ? 1 : 0;
+    } else {
+      KS_CUDA(ntt_inverse_scaled(mp, mp, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
+      c.launches += lv.n_p > 0 ? 2 : 0;
+    }
     y_base = L.s_cx;
     y_bstride = c.st_cx;
   } else {
@@ -1225,8 +1243,13 @@ void ks_moddown(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
       StageTimer tm(c, ST_INTT_P, s);
       LimbMap src{L.s_cx, 0, lv.p_cx_offsets.d, lv.p_jobs.d, 0, 1, c.st_cx};
       LimbMap dst{L.s_ysend, 0, lv.p_offsets.d, lv.p_jobs.d, 0, 1, c.st_ys};
-      KS_CUDA(ntt_inverse_scaled(src, dst, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
-      c.launches += 2;
+      if (p_rows_done) {  // the fused row pass has written the row-passed limbs to ysend
+        KS_CUDA(ntt_inverse_cols_scaled(dst, 2 * lv.n_p, lv.scale_p, T, s, g));
+        c.launches += 1;
+      } else {
+        KS_CUDA(ntt_inverse_scaled(src, dst, 2 * lv.n_p, lv.scale_p, T, s, 1, nullptr, g));
+        c.launches += 2;
+      }
     }
     StageTimer tm(c, ST_COMM, s);
     allgather_group(c, L.comm, L.s_ysend, c.st_ys, L.s_yall, c.st_ya,
@@ -1265,6 +1288,7 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
                      bool rotate, cudaStream_t s) {
   KS_REQUIRE(g >= 1 && g <= c.group, "group larger than the context's scratch");
   const NttTables T = c.tables();
+  bool p_rows_done = false;
   ks_modup_cols(c, L, lv, m, g, s);
   // 4. row pass of every extended limb fused with the inner product
   {
@@ -1274,6 +1298,11 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
       G.n = g;
       G.t = c.st_t;
       G.cx = c.st_cx;
+      // folded inverse row pass of the P slots: in place in cx (one GPU) or
+      // into the all-gather send buffer (input broadcast)
+      p_rows_done = lv.lay.fold_off != nullptr;
+      G.fold = c.world == 1 ? L.s_cx : L.s_ysend;
+      G.fold_b = c.world == 1 ? c.st_cx : c.st_ys;
       for (int b = 0; b < g; ++b) {
         G.in.in[b] = m[b].in;
         G.in.elt[b] = m[b].elt;
@@ -1291,7 +1320,7 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
     }
   }
   ks_aggregate(c, L, lv, g, s);
-  ks_moddown(c, L, lv, m, g, rotate, s);
+  ks_moddown(c, L, lv, m, g, rotate, s, p_rows_done);
 }
 
 // One key switch (a group of one).
@@ -1977,7 +2006,27 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     const Level &lv = level_of(c, level_limbs);
     const size_t bytes = 2 * (size_t)lv.n_q * c.N * 8;
     const cudaStream_t s = (cudaStream_t)stream;
-    const int g = c.group, n_groups = (n + g - 1) / g;
+    const int g = c.group;
+    // Group sizes: the copies are the bottleneck of this path, and the first
+    // copy out waits for the first group's copies in and rotations, the last
+    // rotations for the last copies in; groups of 1, 2, 4 .. at both ends of
+    // the batch shorten that fill and drain (the engines stay busy in between).
+    std::vector<int> sizes, ramp;
+    int ramp_sum = 0;
+    for (int r = 1; r < g; r *= 2) {
+      ramp.push_back(r);
+      ramp_sum += r;
+    }
+    if (n >= 2 * ramp_sum + g) {
+      sizes = ramp;
+      int rest = n - 2 * ramp_sum;
+      for (; rest >= g; rest -= g) sizes.push_back(g);
+      if (rest > 0) sizes.push_back(rest);
+      sizes.insert(sizes.end(), ramp.rbegin(), ramp.rend());
+    } else {
+      for (int i0 = 0; i0 < n; i0 += g) sizes.push_back(std::min(g, n - i0));
+    }
+    const int n_groups = (int)sizes.size();
     const int nl = std::min<int>((int)c.lanes.size(), std::max(n_groups, 1));
     for (int i = 0; i < n; ++i) KS_REQUIRE(host_cts[i] != nullptr, "host ciphertext pointer is null");
     KS_CUDA(cudaSetDevice(c.device));
@@ -1987,8 +2036,8 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     // lanes compute
     KS_CUDA(cudaEventRecord(c.ev_fork, s));
     for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
-    for (int gi = 0; gi < n_groups; ++gi) {
-      const int li = gi % nl, i0 = gi * g, gs = std::min(g, n - i0);
+    for (int gi = 0, i0 = 0; gi < n_groups; i0 += sizes[gi], ++gi) {
+      const int li = gi % nl, gs = sizes[gi];
       Ctx::Lane &L = c.lanes[li];
       const cudaStream_t ls = li == 0 ? s : L.stream;
       u64 *dev[kMaxGroup];

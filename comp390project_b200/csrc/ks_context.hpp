@@ -50,6 +50,10 @@ struct Level {
   DevInts p_jobs;     // [2 * n_p] primes of the owned P slots being inverse-transformed
   DevI64 p_offsets;   // [2 * n_p] word offsets of those slots (in cx for G=1, in ysend otherwise)
   DevI64 p_cx_offsets;  // [2 * n_p] word offsets of the same slots in cx
+  // [2 * n_out]: the fused row pass runs the inverse row pass of the P slots
+  // and writes them at these offsets (p_offsets), -1 for Q slots; empty when
+  // the level does not fold (output aggregation, FP64-sized P primes)
+  DevI64 fold_off;
   DevI64 y_off;       // [2 * alpha] offsets of P limb i of poly p in the y buffer
   ulonglong2 *qhatinv = nullptr;  // [beta][alpha]
   u64 *w = nullptr;               // [beta][QlP][alpha]

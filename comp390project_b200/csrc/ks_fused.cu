@@ -177,20 +177,39 @@ __global__ void __launch_bounds__(kThreads, 3)
   }
 }
 
-// One digit's contribution to an accumulator: acc + y * k mod m_j.  FP:
-// y and acc are the bits of doubles, every term |.| < 0.57 m_j, re-centred
-// every 32 digits; integer: Barrett reduction of y * k + acc.
-template <bool FP>
-__device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool recentre,
-                                       const PrimeDev &P) {
-  if (FP) {
-    const double kd = u64_to_fp(k);
-    double a = first ? 0.0 : as_fp(acc);
-    a = __dadd_rn(a, fp_mulmod(as_fp(y), kd, __dmul_rn(kd, P.qinv), P.qd));
-    if (recentre) a = fp_reduce_sym(a, P.qd, P.qinv);
-    return fp_bits(a);
+// One FP64 inner-product term: acc + y k (mod q, unreduced), with acc
+// brought back to (-q, q) every 32 digits.
+__device__ __forceinline__ u64 ip_term_fp(u64 acc, u64 y, u64 k, bool first, bool recentre,
+                                          const PrimeDev &P) {
+  const double kd = u64_to_fp(k);
+  double a = first ? 0.0 : as_fp(acc);
+  a = __dadd_rn(a, fp_mulmod(as_fp(y), kd, __dmul_rn(kd, P.qinv), P.qd));
+  if (recentre) a = fp_reduce_sym(a, P.qd, P.qinv);
+  return fp_bits(a);
+}
+
+// One integer inner-product term on a 128-bit sum held as four 32-bit TMEM
+// words r[c..c+4): sum += y k, and every 32 digits sum := sum mod q.
+__device__ __forceinline__ void ip_acc128(uint32_t (&r)[8], int c, u64 y, u64 k, bool first,
+                                          bool recentre, const PrimeDev &P) {
+  u128v acc;
+  acc.lo = first ? 0ull : tmem::pack(r[c], r[c + 1]);
+  acc.hi = first ? 0ull : tmem::pack(r[c + 2], r[c + 3]);
+  mac(acc, y, k);
+  if (recentre) {
+    acc.lo = barrett128(acc, P.q, P.br_hi, P.br_lo);
+    acc.hi = 0;
   }
-  return mac_reduce(first ? 0ull : acc, y, k, P.q, P.br_hi, P.br_lo);
+  r[c] = (uint32_t)acc.lo;
+  r[c + 1] = (uint32_t)(acc.lo >> 32);
+  r[c + 2] = (uint32_t)acc.hi;
+  r[c + 3] = (uint32_t)(acc.hi >> 32);
+}
+__device__ __forceinline__ u64 acc128_reduce(const uint32_t (&r)[8], int c, const PrimeDev &P) {
+  u128v acc;
+  acc.lo = tmem::pack(r[c], r[c + 1]);
+  acc.hi = tmem::pack(r[c + 2], r[c + 3]);
+  return barrett128(acc, P.q, P.br_hi, P.br_lo);
 }
 
 // ---------------------------------------------------------------------------
@@ -206,9 +225,10 @@ __device__ __forceinline__ u64 ip_term(u64 acc, u64 y, u64 k, bool first, bool r
 // The key pairs of a lane are copied into shared memory with cp.async when
 // the digit starts, so they arrive while the butterflies run; the next
 // digit's value tile is prefetched into L2.  The 32 accumulators of a
-// thread live in TMEM (64 columns: poly 0 in [0, 32), poly 1 in [32, 64),
-// one u64 as two columns), not in registers.  The extended limbs never
-// return to HBM.
+// thread live in TMEM, not in registers: for FP64 primes 64 columns (poly 0
+// in [0, 32), poly 1 in [32, 64), one u64 as two columns), for integer
+// primes 128 (a 128-bit sum as four columns, reduced once at the end).  The
+// extended limbs never return to HBM.
 struct RowsIpArgs {
   const u64 *t;                  // member b: t + b t_bstride
   u64 *cx;                       // member b: cx + b cx_bstride
@@ -217,6 +237,8 @@ struct RowsIpArgs {
   const u64 *c_ntt[kMaxGroup];   // NTT-form input of member b ...
   uint32_t elt[kMaxGroup];       // ... read through X -> X^elt[b] (1: as it is)
   const u64 *key[kMaxGroup];     // key shard of member b
+  u64 *fold;                     // member b: fold + b fold_bstride (lay.fold_off)
+  long long fold_bstride;
 };
 
 // A CTA is kRipWarps warps; warp w owns the 512 tile words [512w, 512w + 512)
@@ -317,78 +339,150 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
     }
     cp_async_wait_all();  // this lane's own key pairs
     const bool first = di == 0, recentre = (di & 31) == 31;
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      u64 y[4];
-      ulonglong2 k0[2], k1[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int i = 2 * h + q;
-        k0[q] = kst[i * 32];
-        k1[q] = kst[(8 + i) * 32];
-        if (own) {
-          const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), elt, log_n);
-          ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
-          if (src & 1u) {
-            const u64 tmp = v.x;
-            v.x = v.y;
-            v.y = tmp;
-          }
-          y[2 * q] = FP ? fp_bits(u64_to_fp(v.x)) : v.x;
-          y[2 * q + 1] = FP ? fp_bits(u64_to_fp(v.y)) : v.y;
-        } else {
-          const int w = wofs + 64 * i;
-          const int a = padx<LOG_M>(w >> LOG_M, w & (G::M - 1));  // pair's second word: a + 1
-          y[2 * q] = sm[a];
-          y[2 * q + 1] = sm[a + 1];
+    // this lane's pair i of the digit's value tile
+    auto pair = [&](int i) {
+      if (own) {
+        const uint32_t src = galois_src((uint32_t)(tile0 + wofs + 64 * i), elt, log_n);
+        ulonglong2 v = *reinterpret_cast<const ulonglong2 *>(climb + (src & ~1u));
+        if (src & 1u) {
+          const u64 tmp = v.x;
+          v.x = v.y;
+          v.y = tmp;
         }
+        return v;
       }
-      uint32_t r0[8], r1[8];
-      if (!first) {
-        tmem::ld8(tacc + 8 * h, r0);
-        tmem::ld8(tacc + 32 + 8 * h, r1);
-        tmem::wait_ld(r0, r1);
-      }
+      const int w = wofs + 64 * i;
+      const int a = padx<LOG_M>(w >> LOG_M, w & (G::M - 1));  // pair's second word: a + 1
+      return make_ulonglong2(sm[a], sm[a + 1]);
+    };
+    if constexpr (FP) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const u64 b = (u & 1) ? k0[u >> 1].y : k0[u >> 1].x;
-        const u64 a = (u & 1) ? k1[u >> 1].y : k1[u >> 1].x;
-        const u64 v0 = ip_term<FP>(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], b, first, recentre, P);
-        const u64 v1 = ip_term<FP>(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], a, first, recentre, P);
-        r0[2 * u] = (uint32_t)v0;
-        r0[2 * u + 1] = (uint32_t)(v0 >> 32);
-        r1[2 * u] = (uint32_t)v1;
-        r1[2 * u + 1] = (uint32_t)(v1 >> 32);
+      for (int h = 0; h < 4; ++h) {
+        u64 y[4];
+        ulonglong2 k0[2], k1[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int i = 2 * h + q;
+          k0[q] = kst[i * 32];
+          k1[q] = kst[(8 + i) * 32];
+          const ulonglong2 v = pair(i);
+          y[2 * q] = own ? fp_bits(u64_to_fp(v.x)) : v.x;
+          y[2 * q + 1] = own ? fp_bits(u64_to_fp(v.y)) : v.y;
+        }
+        uint32_t r0[8], r1[8];
+        if (!first) {
+          tmem::ld8(tacc + 8 * h, r0);
+          tmem::ld8(tacc + 32 + 8 * h, r1);
+          tmem::wait_ld(r0, r1);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const u64 b = (u & 1) ? k0[u >> 1].y : k0[u >> 1].x;
+          const u64 a = (u & 1) ? k1[u >> 1].y : k1[u >> 1].x;
+          const u64 v0 = ip_term_fp(tmem::pack(r0[2 * u], r0[2 * u + 1]), y[u], b, first, recentre, P);
+          const u64 v1 = ip_term_fp(tmem::pack(r1[2 * u], r1[2 * u + 1]), y[u], a, first, recentre, P);
+          r0[2 * u] = (uint32_t)v0;
+          r0[2 * u + 1] = (uint32_t)(v0 >> 32);
+          r1[2 * u] = (uint32_t)v1;
+          r1[2 * u + 1] = (uint32_t)(v1 >> 32);
+        }
+        tmem::st8(tacc + 8 * h, r0);
+        tmem::st8(tacc + 32 + 8 * h, r1);
       }
-      tmem::st8(tacc + 8 * h, r0);
-      tmem::st8(tacc + 32 + 8 * h, r1);
+    } else {
+      // Integer primes: 128-bit sums of the raw products, reduced only every
+      // 32 digits (y < 4q, k < q < 2^60: a product is below 2^122, 32 of
+      // them and a reduced remainder below 2^128).  Pair i of poly p sits in
+      // columns [64 p + 8 i, 64 p + 8 i + 8): {lo, hi} of word x, then of y.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const ulonglong2 k0 = kst[i * 32], k1 = kst[(8 + i) * 32];
+        const ulonglong2 v = pair(i);
+        uint32_t r0[8], r1[8];
+        if (!first) {
+          tmem::ld8(tacc + 8 * i, r0);
+          tmem::ld8(tacc + 64 + 8 * i, r1);
+          tmem::wait_ld(r0, r1);
+        }
+        ip_acc128(r0, 0, v.x, k0.x, first, recentre, P);
+        ip_acc128(r0, 4, v.y, k0.y, first, recentre, P);
+        ip_acc128(r1, 0, v.x, k1.x, first, recentre, P);
+        ip_acc128(r1, 4, v.y, k1.y, first, recentre, P);
+        tmem::st8(tacc + 8 * i, r0);
+        tmem::st8(tacc + 64 + 8 * i, r1);
+      }
     }
     tmem::wait_st();
     __syncwarp();  // exchange buffer and key stage are reused by the next digit
   }
   u64 *o0 = a_cx + (long long)s * N + tile0 + wofs;
   u64 *o1 = o0 + (long long)lay.n_out * N;
+  if constexpr (FP) {
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    uint32_t r0[8], r1[8];
-    tmem::ld8(tacc + 8 * h, r0);
-    tmem::ld8(tacc + 32 + 8 * h, r1);
-    tmem::wait_ld(r0, r1);
-    u64 v0[4], v1[4];
+    for (int h = 0; h < 4; ++h) {
+      uint32_t r0[8], r1[8];
+      tmem::ld8(tacc + 8 * h, r0);
+      tmem::ld8(tacc + 32 + 8 * h, r1);
+      tmem::wait_ld(r0, r1);
+      u64 v0[4], v1[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      v0[u] = tmem::pack(r0[2 * u], r0[2 * u + 1]);
-      v1[u] = tmem::pack(r1[2 * u], r1[2 * u + 1]);
-      if (FP) {
-        v0[u] = fp_to_canon(as_fp(v0[u]), P.qd, P.qinv);
-        v1[u] = fp_to_canon(as_fp(v1[u]), P.qd, P.qinv);
+      for (int u = 0; u < 4; ++u) {
+        v0[u] = fp_to_canon(as_fp(tmem::pack(r0[2 * u], r0[2 * u + 1])), P.qd, P.qinv);
+        v1[u] = fp_to_canon(as_fp(tmem::pack(r1[2 * u], r1[2 * u + 1])), P.qd, P.qinv);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = 2 * h + q;
+        *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0[2 * q], v0[2 * q + 1]);
+        *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
       }
     }
+  } else {
+    const long long f0 = lay.fold_off ? lay.fold_off[2 * s] : -1;  // CTA-uniform
+    if (f0 < 0) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int i = 2 * h + q;
-      *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) = make_ulonglong2(v0[2 * q], v0[2 * q + 1]);
-      *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) = make_ulonglong2(v1[2 * q], v1[2 * q + 1]);
+      for (int i = 0; i < 8; ++i) {
+        uint32_t r0[8], r1[8];
+        tmem::ld8(tacc + 8 * i, r0);
+        tmem::ld8(tacc + 64 + 8 * i, r1);
+        tmem::wait_ld(r0, r1);
+        *reinterpret_cast<ulonglong2 *>(o0 + 64 * i) =
+            make_ulonglong2(acc128_reduce(r0, 0, P), acc128_reduce(r0, 4, P));
+        *reinterpret_cast<ulonglong2 *>(o1 + 64 * i) =
+            make_ulonglong2(acc128_reduce(r1, 0, P), acc128_reduce(r1, 4, P));
+      }
+    } else {
+      // P slot: the first (row) pass of the inverse transform of both polys
+      // runs here on the finished tile, which goes back to the exchange
+      // buffer in row order; the row-passed tile is written where the
+      // separate inverse row pass would have put it.  Every P prime of a
+      // folding level takes the non-lazy integer inverse path.
+      const ulonglong2 *twi = T.inv + (long long)prime * N;
+      u64 *fb = A.fold + mb * A.fold_bstride + tile0;
+#pragma unroll 1
+      for (int p = 0; p < 2; ++p) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          uint32_t r0[8], r1[8];
+          tmem::ld8(tacc + 64 * p + 8 * i, r0);
+          tmem::ld8(tacc + 64 * p + 8 * (i + 1), r1);
+          tmem::wait_ld(r0, r1);
+          const int w0 = wofs + 64 * i, w1 = w0 + 64;
+          const int a0 = padx<LOG_M>(w0 >> LOG_M, w0 & (G::M - 1));
+          const int a1 = padx<LOG_M>(w1 >> LOG_M, w1 & (G::M - 1));
+          sm[a0] = acc128_reduce(r0, 0, P);
+          sm[a0 + 1] = acc128_reduce(r0, 4, P);
+          sm[a1] = acc128_reduce(r1, 0, P);
+          sm[a1 + 1] = acc128_reduce(r1, 4, P);
+        }
+        __syncwarp();
+        u64 x[kEpt];
+        inv_rows_regs<LOG_M, false>(x, sm, tt, rr, row, log_n, twi, P);
+        u64 *ot = fb + lay.fold_off[2 * s + p];
+#pragma unroll
+        for (int e = 0; e < kEpt; ++e) ot[rr * G::M + lidx<LOG_M, G::HI, 4>(tt, e)] = x[e];
+        __syncwarp();  // the exchange buffer is refilled for poly 1
+      }
     }
   }
 }
@@ -399,11 +493,12 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
 template <int LOG_M, bool FP_SLOTS>
 __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(const __grid_constant__ RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
-  // Warp w uses TMEM lane quarter w % 4 and 64 columns at 64 (w / 4): a CTA
-  // needs 64 columns per group of four warps.  Shared memory caps how many
-  // CTAs share an SM so that their columns never exceed the 512 of an SM,
-  // hence tmem::alloc never waits.
-  constexpr uint32_t kCols = kRipWarps > 4 ? 128 : 64;
+  // Warp w uses TMEM lane quarter w % 4 and kWg columns at kWg (w / 4): 64
+  // for the FP64 sums (one 64-bit word per accumulator), 128 for the integer
+  // 128-bit sums.  Shared memory caps how many CTAs share an SM so that their
+  // columns never exceed the 512 of an SM, hence tmem::alloc never waits.
+  constexpr uint32_t kWg = FP_SLOTS ? 64 : 128;
+  constexpr uint32_t kCols = kWg * (kRipWarps / 4);
   static_assert(kRipWarps == 4 || kRipWarps == 8, "CTA of 4 or 8 warps");
   static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / (512 / kCols + 1),
                 "TMEM columns could be oversubscribed");
@@ -422,7 +517,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   __syncthreads();
   tmem::fence_after_sync();
   // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
-  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + 64u * (warp >> 2);
+  const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + kWg * (warp >> 2);
   if (FP_SLOTS) {
     constexpr int R = rows_ip_rows<LOG_M>();
     stage_row_twiddles<LOG_M, R, kRipThreads>(smtw, T.fwd_fp + (long long)prime * (1 << T.log_n),
@@ -665,6 +760,14 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
   // first pass: the ordinary inverse row pass, src (through elt) -> dst
   cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &dst, elt, mi, group);
   if (e != cudaSuccess) return e;
+  return ntt_inverse_cols_scaled(dst, n_limbs, scale, T, s, group);
+}
+
+cudaError_t ntt_inverse_cols_scaled(const LimbMap &dst, int n_limbs, const ulonglong2 *scale,
+                                    const NttTables &T, cudaStream_t s, int group) {
+  if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (n_limbs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_limbs, group);
   switch (T.log_n) {
@@ -720,6 +823,9 @@ cudaError_t modup_rows_inner_product_group(const GroupArgs &G, const u64 *t, int
     A.elt[b] = G.in.elt[b];
     A.key[b] = G.key[b];
   }
+  A.fold = G.fold;
+  A.fold_bstride = G.fold_b;
+  if (lay.fold_off && !G.fold) return cudaErrorInvalidValue;
   const int s2 = T.log_n - T.log_n / 2;
   switch (s2) {
     case 6: return launch_modup_rows_ip<6>(s, A, G.n, mu, lay, T, side, ev_fork, ev_join);

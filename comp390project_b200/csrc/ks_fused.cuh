@@ -17,6 +17,10 @@ namespace ksb {
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
                                const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
                                uint32_t elt = 1, const MemberIn *mi = nullptr, int group = 1);
+// The column pass of ntt_inverse_scaled alone, in place on dst (the inverse
+// row pass already done).
+cudaError_t ntt_inverse_cols_scaled(const LimbMap &dst, int n_limbs, const ulonglong2 *scale,
+                                    const NttTables &T, cudaStream_t s, int group);
 
 // A group of key switches pushed through each launch together (grid z =
 // member): the member strides (words) of the scratch buffers, and the
@@ -28,6 +32,8 @@ struct GroupArgs {
   const u64 *key[kMaxGroup];             // key shard of each member
   u64 *ct0[kMaxGroup], *ct1[kMaxGroup];  // output polys of each member
   const u64 *g0p[kMaxGroup];             // rotated c0 of each member (null: none)
+  u64 *fold = nullptr;                   // base of the folded P-slot row passes ...
+  long long fold_b = 0;                  // ... and its member stride (KsLayout::fold_off)
 };
 
 // ModUp: for each job (digit d, output slot s) the column pass of the

@@ -48,6 +48,10 @@ struct KsLayout {
   // kind keep the instruction cache warm)
   const int *slots_fp, *slots_int;
   int n_slots_fp, n_slots_int;
+  // [2 n_out] or null: for a P slot s, where the integer launch writes poly
+  // p's tile after the inverse row pass (word offset fold_off[2 s + p] from
+  // the fold base of the member) instead of writing cx; -1 for Q slots
+  const long long *fold_off;
 };
 
 // out[l][i] = in[l][perm_elt(i)] for the NTT-domain automorphism X -> X^elt.
