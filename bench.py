@@ -61,6 +61,10 @@ def parse():
                     help="execution lanes (streams + scratch) for the batched key switches")
     ap.add_argument("--group", type=int, default=4,
                     help="key switches each lane pushes through every launch together (1..8)")
+    ap.add_argument("--mode", choices=["ib", "oa"], default="ib",
+                    help="multi-GPU plan of the key-switch workload: input broadcast (limb-"
+                         "sharded ciphertexts) or output aggregation (replicated ciphertexts, "
+                         "digit-split inner product, all-reduce)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["ks", "ntt", "hoisted", "matmul"], default="ks",
                     help="ks: config-3 rotations (default); ntt: config-2 batched NTT; "
@@ -356,17 +360,23 @@ NVLINK_GBS = 770.0
 NVLINK_NOMINAL_GBS = 900.0  # NVLink 5, per direction per GPU
 
 
-def collective_roofline(prof, n_ks, L, alpha, world, N):
-    """NVLink roofline of the input-broadcast collectives from the serial
-    profile: per key switch a rank receives the other ranks' padded shares of
-    the coefficient-form input ((G-1) ceil(L/G) limbs) and of the special-prime
-    limbs of cx ((G-1) 2 max_r |P limbs of r| limbs)."""
+def collective_roofline(prof, n_ks, L, alpha, world, N, oa=False):
+    """NVLink roofline of the collectives from the serial profile.  Input
+    broadcast: per key switch a rank receives the other ranks' padded shares
+    of the coefficient-form input ((G-1) ceil(L/G) limbs) and of the
+    special-prime limbs of cx ((G-1) 2 max_r |P limbs of r| limbs).  Output
+    aggregation: the all-reduce of cx (2 (L+alpha) limbs), which a ring
+    all-reduce moves as 2 (G-1)/G of the buffer into every rank."""
     ms, calls = prof.get("collective", (0.0, 0))
     if world <= 1 or ms <= 0 or n_ks <= 0:
         return None
-    coef_ml = -(-L // world)
-    max_p_own = max(sum(1 for i in range(alpha) if (L + i) % world == r) for r in range(world))
-    recv = (world - 1) * (coef_ml + 2 * max_p_own) * N * 8
+    if oa:
+        recv = 2 * (world - 1) * 2 * (L + alpha) * N * 8 // world
+    else:
+        coef_ml = -(-L // world)
+        max_p_own = max(sum(1 for i in range(alpha) if (L + i) % world == r)
+                        for r in range(world))
+        recv = (world - 1) * (coef_ml + 2 * max_p_own) * N * 8
     t = ms / n_ks / 1000.0
     ach = recv / t / 1e9
     return {"bound": "nvlink", "bytes_received_per_ks": recv, "ms_per_ks": ms / n_ks,
@@ -786,20 +796,25 @@ def run_reference(args, rank, world):
 def run_ours(args, rank, world):
     import torch
     import torch.distributed as dist
-    from comp390project_b200 import KS_KEY_GALOIS, KsContext, gen_primes, secret_generate
+    from comp390project_b200 import (KS_KEY_GALOIS, KS_MODE_INPUT_BROADCAST,
+                                     KS_MODE_OUTPUT_AGGREGATION, KsContext, gen_primes,
+                                     secret_generate)
 
     dev = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(dev)
     pr = gen_primes(LOG_N, QBITS + PBITS)
     q, p = pr[:len(QBITS)], pr[len(QBITS):]
     L = len(q)
+    oa = args.mode == "oa" and world > 1
+    mode = KS_MODE_OUTPUT_AGGREGATION if oa else KS_MODE_INPUT_BROADCAST
     if world > 1:
-        ctx = KsContext.from_process_group(LOG_N, q, p, device=dev, max_batch=args.lanes,
-                                           batch_group=args.group)
+        ctx = KsContext.from_process_group(LOG_N, q, p, device=dev, mode=mode,
+                                           max_batch=args.lanes, batch_group=args.group)
     else:
         ctx = KsContext(LOG_N, q, p, device=dev, max_batch=args.lanes, batch_group=args.group)
     N = 1 << LOG_N
-    nloc = ctx.n_local_limbs(L)
+    # output aggregation: every rank holds the whole ciphertext
+    nloc = L if oa else ctx.n_local_limbs(L)
     B = args.batch
     steps_of = [i + 1 for i in range(B)]
     # keys: one Galois key per rotation step, generated on the device
@@ -813,7 +828,7 @@ def run_ours(args, rank, world):
     g.manual_seed(1234 + rank)
     cts = torch.empty((B, 2, nloc, N), dtype=torch.int64, device="cuda")
     for sl in range(nloc):
-        j = rank + sl * world
+        j = sl if oa else rank + sl * world
         cts[:, :, sl, :] = torch.randint(0, int(q[j]), (B, 2, N), generator=g, device="cuda",
                                          dtype=torch.int64)
     views = [cts[i] for i in range(B)]
@@ -891,21 +906,32 @@ def run_ours(args, rank, world):
     QlP = L + len(p)
     beta = 7
     U = 8 * N
-    n_out = len(range(rank, L, world)) + sum(1 for i in range(len(p)) if (L + i) % world == rank)
-    n_q = nloc
+    alpha = len(p)
+    if oa:
+        # every output limb on every rank, over this rank's digits d = rank mod G
+        n_out, n_q = QlP, L
+        my_digits = list(range(rank, beta, world))
+        n_dig = len(my_digits)
+        n_in = sum(min(alpha, L - d * alpha) for d in my_digits)  # limbs of those digits
+        n_p_own = alpha
+    else:
+        n_out = len(range(rank, L, world)) + sum(1 for i in range(alpha)
+                                                 if (L + i) % world == rank)
+        n_q = nloc
+        n_dig, n_in = beta, n_q
+        n_p_own = n_out - n_q
     # Algorithmic bytes per key switch on this rank (U = one limb): compulsory
     # inputs once + outputs once of each stage (twiddle/constant tables excluded).
-    n_jobs = beta * n_out - n_q  # extended limbs produced by ModUp (own digit limbs are copies)
-    n_p_own = n_out - n_q
+    n_jobs = n_dig * n_out - n_in  # extended limbs produced by ModUp (own digit limbs are copies)
     alg = {
         "galois": 4 * n_q * U,
-        "intt_input": 2 * n_q * U,
-        "modup_cols": (L + n_jobs) * U,
+        "intt_input": 2 * n_in * U,
+        "modup_cols": ((n_in if oa else L) + n_jobs) * U,
         # extended limbs (column pass done) + own-digit input limbs, both key
         # polys of every digit, cx out
-        "modup_rows_ip": (beta * n_out + 2 * beta * n_out + 2 * n_out) * U,
+        "modup_rows_ip": (n_dig * n_out + 2 * n_dig * n_out + 2 * n_out) * U,
         "intt_p": 4 * n_p_own * U,
-        "moddown_cols": (2 * len(p) + 2 * n_q) * U,
+        "moddown_cols": (2 * alpha + 2 * n_q) * U,
         "moddown_rows": 7 * n_q * U,
     }
     peak, peak_kind = measured_peaks()
@@ -950,7 +976,7 @@ def run_ours(args, rank, world):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_config3()
-    nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N)
+    nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N, oa=oa)
     # the second half of the headline metric: config 2's NTT on the same GPUs
     # (every rank, after the key-switch measurements)
     ntt = None
@@ -965,8 +991,9 @@ def run_ours(args, rank, world):
             "data": "synthetic",
             "config": {"workload": "config3-rotation: 64 ciphertexts, steps 1..64, 64 Galois keys",
                        "N": N, "L": L, "alpha": len(p), "dnum": beta, "batch": B,
-                       "parallelism": "limb-sharded x%d (input broadcast), %d lanes x groups "
-                                      "of %d" % (world, args.lanes, args.group),
+                       "parallelism": "limb-sharded x%d (%s), %d lanes x groups of %d"
+                                      % (world, "output aggregation" if oa else "input broadcast",
+                                         args.lanes, args.group),
                        "cuda_graph": graph is not None,
                        "l2": "inputs (2.3 GB cts + 18.8 GB keys) exceed L2; no flush"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,

@@ -995,15 +995,15 @@ void key_generate(Ctx &c, int kind, uint32_t elt, const int8_t *sk_host, u64 see
 // ---------------------------------------------------------------------------
 enum Stage {
   ST_GALOIS = 0, ST_INTT_IN, ST_MODUP_COLS, ST_MODUP_ROWS_IP, ST_INTT_P, ST_MODDOWN_COLS,
-  ST_MODDOWN_ROWS, ST_COMM, ST_MODUP_ROWS, ST_INNER_PROD, ST_PLAIN_MAC, ST_ADD, ST_COUNT
+  ST_MODDOWN_ROWS, ST_COMM, ST_MODUP_ROWS, ST_INNER_PROD, ST_PLAIN_MAC, ST_COUNT
 };
 // modup_rows and inner_product are the two halves of modup_rows_ip that the
-// hoisted path runs apart (one row pass, one inner product per rotation);
-// plain_mac and add are the plaintext products and sums of the BSGS matmul.
+// hoisted path and the BSGS giant steps run apart (one row pass, one inner
+// product per rotation); plain_mac is the plaintext products of the BSGS matmul.
 static const char *kStageNames[ST_COUNT] = {
     "galois",       "intt_input",   "modup_cols",   "modup_rows_ip", "intt_p",
     "moddown_cols", "moddown_rows", "collective",   "modup_rows",    "inner_product",
-    "plain_mac",    "add"};
+    "plain_mac"};
 
 cudaEvent_t pool_event(Ctx &c) {
   if (!c.event_pool.empty()) {
@@ -1621,10 +1621,13 @@ void do_bsgs_matmul(Ctx &c, const u64 *const *x, const u64 *const *baby, int n_i
   const int n_terms = n_in * n_baby;
   KS_REQUIRE(!c.lanes.empty(), "context has no special primes (NTT-only context)");
   Ctx::Lane &L = c.lanes[0];
+  const NttTables T = c.tables();
+  const bool add_c0 = !c.oa() || c.rank == 0;  // the c0 term once over the ranks
   for (int o = 0; o < n_out; ++o) {
     // g == 0 (if in range) is written straight into y[o] by the first pass;
     // otherwise y[o] starts from zero
     if (g_lo > 0 && have) KS_CUDA(cudaMemsetAsync(y[o], 0, ct_words * 8, s));
+    bool acc_open = false;  // lane 0's cx holds this output's giant-step sum
     for (int g0 = g_lo; g0 < g_hi; g0 += kMacMaxOut) {
       const int ng = std::min(kMacMaxOut, g_hi - g0);
       MacTerms a{};
@@ -1645,14 +1648,43 @@ void do_bsgs_matmul(Ctx &c, const u64 *const *x, const u64 *const *baby, int n_i
           c.launches += have ? 1 : 0;
         }
       }
+      // giant steps g > 0: ModUp of the partial sum's c1, then its inner
+      // product with the giant step's key, read through the automorphism,
+      // plus [P] g(c0), accumulated in the extended basis (lane 0's cx)
       for (int j = 0; j < ng; ++j) {
         const int g = g0 + j;
         if (g == 0) continue;
-        do_apply_galois(c, L, a.out[j], Ql, elt_of_step(c, g * n_baby * unit), s);
-        StageTimer tm(c, ST_ADD, s);
-        KS_CUDA(add_ct(y[o], a.out[j], 2, nq, lv.q_index.d, c.d_primes, c.log_n, s));
-        c.launches += have ? 1 : 0;
+        const uint32_t elt = elt_of_step(c, g * n_baby * unit);
+        const KeyShard &key = key_get(c, KS_KEY_GALOIS, elt);
+        const u64 *c1 = have ? a.out[j] + nq * N : nullptr;
+        KsMember mi;
+        mi.in = c1;
+        ks_modup_cols(c, L, lv, &mi, 1, s);
+        {
+          StageTimer tm(c, ST_MODUP_ROWS, s);
+          LimbMap mt{L.s_t, 0, lv.job_off.d, lv.job_prime.d, 0, 1};
+          KS_CUDA(ntt_forward_rows_only(mt, lv.n_jobs, T, s));
+          c.launches += lv.n_jobs > 0 ? 1 : 0;
+        }
+        StageTimer tm(c, ST_INNER_PROD, s);
+        if (lv.lay.n_digits > 0) {
+          KS_CUDA(inner_product_acc(L.s_t, c1, key.d, key.limbs, L.s_cx, nullptr, a.out[j],
+                                    c.d_pmodq, add_c0, !acc_open, lv.mu, lv.lay, c.d_primes,
+                                    c.log_n, elt, s));
+          c.launches += lv.lay.n_out > 0 ? 1 : 0;
+        } else if (!acc_open) {
+          KS_CUDA(cudaMemsetAsync(L.s_cx, 0, (size_t)2 * lv.n_out * N * 8, s));
+        }
+        acc_open = true;
       }
+    }
+    // one ModDown for all giant steps of the output: y[o] += ModDown(acc)
+    if (acc_open) {
+      ks_aggregate(c, L, lv, 1, s);
+      KsMember mo;
+      mo.ct0 = y[o];
+      mo.ct1 = have ? y[o] + nq * N : nullptr;
+      ks_moddown(c, L, lv, &mo, 1, false, s);
     }
   }
 }

@@ -142,15 +142,22 @@ __global__ void __launch_bounds__(kBlk) k_inner_product_acc(
     r.r0.x = add_mod(r.r0.x, mul_shoup(x.x, pq.x, pq.y, P.q), P.q);
     r.r0.y = add_mod(r.r0.y, mul_shoup(x.y, pq.x, pq.y, P.q), P.q);
   }
-  const ulonglong2 dg = *reinterpret_cast<const ulonglong2 *>(diag + (long long)s * N + k);
   u64 *a0 = acc + (long long)s * N + k;
   u64 *a1 = acc + ((long long)lay.n_out + s) * N + k;
   ulonglong2 v0 = first ? make_ulonglong2(0, 0) : *reinterpret_cast<const ulonglong2 *>(a0);
   ulonglong2 v1 = first ? make_ulonglong2(0, 0) : *reinterpret_cast<const ulonglong2 *>(a1);
-  v0.x = mac_reduce(v0.x, r.r0.x, dg.x, P.q, P.br_hi, P.br_lo);
-  v0.y = mac_reduce(v0.y, r.r0.y, dg.y, P.q, P.br_hi, P.br_lo);
-  v1.x = mac_reduce(v1.x, r.r1.x, dg.x, P.q, P.br_hi, P.br_lo);
-  v1.y = mac_reduce(v1.y, r.r1.y, dg.y, P.q, P.br_hi, P.br_lo);
+  if (diag) {
+    const ulonglong2 dg = *reinterpret_cast<const ulonglong2 *>(diag + (long long)s * N + k);
+    v0.x = mac_reduce(v0.x, r.r0.x, dg.x, P.q, P.br_hi, P.br_lo);
+    v0.y = mac_reduce(v0.y, r.r0.y, dg.y, P.q, P.br_hi, P.br_lo);
+    v1.x = mac_reduce(v1.x, r.r1.x, dg.x, P.q, P.br_hi, P.br_lo);
+    v1.y = mac_reduce(v1.y, r.r1.y, dg.y, P.q, P.br_hi, P.br_lo);
+  } else {  // no plaintext factor: a plain sum of rotations
+    v0.x = add_mod(v0.x, r.r0.x, P.q);
+    v0.y = add_mod(v0.y, r.r0.y, P.q);
+    v1.x = add_mod(v1.x, r.r1.x, P.q);
+    v1.y = add_mod(v1.y, r.r1.y, P.q);
+  }
   *reinterpret_cast<ulonglong2 *>(a0) = v0;
   *reinterpret_cast<ulonglong2 *>(a1) = v1;
 }
@@ -222,23 +229,6 @@ __global__ void __launch_bounds__(kBlk, NG >= 3 ? 2 : 3) k_mac_plain(const MacTe
     *reinterpret_cast<ulonglong2 *>(a.out[j] + stride + lo) =
         make_ulonglong2(barrett128(acc[j][2], q, rh, rl), barrett128(acc[j][3], q, rh, rl));
   }
-}
-
-// out[p][l] = out[p][l] + x[p][l] mod q for n_polys polys of n_limbs slots.
-__global__ void k_add_ct(u64 *__restrict__ out, const u64 *__restrict__ x, int n_limbs,
-                         const int *__restrict__ prime_of_slot, const PrimeDev *primes,
-                         int log_n) {
-  const int N = 1 << log_n;
-  const int l = blockIdx.y % n_limbs;
-  const long long off = (long long)blockIdx.y * N;
-  const int k = (blockIdx.x * kBlk + threadIdx.x) * 2;
-  if (k >= N) return;
-  const u64 q = primes[prime_of_slot[l]].q;
-  ulonglong2 a = *reinterpret_cast<const ulonglong2 *>(out + off + k);
-  const ulonglong2 b = *reinterpret_cast<const ulonglong2 *>(x + off + k);
-  a.x = add_mod(a.x, b.x, q);
-  a.y = add_mod(a.y, b.y, q);
-  *reinterpret_cast<ulonglong2 *>(out + off + k) = a;
 }
 
 // Cyclic-partition copy between the global layout [poly][total][degree]
@@ -400,14 +390,6 @@ cudaError_t mac_plain(const MacTerms &a, int n_limbs, const int *prime_of_slot,
     case 3: k_mac_plain<3><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
     default: k_mac_plain<4><<<g, kBlk, 0, s>>>(a, n_limbs, prime_of_slot, primes, log_n); break;
   }
-  return cudaGetLastError();
-}
-
-cudaError_t add_ct(u64 *out, const u64 *x, int n_polys, int n_limbs, const int *prime_of_slot,
-                   const PrimeDev *primes, int log_n, cudaStream_t s) {
-  if (n_limbs <= 0 || n_polys <= 0) return cudaSuccess;
-  k_add_ct<<<grid2(log_n, n_polys * n_limbs, 2), kBlk, 0, s>>>(out, x, n_limbs, prime_of_slot,
-                                                               primes, log_n);
   return cudaGetLastError();
 }
 

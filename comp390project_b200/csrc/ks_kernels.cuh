@@ -74,7 +74,8 @@ cudaError_t inner_product(const u64 *t, const u64 *c_ntt, const u64 *key, int ke
 // basis (double hoisting): with ip_p the inner product above,
 //   acc[0][s] = (first ? 0 : acc[0][s]) + diag[s] * (ip_0 + [P]_{q_j} c0[c_slot[s]] o elt)
 //   acc[1][s] = (first ? 0 : acc[1][s]) + diag[s] * ip_1
-// (the c0 term only for Q limbs and when add_c0; pmodq[j] = {[P]_{q_j}, Shoup}).
+// (the c0 term only for Q limbs and when add_c0; pmodq[j] = {[P]_{q_j}, Shoup};
+// diag null: no plaintext factor).
 cudaError_t inner_product_acc(const u64 *t, const u64 *c_ntt, const u64 *key, int key_limbs,
                               u64 *acc, const u64 *diag, const u64 *c0, const ulonglong2 *pmodq,
                               bool add_c0, bool first, const ModUpDev &mu, const KsLayout &lay,
@@ -96,9 +97,6 @@ struct MacTerms {
 };
 cudaError_t mac_plain(const MacTerms &a, int n_limbs, const int *prime_of_slot,
                       const PrimeDev *primes, int log_n, cudaStream_t s);
-// out += x  mod q, [n_polys][n_limbs][N].
-cudaError_t add_ct(u64 *out, const u64 *x, int n_polys, int n_limbs, const int *prime_of_slot,
-                   const PrimeDev *primes, int log_n, cudaStream_t s);
 
 // x %= q for each limb (after an integer all-reduce / reduce-scatter of partial sums).
 cudaError_t mod_reduce(u64 *x, int n_limbs, const int *prime_of_slot, const PrimeDev *primes,

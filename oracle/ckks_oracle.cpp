@@ -604,8 +604,15 @@ void ork_linear_transform_hoisted(const ork_ctx *c, const uint64_t *ct, int Ql, 
 //   y[o] = sum_{g in [g_lo, g_hi)} rot_g( sum_{i < n_in} sum_{b < B}
 //            pts[((o n_in + i) G + g) B + b] * rot_b(x[i]) )
 // rot_b (0 < b < B): baby_elts[b - 1] by ork_rotate_hoisted (one ModUp per
-// input); rot_g (g > 0): giant_elts[g] by ork_apply_galois; plaintext products
-// and sums limb by limb mod q_j.
+// input); plaintext products and sums limb by limb mod q_j.  The giant steps
+// g > 0 of one output share one ModDown, as the hoisted linear transform's
+// rotations do: each partial sum s_g gets its own ModUp and inner product
+// with the key of giant_elts[g], read through the automorphism, and
+//   acc_0 += IP_0 + [P]_{q_j} g(s_g.c0) (Q limbs),  acc_1 += IP_1,
+// then y[o] += ModDown(acc).  ModDown(P x + v) = x + ModDown(v) exactly, so
+// this is sum_g rot_g(s_g) up to the rounding of one ModDown per output
+// instead of one per giant step (the rounding depends on which giant steps
+// one call covers: a split over [g_lo, g_hi) ranges rounds per range).
 void ork_bsgs_matmul(const ork_ctx *c, const uint64_t *const *x, int n_in, int Ql, int B,
                      int G, int g_lo, int g_hi, const uint32_t *baby_elts,
                      const uint64_t *const *baby_keys, const uint32_t *giant_elts,
@@ -619,9 +626,18 @@ void ork_bsgs_matmul(const ork_ctx *c, const uint64_t *const *x, int n_in, int Q
       ork_rotate_hoisted(c, x[i], Ql, B - 1, baby_elts, baby_keys,
                          rots.data() + ((size_t)i * B + 1) * CT);
   }
-  std::vector<u64> inner(CT), rotated(CT);
+  const int QlP = Ql + c->alpha, beta = ork_num_digits(c, Ql);
+  std::vector<u64> inner(CT), t((size_t)beta * QlP * N), tg(t.size()), cx((size_t)2 * QlP * N);
+  std::vector<u64> acc((size_t)2 * QlP * N), g0(QN), ks(CT), Pq(Ql);
+  for (int j = 0; j < Ql; ++j) {
+    u64 P = 1;
+    for (int i = 0; i < c->alpha; ++i) P = mulmod(P, c->m[c->L + i] % c->m[j], c->m[j]);
+    Pq[j] = P;
+  }
   for (int o = 0; o < n_out; ++o) {
     std::memset(y[o], 0, CT * 8);
+    std::fill(acc.begin(), acc.end(), 0);
+    bool any_giant = false;
     for (int g = g_lo; g < g_hi; ++g) {
       std::fill(inner.begin(), inner.end(), 0);
       for (int i = 0; i < n_in; ++i)
@@ -638,13 +654,33 @@ void ork_bsgs_matmul(const ork_ctx *c, const uint64_t *const *x, int n_in, int Q
               }
           }
         }
-      const u64 *add = inner.data();
-      if (g > 0) {
-        ork_apply_galois(c, inner.data(), Ql, giant_elts[g], giant_keys[g], rotated.data());
-        add = rotated.data();
+      if (g == 0) {
+        add_inplace(c, y[o], inner.data(), Ql);
+        add_inplace(c, y[o] + QN, inner.data() + QN, Ql);
+        continue;
       }
-      add_inplace(c, y[o], add, Ql);
-      add_inplace(c, y[o] + QN, add + QN, Ql);
+      any_giant = true;
+      ork_modup(c, inner.data() + QN, Ql, t.data());
+      ork_galois_ntt(c, giant_elts[g], t.data(), tg.data(), beta * QlP);
+      ork_inner_product(c, tg.data(), Ql, giant_keys[g], cx.data());
+      ork_galois_ntt(c, giant_elts[g], inner.data(), g0.data(), Ql);
+#pragma omp parallel for schedule(static)
+      for (int j = 0; j < QlP; ++j) {
+        const u64 q = c->m[qlp_key_index(c, Ql, j)];
+        for (int p = 0; p < 2; ++p)
+          for (size_t k = 0; k < N; ++k) {
+            u64 v = cx[((size_t)p * QlP + j) * N + k];
+            if (p == 0 && j < Ql) v = addmod(v, mulmod(Pq[j], g0[(size_t)j * N + k], q), q);
+            u64 &a = acc[((size_t)p * QlP + j) * N + k];
+            a = addmod(a, v, q);
+          }
+      }
+    }
+    if (any_giant) {
+      for (int p = 0; p < 2; ++p)
+        ork_moddown(c, acc.data() + (size_t)p * QlP * N, Ql, ks.data() + (size_t)p * QN);
+      add_inplace(c, y[o], ks.data(), Ql);
+      add_inplace(c, y[o] + QN, ks.data() + QN, Ql);
     }
   }
 }

@@ -39,3 +39,19 @@ def decode_outputs(c, ys):
     o, lay, Ql = c["o"], c["lay"], c["Ql"]
     vecs = [o.decode(o.decrypt(c["s"], y, Ql), Ql, SCALE * SCALE) for y in ys]
     return matmul.unpack(np.real(np.array(vecs)), lay)
+
+
+def split_reference(c, world):
+    """The oracle's product summed over the giant-step ranges of `world`
+    ranks (matmul.giant_ranges), each range evaluated by one call (one
+    ModDown per range), as matmul_giant_parallel computes it."""
+    o, lay, Ql = c["o"], c["lay"], c["Ql"]
+    args = (c["xs"], Ql, lay.unit, lay.n_baby, lay.n_giant, c["pts"], c["keys"])
+    q = np.array([int(o.moduli[j]) for j in range(Ql)], dtype=np.uint64)[None, None, :, None]
+    acc = None
+    for r in matmul.giant_ranges(lay.n_giant, world):
+        if r[1] <= r[0]:
+            continue
+        p = o.bsgs_matmul(*args, g_range=r)
+        acc = p if acc is None else (acc + p) % q
+    return acc

@@ -1,10 +1,12 @@
 """BSGS ciphertext x plaintext matmul through the C ABI (ks_bsgs_matmul):
 baby-step rotations hoisted per input, plaintext products of up to four giant
-steps per pass, giant-step rotations and sums.  Every output word must equal
-the CPU oracle's composition (ork_bsgs_matmul) exactly, for the whole product,
-for a giant-step sub-range with caller-supplied baby steps, and for the
-giant-step split over two GPUs (all-gather of the baby steps, integer
-all-reduce of the partial products); the product decodes to X W."""
+steps per pass, giant-step key switches accumulated in the extended basis
+with one ModDown per output.  Every output word must equal the CPU oracle's
+composition (ork_bsgs_matmul) exactly, for the whole product, for a
+giant-step sub-range with caller-supplied baby steps, and for the giant-step
+split over two GPUs (all-gather of the baby steps, integer all-reduce of the
+partial products; the oracle summed over the same ranges, since each range
+rounds in its own ModDown); the product decodes to X W."""
 import functools
 import os
 import sys
@@ -12,7 +14,7 @@ import sys
 import numpy as np
 import pytest
 
-from tests.matmul_case import case, decode_outputs
+from tests.matmul_case import case, decode_outputs, split_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -143,7 +145,7 @@ def _worker(rank, world, port, q):
         c, ctx, xs, pts, ys = _setup(device=rank)
         matmul.matmul_giant_parallel(ctx, xs, c["Ql"], c["lay"], pts, ys)
         torch.cuda.synchronize()
-        ok = bool(np.array_equal(_host(ys), _want()))
+        ok = bool(np.array_equal(_host(ys), split_reference(c, world)))
         ctx.close()
         q.put((rank, ok))
     except Exception:

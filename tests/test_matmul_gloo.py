@@ -77,14 +77,15 @@ def _worker(rank, world, port, n_baby, result_q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from comp390project_b200 import matmul
-        from tests.matmul_case import case
+        from tests.matmul_case import case, split_reference
         c = case(n_baby)
         lay, Ql, o = c["lay"], c["Ql"], c["o"]
         xs = [torch.from_numpy(x.view(np.int64).copy()) for x in c["xs"]]
         pts = [torch.from_numpy(p.view(np.int64).copy()) for p in c["pts"]]
         ys = torch.zeros((lay.n_out, 2, Ql, o.N), dtype=torch.int64)
         matmul.matmul_giant_parallel(OracleCtx(c), xs, Ql, lay, pts, ys)
-        want = o.bsgs_matmul(c["xs"], Ql, lay.unit, lay.n_baby, lay.n_giant, c["pts"], c["keys"])
+        # the oracle over the same giant-step ranges (one ModDown per range), summed
+        want = split_reference(c, world)
         result_q.put((rank, bool(np.array_equal(_np(ys), want))))
     except Exception:
         import traceback
