@@ -487,9 +487,9 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
   }
 }
 
-// FP_SLOTS: the launch over lay.slots_fp (FP64 bodies only); otherwise the
-// launch over lay.slots_int (the two integer bodies).  One arithmetic kind
-// per kernel keeps its code small enough for the instruction cache.
+// FP_SLOTS: the launch over lay.slots_fp (the FP64 body); otherwise the
+// launch over lay.slots_int (the integer body).  One arithmetic kind per
+// kernel keeps its code small enough for the instruction cache.
 template <int LOG_M, bool FP_SLOTS>
 __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     k_modup_rows_ip(const __grid_constant__ RowsIpArgs A, ModUpDev mu, KsLayout lay, NttTables T) {
@@ -510,13 +510,12 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   double *smtw = reinterpret_cast<double *>(kst + kRipWarps * 2 * 8 * 32);
   const int s = FP_SLOTS ? lay.slots_fp[blockIdx.y] : lay.slots_int[blockIdx.y];
   const int prime = mu.prime_of[lay.out_j[s]];
-  const u64 q = T.primes[prime].q;
   const int warp = threadIdx.x >> 5;
   if (warp == 0) tmem::alloc(&tmem_slot, kCols);
   tmem::fence_before_sync();
   __syncthreads();
   tmem::fence_after_sync();
-  // warp w: TMEM lanes 32 (w % 4) .., columns 64 (w / 4) ..
+  // warp w: TMEM lanes 32 (w % 4) .., columns kWg (w / 4) ..
   const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + kWg * (warp >> 2);
   if (FP_SLOTS) {
     constexpr int R = rows_ip_rows<LOG_M>();
@@ -525,9 +524,10 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
     cp_async_wait_all();
     __syncthreads();
     rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
-  } else if (q < kFwdLazyBound) {
-    rows_ip_body<LOG_M, false, true>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
   } else {
+    // Every integer prime (q0 below 2^58 as well as the P primes) takes
+    // Harvey's [0, 4q) butterflies (valid for q < 2^62): one forward body
+    // per kernel, since two of them overflow the instruction cache.
     rows_ip_body<LOG_M, false, false>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
   }
   tmem::fence_before_sync();
