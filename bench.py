@@ -1016,6 +1016,31 @@ def run_ours(args, rank, world):
     ctx.close()
 
 
+def bind_to_gpu_numa(dev):
+    """Restrict this process to the host cores NVML reports as closest to
+    GPU `dev`, so that its pinned host buffers (first touched by this
+    process) sit in that GPU's NUMA node and the end-to-end copies do not
+    cross the socket interconnect.  Returns the number of cores kept, or None
+    when NVML cannot say (the affinity is then left as it is)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(dev)
+            n_words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, n_words)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, m in enumerate(mask) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:
+        return None
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1023,6 +1048,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if world > 1 and args.impl == "ours":
+        # one rank per GPU: keep each rank on its GPU's host cores (NUMA node)
+        bind_to_gpu_numa(int(os.environ.get("LOCAL_RANK", 0)))
     if world > 1:
         import datetime
 
