@@ -37,13 +37,14 @@ PBITS = [60] * 5
 BATCH = 64
 SCALE = 2.0 ** 40
 METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
-# DRAM bytes per launch (read + write) of each key-switch kernel at config 3,
-# one key switch, from `ncu --set full` (profiles/keyswitch_config3_kernels.md).
+# DRAM bytes (read + write) per key switch of each key-switch stage at config
+# 3, from one ncu capture of a group of 4 key switches divided by 4
+# (profiles/keyswitch_config3_kernels.md); a stage's launches summed.
 PROFILED_TRAFFIC_SOURCE = ("constant from one ncu capture (profiles/keyswitch_config3_kernels.md), "
                            "not measured in this run")
 PROFILED_TRAFFIC = {
-    "galois": 38.1e6, "intt_input": 55.7e6, "modup_cols": 98.2e6, "modup_rows_ip": 504.8e6,
-    "intt_p": 15.9e6, "moddown_cols": 5.4e6, "moddown_rows": 140.2e6,
+    "galois": 25.7e6, "intt_input": 55.4e6, "modup_cols": 133.7e6, "modup_rows_ip": 500.4e6,
+    "intt_p": 5.3e6, "moddown_cols": 27.5e6, "moddown_rows": 146.9e6,
 }
 
 
@@ -924,7 +925,7 @@ def run_ours(args, rank, world):
     # inputs once + outputs once of each stage (twiddle/constant tables excluded).
     n_jobs = n_dig * n_out - n_in  # extended limbs produced by ModUp (own digit limbs are copies)
     alg = {
-        "galois": 4 * n_q * U,
+        "galois": 2 * n_q * U,  # c0 -> g0 (c1 is read through the automorphism later)
         "intt_input": 2 * n_in * U,
         "modup_cols": ((n_in if oa else L) + n_jobs) * U,
         # extended limbs (column pass done) + own-digit input limbs, both key
