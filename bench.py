@@ -42,6 +42,17 @@ METRIC = "key-switches/s at N=2^16,L=35 (rotation, hybrid KS dnum=7)"
 # (profiles/keyswitch_config3_kernels.md); a stage's launches summed.
 PROFILED_TRAFFIC_SOURCE = ("constant from one ncu capture (profiles/keyswitch_config3_kernels.md), "
                            "not measured in this run")
+# the kernels behind each stage of the serial profile (one stage timing per
+# group of key switches brackets all of them)
+STAGE_KERNELS = {
+    "galois": "k_galois_ntt",
+    "intt_input": "ntt_rows (inverse) + k_inv_cols_scaled",
+    "modup_cols": "k_modup_cols",
+    "modup_rows_ip": "k_modup_rows_ip: FP64 launch + integer launch on a side stream, concurrent",
+    "intt_p": "k_inv_cols_scaled (the row pass is folded into k_modup_rows_ip)",
+    "moddown_cols": "k_moddown_cols",
+    "moddown_rows": "k_moddown_rows",
+}
 PROFILED_TRAFFIC = {
     "galois": 25.7e6, "intt_input": 55.4e6, "modup_cols": 133.7e6, "modup_rows_ip": 500.4e6,
     "intt_p": 5.3e6, "moddown_cols": 27.5e6, "moddown_rows": 146.9e6,
@@ -60,7 +71,7 @@ def parse():
                     help="launch the batch directly instead of replaying its CUDA graph")
     ap.add_argument("--lanes", type=int, default=4,
                     help="execution lanes (streams + scratch) for the batched key switches")
-    ap.add_argument("--group", type=int, default=4,
+    ap.add_argument("--group", type=int, default=8,
                     help="key switches each lane pushes through every launch together (1..8)")
     ap.add_argument("--mode", choices=["ib", "oa"], default="ib",
                     help="multi-GPU plan of the key-switch workload: input broadcast (limb-"
@@ -997,7 +1008,8 @@ def run_ours(args, rank, world):
                                          args.lanes, args.group),
                        "cuda_graph": graph is not None,
                        "l2": "inputs (2.3 GB cts + 18.8 GB keys) exceed L2; no flush"},
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": dom, "kernels": STAGE_KERNELS.get(dom),
+                         "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                          "traffic": traffic, "peak_kind": peak_kind,
                          "traffic_source": (PROFILED_TRAFFIC_SOURCE if traffic else None),

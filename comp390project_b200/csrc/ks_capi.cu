@@ -1308,11 +1308,11 @@ void keyswitch_group(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, i
         G.in.elt[b] = m[b].elt;
         G.key[b] = m[b].key->d;
       }
-      // (profiling times the stage on s alone, so it keeps both launches there)
-      const bool fork = !c.profile;
+      // the integer launch on the lane's side stream; the stage timer's
+      // events on s bracket the fork and the join, so a profiled stage is
+      // timed as it runs (both launches overlapped)
       KS_CUDA(modup_rows_inner_product_group(G, L.s_t, m[0].key->limbs, L.s_cx, lv.mu, lv.lay,
-                                             T, s, fork ? L.side : nullptr, L.ev_fork,
-                                             L.ev_join));
+                                             T, s, L.side, L.ev_fork, L.ev_join));
       c.launches += (lv.lay.n_slots_fp > 0 ? 1 : 0) + (lv.lay.n_slots_int > 0 ? 1 : 0);
     } else {  // output aggregation with more ranks than digits: a zero partial sum
       for (int b = 0; b < g; ++b)
