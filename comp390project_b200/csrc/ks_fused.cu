@@ -252,13 +252,20 @@ template <int LOG_M>
 __host__ __device__ constexpr int rows_ip_rows() {  // rows of M words per CTA
   return kRipTile >> LOG_M;
 }
-template <int LOG_M>
+// The FP64 launch stages its CTA's row twiddles in shared memory (true) or
+// reads them from the global table through L1 (false, 16 KB less shared
+// memory per CTA: 4 CTAs per SM instead of 3).  Staged measured faster at
+// config 3 (fused row-pass stage 132 against 139 µs per key switch); the
+// integer launch needs no twiddle stage and runs 4 CTAs per SM either way.
+constexpr bool kRipStageTw = true;
+template <int LOG_M, bool FP_SLOTS>
 __host__ __device__ constexpr size_t rows_ip_smem_bytes() {
   // padded exchange rows + per-warp key stage [warps][2 polys][8 pairs][32 lanes] x 16 B
-  // + the row-pass twiddles of the CTA's rows (FP64 primes; the same for every digit)
+  // + (FP64 launch, staged) the row-pass twiddles of the CTA's rows, the
+  // same for every digit
   return (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) + (1 << LOG_M) / 16) * 8 +
          (size_t)kRipWarps * 2 * 8 * 32 * 16 +
-         (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) - 1) * 8;
+         (FP_SLOTS && kRipStageTw ? (size_t)rows_ip_rows<LOG_M>() * ((1 << LOG_M) - 1) * 8 : 0);
 }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -300,9 +307,15 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
       climb ? climb + (galois_src((uint32_t)tile0, elt, log_n) & ~(uint32_t)(kRipTile - 1))
             : nullptr;
   const ulonglong2 *tw = T.fwd + (long long)prime * N;
-  // FP64 primes: the CTA's row twiddles, staged once in shared memory
-  const TwRowsSmem<LOG_M, rows_ip_rows<LOG_M>()> twf{
-      smtw, (long long)blockIdx.x * rows_ip_rows<LOG_M>(), P.qinv};
+  // FP64 primes: the CTA's row twiddles, staged once in shared memory or
+  // read from the global table
+  const auto twf = [&] {
+    if constexpr (kRipStageTw)
+      return TwRowsSmem<LOG_M, rows_ip_rows<LOG_M>()>{
+          smtw, (long long)blockIdx.x * rows_ip_rows<LOG_M>(), P.qinv};
+    else
+      return TwRowsGlobal<LOG_M>{T.fwd_fp + (long long)prime * N, log_n, P.qinv};
+  }();
   kst += warp * (2 * 8 * 32) + lane;  // [p][i] at kst[(p * 8 + i) * 32]
   // L2 prefetch of digit d's value tile: 128-byte lines (16 words), spread
   // over the CTA's threads.
@@ -500,7 +513,12 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   constexpr uint32_t kWg = FP_SLOTS ? 64 : 128;
   constexpr uint32_t kCols = kWg * (kRipWarps / 4);
   static_assert(kRipWarps == 4 || kRipWarps == 8, "CTA of 4 or 8 warps");
-  static_assert(rows_ip_smem_bytes<LOG_M>() > 232448 / (512 / kCols + 1),
+  // Any mix of the two launches on one SM: at most 232448 / (smallest CTA)
+  // CTAs, each with at most 128 columns.
+  static_assert(kCols <= 128 &&
+                    (rows_ip_smem_bytes<LOG_M, true>() < rows_ip_smem_bytes<LOG_M, false>()
+                         ? rows_ip_smem_bytes<LOG_M, true>()
+                         : rows_ip_smem_bytes<LOG_M, false>()) > 232448 / (512 / 128 + 1),
                 "TMEM columns could be oversubscribed");
   extern __shared__ __align__(16) u64 dsm[];
   __shared__ uint32_t tmem_slot;
@@ -517,12 +535,14 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
   tmem::fence_after_sync();
   // warp w: TMEM lanes 32 (w % 4) .., columns kWg (w / 4) ..
   const uint32_t tacc = tmem_slot + ((uint32_t)(32 * (warp & 3)) << 16) + kWg * (warp >> 2);
-  if (FP_SLOTS) {
-    constexpr int R = rows_ip_rows<LOG_M>();
-    stage_row_twiddles<LOG_M, R, kRipThreads>(smtw, T.fwd_fp + (long long)prime * (1 << T.log_n),
-                                             T.log_n, (long long)blockIdx.x * R);
-    cp_async_wait_all();
-    __syncthreads();
+  if constexpr (FP_SLOTS) {
+    if constexpr (kRipStageTw) {
+      constexpr int R = rows_ip_rows<LOG_M>();
+      stage_row_twiddles<LOG_M, R, kRipThreads>(
+          smtw, T.fwd_fp + (long long)prime * (1 << T.log_n), T.log_n, (long long)blockIdx.x * R);
+      cp_async_wait_all();
+      __syncthreads();
+    }
     rows_ip_body<LOG_M, true, false>(A, mu, lay, T, s, prime, sm, kst, smtw, tacc);
   } else {
     // Every integer prime (q0 below 2^58 as well as the P primes) takes
@@ -542,7 +562,7 @@ __global__ void __launch_bounds__(kRipThreads, 16 / kRipWarps)
 // ModDown: base conversion P -> q_j + forward column pass
 // ---------------------------------------------------------------------------
 template <int LOG_N>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
     k_moddown_cols(const u64 *__restrict__ y_base, const long long *__restrict__ y_off, u64 *z,
                    int n_q, const int *__restrict__ q_index, ModDownDev md, NttTables T,
                    const int *__restrict__ job_ps, int job0, long long y_bstride,
@@ -713,10 +733,11 @@ template <int LOG_M>
 cudaError_t launch_modup_rows_ip(cudaStream_t s, const RowsIpArgs &A, int group,
                                  const ModUpDev &mu, const KsLayout &lay, const NttTables &T,
                                  cudaStream_t side, cudaEvent_t ev_fork, cudaEvent_t ev_join) {
-  constexpr size_t smem = rows_ip_smem_bytes<LOG_M>();
+  constexpr size_t smem_fp = rows_ip_smem_bytes<LOG_M, true>();
+  constexpr size_t smem_int = rows_ip_smem_bytes<LOG_M, false>();
   static std::atomic<unsigned> attr_fp{0}, attr_int{0};
-  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, true>, smem, attr_fp);
-  if (e == cudaSuccess) e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, false>, smem, attr_int);
+  cudaError_t e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, true>, smem_fp, attr_fp);
+  if (e == cudaSuccess) e = ensure_dynamic_smem(k_modup_rows_ip<LOG_M, false>, smem_int, attr_int);
   if (e != cudaSuccess) return e;
   // the integer slots (longer per tile, few tiles) on the side stream when
   // there is one, overlapping the FP64 launch on s
@@ -729,12 +750,12 @@ cudaError_t launch_modup_rows_ip(cudaStream_t s, const RowsIpArgs &A, int group,
       si = side;
     }
     const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_int, group);
-    k_modup_rows_ip<LOG_M, false><<<grid, kRipThreads, smem, si>>>(A, mu, lay, T);
+    k_modup_rows_ip<LOG_M, false><<<grid, kRipThreads, smem_int, si>>>(A, mu, lay, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (lay.n_slots_fp > 0) {
     const dim3 grid((1 << T.log_n) / kRipTile, lay.n_slots_fp, group);
-    k_modup_rows_ip<LOG_M, true><<<grid, kRipThreads, smem, s>>>(A, mu, lay, T);
+    k_modup_rows_ip<LOG_M, true><<<grid, kRipThreads, smem_fp, s>>>(A, mu, lay, T);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (fork) {
