@@ -679,6 +679,11 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       KS_CUDA(cudaStreamCreateWithFlags(&ln.side, cudaStreamNonBlocking));
       KS_CUDA(cudaEventCreateWithFlags(&ln.ev_fork, cudaEventDisableTiming));
       KS_CUDA(cudaEventCreateWithFlags(&ln.ev_join, cudaEventDisableTiming));
+      KS_CUDA(cudaStreamCreateWithFlags(&ln.copy, cudaStreamNonBlocking));
+      for (int h = 0; h < 2; ++h) {
+        KS_CUDA(cudaEventCreateWithFlags(&ln.ev_in[h], cudaEventDisableTiming));
+        KS_CUDA(cudaEventCreateWithFlags(&ln.ev_out[h], cudaEventDisableTiming));
+      }
     }
     KS_CUDA(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
   }
@@ -765,6 +770,11 @@ void ctx_free(Ctx &c) {
     if (ln.side) cudaStreamDestroy(ln.side);
     if (ln.ev_fork) cudaEventDestroy(ln.ev_fork);
     if (ln.ev_join) cudaEventDestroy(ln.ev_join);
+    if (ln.copy) cudaStreamDestroy(ln.copy);
+    for (int h = 0; h < 2; ++h) {
+      if (ln.ev_in[h]) cudaEventDestroy(ln.ev_in[h]);
+      if (ln.ev_out[h]) cudaEventDestroy(ln.ev_out[h]);
+    }
     if (li > 0 && ln.comm) ncclCommDestroy(ln.comm);
   }
   c.lanes.clear();
@@ -2038,7 +2048,11 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     const Level &lv = level_of(c, level_limbs);
     const size_t bytes = 2 * (size_t)lv.n_q * c.N * 8;
     const cudaStream_t s = (cudaStream_t)stream;
-    const int g = c.group;
+    // Double buffering: with group >= 2 each lane's staging buffer holds two
+    // halves, and the copies in of a lane's next group (on the lane's copy
+    // stream) overlap the rotation and copies out of its current one.
+    const bool db = c.group >= 2;
+    const int g = db ? c.group / 2 : c.group;
     // Group sizes: the copies are the bottleneck of this path, and the first
     // copy out waits for the first group's copies in and rotations, the last
     // rotations for the last copies in; groups of 1, 2, 4 .. at both ends of
@@ -2068,20 +2082,31 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     // lanes compute
     KS_CUDA(cudaEventRecord(c.ev_fork, s));
     for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
+    if (db)
+      for (int li = 0; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].copy, c.ev_fork, 0));
     for (int gi = 0, i0 = 0; gi < n_groups; i0 += sizes[gi], ++gi) {
       const int li = gi % nl, gs = sizes[gi];
       Ctx::Lane &L = c.lanes[li];
       const cudaStream_t ls = li == 0 ? s : L.stream;
+      const int h = (gi / nl) & 1;  // staging half of this group (alternates per lane)
       u64 *dev[kMaxGroup];
       uint32_t elts[kMaxGroup];
+      const cudaStream_t cs = db ? L.copy : ls;
+      // the half is free once the copies out of the lane's group before last are done
+      if (db) KS_CUDA(cudaStreamWaitEvent(cs, L.ev_out[h], 0));
       for (int b = 0; b < gs; ++b) {
-        dev[b] = L.s_ct + b * c.st_ct;
+        dev[b] = L.s_ct + ((db ? h * g : 0) + b) * c.st_ct;
         elts[b] = elt_of_step(c, steps[i0 + b]);
-        KS_CUDA(cudaMemcpyAsync(dev[b], host_cts[i0 + b], bytes, cudaMemcpyHostToDevice, ls));
+        KS_CUDA(cudaMemcpyAsync(dev[b], host_cts[i0 + b], bytes, cudaMemcpyHostToDevice, cs));
+      }
+      if (db) {
+        KS_CUDA(cudaEventRecord(L.ev_in[h], cs));
+        KS_CUDA(cudaStreamWaitEvent(ls, L.ev_in[h], 0));
       }
       do_apply_galois_group(c, L, dev, elts, gs, level_limbs, ls);
       for (int b = 0; b < gs; ++b)
         KS_CUDA(cudaMemcpyAsync(host_cts[i0 + b], dev[b], bytes, cudaMemcpyDeviceToHost, ls));
+      if (db) KS_CUDA(cudaEventRecord(L.ev_out[h], ls));
     }
     for (int li = 1; li < nl; ++li) {
       KS_CUDA(cudaEventRecord(c.lanes[li].done, c.lanes[li].stream));

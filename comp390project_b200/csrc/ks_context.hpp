@@ -137,6 +137,11 @@ struct Ctx {
     // of the fused row pass overlaps the FP64 launch on it
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    // host-ciphertext path: copies in run on `copy` into one half of the
+    // staging buffer while the other half's group computes; ev_in[h] / ev_out[h]
+    // mark half h filled / emptied
+    cudaStream_t copy = nullptr;
+    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
     u64 *arena = nullptr;
     u64 *s_g = nullptr, *s_coef = nullptr, *s_coef_all = nullptr, *s_t = nullptr,
         *s_cx = nullptr, *s_ysend = nullptr, *s_yall = nullptr, *s_z = nullptr,
