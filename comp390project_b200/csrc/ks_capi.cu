@@ -2082,8 +2082,11 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
     // lanes compute
     KS_CUDA(cudaEventRecord(c.ev_fork, s));
     for (int li = 1; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].stream, c.ev_fork, 0));
-    if (db)
-      for (int li = 0; li < nl; ++li) KS_CUDA(cudaStreamWaitEvent(c.lanes[li].copy, c.ev_fork, 0));
+    // one in-order stream carries every copy in (lane 0's copy stream): the
+    // groups' inputs arrive in batch order, so the last group's copies out
+    // do not wait behind the inputs of every lane
+    const cudaStream_t cs = db ? c.lanes[0].copy : nullptr;
+    if (db) KS_CUDA(cudaStreamWaitEvent(cs, c.ev_fork, 0));
     for (int gi = 0, i0 = 0; gi < n_groups; i0 += sizes[gi], ++gi) {
       const int li = gi % nl, gs = sizes[gi];
       Ctx::Lane &L = c.lanes[li];
@@ -2091,16 +2094,16 @@ int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *step
       const int h = (gi / nl) & 1;  // staging half of this group (alternates per lane)
       u64 *dev[kMaxGroup];
       uint32_t elts[kMaxGroup];
-      const cudaStream_t cs = db ? L.copy : ls;
+      const cudaStream_t cin = db ? cs : ls;
       // the half is free once the copies out of the lane's group before last are done
-      if (db) KS_CUDA(cudaStreamWaitEvent(cs, L.ev_out[h], 0));
+      if (db) KS_CUDA(cudaStreamWaitEvent(cin, L.ev_out[h], 0));
       for (int b = 0; b < gs; ++b) {
         dev[b] = L.s_ct + ((db ? h * g : 0) + b) * c.st_ct;
         elts[b] = elt_of_step(c, steps[i0 + b]);
-        KS_CUDA(cudaMemcpyAsync(dev[b], host_cts[i0 + b], bytes, cudaMemcpyHostToDevice, cs));
+        KS_CUDA(cudaMemcpyAsync(dev[b], host_cts[i0 + b], bytes, cudaMemcpyHostToDevice, cin));
       }
       if (db) {
-        KS_CUDA(cudaEventRecord(L.ev_in[h], cs));
+        KS_CUDA(cudaEventRecord(L.ev_in[h], cin));
         KS_CUDA(cudaStreamWaitEvent(ls, L.ev_in[h], 0));
       }
       do_apply_galois_group(c, L, dev, elts, gs, level_limbs, ls);

@@ -137,9 +137,9 @@ struct Ctx {
     // of the fused row pass overlaps the FP64 launch on it
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-    // host-ciphertext path: copies in run on `copy` into one half of the
-    // staging buffer while the other half's group computes; ev_in[h] / ev_out[h]
-    // mark half h filled / emptied
+    // host-ciphertext path: copies in (on lane 0's `copy` stream, for every
+    // lane) fill one half of the staging buffer while the other half's group
+    // computes; ev_in[h] / ev_out[h] mark half h filled / emptied
     cudaStream_t copy = nullptr;
     cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
     u64 *arena = nullptr;

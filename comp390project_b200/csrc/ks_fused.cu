@@ -26,7 +26,7 @@ namespace {
 using namespace ntt;
 
 template <int LOG_N>
-__global__ void __launch_bounds__(kThreads) k_inv_cols_scaled(LimbMap m, NttTables T,
+__global__ void __launch_bounds__(kThreads, 4) k_inv_cols_scaled(LimbMap m, NttTables T,
                                                              const ulonglong2 *scale) {
   constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points, stride M2
   using G = ColGeom<LOG_M>;

@@ -21,7 +21,7 @@ __device__ __forceinline__ void limb_of(const LimbMap &m, int i, u64 *&ptr, int 
 }
 
 template <int LOG_N, bool FWD>
-__global__ void __launch_bounds__(kThreads) ntt_cols(LimbMap m, NttTables T) {
+__global__ void __launch_bounds__(kThreads, 4) ntt_cols(LimbMap m, NttTables T) {
   constexpr int LOG_M = LOG_N / 2;  // column pass of 2^LOG_M points; stride M2 is a constant
   using G = ColGeom<LOG_M>;
   __shared__ u64 sm[G::SMEM];

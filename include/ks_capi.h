@@ -204,8 +204,8 @@ int ks_rescale(ks_ctx *ctx, const uint64_t *ct, int level_limbs, uint64_t *out, 
  * spread over the lanes, each with its own device staging buffer, so the
  * copies of one lane overlap the key switches of the others; with
  * ks_params.group >= 2 the staging buffer is split in two halves and a
- * lane's next group is copied in (on a copy stream of the lane) while its
- * current group rotates and is copied out.  Asynchronous on `stream`: the
+ * lane's next group is copied in (on one copy stream shared by the lanes,
+ * in batch order) while its current group rotates and is copied out.  Asynchronous on `stream`: the
  * host buffers may be read only after it completes. */
 int ks_rotate_batch_host(ks_ctx *ctx, uint64_t *const *host_cts, const int *steps, int n,
                          int level_limbs, void *stream);
