@@ -453,11 +453,25 @@ void build_level(Ctx &c, Level &lv, int Ql) {
       out.push_back(make_ulonglong2(a1, h_shoup(a1, q)));
     }
   };
-  for (int d = 0; d < lv.beta; ++d)
-    for (int i = 0; i < a; ++i) {
-      const int j = d * a + i;
-      lv.src_slot.h.push_back(j < Ql ? (j % G) * lv.coef_ml + j / G : 0);
-    }
+  // Input all-gather layout: rank r's share of the coefficient-form input
+  // is coef_words words at r * coef_words; its local slot k sits at
+  // slot_off(k), packed (pack42) for k >= 1 when the context packs.
+  {
+    const long long N = c.N, P = c.pk_words;
+    auto slot_off = [&](int k) {
+      return c.pack ? (k == 0 ? 0 : N + (long long)(k - 1) * P) : (long long)k * N;
+    };
+    lv.coef_words = c.pack ? N + (long long)(lv.coef_ml - 1) * P : (long long)lv.coef_ml * N;
+    for (int d = 0; d < lv.beta; ++d)
+      for (int i = 0; i < a; ++i) {
+        const int j = d * a + i;
+        const int k = j / G;
+        const long long w = (long long)(j % G) * lv.coef_words + slot_off(k);
+        lv.src_ref.h.push_back(j < Ql ? (w << 1) | (c.pack && k >= 1 ? 1 : 0) : 0);
+      }
+    if (c.pack)
+      for (int s = 0; s < lv.n_q; ++s) lv.coef_off.h.push_back(slot_off(s));
+  }
   // Job order of the fused column passes: jobs whose target prime takes the
   // integer path (q_0 and the 60-bit special primes) run 2-3x longer than
   // the FP64 ones and use the integer pipes, so they are spread evenly over
@@ -526,7 +540,8 @@ void build_level(Ctx &c, Level &lv, int Ql) {
     up_ints(lv.rs_prime);
     lv.rs_md = ModDownDev{1, last, nullptr, nullptr, lv.rs_pinv, nullptr, nullptr};
   }
-  up_ints(lv.src_slot);
+  up_i64(lv.src_ref);
+  up_i64(lv.coef_off);
   up_ints(lv.rip_fp);
   up_ints(lv.rip_int);
   up_ints(lv.digits);
@@ -626,6 +641,13 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
       c.max_p_own = std::max(c.max_p_own, cnt);
     }
     build_moddown(c);
+    // pack the input all-gather when every limb after q_0 fits 42 bits
+    if (world > 1 && !c.oa() && c.L >= 2) {
+      bool fits = true;
+      for (int j = 1; j < c.L; ++j) fits = fits && c.primes[j] < (1ull << 42);
+      c.pack = fits;
+      c.pk_words = fits ? (long long)kPackWords * c.N / 16 : 0;
+    }
     c.levels.resize(c.L + 1);
     for (int Ql = 1; Ql <= c.L; ++Ql) build_level(c, c.levels[Ql], Ql);
     // scratch, sized for the top level
@@ -633,7 +655,6 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     const size_t N = c.N;
     const bool ib = !c.replicated();  // input broadcast over world > 1 ranks
     const size_t nq = ib ? n_local(rank, world, c.L) : c.L;
-    const size_t ml = ib ? (c.L + world - 1) / world : c.L;
     const size_t n_key_own = c.own_key.size();
     // per member of a group (member strides of the group layout): automorphism
     // output g0, coefficient input (send buffer of the all-gather) and its
@@ -641,8 +662,8 @@ void ctx_init(Ctx &c, const ks_params *prm, int device, int rank, int world, ncc
     // gathered before ModDown, z, and the staging of a host ciphertext
     const size_t g = c.group;
     c.st_g = 2 * nq * N;
-    c.st_coef = ml * N;
-    c.st_coef_all = ib ? world * ml * N : ml * N;
+    c.st_coef = top.coef_words;
+    c.st_coef_all = ib ? world * c.st_coef : c.st_coef;
     c.st_t = (size_t)top.beta * top.n_out * N;
     c.st_cx = 2 * (size_t)top.n_out * N;
     c.st_ys = ib ? (size_t)c.max_p_own * 2 * N : 0;
@@ -732,7 +753,9 @@ void ctx_free(Ctx &c) {
     f(lv.fold_off.d);
     f(lv.y_off.d);
     f(lv.qhatinv);
-    for (DevInts *t : {&lv.src_slot, &lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
+    f(lv.src_ref.d);
+    f(lv.coef_off.d);
+    for (DevInts *t : {&lv.job_d, &lv.job_s, &lv.job_prime, &lv.md_job_ps,
                        &lv.digits, &lv.cx_prime, &lv.intt_prime, &lv.rip_fp, &lv.rip_int})
       f(t->d);
     f(lv.job_off.d);
@@ -1183,7 +1206,6 @@ void allgather_group(Ctx &c, ncclComm_t const &comm, const u64 *send, long long 
 // then the base extension fused into the column pass -> the lane's t.
 void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int g,
                    cudaStream_t s) {
-  const size_t N = c.N;
   const NttTables T = c.tables();
   {
     StageTimer tm(c, ST_INTT_IN, s);
@@ -1193,19 +1215,28 @@ void ks_modup_cols(Ctx &c, Ctx::Lane &L, const Level &lv, const KsMember *m, int
       mi.elt[b] = m[b].elt;
     }
     LimbMap min{const_cast<u64 *>(m[0].in), 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, 0};
-    LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, c.st_coef};
-    KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s, 1, &mi, g));
+    if (c.pack) {
+      // row pass into the lane's t (free until the column pass below), column
+      // pass into the send buffer with the limbs after slot 0 packed
+      LimbMap tmp{L.s_t, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, c.st_t};
+      LimbMap mc{L.s_coef, 0, lv.coef_off.d, lv.intt_prime.d, 0, 1, c.st_coef};
+      KS_CUDA(ntt_inverse_scaled_pack(min, tmp, mc, lv.n_intt, lv.scale_in, T, s, &mi, g, 1));
+    } else {
+      LimbMap mc{L.s_coef, 0, lv.intt_off.d, lv.intt_prime.d, 0, 1, c.st_coef};
+      KS_CUDA(ntt_inverse_scaled(min, mc, lv.n_intt, lv.scale_in, T, s, 1, &mi, g));
+    }
     c.launches += lv.n_intt > 0 ? 2 : 0;
   }
   if (!c.replicated()) {
     StageTimer tm(c, ST_COMM, s);
     allgather_group(c, L.comm, L.s_coef, c.st_coef, L.s_coef_all, c.st_coef_all,
-                    (size_t)lv.coef_ml * N, g, s);
+                    (size_t)lv.coef_words, g, s);
   }
   {
     StageTimer tm(c, ST_MODUP_COLS, s);
-    KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_slot.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
-                             lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s, g, c.st_coef_all, c.st_t));
+    KS_CUDA(modup_fused_cols(L.s_coef_all, lv.src_ref.d, L.s_t, lv.mu, lv.lay, lv.job_d.d,
+                             lv.job_s.d, lv.n_jobs, lv.n_jobs_fp, T, s, g, c.st_coef_all, c.st_t,
+                             c.pack));
     c.launches += lv.n_jobs > 0 ? 1 : 0;
   }
 }

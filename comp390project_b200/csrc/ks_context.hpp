@@ -63,7 +63,13 @@ struct Level {
   int n_jobs = 0, n_jobs_fp = 0;  // jobs with FP64 targets come first
   DevInts md_job_ps;              // [2 * n_q] ModDown jobs p*n_q + s, FP64 targets first
   int n_md_fp = 0;
-  DevInts src_slot;               // [beta * alpha] slot of Q limb d*alpha+i in the gathered input
+  // [beta * alpha] (word offset << 1) | packed of Q limb d*alpha+i in the
+  // gathered input (packed: the 42-bit form of pack42)
+  DevI64 src_ref;
+  // input broadcast with packing: word offsets of the INTT'd owned limbs in
+  // the all-gather send buffer (slot 0 whole, then packed limbs)
+  DevI64 coef_off;
+  long long coef_words = 0;       // words per rank of the input all-gather
   DevInts job_d, job_s, job_prime;  // [n_jobs]
   DevI64 job_off;                 // [n_jobs] word offset of t[d][s]
   // input INTT: the Q limbs this rank extends (owned limbs; in output-aggregation
@@ -157,6 +163,10 @@ struct Ctx {
   long long st_g = 0, st_coef = 0, st_coef_all = 0, st_t = 0, st_cx = 0, st_ys = 0, st_ya = 0,
             st_z = 0, st_ct = 0;
   int max_p_own = 0;
+  // 42-bit packing of the input all-gather (input broadcast, world > 1, every
+  // Q prime after q_0 below 2^42): a packed limb is pk_words = 11 N / 16 words
+  bool pack = false;
+  long long pk_words = 0;
   // comm (lane 0's communicator)
   ncclComm_t comm = nullptr;
   bool own_comm = false;

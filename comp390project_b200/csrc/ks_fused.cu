@@ -57,6 +57,51 @@ __global__ void __launch_bounds__(kThreads, 4) k_inv_cols_scaled(LimbMap m, NttT
   }
 }
 
+// k_inv_cols_scaled from src (the row-pass output) into dst, limbs
+// li >= pack_from in the 42-bit packed form (pack42; their primes are below
+// 2^42 and take the FP64 path), the others in k_inv_cols_scaled's form.
+template <int LOG_N>
+__global__ void __launch_bounds__(kThreads, 4)
+    k_inv_cols_scaled_pack(LimbMap src, LimbMap dst, NttTables T, const ulonglong2 *scale,
+                           int pack_from) {
+  constexpr int LOG_M = LOG_N / 2;
+  using G = ColGeom<LOG_M>;
+  __shared__ u64 sm[G::SMEM];
+  const int li = blockIdx.y;
+  const u64 *a = src.base + (src.offsets ? src.offsets[li] : (long long)li * src.stride) +
+                 (long long)blockIdx.z * src.bstride;
+  u64 *o = dst.base + (dst.offsets ? dst.offsets[li] : (long long)li * dst.stride) +
+           (long long)blockIdx.z * dst.bstride;
+  const int prime = src.prime_tab ? src.prime_tab[li] : src.first_prime + (li % src.period);
+  if (prime < 0) return;
+  const PrimeDev P = T.primes[prime];
+  constexpr int log_n = LOG_N, N = 1 << LOG_N, M2 = N >> LOG_M;
+  const ulonglong2 *tw = T.inv + (long long)prime * N;
+  const int c = threadIdx.x % G::C, t = (threadIdx.x / G::C) & (G::TT - 1);  // known range t < TT
+  const int col = blockIdx.x * G::C + c;
+  const ulonglong2 s0 = scale[2 * li], s1 = scale[2 * li + 1];
+  auto load = [&](int r, int cl) { return a[(long long)r * M2 + cl]; };
+  auto store = [&](int r, int cl, u64 v) { o[(long long)r * M2 + cl] = v; };
+  if (P.q < kFpBound) {
+    const double2 d0 = make_double2(as_fp(s0.x), as_fp(s0.y));
+    const double2 d1 = make_double2(as_fp(s1.x), as_fp(s1.y));
+    const double2 *twc = T.inv_col + ((long long)prime << LOG_M);
+    if (li >= pack_from) {
+      u64 v[kEpt], w[kPackWords];
+      inv_cols_fp_regs<LOG_M>(sm, col, t, c, log_n, twc, P, d0, d1, load, v);
+      pack42(v, w);
+#pragma unroll
+      for (int k = 0; k < kPackWords; ++k) o[(long long)(t * kPackWords + k) * M2 + col] = w[k];
+    } else {
+      inv_cols_fp<LOG_M, true>(sm, col, t, c, log_n, twc, P, d0, d1, load, store);
+    }
+  } else if (P.q < kInvLazyBound) {
+    inv_cols<LOG_M, true>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
+  } else {
+    inv_cols<LOG_M, false>(sm, col, t, c, log_n, tw, P, s0, s1, load, store);
+  }
+}
+
 // Source limbs of the base conversions: scaled coefficient limbs from
 // ntt_inverse_scaled, canonical, stored as the bits of a double for primes
 // below kFpBound and as uint64 otherwise.
@@ -68,11 +113,28 @@ __device__ __forceinline__ u64 src_u64(u64 bits, bool fp_src) {
 //   y = sum_{i < n_src} [v_i * w_i]_{q}  (each term canonical, sum < 8q),
 // reduced to [0, q).  src(i) points at source limb i, fp_src(i) tells its
 // storage (src_u64).
-template <int LOG_M, class Src, class SrcFp>
-__device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M2, int n_src,
-                                           Src &&src, SrcFp &&fp_src, const u64 *w,
-                                           const u64 *wsh, const PrimeDev &P) {
+// The 16 values of this thread's column in source limb s: canonical uint64
+// from the 42-bit packed form (packed) or as stored (the caller converts).
+template <int LOG_M>
+__device__ __forceinline__ void load_src_col(u64 (&v)[kEpt], const u64 *s, int t, int col,
+                                             int M2, bool packed) {
   using G = ColGeom<LOG_M>;
+  if (packed) {
+    u64 w[kPackWords];
+#pragma unroll
+    for (int k = 0; k < kPackWords; ++k) w[k] = __ldg(s + (long long)(t * kPackWords + k) * M2 + col);
+    unpack42(w, v);
+  } else {
+#pragma unroll
+    for (int e = 0; e < kEpt; ++e)
+      v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
+  }
+}
+
+template <int LOG_M, class Src, class SrcFp, class SrcPk>
+__device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M2, int n_src,
+                                           Src &&src, SrcFp &&fp_src, SrcPk &&pk_src,
+                                           const u64 *w, const u64 *wsh, const PrimeDev &P) {
   u64 acc[kEpt];
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) acc[e] = 0;
@@ -80,11 +142,10 @@ __device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M
   for (int i = 0; i < n_src; ++i) {
     const u64 *s = src(i);
     const u64 wi = __ldg(&w[i]), wp = __ldg(&wsh[i]);
-    const bool fs = fp_src(i);
+    const bool pk = pk_src(i);
+    const bool fs = fp_src(i) && !pk;  // packed limbs hold canonical uint64
     u64 v[kEpt];
-#pragma unroll
-    for (int e = 0; e < kEpt; ++e)
-      v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
+    load_src_col<LOG_M>(v, s, t, col, M2, pk);
 #pragma unroll
     for (int e = 0; e < kEpt; ++e) acc[e] += mul_shoup(src_u64(v[e], fs), wi, wp, P.q);
   }
@@ -97,12 +158,11 @@ __device__ __forceinline__ void bconv_fill(u64 (&x)[kEpt], int t, int col, int M
 // stored; a source limb whose prime is not below 2^50 (the 58-bit q_0) is
 // first reduced mod q with the integer Barrett-style reduce_full so that
 // every product input stays below 2^50.
-template <int LOG_M, class Src, class SrcQ>
+template <int LOG_M, class Src, class SrcQ, class SrcPk>
 __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col, int M2,
-                                              int n_src, Src &&src, SrcQ &&src_q,
+                                              int n_src, Src &&src, SrcQ &&src_q, SrcPk &&pk_src,
                                               const u64 *w, const double *wq,
                                               const PrimeDev &P) {
-  using G = ColGeom<LOG_M>;
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) x[e] = 0.0;
 #pragma unroll 1
@@ -110,11 +170,14 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
     const u64 *s = src(i);
     const double wd = (double)__ldg(&w[i]), wqd = __ldg(&wq[i]);
     const u64 qs = src_q(i);
+    const bool pk = pk_src(i);
     u64 v[kEpt];
+    load_src_col<LOG_M>(v, s, t, col, M2, pk);
+    if (pk) {  // canonical uint64 below 2^42
 #pragma unroll
-    for (int e = 0; e < kEpt; ++e)
-      v[e] = __ldg(s + (long long)lidx<LOG_M, G::HI, 4>(t, e) * M2 + col);
-    if (qs < kFpBound) {
+      for (int e = 0; e < kEpt; ++e)
+        x[e] = __dadd_rn(x[e], fp_mulmod(u64_to_fp(v[e]), wd, wqd, P.qd));
+    } else if (qs < kFpBound) {
 #pragma unroll
       for (int e = 0; e < kEpt; ++e) x[e] = __dadd_rn(x[e], fp_mulmod(as_fp(v[e]), wd, wqd, P.qd));
     } else {
@@ -134,9 +197,9 @@ __device__ __forceinline__ void bconv_fill_fp(double (&x)[kEpt], int t, int col,
 // ---------------------------------------------------------------------------
 // The arithmetic path is chosen per CTA from the target prime (FP64 below
 // kFpBound, integer above); jobs are ordered FP64 first.
-template <int LOG_N>
+template <int LOG_N, bool PACKED>
 __global__ void __launch_bounds__(kThreads, 3)
-    k_modup_cols(const u64 *__restrict__ v_all, const int *__restrict__ src_slot, u64 *t,
+    k_modup_cols(const u64 *__restrict__ v_all, const long long *__restrict__ src_ref, u64 *t,
                  ModUpDev mu, KsLayout lay, const int *__restrict__ job_d,
                  const int *__restrict__ job_s, int job0, NttTables T, long long v_bstride,
                  long long t_bstride) {
@@ -153,14 +216,17 @@ __global__ void __launch_bounds__(kThreads, 3)
   const int n_src = min(mu.alpha, mu.Ql - d * mu.alpha);
   const long long wo = ((long long)d * mu.QlP + j) * mu.alpha;
   v_all += blockIdx.z * v_bstride;  // member of the group
-  auto src = [&](int i) { return v_all + (long long)src_slot[d * mu.alpha + i] * N; };
+  // source limb i of digit d: word offset src_ref >> 1 in the gathered input,
+  // 42-bit packed when bit 0 is set
+  auto src = [&](int i) { return v_all + (src_ref[d * mu.alpha + i] >> 1); };
+  auto pk_src = [&](int i) { return PACKED && (src_ref[d * mu.alpha + i] & 1) != 0; };
   u64 *out = t + blockIdx.z * t_bstride + ((long long)d * lay.n_out + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
   if (P.q < kFpBound) {
     const int *src_prime = mu.prime_of + d * mu.alpha;  // Q limb d*alpha+i has prime index d*alpha+i
     auto filld = [&](double (&x)[kEpt]) {
       bconv_fill_fp<LOG_M>(x, tt, col, M2, n_src, src,
-                           [&](int i) { return T.primes[src_prime[i]].q; }, mu.w + wo,
+                           [&](int i) { return T.primes[src_prime[i]].q; }, pk_src, mu.w + wo,
                            mu.wq + wo, P);
     };
     fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_col + ((long long)prime << LOG_M), P, filld,
@@ -169,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     const int *src_prime = mu.prime_of + d * mu.alpha;
     auto fp_src = [&](int i) { return T.primes[src_prime[i]].q < kFpBound; };
     auto fill = [&](u64 (&x)[kEpt]) {
-      bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, fp_src, mu.w + wo, mu.wsh + wo, P);
+      bconv_fill<LOG_M>(x, tt, col, M2, n_src, src, fp_src, pk_src, mu.w + wo, mu.wsh + wo, P);
     };
     const ulonglong2 *tw = T.fwd + (long long)prime * N;
     if (P.q < kFwdLazyBound) fwd_cols<LOG_M, true>(sm, col, tt, c, log_n, tw, P, fill, store);
@@ -583,7 +649,8 @@ __global__ void __launch_bounds__(kThreads, 3)
   auto src = [&](int i) { return y_base + y_off[p * md.alpha + i]; };
   auto fp_src = [&](int i) { return T.primes[md.first_p + i].q < kFpBound; };
   auto fill = [&](u64 (&x)[kEpt]) {
-    bconv_fill<LOG_M>(x, tt, col, M2, md.alpha, src, fp_src, md.w + wo, md.wsh + wo, P);
+    bconv_fill<LOG_M>(x, tt, col, M2, md.alpha, src, fp_src, [](int) { return false; },
+                      md.w + wo, md.wsh + wo, P);
   };
   u64 *out = z + ((long long)p * n_q + s) * N;
   auto store = [&](int r, int cl, u64 v) { out[(long long)r * M2 + cl] = v; };
@@ -592,8 +659,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     // spreads the work over the FP64 and integer pipes
     auto filld = [&](double (&x)[kEpt]) {
       bconv_fill_fp<LOG_M>(x, tt, col, M2, md.alpha, src,
-                           [&](int i) { return T.primes[md.first_p + i].q; }, md.w + wo,
-                           md.wq + wo, P);
+                           [&](int i) { return T.primes[md.first_p + i].q; },
+                           [](int) { return false; }, md.w + wo, md.wq + wo, P);
     };
     fwd_cols_fpd<LOG_M>(sm, col, tt, c, log_n, T.fwd_col + ((long long)j << LOG_M), P, filld,
                         store);
@@ -784,6 +851,27 @@ cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_lim
   return ntt_inverse_cols_scaled(dst, n_limbs, scale, T, s, group);
 }
 
+cudaError_t ntt_inverse_scaled_pack(const LimbMap &src, const LimbMap &tmp, const LimbMap &dst,
+                                    int n_limbs, const ulonglong2 *scale, const NttTables &T,
+                                    cudaStream_t s, const MemberIn *mi, int group, int pack_from) {
+  if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
+  if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
+  if (n_limbs == 0) return cudaSuccess;
+  cudaError_t e = ntt_inverse_rows_only(src, n_limbs, T, s, &tmp, 1, mi, group);
+  if (e != cudaSuccess) return e;
+  const int s1 = T.log_n / 2;
+  dim3 grid(col_tiles(T.log_n, s1), n_limbs, group);
+  switch (T.log_n) {
+    case 12: k_inv_cols_scaled_pack<12><<<grid, kThreads, 0, s>>>(tmp, dst, T, scale, pack_from); break;
+    case 13: k_inv_cols_scaled_pack<13><<<grid, kThreads, 0, s>>>(tmp, dst, T, scale, pack_from); break;
+    case 14: k_inv_cols_scaled_pack<14><<<grid, kThreads, 0, s>>>(tmp, dst, T, scale, pack_from); break;
+    case 15: k_inv_cols_scaled_pack<15><<<grid, kThreads, 0, s>>>(tmp, dst, T, scale, pack_from); break;
+    case 16: k_inv_cols_scaled_pack<16><<<grid, kThreads, 0, s>>>(tmp, dst, T, scale, pack_from); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t ntt_inverse_cols_scaled(const LimbMap &dst, int n_limbs, const ulonglong2 *scale,
                                     const NttTables &T, cudaStream_t s, int group) {
   if (!ntt_supported_log_n(T.log_n) || n_limbs < 0 || n_limbs > 65535) return cudaErrorInvalidValue;
@@ -802,24 +890,30 @@ cudaError_t ntt_inverse_cols_scaled(const LimbMap &dst, int n_limbs, const ulong
   return cudaGetLastError();
 }
 
-cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
+cudaError_t modup_fused_cols(const u64 *v_all, const long long *src_ref, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
                              int n_fp, const NttTables &T, cudaStream_t s, int group,
-                             long long v_bstride, long long t_bstride) {
+                             long long v_bstride, long long t_bstride, bool packed) {
   if (!ntt_supported_log_n(T.log_n) || n_jobs < 0 || n_jobs > 65535) return cudaErrorInvalidValue;
   if (mu.alpha > KS_MAX_ALPHA || n_fp < 0 || n_fp > n_jobs) return cudaErrorInvalidValue;
   if (group < 1 || group > kMaxGroup) return cudaErrorInvalidValue;
   if (n_jobs == 0) return cudaSuccess;
   const int s1 = T.log_n / 2;
   dim3 grid(col_tiles(T.log_n, s1), n_jobs, group);
+#define KS_MODUP_LAUNCH(LN)                                                                   \
+  (packed ? k_modup_cols<LN, true><<<grid, kThreads, 0, s>>>(v_all, src_ref, t, mu, lay, job_d, \
+                                                              job_s, 0, T, v_bstride, t_bstride) \
+          : k_modup_cols<LN, false><<<grid, kThreads, 0, s>>>(v_all, src_ref, t, mu, lay, job_d, \
+                                                               job_s, 0, T, v_bstride, t_bstride))
   switch (T.log_n) {
-    case 12: k_modup_cols<12><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
-    case 13: k_modup_cols<13><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
-    case 14: k_modup_cols<14><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
-    case 15: k_modup_cols<15><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
-    case 16: k_modup_cols<16><<<grid, kThreads, 0, s>>>(v_all, src_slot, t, mu, lay, job_d, job_s, 0, T, v_bstride, t_bstride); break;
+    case 12: KS_MODUP_LAUNCH(12); break;
+    case 13: KS_MODUP_LAUNCH(13); break;
+    case 14: KS_MODUP_LAUNCH(14); break;
+    case 15: KS_MODUP_LAUNCH(15); break;
+    case 16: KS_MODUP_LAUNCH(16); break;
     default: return cudaErrorInvalidValue;
   }
+#undef KS_MODUP_LAUNCH
   return cudaGetLastError();
 }
 

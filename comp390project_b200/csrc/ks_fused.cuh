@@ -17,6 +17,13 @@ namespace ksb {
 cudaError_t ntt_inverse_scaled(const LimbMap &src, const LimbMap &dst, int n_limbs,
                                const ulonglong2 *scale, const NttTables &T, cudaStream_t s,
                                uint32_t elt = 1, const MemberIn *mi = nullptr, int group = 1);
+// ntt_inverse_scaled (with a member's input read as is) through a scratch
+// map: the row pass writes tmp, the column pass reads tmp and writes dst,
+// limbs li >= pack_from in the 42-bit packed form of pack42 (their primes
+// must be below 2^42).
+cudaError_t ntt_inverse_scaled_pack(const LimbMap &src, const LimbMap &tmp, const LimbMap &dst,
+                                    int n_limbs, const ulonglong2 *scale, const NttTables &T,
+                                    cudaStream_t s, const MemberIn *mi, int group, int pack_from);
 // The column pass of ntt_inverse_scaled alone, in place on dst (the inverse
 // row pass already done).
 cudaError_t ntt_inverse_cols_scaled(const LimbMap &dst, int n_limbs, const ulonglong2 *scale,
@@ -38,16 +45,18 @@ struct GroupArgs {
 
 // ModUp: for each job (digit d, output slot s) the column pass of the
 // forward NTT of  y[k] = sum_i v_i[k] * w[d][j][i] mod m_j  (j = out_j[s]),
-// where v_i are the digit's scaled coefficient limbs (v_all at limb slot
-// src_slot[d*alpha + i]).  Result (column pass done) -> t[d][s].
+// where v_i are the digit's scaled coefficient limbs (v_all +
+// (src_ref[d*alpha + i] >> 1) words, in the 42-bit packed form of pack42
+// when bit 0 of src_ref is set).  Result (column pass done) -> t[d][s].
 // n_fp of the jobs have targets below kFpBound (FP64 path); the path is
 // chosen per CTA from the target prime, so the job order is free (the
 // context spreads the integer jobs evenly over the list).
 // group > 1: member b reads v_all + b v_bstride and writes t + b t_bstride.
-cudaError_t modup_fused_cols(const u64 *v_all, const int *src_slot, u64 *t, const ModUpDev &mu,
+cudaError_t modup_fused_cols(const u64 *v_all, const long long *src_ref, u64 *t, const ModUpDev &mu,
                              const KsLayout &lay, const int *job_d, const int *job_s, int n_jobs,
                              int n_fp, const NttTables &T, cudaStream_t s, int group = 1,
-                             long long v_bstride = 0, long long t_bstride = 0);
+                             long long v_bstride = 0, long long t_bstride = 0,
+                             bool packed = false);
 
 // ModUp row pass (t[d][s] from modup_fused_cols, d outside the digit of
 // out_j[s]; that digit reads c_ntt slot c_slot[s]) fused with the inner

@@ -28,6 +28,9 @@ struct LimbMap {
 // third grid dimension is the member).  Buffers the caller owns differ per
 // member and are passed by value; scratch buffers sit at uniform strides.
 constexpr int kMaxGroup = 8;
+// Words of one thread's 16 column values in the 42-bit packed form (pack42):
+// a packed limb of N words takes kPackWords * N / 16.
+constexpr int kPackWords = 11;
 struct MemberIn {             // per-member input limbs read through an automorphism
   const u64 *in[kMaxGroup];   // null in[0]: use the LimbMap's own base
   uint32_t elt[kMaxGroup];

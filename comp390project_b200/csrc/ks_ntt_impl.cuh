@@ -16,6 +16,7 @@
 // contiguous words.
 #pragma once
 #include "ks_arith.cuh"
+#include "ks_ntt.cuh"
 
 namespace ksb {
 namespace ntt {
@@ -122,6 +123,32 @@ struct ColGeom {
   static constexpr int HI = LOG_M - 4, NLO = LOG_M - 4;
   static constexpr int SMEM = M * C;  // words
 };
+// 42-bit packing of one thread's column values (the kEpt = 16 words at rows
+// lidx<LOG_M, HI, 4>(t, e) of its column, each below 2^42): five triplets in
+// two words each (a | b << 42, b >> 22 | c << 20) and the last value alone,
+// 11 words; word w of thread t of a column sits at row t * 11 + w of the
+// packed limb (11 N / 16 words).  The input all-gather of input broadcast
+// moves limbs in this form (kPackWords, ks_ntt.cuh).
+__device__ __forceinline__ void pack42(const u64 (&v)[16], u64 (&w)[kPackWords]) {
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const u64 a = v[3 * k], b = v[3 * k + 1], c = v[3 * k + 2];
+    w[2 * k] = a | (b << 42);
+    w[2 * k + 1] = (b >> 22) | (c << 20);
+  }
+  w[10] = v[15];
+}
+__device__ __forceinline__ void unpack42(const u64 (&w)[kPackWords], u64 (&v)[16]) {
+  constexpr u64 m42 = (1ull << 42) - 1, m20 = (1ull << 20) - 1;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    v[3 * k] = w[2 * k] & m42;
+    v[3 * k + 1] = (w[2 * k] >> 42) | ((w[2 * k + 1] & m20) << 22);
+    v[3 * k + 2] = w[2 * k + 1] >> 20;
+  }
+  v[15] = w[10];
+}
+
 template <int LOG_M>
 struct RowGeom {
   static constexpr int M = 1 << LOG_M, LOG_T = LOG_M - 4, TT = 1 << LOG_T, R = kThreads / TT;
@@ -438,6 +465,28 @@ __device__ __forceinline__ void inv_cols_fp(u64 *sm, int col, int t, int c, int 
     else
       store(lidx<LOG_M, G::HI, 4>(t, e), col, fp_to_canon(x[e], P.qd, P.qinv));
   }
+}
+
+// inv_cols_fp with the canonical outputs (times the last-stage scale) left
+// in registers: out[e] is row lidx<LOG_M, HI, 4>(t, e) of the column.
+template <int LOG_M, class Load>
+__device__ __forceinline__ void inv_cols_fp_regs(u64 *sm, int col, int t, int c, int log_n,
+                                                 const double2 *tw, const PrimeDev &P, double2 s0,
+                                                 double2 s1, Load &&load, u64 (&out)[kEpt]) {
+  using G = ColGeom<LOG_M>;
+  const TwCols<LOG_M> twg{tw};
+  double x[kEpt];
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(load(lidx<LOG_M, 0, G::NLO>(t, e), col));
+  inv_round_fp<LOG_M, 0, G::NLO, false>(x, t, 0, twg, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) sm[lidx<LOG_M, 0, G::NLO>(t, e) * G::C + c] = fp_bits(x[e]);
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) x[e] = as_fp(sm[lidx<LOG_M, G::HI, 4>(t, e) * G::C + c]);
+  inv_round_fp<LOG_M, G::HI, 4, true>(x, t, 0, twg, P, s0, s1);
+#pragma unroll
+  for (int e = 0; e < kEpt; ++e) out[e] = fp_to_canon(x[e], P.qd, P.qinv);
 }
 
 // Forward row pass; the tile holds first-pass bits; canonical outputs in xo
