@@ -372,13 +372,15 @@ NVLINK_GBS = 770.0
 NVLINK_NOMINAL_GBS = 900.0  # NVLink 5, per direction per GPU
 
 
-def collective_roofline(prof, n_ks, L, alpha, world, N, oa=False):
+def collective_roofline(prof, n_ks, L, alpha, world, N, oa=False, packed=False):
     """NVLink roofline of the collectives from the serial profile.  Input
     broadcast: per key switch a rank receives the other ranks' padded shares
     of the coefficient-form input ((G-1) ceil(L/G) limbs) and of the
-    special-prime limbs of cx ((G-1) 2 max_r |P limbs of r| limbs).  Output
-    aggregation: the all-reduce of cx (2 (L+alpha) limbs), which a ring
-    all-reduce moves as 2 (G-1)/G of the buffer into every rank."""
+    special-prime limbs of cx ((G-1) 2 max_r |P limbs of r| limbs); with
+    42-bit packing (`packed`) a rank's share of the input is one whole limb
+    plus ceil(L/G) - 1 limbs of 11/16 of the size.  Output aggregation: the
+    all-reduce of cx (2 (L+alpha) limbs), which a ring all-reduce moves as
+    2 (G-1)/G of the buffer into every rank."""
     ms, calls = prof.get("collective", (0.0, 0))
     if world <= 1 or ms <= 0 or n_ks <= 0:
         return None
@@ -388,7 +390,8 @@ def collective_roofline(prof, n_ks, L, alpha, world, N, oa=False):
         coef_ml = -(-L // world)
         max_p_own = max(sum(1 for i in range(alpha) if (L + i) % world == r)
                         for r in range(world))
-        recv = (world - 1) * (coef_ml + 2 * max_p_own) * N * 8
+        share = (1 + (coef_ml - 1) * 11 / 16) if packed else coef_ml
+        recv = int((world - 1) * (share + 2 * max_p_own) * N * 8)
     t = ms / n_ks / 1000.0
     ach = recv / t / 1e9
     return {"bound": "nvlink", "bytes_received_per_ks": recv, "ms_per_ks": ms / n_ks,
@@ -988,7 +991,9 @@ def run_ours(args, rank, world):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_config3()
-    nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N, oa=oa)
+    # the context packs the input all-gather when every Q prime after q0 is below 2^42
+    packed = not oa and world > 1 and all(int(x) < (1 << 42) for x in q[1:])
+    nvlink = collective_roofline(prof, prof_ks, L, len(p), world, N, oa=oa, packed=packed)
     # the second half of the headline metric: config 2's NTT on the same GPUs
     # (every rank, after the key-switch measurements)
     ntt = None
