@@ -59,8 +59,15 @@ __global__ void __launch_bounds__(kThreads, 4) ntt_cols(LimbMap m, NttTables T) 
 // elt (inverse direction only): the input is read through the automorphism
 // X -> X^elt (input slot galois_src(i) feeds slot i; the tile gathers from
 // one aligned source tile); elt = 1 reads it as it is.
+// The row twiddles of FP64 primes: staged per CTA in shared memory (true)
+// or read from the global table through L1 (false: no twiddle block, 4 CTAs
+// per SM).  Each CTA uses its twiddles once, so staging only adds a copy:
+// reading them from L1 took the config-2 forward transform from 2.20 to
+// 1.99 ms and the inverse from 2.43 to 2.14 ms.
+constexpr bool kRowsStageTw = false;
 template <int LOG_M, bool FWD>
-__global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttTables T,
+__global__ void __launch_bounds__(kThreads, kRowsStageTw ? 3 : 4)
+    ntt_rows(LimbMap m, LimbMap mo, NttTables T,
                                                      uint32_t elt,
                                                      const __grid_constant__ MemberIn mi) {
   using G = RowGeom<LOG_M>;
@@ -89,15 +96,18 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
   const long long row0 = (long long)blockIdx.x * G::R, row = row0 + rr;
   u64 x[kEpt];
   const bool fp = P.q < kFpBound;
-  if (fp) {
-    stage_row_twiddles<LOG_M, G::R>(smtw, (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N,
-                                    log_n, row0);
-  }
+  const double *twfp = (FWD ? T.fwd_fp : T.inv_fp) + (long long)prime * N;
+  if (kRowsStageTw && fp) stage_row_twiddles<LOG_M, G::R>(smtw, twfp, log_n, row0);
+  const TwRowsGlobal<LOG_M> twg{twfp, log_n, P.qinv};
   if (FWD) {
     if (fp) {
-      cp_async_wait_all();
-      __syncthreads();
-      fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
+      if (kRowsStageTw) {
+        cp_async_wait_all();
+        __syncthreads();
+        fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
+      } else {
+        fwd_rows_regs_fp_tw<LOG_M, true>(x, sm, twg, tile, t, rr, row, P);
+      }
     } else if (P.q < kFwdLazyBound) {
       fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
     } else {
@@ -128,9 +138,12 @@ __global__ void __launch_bounds__(kThreads) ntt_rows(LimbMap m, LimbMap mo, NttT
             stile[galois_src(t0 + lin, elt, log_n) & (uint32_t)(kTile - 1)];
       }
     }
-    if (fp) cp_async_wait_all();
+    if (kRowsStageTw && fp) cp_async_wait_all();
     __syncthreads();
-    if (fp) inv_rows_regs_fp<LOG_M>(x, sm, smtw, t, rr, row, row0, P);
+    if (fp) {
+      if (kRowsStageTw) inv_rows_regs_fp<LOG_M>(x, sm, smtw, t, rr, row, row0, P);
+      else inv_rows_regs_fp_tw<LOG_M>(x, sm, twg, t, rr, row, P);
+    }
     else if (P.q < kInvLazyBound) inv_rows_regs<LOG_M, true>(x, sm, t, rr, row, log_n, tw, P);
     else inv_rows_regs<LOG_M, false>(x, sm, t, rr, row, log_n, tw, P);
 #pragma unroll
@@ -149,7 +162,8 @@ template <int LOG_M, bool FWD>
 cudaError_t launch_rows(const LimbMap &m, const LimbMap &mo, int n_limbs, const NttTables &T,
                         cudaStream_t s, uint32_t elt = 1, const MemberIn *mi = nullptr,
                         int group = 1) {
-  constexpr size_t smem = row_smem_bytes<LOG_M>();
+  constexpr size_t smem =
+      kRowsStageTw ? row_smem_bytes<LOG_M>() : (size_t)RowGeom<LOG_M>::SMEM * 8;
   static std::atomic<unsigned> attr_done{0};
   cudaError_t e = ensure_dynamic_smem(ntt_rows<LOG_M, FWD>, smem, attr_done);
   if (e != cudaSuccess) return e;

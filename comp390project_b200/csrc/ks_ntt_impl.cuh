@@ -532,12 +532,11 @@ __device__ __forceinline__ void fwd_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const
 
 // Inverse row pass (first pass) over a tile staged in smem as canonical
 // uint64; outputs (bits of doubles, |x| <= q/2 + 1) in xo, pattern HI.
-template <int LOG_M>
-__device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
-                                                 int t, int rr, long long row, long long row0,
-                                                 const PrimeDev &P) {
+template <int LOG_M, class Tw>
+__device__ __forceinline__ void inv_rows_regs_fp_tw(u64 (&xo)[kEpt], u64 *sm, const Tw &tw,
+                                                    int t, int rr, long long row,
+                                                    const PrimeDev &P) {
   using G = RowGeom<LOG_M>;
-  const TwRowsSmem<LOG_M, G::R> tw{smtw, row0, P.qinv};
   const double2 none = make_double2(0, 0);
   double x[kEpt];
 #pragma unroll
@@ -551,6 +550,13 @@ __device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const
   inv_round_fp<LOG_M, G::HI, 4, false>(x, t, row, tw, P, none, none);
 #pragma unroll
   for (int e = 0; e < kEpt; ++e) xo[e] = fp_bits(fp_reduce_sym(x[e], P.qd, P.qinv));
+}
+template <int LOG_M>
+__device__ __forceinline__ void inv_rows_regs_fp(u64 (&xo)[kEpt], u64 *sm, const double *smtw,
+                                                 int t, int rr, long long row, long long row0,
+                                                 const PrimeDev &P) {
+  const TwRowsSmem<LOG_M, RowGeom<LOG_M>::R> tw{smtw, row0, P.qinv};
+  inv_rows_regs_fp_tw<LOG_M>(xo, sm, tw, t, rr, row, P);
 }
 
 // Shared memory of a row-pass CTA: the exchange buffer then (FP64 path) the
