@@ -678,9 +678,13 @@ struct MdGroup {
   const u64 *g0[kMaxGroup];
 };
 
+// FP64 row twiddles of the ModDown row pass from the global table through L1
+// (each CTA uses its rows' twiddles once) with no shared-memory twiddle
+// block: 4 CTAs per SM.
+constexpr bool kMdRowsStageTw = false;
 // Row pass of z with the ModDown finish fused into the epilogue.
 template <int LOG_M>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, kMdRowsStageTw ? 3 : 4)
     k_moddown_rows(const u64 *__restrict__ z, int n_q, const int *__restrict__ q_index,
                    const int *__restrict__ cx_slot, const u64 *__restrict__ cx,
                    long long cx_stride_poly, const __grid_constant__ MdGroup grp, int rotate,
@@ -708,7 +712,8 @@ __global__ void __launch_bounds__(kThreads)
   const u64 *g0t = g0 ? g0 + (long long)s * N + tile0 : nullptr;
   const u64 *base = (p == 0) ? (rotate ? g0t : dst) : (rotate ? nullptr : dst);
   const bool fp = P.q < kFpBound;
-  if (fp) stage_row_twiddles<LOG_M, G::R>(smtw, T.fwd_fp + (long long)j * N, log_n, row0);
+  if (kMdRowsStageTw && fp)
+    stage_row_twiddles<LOG_M, G::R>(smtw, T.fwd_fp + (long long)j * N, log_n, row0);
   // Pull the epilogue operands into L2 while the butterflies run: one
   // prefetch per 128-byte line of the tile (4096 words = 256 lines).
   {
@@ -718,9 +723,14 @@ __global__ void __launch_bounds__(kThreads)
   }
   u64 x[kEpt];
   if (fp) {
-    cp_async_wait_all();
-    __syncthreads();
-    fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
+    if (kMdRowsStageTw) {
+      cp_async_wait_all();
+      __syncthreads();
+      fwd_rows_regs_fp<LOG_M>(x, sm, smtw, tile, t, rr, row, row0, P);
+    } else {
+      const TwRowsGlobal<LOG_M> twg{T.fwd_fp + (long long)j * N, log_n, P.qinv};
+      fwd_rows_regs_fp_tw<LOG_M, true>(x, sm, twg, tile, t, rr, row, P);
+    }
   } else {
     const ulonglong2 *tw = T.fwd + (long long)j * N;
     if (P.q < kFwdLazyBound) fwd_rows_regs<LOG_M, true>(x, sm, tile, t, rr, row, log_n, tw, P);
@@ -787,7 +797,8 @@ cudaError_t launch_moddown_rows(dim3 grid, cudaStream_t s, const u64 *z, int n_q
                                const int *q_index, const int *cx_slot, const u64 *cx,
                                long long cx_stride_poly, const MdGroup &grp, int rot,
                                const u64 *diag, const ModDownDev &md, const NttTables &T) {
-  constexpr size_t smem = row_smem_bytes<LOG_M>();
+  constexpr size_t smem =
+      kMdRowsStageTw ? row_smem_bytes<LOG_M>() : (size_t)RowGeom<LOG_M>::SMEM * 8;
   static std::atomic<unsigned> attr_done{0};
   cudaError_t e = ensure_dynamic_smem(k_moddown_rows<LOG_M>, smem, attr_done);
   if (e != cudaSuccess) return e;
