@@ -81,7 +81,8 @@ def partition_ref():
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT", "/root/reference")
+    default = os.path.join(os.path.dirname(ROOT), "reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REF_ROOT", default)
     with open(os.path.join(HERE, "prime_kat.json"), "w") as f:
         json.dump(prime_kat(ref), f, indent=1)
     with open(os.path.join(HERE, "partition_ref.json"), "w") as f:
