@@ -54,8 +54,8 @@ STAGE_KERNELS = {
     "moddown_rows": "k_moddown_rows",
 }
 PROFILED_TRAFFIC = {
-    "galois": 25.7e6, "intt_input": 55.4e6, "modup_cols": 133.7e6, "modup_rows_ip": 500.4e6,
-    "intt_p": 5.3e6, "moddown_cols": 27.5e6, "moddown_rows": 146.9e6,
+    "galois": 25.7e6, "intt_input": 55.3e6, "modup_cols": 133.5e6, "modup_rows_ip": 498.2e6,
+    "intt_p": 5.3e6, "moddown_cols": 29.0e6, "moddown_rows": 160.7e6,
 }
 
 
