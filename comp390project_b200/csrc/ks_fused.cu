@@ -255,21 +255,27 @@ __device__ __forceinline__ u64 ip_term_fp(u64 acc, u64 y, u64 k, bool first, boo
 }
 
 // One integer inner-product term on a 128-bit sum held as four 32-bit TMEM
-// words r[c..c+4): sum += y k, and every 32 digits sum := sum mod q.
-__device__ __forceinline__ void ip_acc128(uint32_t (&r)[8], int c, u64 y, u64 k, bool first,
-                                          bool recentre, const PrimeDev &P) {
+// words r[c..c+4): sum += y k.
+__device__ __forceinline__ void ip_acc128(uint32_t (&r)[8], int c, u64 y, u64 k, bool first) {
   u128v acc;
   acc.lo = first ? 0ull : tmem::pack(r[c], r[c + 1]);
   acc.hi = first ? 0ull : tmem::pack(r[c + 2], r[c + 3]);
   mac(acc, y, k);
-  if (recentre) {
-    acc.lo = barrett128(acc, P.q, P.br_hi, P.br_lo);
-    acc.hi = 0;
-  }
   r[c] = (uint32_t)acc.lo;
   r[c + 1] = (uint32_t)(acc.lo >> 32);
   r[c + 2] = (uint32_t)acc.hi;
   r[c + 3] = (uint32_t)(acc.hi >> 32);
+}
+// sum := sum mod q in place (every 32 digits, so that 32 more products fit).
+__device__ __forceinline__ void acc128_to_reduced(uint32_t (&r)[8], int c, const PrimeDev &P) {
+  u128v acc;
+  acc.lo = tmem::pack(r[c], r[c + 1]);
+  acc.hi = tmem::pack(r[c + 2], r[c + 3]);
+  const u64 v = barrett128(acc, P.q, P.br_hi, P.br_lo);
+  r[c] = (uint32_t)v;
+  r[c + 1] = (uint32_t)(v >> 32);
+  r[c + 2] = 0;
+  r[c + 3] = 0;
 }
 __device__ __forceinline__ u64 acc128_reduce(const uint32_t (&r)[8], int c, const PrimeDev &P) {
   u128v acc;
@@ -483,12 +489,24 @@ __device__ __forceinline__ void rows_ip_body(const RowsIpArgs &A, const ModUpDev
           tmem::ld8(tacc + 64 + 8 * i, r1);
           tmem::wait_ld(r0, r1);
         }
-        ip_acc128(r0, 0, v.x, k0.x, first, recentre, P);
-        ip_acc128(r0, 4, v.y, k0.y, first, recentre, P);
-        ip_acc128(r1, 0, v.x, k1.x, first, recentre, P);
-        ip_acc128(r1, 4, v.y, k1.y, first, recentre, P);
+        ip_acc128(r0, 0, v.x, k0.x, first);
+        ip_acc128(r0, 4, v.y, k0.y, first);
+        ip_acc128(r1, 0, v.x, k1.x, first);
+        ip_acc128(r1, 4, v.y, k1.y, first);
         tmem::st8(tacc + 8 * i, r0);
         tmem::st8(tacc + 64 + 8 * i, r1);
+      }
+      if (recentre) {  // rare (every 32 digits): kept out of the unrolled loop
+        tmem::wait_st();
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i) {
+          uint32_t r[8];
+          tmem::ld8(tacc + 8 * i, r);
+          tmem::wait_ld(r);
+          acc128_to_reduced(r, 0, P);
+          acc128_to_reduced(r, 4, P);
+          tmem::st8(tacc + 8 * i, r);
+        }
       }
     }
     tmem::wait_st();

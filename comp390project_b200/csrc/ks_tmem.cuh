@@ -56,6 +56,12 @@ __device__ __forceinline__ void wait_ld(uint32_t (&a)[8], uint32_t (&b)[8]) {
                  "+r"(a[6]), "+r"(a[7]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]),
                  "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]));
 }
+// Waits for this thread's outstanding tcgen05.ld into one register block.
+__device__ __forceinline__ void wait_ld(uint32_t (&a)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+                 "+r"(a[6]), "+r"(a[7]));
+}
 __device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
                    taddr),

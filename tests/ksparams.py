@@ -24,6 +24,9 @@ REFTEST = dict(log_n=13, qbits=(60, 40, 40, 40), pbits=(60,))
 # (N = 16384; and 32768): column pass of 2^7 points
 N14 = dict(log_n=14, qbits=(50, 40, 40, 40), pbits=(55, 55))
 N15 = dict(log_n=15, qbits=(55,) + (40,) * 4, pbits=(58, 58, 58))
+# one special prime, so every Q prime is a digit: 34 digits, more than the 32
+# products the inner product sums before it reduces its accumulators
+MANYDIG = dict(log_n=12, qbits=(50,) + (40,) * 33, pbits=(55,))
 
 
 def split(cfg):
@@ -35,7 +38,7 @@ def split(cfg):
 @functools.lru_cache(maxsize=None)
 def oracle_for(name):
     cfg = {"cfg1": CFG1, "cfg3": CFG3, "small": SMALL, "reftest": REFTEST, "n14": N14,
-           "n15": N15}[name]
+           "n15": N15, "manydig": MANYDIG}[name]
     log_n, q, p = split(cfg)
     return Oracle(log_n, q, p)
 

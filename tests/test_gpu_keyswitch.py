@@ -2,7 +2,7 @@
 import numpy as np
 import pytest
 
-from tests.ksparams import CFG1, CFG3, SMALL, oracle_for, split
+from tests.ksparams import CFG1, CFG3, MANYDIG, SMALL, oracle_for, split
 
 pytestmark = pytest.mark.gpu
 
@@ -120,7 +120,9 @@ def _encrypted(o, Ql, seed, s):
 
 
 @pytest.mark.parametrize("name,cfg,Ql,step", [("cfg1", CFG1, 3, 1), ("small", SMALL, 7, 5),
-                                              ("small", SMALL, 5, -3), ("small", SMALL, 1, 2)])
+                                              ("small", SMALL, 5, -3), ("small", SMALL, 1, 2),
+                                              ("manydig", MANYDIG, 34, 3),
+                                              ("manydig", MANYDIG, 33, -1)])
 def test_rotate_bitexact(name, cfg, Ql, step, cuda_device):
     o = oracle_for(name)
     ctx = _ctx(cfg)
