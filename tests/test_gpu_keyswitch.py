@@ -303,15 +303,18 @@ def test_rotate_batch_groups(name, lanes, group, n, cuda_device):
     ctx.close()
 
 
-def test_rotate_batch_host_matches_device_batch(cuda_device):
+@pytest.mark.parametrize("lanes,group,n", [(2, 2, 5), (1, 1, 3), (2, 8, 21), (3, 4, 13)])
+def test_rotate_batch_host_matches_device_batch(lanes, group, n, cuda_device):
     """ks_rotate_batch_host (host ciphertexts, copies pipelined over lanes)
-    returns the words of ks_rotate_batch on device copies."""
+    returns the words of ks_rotate_batch on device copies: a single staging
+    buffer per lane (group 1), and double-buffered staging with the tapered
+    group sizes, several groups per lane and each half reused."""
     from comp390project_b200 import KS_KEY_GALOIS, KsContext
     o = oracle_for("small")
     log_n, q, p = split(SMALL)
-    ctx = KsContext(log_n, q, p, device=0, max_batch=2, batch_group=2)
+    ctx = KsContext(log_n, q, p, device=0, max_batch=lanes, batch_group=group)
     s = o.secret(8, 64)
-    steps = [1, 2, 3, 1, 2]
+    steps = [1 + i % 3 for i in range(n)]
     for st in sorted(set(steps)):
         e = o.galois_elt(st)
         ctx.key_upload(KS_KEY_GALOIS, e, o.keygen_galois(s, e, 80 + st))
