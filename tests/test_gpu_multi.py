@@ -3,8 +3,10 @@ communicators created by the library from an id broadcast over a gloo
 process group.  Input broadcast: every rank holds its cyclic share of the
 limbs and the gathered result must equal the single-process CPU oracle bit
 for bit.  Output aggregation: every rank holds the whole ciphertext and its
-digits of the key, and every rank's result must equal the oracle.  Skipped
-when fewer than two GPUs are visible."""
+digits of the key, and every rank's result must equal the oracle.  Rank 0
+evaluates the oracle references and every rank compares a digest of its
+result with rank 0's, so the CPU oracle runs once per check, not once per
+rank.  Skipped when fewer than two GPUs are visible."""
 import os
 import sys
 
@@ -20,6 +22,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _worker(rank, world, port, q, name, mode):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    # the ranks share the host's cores for the oracle's OpenMP loops
+    os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // world))
+    import hashlib
+
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -69,12 +75,22 @@ def _worker(rank, world, port, q, name, mode):
                 full[:, j] = out[j % world][:, j // world].numpy().view(np.uint64)
             return full
 
+        def check(full, ref):
+            """Every rank's full result must equal rank 0's (a digest over
+            gloo), and rank 0 alone evaluates the oracle reference `ref()`."""
+            h = int.from_bytes(hashlib.sha256(np.ascontiguousarray(full).tobytes()).digest()[:8],
+                               "little", signed=True)
+            t = torch.tensor([h], dtype=torch.int64)
+            dist.broadcast(t, 0)
+            same = int(t.item()) == h
+            return same and (rank != 0 or np.array_equal(full, ref()))
+
         ok = True
         # single rotation
         d = local(cts[0])
         ctx.rotate(d, Ql, steps[0])
         torch.cuda.synchronize()
-        ok &= np.array_equal(gather(d, 2), o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
+        ok &= check(gather(d, 2), lambda: o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
         # batch of three: a group of two on lane 0 (grouped all-gathers /
         # all-reduce) and a group of one on lane 1 (its own split communicator)
         bsteps = steps + [1]
@@ -82,12 +98,13 @@ def _worker(rank, world, port, q, name, mode):
         ctx.rotate_batch(ds, bsteps, Ql)
         torch.cuda.synchronize()
         for c, dd, st in zip(cts, ds, bsteps):
-            ok &= np.array_equal(gather(dd, 2), o.apply_galois(c, Ql, o.galois_elt(st), keys[st]))
+            ok &= check(gather(dd, 2),
+                        lambda c=c, st=st: o.apply_galois(c, Ql, o.galois_elt(st), keys[st]))
         # relinearisation
         d3 = local(c3)
         ctx.relinearize(d3, Ql)
         torch.cuda.synchronize()
-        ok &= np.array_equal(gather(d3, 2), o.relinearize(c3, Ql, rk))
+        ok &= check(gather(d3, 2), lambda: o.relinearize(c3, Ql, rk))
         # a lower level (short last digit)
         Ql2 = Ql - 3
         c2 = cts[0][:, :Ql2]
@@ -105,7 +122,7 @@ def _worker(rank, world, port, q, name, mode):
             full2 = np.zeros((2, Ql2, N), dtype=np.uint64)
             for j in range(Ql2):
                 full2[:, j] = outs[j % world][:, j // world].numpy().view(np.uint64)
-        ok &= np.array_equal(full2, o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
+        ok &= check(full2, lambda: o.apply_galois(c2, Ql2, o.galois_elt(1), keys[1]))
         # key distribution: rank 0 holds the full key on its device, every
         # rank receives its shard over NCCL point-to-point
         ctx.key_drop(KS_KEY_GALOIS, o.galois_elt(1))
@@ -114,7 +131,7 @@ def _worker(rank, world, port, q, name, mode):
         dk = local(cts[0])
         ctx.rotate(dk, Ql, 1)
         torch.cuda.synchronize()
-        ok &= np.array_equal(gather(dk, 2), o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
+        ok &= check(gather(dk, 2), lambda: o.apply_galois(cts[0], Ql, o.galois_elt(1), keys[1]))
         # rescale: the owner of the last limb broadcasts it (input broadcast)
         mine3 = list(range(rank, Ql - 1, world)) if not oa else list(range(Ql - 1))
         dr = local(cts[1])
